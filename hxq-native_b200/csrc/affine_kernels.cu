@@ -1,0 +1,240 @@
+// affine_kernels.cu -- affine group-quantized fused matmul on sm_100a.
+//
+//   Y[n,o] = sum_g ( s[o,g] * sum_{k in g} x[n,k]*q[o,k]
+//                  + off[o,g] * sum_{k in g} x[n,k] ) + bias[o]
+// (reference hxq-native src/hxq_affine.c:23-66; GPU entry points replace
+// src/hxq_affine_cuda.cu:184-294).
+//
+// Streaming dequant-GEMV for small token counts: one warp per output row,
+// 16 codes per lane per 128-bit load, codes widened to fp32 exactly with a
+// byte permute into the mantissa of 2^23, token activations read through
+// L1, the group scale applied per 16-code slice and the offset term from
+// the slice's activation sum, one warp reduction per row, bias fused into
+// the store.  Larger token counts use the tcgen05 GEMM (affine_gemm.cu)
+// when the shape allows it.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hxq_affine.h"
+#include "hxq_cuda.h"
+
+namespace hxq {
+namespace {
+
+constexpr int kGemvTokens = 8;   // tokens per pass of the GEMV
+
+__device__ __forceinline__ float code_to_float(uint32_t word, uint32_t i)
+{
+    // [byte_i, 0, 0, 0x4B] is the float 2^23 + byte_i; subtracting 2^23 is exact
+    return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u + i)) - 8388608.0f;
+}
+
+template <typename XT> struct XLoad;
+template <> struct XLoad<float> {
+    // 16 consecutive activations
+    static __device__ __forceinline__ void load16(const float *p, float v[16])
+    {
+        const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 t = __ldg(q + i);
+            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+        }
+    }
+};
+template <> struct XLoad<uint16_t> {
+    static __device__ __forceinline__ void load16(const uint16_t *p, float v[16])
+    {
+        const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint4 t = __ldg(q + i);
+            const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+                v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+            }
+        }
+    }
+};
+
+template <typename XT> __device__ __forceinline__ float xval(const XT *p);
+template <> __device__ __forceinline__ float xval<float>(const float *p) { return *p; }
+template <> __device__ __forceinline__ float xval<uint16_t>(const uint16_t *p)
+{
+    return __uint_as_float((uint32_t)*p << 16);
+}
+
+// Requirements: group_size % 16 == 0, in_f % 16 == 0, x and codes 16-B aligned.
+template <typename XT, int NT>
+__global__ void __launch_bounds__(256)
+affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
+                   const float *__restrict__ scales, const float *__restrict__ offsets,
+                   const float *__restrict__ bias, float *__restrict__ y,
+                   uint32_t n0, uint32_t ntok, uint32_t in_f, uint32_t out_f,
+                   uint32_t gs)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t ng = in_f / gs;
+    const uint32_t slices = in_f / 16u;
+    for (uint32_t o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_f; o += warps) {
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        const uint4 *crow = reinterpret_cast<const uint4 *>(codes + (size_t)o * in_f);
+        for (uint32_t sl = lane; sl < slices; sl += 32u) {
+            const uint4 cw = __ldg(crow + sl);
+            float q[16];
+            const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) q[4 * j + b] = code_to_float(w[j], (uint32_t)b);
+            const uint32_t g = (sl * 16u) / gs;
+            const float s = __ldg(scales + (size_t)o * ng + g);
+            const float f = __ldg(offsets + (size_t)o * ng + g);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if ((uint32_t)t < ntok) {
+                    float xv[16];
+                    XLoad<XT>::load16(x + (size_t)(n0 + t) * in_f + sl * 16u, xv);
+                    float dot = 0.0f, xs = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        dot = fmaf(xv[i], q[i], dot);
+                        xs += xv[i];
+                    }
+                    acc[t] = fmaf(s, dot, fmaf(f, xs, acc[t]));
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            float v = acc[t];
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+            acc[t] = v;
+        }
+        if (lane == 0) {
+            const float bo = bias ? __ldg(bias + o) : 0.0f;
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if ((uint32_t)t < ntok) y[(size_t)(n0 + t) * out_f + o] = acc[t] + bo;
+        }
+    }
+}
+
+// Any shape: one thread per output, the reference's loop order.
+template <typename XT>
+__global__ void affine_generic_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
+                                      const float *__restrict__ scales,
+                                      const float *__restrict__ offsets,
+                                      const float *__restrict__ bias, float *__restrict__ y,
+                                      uint32_t N, uint32_t in_f, uint32_t out_f, uint32_t gs)
+{
+    const uint32_t ng = in_f / gs;
+    const uint64_t total = (uint64_t)N * out_f;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t n = (uint32_t)(i / out_f), o = (uint32_t)(i - (uint64_t)n * out_f);
+        const XT *xr = x + (size_t)n * in_f;
+        const uint8_t *qr = codes + (size_t)o * in_f;
+        float acc = 0.0f;
+        for (uint32_t g = 0; g < ng; ++g) {
+            float dot = 0.0f, xs = 0.0f;
+            for (uint32_t k = g * gs; k < (g + 1u) * gs; ++k) {
+                const float xv = xval<XT>(xr + k);
+                dot = __fadd_rn(dot, __fmul_rn(xv, (float)qr[k]));
+                xs = __fadd_rn(xs, xv);
+            }
+            acc = __fadd_rn(acc, __fadd_rn(__fmul_rn(scales[(size_t)o * ng + g], dot),
+                                           __fmul_rn(offsets[(size_t)o * ng + g], xs)));
+        }
+        if (bias) acc = __fadd_rn(acc, bias[o]);
+        y[i] = acc;
+    }
+}
+
+bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
+
+template <typename XT>
+int run_affine(const XT *x, const uint8_t *codes, const float *scales, const float *offsets,
+               const float *bias, float *y, uint32_t N, uint32_t in_f, uint32_t out_f,
+               uint32_t gs, cudaStream_t s)
+{
+    if (!x || !codes || !scales || !offsets || !y) return -1;
+    if (gs == 0 || in_f % gs != 0) return -1;
+    if (N == 0 || out_f == 0) return 0;
+    if (in_f == 0) {  // empty reduction: bias only
+        affine_generic_kernel<XT><<<1, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
+        return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    const bool fast = gs % 16u == 0 && in_f % 16u == 0 && aligned(x, 16) && aligned(codes, 16);
+    if (fast) {
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        uint32_t blocks = (out_f + 7u) / 8u;
+        const uint32_t cap = (uint32_t)sms * 8u;
+        if (blocks > cap) blocks = cap;
+        for (uint32_t n0 = 0; n0 < N; n0 += kGemvTokens) {
+            const uint32_t nt = N - n0 < (uint32_t)kGemvTokens ? N - n0 : (uint32_t)kGemvTokens;
+            if (nt == 1)
+                affine_gemv_kernel<XT, 1><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+            else if (nt <= 4)
+                affine_gemv_kernel<XT, 4><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+            else
+                affine_gemv_kernel<XT, kGemvTokens><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+        }
+    } else {
+        uint64_t blocks = ((uint64_t)N * out_f + 255u) / 256u;
+        if (blocks > 148u * 32u) blocks = 148u * 32u;
+        affine_generic_kernel<XT><<<(uint32_t)blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+}  // namespace hxq
+
+extern "C" {
+
+int hxq_affine_group_matmul(const float *d_x, const hxq_affine_tensor_t *t, float *d_output,
+                            uint32_t N)
+{
+    if (!t) return -1;
+    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, d_output, N,
+                                  t->in_features, t->out_features, t->group_size, (cudaStream_t)0);
+}
+
+int hxq_affine_matmul_flat(const float *d_x, const uint8_t *d_indices, const float *d_scales,
+                           const float *d_offsets, const float *d_bias, float *d_output,
+                           uint32_t N, uint32_t in_f, uint32_t out_f, uint32_t group_size)
+{
+    return hxq::run_affine<float>(d_x, d_indices, d_scales, d_offsets, d_bias, d_output, N, in_f,
+                                  out_f, group_size, (cudaStream_t)0);
+}
+
+int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t,
+                                 float *d_output, uint32_t N, void *stream)
+{
+    if (!t) return -1;
+    return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias,
+                                     d_output, N, t->in_features, t->out_features,
+                                     t->group_size, static_cast<cudaStream_t>(stream));
+}
+
+int hxq_affine_group_matmul_async(const float *d_x, const hxq_affine_tensor_t *t,
+                                  float *d_output, uint32_t N, void *stream)
+{
+    if (!t) return -1;
+    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, d_output, N,
+                                  t->in_features, t->out_features, t->group_size,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

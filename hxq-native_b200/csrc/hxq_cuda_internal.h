@@ -1,0 +1,112 @@
+// hxq_cuda_internal.h -- structures shared by the CUDA runtime layer and the
+// sm_100a kernels of the HXQ decompress path.  Internal; not installed.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "hxq_cuda.h"
+
+namespace hxq {
+
+// A chunk is the unit of work of one warp: 2048 consecutive weights of one
+// job.  12-bit indices: 512 byte triples = 1536 B.  Scalar: 2048 B.
+constexpr uint32_t kChunkW        = 2048;
+constexpr uint32_t kChunkBytes12  = 1536;
+constexpr uint32_t kChunkBytes8   = 2048;
+constexpr uint32_t kWarps         = 8;      // warps per CTA of the fast kernel
+constexpr uint32_t kThreads       = kWarps * 32;
+constexpr uint32_t kMaxJobs       = HXQ_CUDA_MAX_BATCH;
+// Device index buffers are padded by this much past the last whole chunk so
+// the unpack may read one word beyond a chunk without leaving the buffer.
+constexpr uint32_t kIdxPad        = 16;
+
+enum ImageKind : uint32_t {
+    kKindScalar   = 0,   // uint8 indices, fast kernel
+    kKindVq12     = 1,   // 12-bit, in_features % 4 == 0, fast kernel
+    kKindVq12Any  = 2,   // 12-bit, any in_features, generic kernel
+    kKindAffine   = 3,   // affine codes, generic kernel
+    kKindRaw      = 4,   // corrections on an existing buffer (read-modify-write)
+};
+
+// Sidecar entry as stored on the device.  Entries are stably sorted by
+// position, so equal coordinates are adjacent and keep array order.
+//   fast kinds:    x = (offset in chunk) | (run length << 16); run length is
+//                  0 on all but the first entry of a run of equal positions.
+//   generic kinds: x = flat position in the image; y = value bits.
+struct SideEntry { uint32_t x; uint32_t y; };
+
+// One job of a launch of the fast kernel.
+struct VqJob {
+    const uint4     *idx;        // chunk-padded index bytes
+    const float     *cb;         // fp32 codebook, k * vdim floats
+    const uint32_t  *chunk_ptr;  // [n_chunks + 1] first entry of each chunk
+    const SideEntry *ent;        // sidecar entries
+    void            *out;        // fp32 or bf16 output, 16-B aligned
+    uint64_t         numel;      // weights in the job
+    uint64_t         chunk_begin;// first global chunk index of the job
+    uint32_t         n_chunks;
+    uint32_t         k;          // codebook entries (index bound)
+    uint32_t         slot_base;  // first reduction slot of the job
+    uint32_t         cta_lo;     // first CTA whose range meets the job
+    uint32_t         n_cta;      // CTAs whose range meets the job
+    uint32_t         pad_;
+    double          *sumsq;      // optional device output
+    float           *conf;       // optional device output
+};
+
+struct VqLaunch {
+    VqJob     job[kMaxJobs];
+    uint32_t  n_jobs;
+    uint32_t  grid;
+    uint64_t  total_chunks;
+    double   *slots;             // reduction slots (scratch)
+    uint32_t *counters;          // per-job arrival counters (scratch, zero)
+    uint32_t *err;               // device error word (scratch)
+};
+
+// Device scratch owned by the runtime, one per (device, stream).  The
+// decompress kernels leave `counters` at zero when they finish.
+struct Scratch {
+    double   *slots     = nullptr;
+    uint32_t  n_slots   = 0;
+    uint32_t *counters  = nullptr;   // kMaxJobs
+    uint32_t *err       = nullptr;   // 1 word
+    double   *sumsq     = nullptr;   // kMaxJobs results for internal calls
+    float    *conf      = nullptr;   // kMaxJobs
+};
+
+// Error bits written to the device error word.
+constexpr uint32_t kErrIndexOOB = 1u;
+
+// Launch helpers implemented in vq_kernels.cu.  All return cudaError_t of
+// the launch.  `sms` is the device's SM count.
+cudaError_t configure_vq_kernels();
+cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
+                           int check_k, cudaStream_t s);
+uint32_t    fast_grid(uint64_t total_chunks, int sms);
+
+// Generic kernels (any shape/alignment; one image per launch).
+struct GenericJob {
+    uint32_t          kind;       // kKindScalar / kKindVq12Any / kKindAffine / kKindVq12
+    const uint8_t    *idx;        // raw index bytes of the image rows
+    const float      *cb;
+    const float      *scales;     // affine
+    const float      *offsets;    // affine
+    uint32_t          rows, in_f, k, gs;
+    uint32_t          triples_per_row; // 12-bit
+    const SideEntry  *ent;        // sidecar entries
+    uint32_t          n_ent;
+    // non-null when `ent` uses the chunk-relative encoding of fast images
+    const uint32_t   *chunk_ptr;
+    uint32_t          n_chunks;
+    void             *out;
+    int               bf16;
+    double           *sumsq;
+    float            *conf;
+};
+cudaError_t launch_generic(const GenericJob &j, const Scratch &sc,
+                           cudaStream_t s);
+
+}  // namespace hxq

@@ -1,0 +1,1096 @@
+// hxq_cuda_rt.cu -- host runtime of the CUDA backend (C-ABI layer).
+//
+// Owns everything the kernels need that the reference API does not carry:
+//   * a side table from hxq_tensor_t* to the tensor's device image (the
+//     struct layout is frozen by the reference ABI, so device state cannot
+//     live in it);
+//   * the registry of device arenas (hxq_shared_buffer_t with HBM data);
+//   * per (device, stream) scratch for the kernels' reductions and errors;
+//   * image construction: index bytes padded to whole chunks, codebook,
+//     sidecar entries filtered to the reference's in-range rule, stably
+//     sorted by position and indexed per chunk;
+//   * launch planning for batched decompress.
+// Every CUDA error is mapped to an hxq status; nothing falls back to the CPU.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <numeric>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "hxq_cuda_internal.h"
+#include "hxq_internal.h"
+
+using namespace hxq;
+
+struct hxq_cuda_image {
+    int       device = -1;
+    uint32_t  kind = 0;
+    uint32_t  rows = 0, in_f = 0, k = 0, vdim = 0, gs = 0;
+    uint32_t  triples_per_row = 0;
+    uint64_t  numel = 0;
+    bool      check_k = false;
+    // one block holding every array below, laid out at the offsets o_*;
+    // resident images own d_block, streamed images keep h_block (pinned)
+    // and point d_block at wherever hxq_cuda_image_upload copied it
+    void     *d_block = nullptr;
+    void     *h_block = nullptr;
+    bool      owns_device = false;
+    size_t    block_bytes = 0;
+    size_t    o_idx = 0, o_cb = 0, o_sc = 0, o_of = 0, o_cp = 0, o_en = 0;
+    bool      has_cb = false, has_aff = false, has_cp = false;
+    uint8_t  *d_idx = nullptr;
+    float    *d_cb = nullptr;
+    float    *d_scales = nullptr, *d_offsets = nullptr;
+    uint32_t *d_chunk_ptr = nullptr;
+    SideEntry *d_ent = nullptr;
+    uint32_t  n_chunks = 0;
+    uint32_t  n_ent = 0;
+    double    sumsq = 0.0;
+};
+
+namespace {
+
+std::mutex g_mu;
+std::atomic<unsigned long long> g_launches{0};
+
+struct Snapshot {
+    const float *codebook; uint32_t k, vdim;
+    const uint8_t *idx; size_t idx_len;
+    const uint32_t *sr, *sc; const float *sv; uint32_t nnz;
+    uint32_t out_f, in_f; int mode;
+    const float *as, *ao; uint32_t gs;
+    int device;
+    bool operator==(const Snapshot &o) const { return std::memcmp(this, &o, sizeof(*this)) == 0; }
+};
+
+Snapshot snap(const hxq_tensor_t *t, int device)
+{
+    Snapshot s;
+    std::memset(&s, 0, sizeof(s));
+    s.codebook = t->codebook; s.k = t->k; s.vdim = t->vector_dim;
+    s.idx = t->indices_raw; s.idx_len = t->indices_len;
+    s.sr = t->sidecar_rows; s.sc = t->sidecar_cols; s.sv = t->sidecar_vals; s.nnz = t->sidecar_nnz;
+    s.out_f = t->out_features; s.in_f = t->in_features; s.mode = (int)t->mode;
+    s.as = t->affine_scales; s.ao = t->affine_offsets; s.gs = t->affine_group_size;
+    s.device = device;
+    return s;
+}
+
+struct Cached { Snapshot snap; hxq_cuda_image *img; };
+std::unordered_map<const hxq_tensor_t *, Cached> g_images;
+std::unordered_map<const hxq_shared_buffer_t *, int> g_arenas;   // buf -> device
+
+struct DevCtx {
+    bool      ready = false;
+    int       sms = 0;
+    std::map<cudaStream_t, Scratch> scratch;
+    void     *readback = nullptr;     // pinned host, 4 KB
+    float    *stage = nullptr;        // internal device buffer for host-buffer dequant
+    size_t    stage_floats = 0;
+};
+constexpr int kMaxDev = 64;
+DevCtx g_dev[kMaxDev];
+int g_cuda_present = -1;
+
+hxq_error_t map_cuda(cudaError_t e)
+{
+    if (e == cudaSuccess) return HXQ_OK;
+    if (e == cudaErrorMemoryAllocation) return HXQ_ERR_ALLOC_FAILED;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return HXQ_ERR_BACKEND_UNAVAILABLE;
+    return HXQ_ERR_CUDA;
+}
+
+bool cuda_present()
+{
+    if (g_cuda_present < 0) {
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess) cudaGetLastError();
+        g_cuda_present = (e == cudaSuccess && n > 0) ? 1 : 0;
+    }
+    return g_cuda_present == 1;
+}
+
+// Driver entry point, resolved without linking libcuda.
+typedef CUresult (*PrimaryCtxGetStateFn)(CUdevice, unsigned int *, int *);
+PrimaryCtxGetStateFn primary_state_fn()
+{
+    static PrimaryCtxGetStateFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuDevicePrimaryCtxGetState", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PrimaryCtxGetStateFn>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// True when some device already has an active primary context, i.e. device
+// memory may exist in this process.  Never creates a context itself.
+bool any_context_active()
+{
+    PrimaryCtxGetStateFn fn = primary_state_fn();
+    if (!fn) return true;  // cannot tell: let the pointer query decide
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return false; }
+    for (int d = 0; d < n; ++d) {
+        unsigned int flags = 0; int active = 0;
+        if (fn((CUdevice)d, &flags, &active) == CUDA_SUCCESS && active) return true;
+    }
+    return false;
+}
+
+hxq_error_t current_device(int *dev)
+{
+    if (!cuda_present()) return HXQ_ERR_BACKEND_UNAVAILABLE;
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess || *dev < 0 || *dev >= kMaxDev) { cudaGetLastError(); return HXQ_ERR_CUDA; }
+    return HXQ_OK;
+}
+
+// Per-device setup; caller holds g_mu.
+hxq_error_t dev_ready(int dev)
+{
+    DevCtx &d = g_dev[dev];
+    if (d.ready) return HXQ_OK;
+    int sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = configure_vq_kernels();
+    if (e == cudaSuccess) e = cudaMallocHost(&d.readback, 4096);
+    if (e != cudaSuccess) { cudaGetLastError(); return map_cuda(e); }
+    d.sms = sms;
+    d.ready = true;
+    return HXQ_OK;
+}
+
+// Scratch layout: [err u32 x 4][conf f32 x kMaxJobs][sumsq f64 x kMaxJobs]
+// [counters u32 x kMaxJobs][slots f64 x n_slots].  Zeroed once; kernels
+// leave counters at zero.  Caller holds g_mu.
+hxq_error_t get_scratch(int dev, cudaStream_t s, Scratch **out)
+{
+    DevCtx &d = g_dev[dev];
+    auto it = d.scratch.find(s);
+    if (it != d.scratch.end()) { *out = &it->second; return HXQ_OK; }
+    const uint32_t n_slots = (uint32_t)(kMaxJobs + 8u * (uint32_t)std::max(d.sms, 148) + 1024u);
+    const size_t bytes = 16 + kMaxJobs * 4 + kMaxJobs * 8 + kMaxJobs * 4 + (size_t)n_slots * 8;
+    unsigned char *base = nullptr;
+    cudaError_t e = cudaMalloc(&base, bytes);
+    if (e == cudaSuccess) e = cudaMemset(base, 0, bytes);
+    if (e != cudaSuccess) { cudaGetLastError(); if (base) cudaFree(base); return map_cuda(e); }
+    Scratch sc;
+    sc.err = reinterpret_cast<uint32_t *>(base);
+    sc.conf = reinterpret_cast<float *>(base + 16);
+    sc.sumsq = reinterpret_cast<double *>(base + 16 + kMaxJobs * 4);
+    sc.counters = reinterpret_cast<uint32_t *>(base + 16 + kMaxJobs * 12);
+    sc.slots = reinterpret_cast<double *>(base + 16 + kMaxJobs * 16);
+    sc.n_slots = n_slots;
+    auto res = d.scratch.emplace(s, sc);
+    *out = &res.first->second;
+    return HXQ_OK;
+}
+
+size_t align256(size_t x) { return (x + 255u) & ~(size_t)255u; }
+
+// ---------------------------------------------------------------------------
+// Image construction
+
+struct HostEntry { uint64_t pos; float val; };
+
+// Sidecar entries of rows [r0, r1) that the reference would apply (r < out_f
+// and c < in_f, src/hxq.c:343), in array order, positions relative to r0.
+void collect_sidecar(const hxq_tensor_t *t, uint32_t r0, uint32_t r1,
+                     std::vector<HostEntry> &ents, double &sumsq)
+{
+    sumsq = 0.0;
+    ents.clear();
+    if (t->sidecar_nnz == 0 || !t->sidecar_rows || !t->sidecar_cols || !t->sidecar_vals) return;
+    const uint32_t in_f = t->in_features, out_f = t->out_features;
+    for (uint32_t i = 0; i < t->sidecar_nnz; ++i) {
+        const uint32_t r = t->sidecar_rows[i], c = t->sidecar_cols[i];
+        if (r >= out_f || c >= in_f || r < r0 || r >= r1) continue;
+        const float v = t->sidecar_vals[i];
+        ents.push_back({(uint64_t)(r - r0) * in_f + c, v});
+        sumsq += (double)v * (double)v;
+    }
+    bool sorted = true;
+    for (size_t i = 1; i < ents.size() && sorted; ++i) sorted = ents[i - 1].pos <= ents[i].pos;
+    if (!sorted)
+        std::stable_sort(ents.begin(), ents.end(),
+                         [](const HostEntry &a, const HostEntry &b) { return a.pos < b.pos; });
+}
+
+// Error the reference decoder reports for a 12-bit stream that is too
+// short: INDEX_OOB if an index before the shortfall is >= k, else
+// PACK_FORMAT (src/hxq.c:262,271 -- length is checked before the indices
+// of each triple).
+hxq_error_t short_stream_error(const hxq_tensor_t *t, size_t start, size_t avail_bytes)
+{
+    const size_t n_trip = avail_bytes / 3u;
+    for (size_t i = 0; i < n_trip; ++i) {
+        uint16_t a, b;
+        hxq_unpack_12bit_pair(t->indices_raw + start + 3u * i, &a, &b);
+        if (a >= t->k || b >= t->k) return HXQ_ERR_INDEX_OOB;
+    }
+    return HXQ_ERR_PACK_FORMAT;
+}
+
+// Point the image's device arrays into a block at `base` (layout o_*).
+void bind_image(hxq_cuda_image *img, void *base)
+{
+    unsigned char *b = static_cast<unsigned char *>(base);
+    img->d_block = base;
+    img->d_idx = b + img->o_idx;
+    img->d_cb = img->has_cb ? reinterpret_cast<float *>(b + img->o_cb) : nullptr;
+    img->d_scales = img->has_aff ? reinterpret_cast<float *>(b + img->o_sc) : nullptr;
+    img->d_offsets = img->has_aff ? reinterpret_cast<float *>(b + img->o_of) : nullptr;
+    img->d_chunk_ptr = img->has_cp ? reinterpret_cast<uint32_t *>(b + img->o_cp) : nullptr;
+    img->d_ent = reinterpret_cast<SideEntry *>(b + img->o_en);
+}
+
+hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev,
+                        bool streamed, hxq_cuda_image **out)
+{
+    if (!t || !out) return HXQ_ERR_NULL_PTR;
+    if (!t->indices_raw) return HXQ_ERR_NULL_PTR;
+    if (t->mode != HXQ_AFFINE_G128 && !t->codebook) return HXQ_ERR_NULL_PTR;
+    if (r0 > r1 || r1 > t->out_features) return HXQ_ERR_INVALID_ARG;
+
+    hxq_cuda_image *img = new (std::nothrow) hxq_cuda_image();
+    if (!img) return HXQ_ERR_ALLOC_FAILED;
+    img->device = dev;
+    img->rows = r1 - r0;
+    img->in_f = t->in_features;
+    img->k = t->k;
+    img->vdim = t->vector_dim;
+    img->numel = (uint64_t)img->rows * img->in_f;
+
+    size_t idx_off = 0, idx_len = 0;   // byte range of the rows in indices_raw
+    switch (t->mode) {
+    case HXQ_SCALAR_VQ: {
+        img->kind = kKindScalar;
+        idx_off = (size_t)r0 * img->in_f;
+        idx_len = (size_t)img->numel;
+        if (idx_off + idx_len > t->indices_len) { delete img; return HXQ_ERR_PACK_FORMAT; }
+        break;
+    }
+    case HXQ_VQ2D_12BIT: {
+        // The reference reads cb[2*idx+1] whatever vector_dim is; with
+        // vector_dim 1 that leaves the codebook, so it is refused here.
+        if (t->vector_dim != 2) { delete img; return HXQ_ERR_INVALID_DIM; }
+        const uint32_t ppr = img->in_f / 2u;
+        img->triples_per_row = (ppr + 1u) / 2u;
+        idx_off = (size_t)r0 * img->triples_per_row * 3u;
+        idx_len = (size_t)img->rows * img->triples_per_row * 3u;
+        if (idx_off + idx_len > t->indices_len) {
+            const size_t avail = t->indices_len > idx_off ? t->indices_len - idx_off : 0;
+            hxq_error_t e = short_stream_error(t, idx_off, avail);
+            delete img;
+            return e;
+        }
+        img->kind = (img->in_f % 4u == 0u) ? kKindVq12 : kKindVq12Any;
+        img->check_k = t->k < 4096u;
+        break;
+    }
+    case HXQ_AFFINE_G128: {
+        if (!t->affine_scales || !t->affine_offsets || t->affine_group_size == 0 ||
+            img->in_f % t->affine_group_size != 0) { delete img; return HXQ_ERR_NULL_PTR; }
+        img->kind = kKindAffine;
+        img->gs = t->affine_group_size;
+        idx_off = (size_t)r0 * img->in_f;
+        idx_len = (size_t)img->numel;
+        if (idx_off + idx_len > t->indices_len) { delete img; return HXQ_ERR_PACK_FORMAT; }
+        break;
+    }
+    default:
+        delete img;
+        return HXQ_ERR_INVALID_DIM;
+    }
+
+    std::vector<HostEntry> ents;
+    collect_sidecar(t, r0, r1, ents, img->sumsq);
+    const bool fast = img->kind == kKindScalar || img->kind == kKindVq12;
+    if (!fast && img->numel > 0xFFFFFFFFull) { delete img; return HXQ_ERR_INVALID_ARG; }
+
+    // device-side sidecar encoding
+    std::vector<SideEntry> dev_ents(ents.size());
+    std::vector<uint32_t> chunk_ptr;
+    if (fast) {
+        img->n_chunks = (uint32_t)((img->numel + kChunkW - 1) / kChunkW);
+        chunk_ptr.assign((size_t)img->n_chunks + 1u, 0u);
+        size_t i = 0;
+        while (i < ents.size()) {
+            size_t jx = i;
+            while (jx < ents.size() && ents[jx].pos == ents[i].pos) ++jx;
+            const size_t run = jx - i;
+            if (run > 0xFFFFu) { delete img; return HXQ_ERR_INVALID_ARG; }
+            const uint32_t off = (uint32_t)(ents[i].pos % kChunkW);
+            for (size_t m = i; m < jx; ++m) {
+                uint32_t bits;
+                std::memcpy(&bits, &ents[m].val, 4);
+                dev_ents[m].x = off | (m == i ? (uint32_t)run << 16 : 0u);
+                dev_ents[m].y = bits;
+            }
+            i = jx;
+        }
+        // chunk_ptr[c] = first entry whose chunk >= c
+        size_t e = 0;
+        for (uint32_t c = 0; c <= img->n_chunks; ++c) {
+            while (e < ents.size() && ents[e].pos / kChunkW < c) ++e;
+            chunk_ptr[c] = (uint32_t)e;
+        }
+    } else {
+        for (size_t m = 0; m < ents.size(); ++m) {
+            uint32_t bits;
+            std::memcpy(&bits, &ents[m].val, 4);
+            dev_ents[m].x = (uint32_t)ents[m].pos;
+            dev_ents[m].y = bits;
+        }
+    }
+    img->n_ent = (uint32_t)dev_ents.size();
+
+    // one block: idx | cb | scales | offsets | chunk_ptr | entries
+    const size_t chunk_bytes = img->kind == kKindVq12 ? kChunkBytes12 : kChunkBytes8;
+    const size_t idx_alloc = fast ? (size_t)img->n_chunks * chunk_bytes + kIdxPad
+                                  : std::max<size_t>(idx_len, 16);
+    const size_t cb_floats = img->kind == kKindAffine ? 0 : (size_t)t->k * t->vector_dim;
+    const size_t ng = img->gs ? img->in_f / img->gs : 0;
+    const size_t aff_floats = img->kind == kKindAffine ? (size_t)img->rows * ng : 0;
+    size_t off = 0;
+    img->o_idx = off;  off = align256(off + idx_alloc);
+    img->o_cb = off;   off = align256(off + cb_floats * 4);
+    img->o_sc = off;   off = align256(off + aff_floats * 4);
+    img->o_of = off;   off = align256(off + aff_floats * 4);
+    img->o_cp = off;   off = align256(off + chunk_ptr.size() * 4);
+    img->o_en = off;   off = align256(off + std::max<size_t>(dev_ents.size(), 1) * sizeof(SideEntry));
+    img->block_bytes = off;
+    img->has_cb = cb_floats > 0;
+    img->has_aff = aff_floats > 0;
+    img->has_cp = !chunk_ptr.empty();
+
+    unsigned char *hb = nullptr;
+    cudaError_t ce;
+    if (streamed) {
+        ce = cudaHostAlloc(reinterpret_cast<void **>(&hb), img->block_bytes, cudaHostAllocDefault);
+        if (ce != cudaSuccess) { cudaGetLastError(); delete img; return map_cuda(ce); }
+    } else {
+        hb = static_cast<unsigned char *>(std::malloc(img->block_bytes));
+        if (!hb) { delete img; return HXQ_ERR_ALLOC_FAILED; }
+    }
+    std::memset(hb, 0, img->block_bytes);
+    if (idx_len) std::memcpy(hb + img->o_idx, t->indices_raw + idx_off, idx_len);
+    if (cb_floats) std::memcpy(hb + img->o_cb, t->codebook, cb_floats * 4);
+    if (aff_floats) {
+        std::memcpy(hb + img->o_sc, t->affine_scales + (size_t)r0 * ng, aff_floats * 4);
+        std::memcpy(hb + img->o_of, t->affine_offsets + (size_t)r0 * ng, aff_floats * 4);
+    }
+    if (!chunk_ptr.empty()) std::memcpy(hb + img->o_cp, chunk_ptr.data(), chunk_ptr.size() * 4);
+    if (!dev_ents.empty()) std::memcpy(hb + img->o_en, dev_ents.data(), dev_ents.size() * sizeof(SideEntry));
+
+    if (streamed) {
+        img->h_block = hb;
+    } else {
+        unsigned char *blk = nullptr;
+        ce = cudaMalloc(&blk, img->block_bytes);
+        if (ce == cudaSuccess) ce = cudaMemcpy(blk, hb, img->block_bytes, cudaMemcpyHostToDevice);
+        std::free(hb);
+        if (ce != cudaSuccess) {
+            cudaGetLastError();
+            if (blk) cudaFree(blk);
+            delete img;
+            return map_cuda(ce);
+        }
+        img->owns_device = true;
+        bind_image(img, blk);
+    }
+    *out = img;
+    return HXQ_OK;
+}
+
+void destroy_image(hxq_cuda_image *img)
+{
+    if (!img) return;
+    if (img->h_block) cudaFreeHost(img->h_block);
+    if (img->d_block && img->owns_device) {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (cur != img->device) cudaSetDevice(img->device);
+        cudaFree(img->d_block);
+        if (cur >= 0 && cur != img->device) cudaSetDevice(cur);
+        cudaGetLastError();
+    }
+    delete img;
+}
+
+// ---------------------------------------------------------------------------
+// Launch planning
+
+bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// CTA c of a fast launch covers chunks [f(c), f(c+1)), f(c) = total*c/grid.
+uint64_t cta_begin(uint64_t total, uint32_t grid, uint32_t c) { return total * c / grid; }
+
+// First CTA whose range contains chunk `ch` (largest c with f(c) <= ch).
+uint32_t cta_of(uint64_t total, uint32_t grid, uint64_t ch)
+{
+    uint32_t lo = 0, hi = grid - 1;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo + 1) / 2;
+        if (cta_begin(total, grid, mid) <= ch) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
+                              hxq_cuda_image *const *imgs, char *out_base,
+                              const size_t *offs, size_t elem, int bf16,
+                              double *d_sumsq, float *d_conf, const Scratch &sc,
+                              int sms, cudaStream_t s)
+{
+    if (which.empty()) return HXQ_OK;
+    VqLaunch p;
+    std::memset(&p, 0, sizeof(p));
+    uint64_t total = 0;
+    for (uint32_t n = 0; n < which.size(); ++n) {
+        const uint32_t i = which[n];
+        const hxq_cuda_image *im = imgs[i];
+        VqJob &J = p.job[n];
+        J.idx = reinterpret_cast<const uint4 *>(im->d_idx);
+        J.cb = im->d_cb;
+        J.chunk_ptr = im->d_chunk_ptr;
+        J.ent = im->d_ent;
+        J.out = out_base + offs[i] * elem;
+        J.numel = im->numel;
+        J.chunk_begin = total;
+        J.n_chunks = im->n_chunks;
+        J.k = im->k;
+        J.sumsq = d_sumsq ? d_sumsq + i : nullptr;
+        J.conf = d_conf ? d_conf + i : nullptr;
+        total += im->n_chunks;
+    }
+    p.n_jobs = (uint32_t)which.size();
+    p.total_chunks = total;
+    p.grid = fast_grid(total, sms);
+    uint32_t slot = 0;
+    for (uint32_t n = 0; n < p.n_jobs; ++n) {
+        VqJob &J = p.job[n];
+        const uint32_t c0 = cta_of(total, p.grid, J.chunk_begin);
+        const uint32_t c1 = cta_of(total, p.grid, J.chunk_begin + J.n_chunks - 1);
+        J.cta_lo = c0;
+        J.n_cta = c1 - c0 + 1u;
+        J.slot_base = slot;
+        slot += J.n_cta;
+    }
+    if (slot > sc.n_slots) return HXQ_ERR_INVALID_ARG;
+    p.slots = sc.slots;
+    p.counters = sc.counters;
+    p.err = sc.err;
+    const hxq_cuda_image *first = imgs[which[0]];
+    const cudaError_t e = launch_vq_fast(p, first->kind, bf16, first->check_k ? 1 : 0, s);
+    if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return map_cuda(e);
+}
+
+hxq_error_t launch_images(hxq_cuda_image *const *imgs, uint32_t n, void *d_out,
+                          const size_t *offs, int bf16, double *d_sumsq,
+                          float *d_conf, int dev, cudaStream_t s)
+{
+    Scratch *sc = nullptr;
+    hxq_error_t err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+        if ((err = get_scratch(dev, s, &sc)) != HXQ_OK) return err;
+    }
+    const int sms = g_dev[dev].sms;
+    const size_t elem = bf16 ? 2u : 4u;
+    char *base = static_cast<char *>(d_out);
+    // group: fast scalar, fast 12-bit (k checked or not); the rest generic
+    std::vector<uint32_t> g_scalar, g_vq12, g_vq12k, generic;
+    for (uint32_t i = 0; i < n; ++i) {
+        const hxq_cuda_image *im = imgs[i];
+        if (im->device != dev) return HXQ_ERR_INVALID_ARG;
+        if (!im->d_block) return HXQ_ERR_INVALID_ARG;  // streamed image never uploaded
+        if (im->numel == 0) {
+            cudaError_t ce = cudaSuccess;
+            if (d_sumsq) ce = cudaMemsetAsync(d_sumsq + i, 0, sizeof(double), s);
+            if (ce == cudaSuccess && d_conf) ce = cudaMemsetAsync(d_conf + i, 0, sizeof(float), s);
+            if (ce != cudaSuccess) return map_cuda(ce);
+            continue;
+        }
+        const bool ok_align = aligned16(base + offs[i] * elem);
+        if (im->kind == kKindScalar && ok_align) g_scalar.push_back(i);
+        else if (im->kind == kKindVq12 && ok_align) (im->check_k ? g_vq12k : g_vq12).push_back(i);
+        else generic.push_back(i);
+    }
+    if ((err = launch_fast_group(g_vq12, imgs, base, offs, elem, bf16, d_sumsq, d_conf, *sc, sms, s)) != HXQ_OK) return err;
+    if ((err = launch_fast_group(g_vq12k, imgs, base, offs, elem, bf16, d_sumsq, d_conf, *sc, sms, s)) != HXQ_OK) return err;
+    if ((err = launch_fast_group(g_scalar, imgs, base, offs, elem, bf16, d_sumsq, d_conf, *sc, sms, s)) != HXQ_OK) return err;
+    for (uint32_t i : generic) {
+        const hxq_cuda_image *im = imgs[i];
+        GenericJob j;
+        std::memset(&j, 0, sizeof(j));
+        j.kind = im->kind;
+        j.idx = im->d_idx;
+        j.cb = im->d_cb;
+        j.scales = im->d_scales;
+        j.offsets = im->d_offsets;
+        j.rows = im->rows;
+        j.in_f = im->in_f;
+        j.k = im->k;
+        j.gs = im->gs;
+        j.triples_per_row = im->kind == kKindVq12 ? im->in_f / 4u : im->triples_per_row;
+        j.out = base + offs[i] * elem;
+        j.bf16 = bf16;
+        j.sumsq = d_sumsq ? d_sumsq + i : nullptr;
+        j.conf = d_conf ? d_conf + i : nullptr;
+        j.ent = im->d_ent;
+        j.n_ent = im->n_ent;
+        if (im->kind == kKindScalar || im->kind == kKindVq12) {
+            if (im->numel > 0xFFFFFFFFull) return HXQ_ERR_INVALID_ARG;
+            j.chunk_ptr = im->d_chunk_ptr;
+            j.n_chunks = im->n_chunks;
+        }
+        const cudaError_t ce = launch_generic(j, *sc, s);
+        if (ce != cudaSuccess) return map_cuda(ce);
+        g_launches.fetch_add((im->numel ? 1u : 0u) + (im->n_ent ? 1u : 0u), std::memory_order_relaxed);
+    }
+    return HXQ_OK;
+}
+
+// Wait for `s`, then read and clear the device error word.
+hxq_error_t sync_and_check(int dev, cudaStream_t s, float *conf_out)
+{
+    Scratch *sc = nullptr;
+    void *rb = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        hxq_error_t err = get_scratch(dev, s, &sc);
+        if (err != HXQ_OK) return err;
+        rb = g_dev[dev].readback;
+    }
+    // err word and conf[0] are adjacent at the start of the scratch block
+    cudaError_t ce = cudaMemcpyAsync(rb, sc->err, 16 + 4, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    const uint32_t word = *static_cast<uint32_t *>(rb);
+    if (conf_out) std::memcpy(conf_out, static_cast<char *>(rb) + 16, 4);
+    if (word) {
+        ce = cudaMemsetAsync(sc->err, 0, 4, s);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+        if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+        if (word & kErrIndexOOB) return HXQ_ERR_INDEX_OOB;
+    }
+    return HXQ_OK;
+}
+
+// Cached full-tensor image of t on the current device (caller holds no lock).
+hxq_error_t tensor_image(const hxq_tensor_t *t, int dev, hxq_cuda_image **out)
+{
+    const Snapshot now = snap(t, dev);
+    hxq_cuda_image *stale = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_images.find(t);
+        if (it != g_images.end()) {
+            if (it->second.snap == now) { *out = it->second.img; return HXQ_OK; }
+            stale = it->second.img;
+            g_images.erase(it);
+        }
+    }
+    destroy_image(stale);
+    hxq_cuda_image *img = nullptr;
+    hxq_error_t err = build_image(t, 0, t->out_features, dev, false, &img);
+    if (err != HXQ_OK) return err;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_images[t] = Cached{now, img};
+    *out = img;
+    return HXQ_OK;
+}
+
+hxq_error_t decompress_sync(hxq_tensor_t *t, void *d_out, int bf16, float *l2)
+{
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    hxq_cuda_image *img = nullptr;
+    if ((err = tensor_image(t, dev, &img)) != HXQ_OK) return err;
+    Scratch *sc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = get_scratch(dev, (cudaStream_t)0, &sc)) != HXQ_OK) return err;
+    }
+    const size_t off0 = 0;
+    err = launch_images(&img, 1, d_out, &off0, bf16, sc->sumsq, sc->conf, dev, (cudaStream_t)0);
+    if (err != HXQ_OK) return err;
+    return sync_and_check(dev, (cudaStream_t)0, l2);
+}
+
+}  // namespace
+
+// ===========================================================================
+// Internal interface used by the C host library (hxq_internal.h)
+
+extern "C" {
+
+int hxqi_cuda_available(void) { return cuda_present() ? 1 : 0; }
+
+int hxqi_cuda_ptr_is_device(const void *p)
+{
+    if (!p) return 0;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        for (const auto &kv : g_arenas)
+            if (kv.first->data == p) return 1;
+    }
+    if (!cuda_present() || !any_context_active()) return 0;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) ? 1 : 0;
+}
+
+void hxqi_cuda_forget_tensor(const hxq_tensor_t *t)
+{
+    hxq_cuda_image *img = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_images.find(t);
+        if (it == g_images.end()) return;
+        img = it->second.img;
+        g_images.erase(it);
+    }
+    destroy_image(img);
+}
+
+int hxqi_cuda_is_arena(const hxq_shared_buffer_t *buf)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_arenas.count(buf) ? 1 : 0;
+}
+
+void hxqi_cuda_arena_forget(const hxq_shared_buffer_t *buf)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_arenas.erase(buf);
+}
+
+void hxqi_cuda_arena_release(hxq_shared_buffer_t *buf)
+{
+    int dev = -1;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_arenas.find(buf);
+        if (it == g_arenas.end()) return;
+        dev = it->second;
+        g_arenas.erase(it);
+    }
+    if (buf->data) {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (cur != dev) cudaSetDevice(dev);
+        cudaFree(buf->data);
+        if (cur >= 0 && cur != dev) cudaSetDevice(cur);
+        cudaGetLastError();
+    }
+    buf->data = nullptr;
+    buf->capacity = 0;
+    buf->high_water = 0;
+}
+
+// Grow a device arena to at least `floats` floats, keeping its contents.
+hxq_error_t hxqi_cuda_arena_reserve(hxq_shared_buffer_t *buf, size_t floats)
+{
+    if (floats <= buf->capacity) return HXQ_OK;
+    int dev = 0;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_arenas.find(buf);
+        if (it == g_arenas.end()) return HXQ_ERR_INVALID_ARG;
+        dev = it->second;
+    }
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev) cudaSetDevice(dev);
+    float *nd = nullptr;
+    cudaError_t ce = cudaMalloc(&nd, floats * sizeof(float));
+    if (ce == cudaSuccess && buf->data && buf->capacity)
+        ce = cudaMemcpy(nd, buf->data, buf->capacity * sizeof(float), cudaMemcpyDeviceToDevice);
+    if (ce == cudaSuccess) {
+        if (buf->data) cudaFree(buf->data);
+        buf->data = nd;
+        buf->capacity = floats;
+    } else {
+        cudaGetLastError();
+        if (nd) cudaFree(nd);
+    }
+    if (cur >= 0 && cur != dev) cudaSetDevice(cur);
+    return map_cuda(ce);
+}
+
+hxq_error_t hxqi_cuda_decompress(hxq_tensor_t *t, void *d_out, int bf16, float *l2)
+{
+    return decompress_sync(t, d_out, bf16, l2);
+}
+
+// GPU decompress into an internal device buffer, then copy to host memory.
+hxq_error_t hxqi_cuda_decompress_to_host(hxq_tensor_t *t, float *h_out, float *l2)
+{
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    const size_t n = (size_t)t->out_features * t->in_features;
+    float *stage = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+        DevCtx &d = g_dev[dev];
+        if (d.stage_floats < n) {
+            if (d.stage) cudaFree(d.stage);
+            d.stage = nullptr;
+            d.stage_floats = 0;
+            cudaError_t ce = cudaMalloc(&d.stage, std::max<size_t>(n, 4) * sizeof(float));
+            if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+            d.stage_floats = std::max<size_t>(n, 4);
+        }
+        stage = d.stage;
+    }
+    // columns the 12-bit decoder leaves untouched must keep the caller's data
+    cudaError_t ce = cudaSuccess;
+    if (n) ce = cudaMemcpy(stage, h_out, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    float conf = 0.0f;
+    if ((err = decompress_sync(t, stage, 0, &conf)) != HXQ_OK) return err;
+    if (n) ce = cudaMemcpy(h_out, stage, n * sizeof(float), cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    *l2 = conf;
+    return HXQ_OK;
+}
+
+// ===========================================================================
+// Public additive API (hxq_cuda.h)
+
+const char *hxq_error_string(hxq_error_t err)
+{
+    switch ((int)err) {
+    case HXQ_OK: return "ok";
+    case HXQ_ERR_NULL_PTR: return "null pointer";
+    case HXQ_ERR_INVALID_K: return "codebook size must be 256 or 4096";
+    case HXQ_ERR_INVALID_DIM: return "invalid vector dimension or mode";
+    case HXQ_ERR_ALLOC_FAILED: return "allocation failed";
+    case HXQ_ERR_INDEX_OOB: return "index >= codebook size";
+    case HXQ_ERR_PACK_FORMAT: return "packed index data too short";
+    case HXQ_ERR_SIDECAR_OOB: return "sidecar coordinate out of range";
+    case 32: return "CUDA runtime error";
+    case 33: return "backend unavailable";
+    case 34: return "invalid argument";
+    case 35: return "NCCL error";
+    default: return "unknown error";
+    }
+}
+
+const char *hxq_b200_version(void) { return "hxq-b200 0.1.0 (sm_100a)"; }
+
+int hxq_cuda_device_count(void)
+{
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
+}
+
+hxq_error_t hxq_cuda_arena_init(hxq_shared_buffer_t *buf, size_t capacity_floats)
+{
+    if (!buf) return HXQ_ERR_NULL_PTR;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    float *d = nullptr;
+    if (capacity_floats) {
+        cudaError_t ce = cudaMalloc(&d, capacity_floats * sizeof(float));
+        if (ce == cudaSuccess) ce = cudaMemset(d, 0, capacity_floats * sizeof(float));
+        if (ce != cudaSuccess) { cudaGetLastError(); if (d) cudaFree(d); return map_cuda(ce); }
+    }
+    buf->data = d;
+    buf->capacity = capacity_floats;
+    buf->high_water = 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_arenas[buf] = dev;
+    return HXQ_OK;
+}
+
+int hxq_cuda_buffer_is_device(const hxq_shared_buffer_t *buf)
+{
+    return buf ? hxqi_cuda_is_arena(buf) : 0;
+}
+
+hxq_error_t hxq_cuda_decompress(hxq_tensor_t *t, void *d_out, hxq_out_dtype_t dtype)
+{
+    if (!t || !d_out) return HXQ_ERR_NULL_PTR;
+    if (dtype != HXQ_OUT_F32 && dtype != HXQ_OUT_BF16) return HXQ_ERR_INVALID_ARG;
+    if (!t->indices_raw) return HXQ_ERR_NULL_PTR;
+    if (t->mode != HXQ_AFFINE_G128 && !t->codebook) return HXQ_ERR_NULL_PTR;
+    float l2 = 0.0f;
+    hxq_error_t err = decompress_sync(t, d_out, dtype == HXQ_OUT_BF16, &l2);
+    if (err != HXQ_OK) return err;
+    t->sidecar_l2_norm = l2;
+    return HXQ_OK;
+}
+
+hxq_error_t hxq_dequant_bf16(hxq_tensor_t *t, hxq_shared_buffer_t *arena, hxq_result_t *result)
+{
+    if (!t || !arena || !result) return HXQ_ERR_NULL_PTR;
+    if (!hxqi_cuda_is_arena(arena)) return HXQ_ERR_INVALID_ARG;
+    const size_t n = (size_t)t->out_features * t->in_features;
+    const size_t floats = (n + 1) / 2;
+    hxq_error_t err = hxqi_cuda_arena_reserve(arena, floats);
+    if (err != HXQ_OK) return err;
+    if (floats > arena->high_water) arena->high_water = floats;
+    if ((err = hxq_cuda_decompress(t, arena->data, HXQ_OUT_BF16)) != HXQ_OK) return err;
+    result->weights = arena->data;
+    result->confidence = t->sidecar_l2_norm;
+    result->out_features = t->out_features;
+    result->in_features = t->in_features;
+    return HXQ_OK;
+}
+
+void hxq_cuda_tensor_invalidate(const hxq_tensor_t *t) { hxqi_cuda_forget_tensor(t); }
+
+hxq_error_t hxq_cuda_image_create(const hxq_tensor_t *t, uint32_t row_begin,
+                                  uint32_t row_end, hxq_cuda_image_t **img)
+{
+    if (!t || !img) return HXQ_ERR_NULL_PTR;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    return build_image(t, row_begin, row_end, dev, false, img);
+}
+
+hxq_error_t hxq_cuda_image_create_streamed(const hxq_tensor_t *t, uint32_t row_begin,
+                                           uint32_t row_end, hxq_cuda_image_t **img)
+{
+    if (!t || !img) return HXQ_ERR_NULL_PTR;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    return build_image(t, row_begin, row_end, dev, true, img);
+}
+
+size_t hxq_cuda_image_block_bytes(const hxq_cuda_image_t *img) { return img ? img->block_bytes : 0; }
+
+hxq_error_t hxq_cuda_image_upload(hxq_cuda_image_t *img, void *d_dst, void *stream)
+{
+    if (!img || !d_dst) return HXQ_ERR_NULL_PTR;
+    if (!img->h_block || ((uintptr_t)d_dst & 255u)) return HXQ_ERR_INVALID_ARG;
+    const cudaError_t ce = cudaMemcpyAsync(d_dst, img->h_block, img->block_bytes,
+                                           cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    bind_image(img, d_dst);
+    return HXQ_OK;
+}
+
+unsigned long long hxq_cuda_launch_count(void) { return g_launches.load(); }
+
+void hxq_cuda_image_destroy(hxq_cuda_image_t *img) { destroy_image(img); }
+
+size_t hxq_cuda_image_numel(const hxq_cuda_image_t *img) { return img ? (size_t)img->numel : 0; }
+
+size_t hxq_cuda_image_device_bytes(const hxq_cuda_image_t *img) { return img ? img->block_bytes : 0; }
+
+double hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img) { return img ? img->sumsq : 0.0; }
+
+hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n,
+                                       void *d_out, const size_t *out_offsets,
+                                       hxq_out_dtype_t dtype, double *d_sumsq,
+                                       float *d_conf, void *stream)
+{
+    if (n == 0) return HXQ_OK;
+    if (!imgs || !d_out || !out_offsets) return HXQ_ERR_NULL_PTR;
+    if (n > kMaxJobs) return HXQ_ERR_INVALID_ARG;
+    if (dtype != HXQ_OUT_F32 && dtype != HXQ_OUT_BF16) return HXQ_ERR_INVALID_ARG;
+    for (uint32_t i = 0; i < n; ++i)
+        if (!imgs[i]) return HXQ_ERR_NULL_PTR;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    return launch_images(imgs, n, d_out, out_offsets, dtype == HXQ_OUT_BF16, d_sumsq, d_conf,
+                         dev, static_cast<cudaStream_t>(stream));
+}
+
+hxq_error_t hxq_cuda_stream_synchronize(void *stream)
+{
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    return sync_and_check(dev, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The reference's undeclared GPU launchers (src/hxq_cuda.cu:209-288), on the
+// generic kernels.  Index layout is the one hxq.c decodes (each row holds
+// ceil((in_f/2)/2) triples), which equals the launcher's flat pair stream
+// whenever in_f/2 is even.
+
+namespace {
+
+int raw_launch(uint32_t kind, const float *cb, const uint8_t *idx, float *out,
+               uint32_t out_f, uint32_t in_f)
+{
+    int dev = 0;
+    if (current_device(&dev) != HXQ_OK || !cb || !idx || !out) return -1;
+    Scratch *sc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (dev_ready(dev) != HXQ_OK || get_scratch(dev, (cudaStream_t)0, &sc) != HXQ_OK) return -1;
+    }
+    GenericJob j;
+    std::memset(&j, 0, sizeof(j));
+    j.kind = kind;
+    j.idx = idx;
+    j.cb = cb;
+    j.rows = out_f;
+    j.in_f = in_f;
+    j.k = kind == kKindScalar ? 256u : 4096u;
+    j.triples_per_row = (in_f / 2u + 1u) / 2u;
+    j.out = out;
+    if (launch_generic(j, *sc, (cudaStream_t)0) != cudaSuccess) { cudaGetLastError(); return -1; }
+    return 0;
+}
+
+typedef CUresult (*AddrRangeFn)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+// Bytes from p to the end of the device allocation holding it (0 if unknown).
+size_t bytes_to_alloc_end(const void *p)
+{
+    static AddrRangeFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddrRangeFn>(f);
+        else
+            cudaGetLastError();
+    }
+    if (!fn) return 0;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)(uintptr_t)p) != CUDA_SUCCESS) return 0;
+    const uintptr_t end = (uintptr_t)base + size;
+    return end > (uintptr_t)p ? end - (uintptr_t)p : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hxq_cuda_decompress_scalar(const float *d_codebook, const uint8_t *d_indices,
+                               float *d_output, uint32_t out_f, uint32_t in_f)
+{
+    return raw_launch(kKindScalar, d_codebook, d_indices, d_output, out_f, in_f);
+}
+
+int hxq_cuda_decompress_vq2d_12bit(const float *d_codebook, const uint8_t *d_packed,
+                                   float *d_output, uint32_t out_f, uint32_t in_f)
+{
+    // With an odd pair count per row the reference launcher's flat pair
+    // stream is shorter than hxq.c's per-row layout; refuse rather than read
+    // past a buffer sized for the former.
+    if ((in_f / 2u) % 2u != 0u) return -1;
+    return raw_launch(kKindVq12Any, d_codebook, d_packed, d_output, out_f, in_f);
+}
+
+// The reference launcher applies every entry with no bound at all; here an
+// entry is applied when its element lies inside the allocation holding
+// d_output (so a bad coordinate cannot write outside it), equal coordinates
+// in array order.  Returns sqrt of the applied squares, or -1 on error.
+float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
+                             const float *d_vals, float *d_output, uint32_t in_f,
+                             uint32_t nnz)
+{
+    if (nnz == 0) return 0.0f;
+    int dev = 0;
+    if (!d_rows || !d_cols || !d_vals || !d_output || current_device(&dev) != HXQ_OK) return -1.0f;
+    const size_t limit = bytes_to_alloc_end(d_output) / sizeof(float);
+    if (limit == 0) return -1.0f;
+    std::vector<uint32_t> r(nnz), c(nnz);
+    std::vector<float> v(nnz);
+    if (cudaMemcpy(r.data(), d_rows, nnz * 4u, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(c.data(), d_cols, nnz * 4u, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(v.data(), d_vals, nnz * 4u, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return -1.0f;
+    }
+    std::vector<HostEntry> ents;
+    ents.reserve(nnz);
+    for (uint32_t i = 0; i < nnz; ++i) {
+        const uint64_t pos = (uint64_t)r[i] * in_f + c[i];
+        if (pos < limit && pos <= 0xFFFFFFFFull) ents.push_back({pos, v[i]});
+    }
+    std::stable_sort(ents.begin(), ents.end(),
+                     [](const HostEntry &a, const HostEntry &b) { return a.pos < b.pos; });
+    std::vector<SideEntry> de(ents.size());
+    for (size_t i = 0; i < ents.size(); ++i) {
+        de[i].x = (uint32_t)ents[i].pos;
+        std::memcpy(&de[i].y, &ents[i].val, 4);
+    }
+    if (de.empty()) return 0.0f;
+    Scratch *sc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (dev_ready(dev) != HXQ_OK || get_scratch(dev, (cudaStream_t)0, &sc) != HXQ_OK) return -1.0f;
+    }
+    SideEntry *d_ent = nullptr;
+    if (cudaMalloc(&d_ent, de.size() * sizeof(SideEntry)) != cudaSuccess) { cudaGetLastError(); return -1.0f; }
+    float conf = -1.0f;
+    GenericJob j;
+    std::memset(&j, 0, sizeof(j));
+    j.kind = kKindRaw;
+    j.in_f = in_f;
+    j.ent = d_ent;
+    j.n_ent = (uint32_t)de.size();
+    j.out = d_output;
+    j.conf = sc->conf;
+    if (cudaMemcpy(d_ent, de.data(), de.size() * sizeof(SideEntry), cudaMemcpyHostToDevice) == cudaSuccess &&
+        launch_generic(j, *sc, (cudaStream_t)0) == cudaSuccess &&
+        sync_and_check(dev, (cudaStream_t)0, &conf) == HXQ_OK) {
+        cudaFree(d_ent);
+        return conf;
+    }
+    cudaGetLastError();
+    cudaFree(d_ent);
+    return -1.0f;
+}
+
+}  // extern "C"

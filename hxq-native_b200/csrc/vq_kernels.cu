@@ -1,0 +1,563 @@
+// vq_kernels.cu -- sm_100a kernels of the HXQ VQ decompress path.
+//
+// Fast kernel (scalar k=256 and 12-bit k=4096 x dim 2 with in_features % 4
+// == 0).  Semantics follow the reference CPU decoder (hxq-native
+// src/hxq.c:218-235 scalar, :239-298 12-bit, :330-350 sidecar):
+//   W = codebook[index], then in-range sidecar deltas added in array order,
+//   confidence = sqrt(sum of squared in-range deltas).
+// Design (not a port of src/hxq_cuda.cu):
+//   * the tensor is a flat stream of 2048-weight chunks; one warp owns one
+//     chunk at a time and needs no CTA-wide barrier inside a chunk;
+//   * index bytes arrive as coalesced 128-bit non-allocating loads
+//     (3 x 512 B per warp for 12-bit, 4 x 512 B for scalar), are staged in a
+//     per-warp shared buffer and unpacked with one PRMT per byte triple;
+//   * the codebook sits in shared memory once per CTA and job: 4096 float2
+//     (fp32 out), 4096 packed bf16x2 (bf16 out), or for k=256 a 32-way
+//     lane-replicated copy that makes the scalar gather bank-conflict free;
+//   * every warp store is a fully coalesced 512 B (fp32) / 256 B (bf16) row;
+//   * the sidecar is a fused epilogue: the chunk's entries (pre-sorted by
+//     position at upload, equal positions adjacent and in array order) are
+//     applied by the same warp, the base value re-derived from the staged
+//     index so no global read-modify-write is needed; squared deltas are
+//     accumulated in fp64, reduced with warp shuffles, per CTA into a fixed
+//     slot, and the last CTA of a job adds the slots in order (deterministic,
+//     no host round trip);
+//   * one launch covers up to 64 jobs (e.g. a whole transformer layer) over
+//     a grid of 4 CTAs per SM with contiguous chunk ranges per CTA.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "hxq_cuda_internal.h"
+
+namespace hxq {
+namespace {
+
+constexpr uint32_t kCbBytes = 32768;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const uint4 *p)
+{
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ SideEntry ld_entry(const SideEntry *p)
+{
+    uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+    return SideEntry{v.x, v.y};
+}
+
+__device__ __forceinline__ double warp_sum(double v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Byte triple j of a staged chunk as a big-endian 24-bit number
+// B = b0 << 16 | b1 << 8 | b2, so index a = B >> 12 and b = B & 0xFFF
+// (the pair layout of hxq.h:245-252).  Reads words q and q+1, q = 3j/4.
+__device__ __forceinline__ uint32_t triple_be(const uint32_t *sw, uint32_t j)
+{
+    const uint32_t byte = 3u * j;
+    const uint32_t q = byte >> 2, s = byte & 3u;
+    const uint32_t w0 = sw[q], w1 = sw[q + 1];
+    // selector nibbles: result byte0 = src byte s+2, byte1 = s+1, byte2 = s
+    return __byte_perm(w0, w1, 0x3012u + s * 0x1111u);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <uint32_t KIND, bool BF16>
+__device__ __forceinline__ void load_codebook(unsigned char *cb_area,
+                                              const VqJob &J, uint32_t tid)
+{
+    if (KIND == kKindVq12) {
+        const uint32_t n = J.k < 4096u ? J.k : 4096u;
+        const float2 *src = reinterpret_cast<const float2 *>(J.cb);
+        if (!BF16) {
+            float2 *dst = reinterpret_cast<float2 *>(cb_area);
+            for (uint32_t i = tid; i < n; i += kThreads) dst[i] = __ldg(src + i);
+        } else {
+            uint32_t *dst = reinterpret_cast<uint32_t *>(cb_area);
+            for (uint32_t i = tid; i < n; i += kThreads) {
+                float2 v = __ldg(src + i);
+                dst[i] = pack_bf16x2(v.x, v.y);
+            }
+        }
+    } else {
+        // lane-replicated scalar table: entry e for lane l at e*32 + l
+        float *dst = reinterpret_cast<float *>(cb_area);
+        for (uint32_t i = tid; i < 256u * 32u; i += kThreads)
+            dst[i] = __ldg(J.cb + (i >> 5));
+    }
+}
+
+// One 12-bit chunk (512 triples, 2048 weights).
+template <bool BF16, bool CHECK_K>
+__device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c,
+                                           const unsigned char *cb_area,
+                                           uint4 *stage, uint32_t lane,
+                                           double &acc, uint32_t &errflag)
+{
+    const uint4 *src = J.idx + (size_t)c * (kChunkBytes12 / 16u);
+    const uint4 r0 = ld_stream_v4(src + lane);
+    const uint4 r1 = ld_stream_v4(src + 32 + lane);
+    const uint4 r2 = ld_stream_v4(src + 64 + lane);
+    const uint32_t e0 = __ldg(J.chunk_ptr + c);
+    const uint32_t e1 = __ldg(J.chunk_ptr + c + 1);
+    SideEntry ent{0u, 0u};
+    if (e0 + lane < e1) ent = ld_entry(J.ent + e0 + lane);
+
+    __syncwarp();  // previous chunk's readers of `stage` are done
+    stage[lane] = r0;
+    stage[32 + lane] = r1;
+    stage[64 + lane] = r2;
+    __syncwarp();
+
+    const uint64_t w0 = (uint64_t)c * kChunkW;
+    const uint64_t left = J.numel - w0;
+    const uint32_t ntrip = (left >= kChunkW ? kChunkW : (uint32_t)left) >> 2;
+    const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);
+
+#pragma unroll 4
+    for (uint32_t m = 0; m < 16u; ++m) {
+        const uint32_t jt = m * 32u + lane;
+        if (jt < ntrip) {
+            const uint32_t B = triple_be(sw, jt);
+            const uint32_t a = (B >> 12) & 0xFFFu, b = B & 0xFFFu;
+            if (CHECK_K && (a >= J.k || b >= J.k)) errflag |= kErrIndexOOB;
+            if (!BF16) {
+                const float2 *cb = reinterpret_cast<const float2 *>(cb_area);
+                const float2 va = cb[a], vb = cb[b];
+                float4 *dst = reinterpret_cast<float4 *>(J.out) + (w0 >> 2) + jt;
+                *dst = make_float4(va.x, va.y, vb.x, vb.y);
+            } else {
+                const uint32_t *cb = reinterpret_cast<const uint32_t *>(cb_area);
+                uint2 *dst = reinterpret_cast<uint2 *>(J.out) + (w0 >> 2) + jt;
+                *dst = make_uint2(cb[a], cb[b]);
+            }
+        }
+    }
+
+    if (e1 == e0) return;  // warp-uniform
+    __syncwarp();          // base stores of the chunk precede the corrections
+    for (uint32_t base = e0; base < e1; base += 32u) {
+        const uint32_t e = base + lane;
+        if (e >= e1) continue;
+        const SideEntry en = (base == e0) ? ent : ld_entry(J.ent + e);
+        const float v = __uint_as_float(en.y);
+        acc += (double)v * (double)v;
+        const uint32_t run = en.x >> 16;
+        if (run == 0u) continue;
+        const uint32_t off = en.x & 0xFFFFu;
+        const uint32_t B = triple_be(sw, off >> 2);
+        const uint32_t id = ((off >> 1) & 1u) ? (B & 0xFFFu) : ((B >> 12) & 0xFFFu);
+        if (CHECK_K && id >= J.k) continue;  // already flagged by the gather
+        float val;
+        if (!BF16)
+            val = reinterpret_cast<const float *>(cb_area)[2u * id + (off & 1u)];
+        else
+            val = __ldg(J.cb + 2u * id + (off & 1u));
+        val = __fadd_rn(val, v);
+        for (uint32_t r = 1; r < run; ++r)
+            val = __fadd_rn(val, __uint_as_float(ld_entry(J.ent + e + r).y));
+        if (!BF16)
+            reinterpret_cast<float *>(J.out)[w0 + off] = val;
+        else
+            reinterpret_cast<__nv_bfloat16 *>(J.out)[w0 + off] = __float2bfloat16_rn(val);
+    }
+}
+
+// One scalar chunk (2048 uint8 indices, 2048 weights).
+template <bool BF16>
+__device__ __forceinline__ void chunk_scalar(const VqJob &J, uint32_t c,
+                                             const unsigned char *cb_area,
+                                             uint4 *stage, uint32_t lane,
+                                             double &acc)
+{
+    const uint4 *src = J.idx + (size_t)c * (kChunkBytes8 / 16u);
+    const uint4 r0 = ld_stream_v4(src + lane);
+    const uint4 r1 = ld_stream_v4(src + 32 + lane);
+    const uint4 r2 = ld_stream_v4(src + 64 + lane);
+    const uint4 r3 = ld_stream_v4(src + 96 + lane);
+    const uint32_t e0 = __ldg(J.chunk_ptr + c);
+    const uint32_t e1 = __ldg(J.chunk_ptr + c + 1);
+    SideEntry ent{0u, 0u};
+    if (e0 + lane < e1) ent = ld_entry(J.ent + e0 + lane);
+
+    __syncwarp();
+    stage[lane] = r0;
+    stage[32 + lane] = r1;
+    stage[64 + lane] = r2;
+    stage[96 + lane] = r3;
+    __syncwarp();
+
+    const uint64_t w0 = (uint64_t)c * kChunkW;
+    const uint64_t left = J.numel - w0;
+    const uint32_t nw = left >= kChunkW ? kChunkW : (uint32_t)left;
+    const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);
+    const float *cbr = reinterpret_cast<const float *>(cb_area);
+
+#pragma unroll 4
+    for (uint32_t p = 0; p < 16u; ++p) {
+        const uint32_t w = p * 32u + lane;
+        const uint32_t first = 4u * w;
+        if (first >= nw) continue;
+        const uint32_t word = sw[w];
+        const float f0 = cbr[((word      ) & 0xFFu) * 32u + lane];
+        const float f1 = cbr[((word >>  8) & 0xFFu) * 32u + lane];
+        const float f2 = cbr[((word >> 16) & 0xFFu) * 32u + lane];
+        const float f3 = cbr[((word >> 24)        ) * 32u + lane];
+        if (first + 4u <= nw) {
+            if (!BF16) {
+                reinterpret_cast<float4 *>(J.out)[(w0 >> 2) + w] = make_float4(f0, f1, f2, f3);
+            } else {
+                reinterpret_cast<uint2 *>(J.out)[(w0 >> 2) + w] =
+                    make_uint2(pack_bf16x2(f0, f1), pack_bf16x2(f2, f3));
+            }
+        } else {  // ragged tail of the last chunk
+            const float f[4] = {f0, f1, f2, f3};
+            for (uint32_t i = 0; first + i < nw; ++i) {
+                if (!BF16) reinterpret_cast<float *>(J.out)[w0 + first + i] = f[i];
+                else reinterpret_cast<__nv_bfloat16 *>(J.out)[w0 + first + i] = __float2bfloat16_rn(f[i]);
+            }
+        }
+    }
+
+    if (e1 == e0) return;
+    __syncwarp();
+    const uint8_t *sb = reinterpret_cast<const uint8_t *>(stage);
+    for (uint32_t base = e0; base < e1; base += 32u) {
+        const uint32_t e = base + lane;
+        if (e >= e1) continue;
+        const SideEntry en = (base == e0) ? ent : ld_entry(J.ent + e);
+        const float v = __uint_as_float(en.y);
+        acc += (double)v * (double)v;
+        const uint32_t run = en.x >> 16;
+        if (run == 0u) continue;
+        const uint32_t off = en.x & 0xFFFFu;
+        float val = cbr[(uint32_t)sb[off] * 32u];
+        val = __fadd_rn(val, v);
+        for (uint32_t r = 1; r < run; ++r)
+            val = __fadd_rn(val, __uint_as_float(ld_entry(J.ent + e + r).y));
+        if (!BF16)
+            reinterpret_cast<float *>(J.out)[w0 + off] = val;
+        else
+            reinterpret_cast<__nv_bfloat16 *>(J.out)[w0 + off] = __float2bfloat16_rn(val);
+    }
+}
+
+template <uint32_t KIND>
+__host__ __device__ constexpr uint32_t stage_bytes()
+{
+    return (KIND == kKindVq12 ? kChunkBytes12 : kChunkBytes8) + kIdxPad;
+}
+
+template <uint32_t KIND>
+__host__ __device__ constexpr uint32_t fast_smem_bytes()
+{
+    return kCbBytes + kWarps * stage_bytes<KIND>() + kWarps * sizeof(double);
+}
+
+template <uint32_t KIND, bool BF16, bool CHECK_K>
+__global__ void __launch_bounds__(kThreads, 4)
+vq_fast_kernel(const __grid_constant__ VqLaunch p)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    unsigned char *cb_area = smem;
+    uint4 *stage = reinterpret_cast<uint4 *>(smem + kCbBytes + warp * stage_bytes<KIND>());
+    double *red = reinterpret_cast<double *>(smem + kCbBytes + kWarps * stage_bytes<KIND>());
+
+    const uint32_t cta = blockIdx.x;
+    const uint64_t lo = p.total_chunks * cta / p.grid;
+    const uint64_t hi = p.total_chunks * (cta + 1u) / p.grid;
+
+    uint32_t j = 0;
+    while (j + 1u < p.n_jobs && p.job[j].chunk_begin + p.job[j].n_chunks <= lo) ++j;
+
+    uint32_t errflag = 0;
+    uint64_t pos = lo;
+    while (pos < hi && j < p.n_jobs) {
+        const VqJob &J = p.job[j];
+        const uint64_t jend = J.chunk_begin + J.n_chunks;
+        const uint64_t seg_end = hi < jend ? hi : jend;
+
+        __syncthreads();  // codebook and red[] of the previous segment released
+        load_codebook<KIND, BF16>(cb_area, J, tid);
+        __syncthreads();
+
+        double acc = 0.0;
+        for (uint64_t ch = pos + warp; ch < seg_end; ch += kWarps) {
+            const uint32_t c = (uint32_t)(ch - J.chunk_begin);
+            if (KIND == kKindVq12)
+                chunk_vq12<BF16, CHECK_K>(J, c, cb_area, stage, lane, acc, errflag);
+            else
+                chunk_scalar<BF16>(J, c, cb_area, stage, lane, acc);
+        }
+
+        acc = warp_sum(acc);
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        if (tid == 0) {
+            double s = 0.0;
+#pragma unroll
+            for (uint32_t w = 0; w < kWarps; ++w) s += red[w];
+            p.slots[J.slot_base + (cta - J.cta_lo)] = s;
+            __threadfence();
+            const uint32_t prev = atomicAdd(p.counters + j, 1u);
+            if (prev + 1u == J.n_cta) {
+                __threadfence();
+                double tot = 0.0;
+                for (uint32_t i = 0; i < J.n_cta; ++i) tot += __ldcg(p.slots + J.slot_base + i);
+                if (J.sumsq) *J.sumsq = tot;
+                if (J.conf) *J.conf = (float)sqrt(tot);
+                p.counters[j] = 0u;  // leave scratch zeroed for the next launch
+            }
+        }
+        pos = seg_end;
+        ++j;
+    }
+    if (CHECK_K && errflag) atomicOr(p.err, errflag);
+}
+
+template <uint32_t KIND, bool BF16, bool CHECK_K>
+cudaError_t launch_one(const VqLaunch &p, cudaStream_t s)
+{
+    constexpr uint32_t smem = fast_smem_bytes<KIND>();
+    vq_fast_kernel<KIND, BF16, CHECK_K><<<p.grid, kThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Generic kernels: any shape and output alignment, one image per launch.
+
+__device__ __forceinline__ void store_out(void *out, uint64_t i, float v, int bf16)
+{
+    if (bf16) reinterpret_cast<__nv_bfloat16 *>(out)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float *>(out)[i] = v;
+}
+
+__global__ void generic_decompress_kernel(const __grid_constant__ GenericJob j,
+                                          uint32_t *err)
+{
+    uint32_t errflag = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j.kind == kKindVq12 || j.kind == kKindVq12Any) {
+        const uint64_t units = (uint64_t)j.rows * j.triples_per_row;
+        for (uint64_t u = tid; u < units; u += stride) {
+            const uint32_t r = (uint32_t)(u / j.triples_per_row);
+            const uint32_t t = (uint32_t)(u - (uint64_t)r * j.triples_per_row);
+            const uint8_t *pb = j.idx + u * 3u;
+            const uint32_t b0 = pb[0], b1 = pb[1], b2 = pb[2];
+            const uint32_t a = (b0 << 4) | (b1 >> 4);
+            const uint32_t b = ((b1 & 0xFu) << 8) | b2;
+            if (a >= j.k || b >= j.k) { errflag = kErrIndexOOB; continue; }
+            const uint64_t rowbase = (uint64_t)r * j.in_f;
+            const uint32_t ca = 4u * t, cbc = ca + 2u;
+            if (ca + 1u < j.in_f) {
+                store_out(j.out, rowbase + ca, j.cb[2u * a], j.bf16);
+                store_out(j.out, rowbase + ca + 1u, j.cb[2u * a + 1u], j.bf16);
+            }
+            if (cbc + 1u < j.in_f) {
+                store_out(j.out, rowbase + cbc, j.cb[2u * b], j.bf16);
+                store_out(j.out, rowbase + cbc + 1u, j.cb[2u * b + 1u], j.bf16);
+            }
+        }
+    } else if (j.kind == kKindRaw) {
+        // nothing to reconstruct
+    } else if (j.kind == kKindScalar) {
+        const uint64_t n = (uint64_t)j.rows * j.in_f;
+        for (uint64_t i = tid; i < n; i += stride) store_out(j.out, i, j.cb[j.idx[i]], j.bf16);
+    } else {  // affine: rounded product, then rounded add (src/hxq.c:320)
+        const uint64_t n = (uint64_t)j.rows * j.in_f;
+        const uint32_t ng = j.in_f / j.gs;
+        for (uint64_t i = tid; i < n; i += stride) {
+            const uint32_t o = (uint32_t)(i / j.in_f);
+            const uint32_t c = (uint32_t)(i - (uint64_t)o * j.in_f);
+            const uint64_t g = (uint64_t)o * ng + c / j.gs;
+            const float w = __fadd_rn(__fmul_rn((float)j.idx[i], j.scales[g]), j.offsets[g]);
+            store_out(j.out, i, w, j.bf16);
+        }
+    }
+    if (errflag) atomicOr(err, errflag);
+}
+
+// Value a position holds before its sidecar corrections.  For 12-bit rows
+// whose last pair is incomplete the reference never writes that column, so
+// the correction lands on whatever the buffer held: read it back.
+__device__ __forceinline__ bool base_value(const GenericJob &j, uint32_t pos, float &v)
+{
+    if (j.kind == kKindScalar) {
+        v = j.cb[j.idx[pos]];
+        return true;
+    }
+    if (j.kind == kKindRaw) {
+        v = reinterpret_cast<const float *>(j.out)[pos];
+        return true;
+    }
+    const uint32_t r = pos / j.in_f, c = pos - r * j.in_f;
+    if (j.kind == kKindAffine) {
+        const uint32_t ng = j.in_f / j.gs;
+        const uint64_t g = (uint64_t)r * ng + c / j.gs;
+        v = __fadd_rn(__fmul_rn((float)j.idx[pos], j.scales[g]), j.offsets[g]);
+        return true;
+    }
+    if ((c | 1u) < j.in_f) {
+        const uint8_t *pb = j.idx + ((uint64_t)r * j.triples_per_row + (c >> 2)) * 3u;
+        const uint32_t b0 = pb[0], b1 = pb[1], b2 = pb[2];
+        const uint32_t id = ((c >> 1) & 1u) ? (((b1 & 0xFu) << 8) | b2) : ((b0 << 4) | (b1 >> 4));
+        if (id >= j.k) return false;
+        v = j.cb[2u * id + (c & 1u)];
+        return true;
+    }
+    if (j.bf16)
+        v = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(j.out)[pos]);
+    else
+        v = reinterpret_cast<const float *>(j.out)[pos];
+    return true;
+}
+
+// Chunk of entry e in the chunk-relative encoding: the last c with
+// chunk_ptr[c] <= e.
+__device__ __forceinline__ uint32_t chunk_of_entry(const uint32_t *cp, uint32_t n_chunks, uint32_t e)
+{
+    uint32_t lo = 0, hi = n_chunks - 1u;
+    while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo + 1u) / 2u;
+        if (__ldg(cp + mid) <= e) lo = mid; else hi = mid - 1u;
+    }
+    return lo;
+}
+
+__global__ void generic_sidecar_kernel(const __grid_constant__ GenericJob j,
+                                       double *slots, uint32_t *counter)
+{
+    __shared__ double red[32];
+    double acc = 0.0;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < j.n_ent; e += stride) {
+        const SideEntry en = ld_entry(j.ent + e);
+        const float v = __uint_as_float(en.y);
+        acc += (double)v * (double)v;
+        uint32_t pos, run;
+        if (j.chunk_ptr) {  // fast-image encoding: run length marks the head
+            run = en.x >> 16;
+            if (run == 0u) continue;
+            pos = chunk_of_entry(j.chunk_ptr, j.n_chunks, e) * kChunkW + (en.x & 0xFFFFu);
+        } else {
+            if (e > 0 && ld_entry(j.ent + e - 1).x == en.x) continue;  // not a run head
+            pos = en.x;
+            run = 1u;
+            while (e + run < j.n_ent && ld_entry(j.ent + e + run).x == pos) ++run;
+        }
+        float val;
+        if (!base_value(j, pos, val)) continue;
+        val = __fadd_rn(val, v);
+        for (uint32_t r = 1; r < run; ++r) val = __fadd_rn(val, __uint_as_float(ld_entry(j.ent + e + r).y));
+        store_out(j.out, pos, val, j.bf16);
+    }
+    acc = warp_sum(acc);
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (uint32_t w = 0; w < blockDim.x / 32u; ++w) s += red[w];
+        slots[blockIdx.x] = s;
+        __threadfence();
+        const uint32_t prev = atomicAdd(counter, 1u);
+        if (prev + 1u == gridDim.x) {
+            __threadfence();
+            double tot = 0.0;
+            for (uint32_t i = 0; i < gridDim.x; ++i) tot += __ldcg(slots + i);
+            if (j.sumsq) *j.sumsq = tot;
+            if (j.conf) *j.conf = (float)sqrt(tot);
+            *counter = 0u;
+        }
+    }
+}
+
+template <uint32_t KIND, bool BF16, bool CHECK_K>
+cudaError_t configure_one()
+{
+    return cudaFuncSetAttribute(vq_fast_kernel<KIND, BF16, CHECK_K>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                fast_smem_bytes<KIND>());
+}
+
+}  // namespace
+
+// Opt every fast-kernel instantiation into its dynamic shared memory size;
+// called once per device before the first launch.
+cudaError_t configure_vq_kernels()
+{
+    cudaError_t e;
+    if ((e = configure_one<kKindVq12, false, false>()) != cudaSuccess) return e;
+    if ((e = configure_one<kKindVq12, false, true>()) != cudaSuccess) return e;
+    if ((e = configure_one<kKindVq12, true, false>()) != cudaSuccess) return e;
+    if ((e = configure_one<kKindVq12, true, true>()) != cudaSuccess) return e;
+    if ((e = configure_one<kKindScalar, false, false>()) != cudaSuccess) return e;
+    return configure_one<kKindScalar, true, false>();
+}
+
+uint32_t fast_grid(uint64_t total_chunks, int sms)
+{
+    uint64_t g = (uint64_t)(sms > 0 ? sms : 148) * 4u;
+    if (g > total_chunks) g = total_chunks;
+    return (uint32_t)(g == 0 ? 1 : g);
+}
+
+cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
+                           int check_k, cudaStream_t s)
+{
+    if (kind == kKindVq12) {
+        if (bf16) return check_k ? launch_one<kKindVq12, true, true>(p, s)
+                                 : launch_one<kKindVq12, true, false>(p, s);
+        return check_k ? launch_one<kKindVq12, false, true>(p, s)
+                       : launch_one<kKindVq12, false, false>(p, s);
+    }
+    return bf16 ? launch_one<kKindScalar, true, false>(p, s)
+                : launch_one<kKindScalar, false, false>(p, s);
+}
+
+cudaError_t launch_generic(const GenericJob &j, const Scratch &sc, cudaStream_t s)
+{
+    uint64_t units;
+    if (j.kind == kKindVq12 || j.kind == kKindVq12Any)
+        units = (uint64_t)j.rows * j.triples_per_row;
+    else if (j.kind == kKindRaw)
+        units = 0;
+    else
+        units = (uint64_t)j.rows * j.in_f;
+    if (units > 0) {
+        uint64_t blocks = (units + 255u) / 256u;
+        if (blocks > 148u * 16u) blocks = 148u * 16u;
+        generic_decompress_kernel<<<(uint32_t)blocks, 256, 0, s>>>(j, sc.err);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (j.n_ent > 0) {
+        uint32_t blocks = (j.n_ent + 255u) / 256u;
+        if (blocks > sc.n_slots) blocks = sc.n_slots;
+        // the kernel applies runs in order only within one launch, and its
+        // base_value for unwritten 12-bit columns reads the output, so it
+        // must run after the decompress kernel (same stream).
+        generic_sidecar_kernel<<<blocks, 256, 0, s>>>(j, sc.slots, sc.counters);
+        return cudaGetLastError();
+    }
+    cudaError_t e = cudaSuccess;
+    if (j.sumsq) e = cudaMemsetAsync(j.sumsq, 0, sizeof(double), s);
+    if (e == cudaSuccess && j.conf) e = cudaMemsetAsync(j.conf, 0, sizeof(float), s);
+    return e;
+}
+
+}  // namespace hxq

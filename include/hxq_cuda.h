@@ -1,0 +1,158 @@
+/*
+ * hxq_cuda.h -- additive B200 (sm_100a) API of the HXQ codec.
+ *
+ * Nothing here replaces a reference symbol; these are the extra entry
+ * points that make the CUDA backend usable at model scale:
+ *   - a device arena (a hxq_shared_buffer_t whose data lives in HBM),
+ *   - stream-ordered and bf16-output decompress,
+ *   - "images": device copies of whole tensors or of row slices, which a
+ *     multi-GPU driver uses to shard weight matrices by out_features,
+ *   - batched decompress of many images in one kernel launch,
+ *   - the reference's undeclared GPU launchers (src/hxq_cuda.cu:209-288)
+ *     re-implemented on the new kernels,
+ *   - bf16-activation and stream variants of the affine matmul.
+ * Streams are passed as `void *` (a cudaStream_t; NULL = the legacy
+ * default stream, which orders with every blocking stream of the device,
+ * e.g. PyTorch's default stream) so the header needs no CUDA include.
+ */
+#ifndef HXQ_CUDA_H
+#define HXQ_CUDA_H
+
+#include "hxq.h"
+#include "hxq_affine.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes beyond the reference enum (values the reference never
+ * returns, so existing switch statements fall to their default). */
+#define HXQ_ERR_CUDA                 ((hxq_error_t)32) /* CUDA runtime failure   */
+#define HXQ_ERR_BACKEND_UNAVAILABLE  ((hxq_error_t)33) /* no device / backend    */
+#define HXQ_ERR_INVALID_ARG          ((hxq_error_t)34) /* bad size, range, dtype */
+#define HXQ_ERR_NCCL                 ((hxq_error_t)35) /* collective failed      */
+
+/* Human-readable name of any status code above or in hxq.h. */
+const char *hxq_error_string(hxq_error_t err);
+
+/* Version of this implementation (the API level is HXQ_VERSION_STRING). */
+const char *hxq_b200_version(void);
+
+/* Number of visible CUDA devices (0 when there is none or no driver). */
+int hxq_cuda_device_count(void);
+
+/* -- Device arena -------------------------------------------------------
+ * A shared buffer whose `data` is device memory on the current device.
+ * hxq_dequant / hxq_tensor_decompress_shared grow it as the reference's
+ * realloc does (new allocation, old contents copied over) and
+ * hxq_shared_buffer_free releases it. */
+hxq_error_t hxq_cuda_arena_init(hxq_shared_buffer_t *buf,
+                                size_t capacity_floats);
+/* 1 if `buf` is a device arena, 0 if it is a host buffer. */
+int hxq_cuda_buffer_is_device(const hxq_shared_buffer_t *buf);
+
+/* -- Output element type ------------------------------------------------ */
+typedef enum {
+    HXQ_OUT_F32  = 0,    /* fp32, bit-exact with the reference            */
+    HXQ_OUT_BF16 = 1,    /* bf16 = round-to-nearest-even of the fp32 value */
+} hxq_out_dtype_t;
+
+/* Decompress into device memory in the given dtype; same semantics as
+ * hxq_tensor_decompress (which is the fp32 case).  Synchronous. */
+hxq_error_t hxq_cuda_decompress(hxq_tensor_t *t, void *d_out,
+                                hxq_out_dtype_t dtype);
+
+/* bf16 meta-kernel into a device arena: result->weights points at bf16
+ * data (cast it to uint16_t / __nv_bfloat16).  The arena's capacity is
+ * counted in floats, so a bf16 tensor needs half of out_f*in_f. */
+hxq_error_t hxq_dequant_bf16(hxq_tensor_t *t, hxq_shared_buffer_t *arena,
+                             hxq_result_t *result);
+
+/* Drop the device copy of `t` (the next CUDA decompress rebuilds it).
+ * Loaders and hxq_tensor_free already do this; call it after changing a
+ * loaded host array in place. */
+void hxq_cuda_tensor_invalidate(const hxq_tensor_t *t);
+
+/* -- Images and batched decompress -------------------------------------- */
+
+/* A device copy of rows [row_begin, row_end) of a loaded VQ tensor
+ * (scalar or 12-bit), on the device current at creation.  The image does
+ * not reference `t` afterwards. */
+typedef struct hxq_cuda_image hxq_cuda_image_t;
+
+hxq_error_t hxq_cuda_image_create(const hxq_tensor_t *t, uint32_t row_begin,
+                                  uint32_t row_end, hxq_cuda_image_t **img);
+void        hxq_cuda_image_destroy(hxq_cuda_image_t *img);
+/* rows * in_features of the image. */
+size_t      hxq_cuda_image_numel(const hxq_cuda_image_t *img);
+/* Device bytes held by the image (index bytes, codebook, sidecar). */
+size_t      hxq_cuda_image_device_bytes(const hxq_cuda_image_t *img);
+/* Sum of squared in-range sidecar deltas of the image, computed on the
+ * host at creation (double); the shards of one tensor add up to the
+ * tensor's, and sqrt of the total is its confidence. */
+double      hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img);
+
+/* Streamed image: the same preprocessed block, kept in pinned host memory
+ * instead of HBM, for weights that live on the host and cross PCIe each
+ * time they are used.  hxq_cuda_image_upload copies the block
+ * (hxq_cuda_image_block_bytes of it) to d_dst (256-B aligned device
+ * memory) on `stream` and makes the image decompress from there; order the
+ * decompress after the copy (same stream or an event), and do not reuse
+ * d_dst while a decompress of the image may still read it. */
+hxq_error_t hxq_cuda_image_create_streamed(const hxq_tensor_t *t, uint32_t row_begin,
+                                           uint32_t row_end, hxq_cuda_image_t **img);
+size_t      hxq_cuda_image_block_bytes(const hxq_cuda_image_t *img);
+hxq_error_t hxq_cuda_image_upload(hxq_cuda_image_t *img, void *d_dst, void *stream);
+
+/* Kernels this library has launched in this process (all devices). */
+unsigned long long hxq_cuda_launch_count(void);
+
+/* Decompress n images in one stream-ordered launch.  Image i is written
+ * at element offset out_offsets[i] of d_out (elements of `dtype`).
+ * d_sumsq (n doubles) and d_conf (n floats) are optional device outputs:
+ * each image's sum of squared deltas and sqrt of it, reduced on the GPU.
+ * Device-side errors (an index >= k) are reported by
+ * hxq_cuda_stream_synchronize.  n <= HXQ_CUDA_MAX_BATCH. */
+#define HXQ_CUDA_MAX_BATCH 64
+hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs,
+                                       uint32_t n, void *d_out,
+                                       const size_t *out_offsets,
+                                       hxq_out_dtype_t dtype, double *d_sumsq,
+                                       float *d_conf, void *stream);
+
+/* Wait for `stream` and report (and clear) errors its decompress kernels
+ * recorded on the device. */
+hxq_error_t hxq_cuda_stream_synchronize(void *stream);
+
+/* -- The reference's GPU launchers (src/hxq_cuda.cu:209-288) -------------
+ * Exported, undeclared in the reference; device pointers throughout.
+ * Return 0 on success and -1 on error (the reference's convention). */
+int   hxq_cuda_decompress_scalar(const float *d_codebook,
+                                 const uint8_t *d_indices, float *d_output,
+                                 uint32_t out_f, uint32_t in_f);
+int   hxq_cuda_decompress_vq2d_12bit(const float *d_codebook,
+                                     const uint8_t *d_packed, float *d_output,
+                                     uint32_t out_f, uint32_t in_f);
+/* Adds the in-range entries to d_output (in array order per coordinate)
+ * and returns sqrt(sum v^2); negative on error. */
+float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
+                             const float *d_vals, float *d_output,
+                             uint32_t in_f, uint32_t nnz);
+
+/* -- Affine matmul variants --------------------------------------------- */
+
+/* bf16 activations (uint16_t bit patterns, [N, in_f]); fp32 output.
+ * Products of bf16 x and integer codes are exact, accumulation is fp32. */
+int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16,
+                                 const hxq_affine_tensor_t *tensor,
+                                 float *d_output, uint32_t N, void *stream);
+/* fp32 activations on a caller stream. */
+int hxq_affine_group_matmul_async(const float *d_x,
+                                  const hxq_affine_tensor_t *tensor,
+                                  float *d_output, uint32_t N, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HXQ_CUDA_H */

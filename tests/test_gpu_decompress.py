@@ -1,0 +1,306 @@
+"""CUDA decompress path against the reference: golden vectors produced by the
+reference library, and the oracle on seeded inputs at the benchmark sizes.
+
+Bar: weights bit-exact (fp32) or equal to round-to-nearest-even of the
+reference's fp32 value (bf16); status codes identical; confidence within
+relative 1e-5 of the reference's own sequential fp32 sum (the north-star
+tolerance) and within 1e-6 of the exactly computed value.
+All calls go through the C ABI of libhxq.so.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import golden_names, load_golden
+from hxq_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+CONF_REL_REF = 1e-5     # vs the reference's fp32 running sum
+CONF_REL_EXACT = 1e-6   # vs the sum computed in double
+
+
+def _dev(torch, host: np.ndarray):
+    return torch.from_numpy(np.ascontiguousarray(host)).cuda()
+
+
+def _check_conf(got, ref_conf, exact):
+    if exact == 0.0:
+        assert got == 0.0
+        return
+    assert abs(got - ref_conf) <= CONF_REL_REF * abs(ref_conf), (got, ref_conf)
+    assert abs(got - exact) <= CONF_REL_EXACT * exact, (got, exact)
+
+
+def _bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def _golden_tensor(H, g):
+    t = H.Tensor()
+    if g["mode"] == 3:
+        assert t.load_affine(g["codes"], g["scales"], g["offsets"], g["out_f"], g["in_f"], g["gs"]) == 0
+    else:
+        assert t.load_codebook(g["codebook"], g.get("call_k") or g["k"], g["vdim"]) == 0
+        if g["mode"] == 0:
+            assert t.load_indices_8bit(g["indices"], g["out_f"], g["in_f"]) == 0
+        else:
+            assert t.load_indices_12bit(g["packed"], g["out_f"], g["in_f"], length=g.get("call_idx_len")) == 0
+    if g.get("rows") is not None and len(g["rows"]):
+        assert t.load_sidecar(g["rows"], g["cols"], g["vals"]) == 0
+    return t
+
+
+@pytest.mark.parametrize("name", [n for n in golden_names() if not n.startswith("affine_mm")])
+def test_golden_fp32_device_output(H, L, oracle, cuda, name):
+    torch = cuda
+    g = load_golden(name)
+    t = _golden_tensor(H, g)
+    t.t.sidecar_l2_norm = -1.0
+    out = _dev(torch, g["out_init"])
+    torch.cuda.synchronize()
+    err = L.hxq_tensor_decompress(t.ref, out.data_ptr())
+    assert err == g["expect_err"]
+    if err != 0:
+        assert t.confidence == -1.0
+        return
+    w = out.cpu().numpy()
+    assert np.array_equal(_bits(w), _bits(g["expect_w"]))
+    _check_conf(t.confidence, float(g["expect_conf"]), oracle.l2_exact(g))
+
+
+@pytest.mark.parametrize("name", ["vq12_64x256", "vq12_odd_6x10", "vq12_dups_16x64", "vq12_k256_32x128",
+                                  "scalar_64x96", "scalar_dups_9x13", "affine_dq_16x256"])
+def test_golden_bf16_device_output(H, L, cuda, name):
+    torch = cuda
+    g = load_golden(name)
+    t = _golden_tensor(H, g)
+    n = g["out_f"] * g["in_f"]
+    out = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+    assert L.hxq_cuda_decompress(t.ref, out.data_ptr(), H.HXQ_OUT_BF16) == 0
+    got = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.array_equal(got, synth.bf16_round(g["expect_w"]))
+
+
+def test_c1_full_vq12_2048(H, L, oracle, cuda):
+    torch = cuda
+    d = synth.vq12(2048, 2048, synth.SEED_C1)
+    err, w_ref, conf_ref = oracle.decompress(d)
+    assert err == 0
+    t = H.Tensor().load(d)
+    out = torch.empty(2048 * 2048, dtype=torch.float32, device="cuda")
+    for _ in range(2):  # second call reuses the cached device image and scratch
+        out.fill_(float("nan"))
+        torch.cuda.synchronize()
+        assert L.hxq_tensor_decompress(t.ref, out.data_ptr()) == 0
+        assert np.array_equal(_bits(out.cpu().numpy()), _bits(w_ref))
+        _check_conf(t.confidence, conf_ref, oracle.l2_exact(d))
+    first = t.confidence
+    assert L.hxq_tensor_decompress(t.ref, out.data_ptr()) == 0
+    assert t.confidence == first  # deterministic reduction
+
+
+def test_c2_scalar_arena_fp32_and_bf16(H, L, oracle, cuda):
+    d = synth.scalar(4096, 4096, synth.SEED_C2)
+    small = synth.scalar(64, 128, 5, frac=0.01)
+    err, w_ref, conf_ref = oracle.decompress(d)
+    t, ts = H.Tensor().load(d), H.Tensor().load(small)
+    arena = H.SharedBuffer()
+    assert L.hxq_cuda_arena_init(C.byref(arena), 1024) == 0
+    assert L.hxq_cuda_buffer_is_device(C.byref(arena)) == 1
+    r = H.Result()
+    # reused arena: small tensor, big tensor (grows), small again
+    for tt, dd in ((ts, small), (t, d), (ts, small)):
+        for backend in (H.HXQ_BACKEND_CUDA, H.HXQ_BACKEND_AUTO):
+            assert L.hxq_dequant(tt.ref, C.byref(arena), backend, C.byref(r)) == 0
+            n = dd["out_f"] * dd["in_f"]
+            host = np.empty(n, np.float32)
+            assert r.out_features == dd["out_f"] and r.in_features == dd["in_f"]
+            _copy_d2h(cuda, r.weights, host)
+            e2, w2, c2 = oracle.decompress(dd)
+            assert np.array_equal(_bits(host), _bits(w2))
+            _check_conf(r.confidence, c2, oracle.l2_exact(dd))
+    assert arena.high_water == 4096 * 4096 and arena.capacity >= 4096 * 4096
+    # bf16 into the same arena
+    assert L.hxq_dequant_bf16(t.ref, C.byref(arena), C.byref(r)) == 0
+    got = np.empty(4096 * 4096, np.uint16)
+    _copy_d2h(cuda, r.weights, got)
+    assert np.array_equal(got, synth.bf16_round(w_ref))
+    _check_conf(r.confidence, conf_ref, oracle.l2_exact(d))
+    # CPU backend refuses a device arena
+    assert L.hxq_dequant(t.ref, C.byref(arena), H.HXQ_BACKEND_CPU, C.byref(r)) == H.HXQ_ERR_INVALID_ARG
+    L.hxq_shared_buffer_free(C.byref(arena))
+    assert arena.capacity == 0 and L.hxq_cuda_buffer_is_device(C.byref(arena)) == 0
+
+
+def _copy_d2h(torch, dptr, host: np.ndarray):
+    """Copy n elements at a raw device pointer into a numpy array."""
+    from hxq_b200 import device_view
+    torch.cuda.synchronize()
+    host[:] = device_view(torch, dptr, host.size, host.dtype).cpu().numpy()
+
+
+def test_dequant_cuda_backend_host_buffer(H, L, oracle, cuda):
+    d = synth.vq12(512, 1024, 77)
+    t = H.Tensor().load(d)
+    buf = H.SharedBuffer()
+    assert L.hxq_shared_buffer_init(C.byref(buf), 16) == 0
+    r = H.Result()
+    assert L.hxq_dequant(t.ref, C.byref(buf), H.HXQ_BACKEND_CUDA, C.byref(r)) == 0
+    w = np.ctypeslib.as_array(C.cast(r.weights, C.POINTER(C.c_float)), shape=(512 * 1024,)).copy()
+    err, w_ref, conf = oracle.decompress(d)
+    assert np.array_equal(_bits(w), _bits(w_ref))
+    _check_conf(r.confidence, conf, oracle.l2_exact(d))
+    assert buf.high_water == 512 * 1024
+    L.hxq_shared_buffer_free(C.byref(buf))
+
+
+def _image(H, L, t, r0, r1):
+    img = C.c_void_p()
+    assert L.hxq_cuda_image_create(t.ref, r0, r1, C.byref(img)) == 0
+    return img
+
+
+def test_batched_images_mixed_kinds(H, L, oracle, cuda):
+    torch = cuda
+    ds = [synth.vq12(256, 512, 1), synth.scalar(100, 300, 2, frac=0.02), synth.vq12(64, 1024, 3, k=256),
+          synth.vq12(37, 30, 4, frac=0.05),   # in_f % 4 != 0: generic kernel
+          synth.vq12(128, 4096, 5), synth.scalar(7, 5, 6, frac=0.3)]
+    ts = [H.Tensor().load(d) for d in ds]
+    imgs = [_image(H, L, t, 0, d["out_f"]) for t, d in zip(ts, ds)]
+    sizes = [d["out_f"] * d["in_f"] for d in ds]
+    offs = np.zeros(len(ds), np.uint64)
+    pos = 0
+    for i, n in enumerate(sizes):
+        offs[i] = pos
+        pos += (n + 63) // 64 * 64 + 4  # +4 floats: the next slot is only 16-B aligned
+    out = torch.full((pos,), float("nan"), dtype=torch.float32, device="cuda")
+    sumsq = torch.zeros(len(ds), dtype=torch.float64, device="cuda")
+    conf = torch.zeros(len(ds), dtype=torch.float32, device="cuda")
+    arr = (C.c_void_p * len(ds))(*[i.value for i in imgs])
+    offs_c = (C.c_size_t * len(ds))(*[int(o) for o in offs])
+    torch.cuda.synchronize()
+    assert L.hxq_cuda_decompress_images(arr, len(ds), out.data_ptr(), offs_c, H.HXQ_OUT_F32,
+                                        sumsq.data_ptr(), conf.data_ptr(), None) == 0
+    assert L.hxq_cuda_stream_synchronize(None) == 0
+    host = out.cpu().numpy()
+    ss, cf = sumsq.cpu().numpy(), conf.cpu().numpy()
+    for i, d in enumerate(ds):
+        init = np.full(sizes[i], np.nan, np.float32)
+        err, w_ref, c_ref = oracle.decompress(d, out=init)
+        got = host[int(offs[i]): int(offs[i]) + sizes[i]]
+        assert np.array_equal(_bits(got), _bits(w_ref)), i
+        exact = oracle.l2_exact(d)
+        assert abs(ss[i] - exact * exact) <= 1e-12 + 1e-9 * exact * exact
+        assert abs(L.hxq_cuda_image_sidecar_sumsq(imgs[i]) - exact * exact) <= 1e-9 * max(exact * exact, 1e-30)
+        _check_conf(float(cf[i]), c_ref, exact)
+    for im in imgs:
+        L.hxq_cuda_image_destroy(im)
+
+
+def test_row_shards_reassemble(H, L, oracle, cuda):
+    torch = cuda
+    d = synth.vq12(1376 * 3, 4096, 9)  # 11008/8-style ragged row count per shard
+    t = H.Tensor().load(d)
+    bounds = [0, 1376, 2752, d["out_f"]]
+    imgs = [_image(H, L, t, bounds[i], bounds[i + 1]) for i in range(3)]
+    out = torch.empty(d["out_f"] * d["in_f"], dtype=torch.float32, device="cuda")
+    sumsq = torch.zeros(3, dtype=torch.float64, device="cuda")
+    arr = (C.c_void_p * 3)(*[i.value for i in imgs])
+    offs = (C.c_size_t * 3)(*[b * d["in_f"] for b in bounds[:3]])
+    assert L.hxq_cuda_decompress_images(arr, 3, out.data_ptr(), offs, 0, sumsq.data_ptr(), None, None) == 0
+    assert L.hxq_cuda_stream_synchronize(None) == 0
+    err, w_ref, c_ref = oracle.decompress(d)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(w_ref))
+    total = float(sumsq.sum().item())
+    _check_conf(float(np.float32(np.sqrt(total))), c_ref, oracle.l2_exact(d))
+    for im in imgs:
+        L.hxq_cuda_image_destroy(im)
+
+
+def test_unaligned_output_uses_generic_path(H, L, oracle, cuda):
+    torch = cuda
+    for d in (synth.vq12(33, 64, 11, frac=0.05), synth.scalar(40, 50, 12, frac=0.05)):
+        t = H.Tensor().load(d)
+        n = d["out_f"] * d["in_f"]
+        buf = torch.zeros(n + 1, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        assert L.hxq_tensor_decompress(t.ref, buf.data_ptr() + 4) == 0
+        err, w_ref, c_ref = oracle.decompress(d)
+        assert np.array_equal(_bits(buf.cpu().numpy()[1:]), _bits(w_ref))
+        _check_conf(t.confidence, c_ref, oracle.l2_exact(d))
+
+
+def test_index_oob_reported_and_cleared(H, L, oracle, cuda):
+    torch = cuda
+    g = load_golden("vq12_oob_8x64")
+    t = _golden_tensor(H, g)
+    out = torch.zeros(8 * 64, dtype=torch.float32, device="cuda")
+    t.t.sidecar_l2_norm = 3.0
+    assert L.hxq_tensor_decompress(t.ref, out.data_ptr()) == H.HXQ_ERR_INDEX_OOB
+    assert t.confidence == 3.0
+    d = synth.vq12(8, 64, 3)
+    t2 = H.Tensor().load(d)
+    assert L.hxq_tensor_decompress(t2.ref, out.data_ptr()) == 0  # error word was cleared
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(oracle.decompress(d)[1]))
+
+
+def test_reload_invalidates_device_copy(H, L, oracle, cuda):
+    torch = cuda
+    a, b = synth.vq12(64, 128, 21), synth.vq12(64, 128, 22)
+    t = H.Tensor().load(a)
+    out = torch.empty(64 * 128, dtype=torch.float32, device="cuda")
+    assert L.hxq_tensor_decompress(t.ref, out.data_ptr()) == 0
+    assert t.load_indices_12bit(b["packed"], 64, 128) == 0
+    assert t.load_codebook(b["codebook"], 4096, 2) == 0
+    assert t.load_sidecar(b["rows"], b["cols"], b["vals"]) == 0
+    assert L.hxq_tensor_decompress(t.ref, out.data_ptr()) == 0
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(oracle.decompress(b)[1]))
+
+
+def test_reference_gpu_launchers(H, L, oracle, cuda):
+    torch = cuda
+    d = synth.vq12(96, 256, 31, frac=0.01)
+    dn = dict(d, rows=None)
+    cb, pk = _dev(torch, d["codebook"]), _dev(torch, d["packed"])
+    out = torch.empty(96 * 256, dtype=torch.float32, device="cuda")
+    assert L.hxq_cuda_decompress_vq2d_12bit(cb.data_ptr(), pk.data_ptr(), out.data_ptr(), 96, 256) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(oracle.decompress(dn)[1]))
+    r, c, v = _dev(torch, d["rows"]), _dev(torch, d["cols"]), _dev(torch, d["vals"])
+    conf = L.hxq_cuda_apply_sidecar(r.data_ptr(), c.data_ptr(), v.data_ptr(), out.data_ptr(), 256, len(d["rows"]))
+    err, w_ref, c_ref = oracle.decompress(d)
+    assert np.array_equal(_bits(out.cpu().numpy()), _bits(w_ref))
+    _check_conf(conf, c_ref, oracle.l2_exact(d))
+    s = synth.scalar(50, 70, 32)
+    sn = dict(s, rows=None)
+    cb2, ix = _dev(torch, s["codebook"]), _dev(torch, s["indices"])
+    out2 = torch.empty(50 * 70, dtype=torch.float32, device="cuda")
+    assert L.hxq_cuda_decompress_scalar(cb2.data_ptr(), ix.data_ptr(), out2.data_ptr(), 50, 70) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(out2.cpu().numpy()), _bits(oracle.decompress(sn)[1]))
+
+
+def test_llama7b_layer0_batch(H, L, oracle, cuda):
+    """One 7B layer (q,k,v,o,gate,up,down) in one launch, each bit-exact."""
+    torch = cuda
+    ds = [synth.vq12(o, i, synth.llama7b_seed(0, p)) for p, (_, o, i) in enumerate(synth.LLAMA7B_PROJ)]
+    ts = [H.Tensor().load(d) for d in ds]
+    imgs = [_image(H, L, t, 0, d["out_f"]) for t, d in zip(ts, ds)]
+    sizes = [d["out_f"] * d["in_f"] for d in ds]
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    out = torch.empty(int(sum(sizes)), dtype=torch.float32, device="cuda")
+    conf = torch.zeros(7, dtype=torch.float32, device="cuda")
+    arr = (C.c_void_p * 7)(*[i.value for i in imgs])
+    offs_c = (C.c_size_t * 7)(*[int(o) for o in offs])
+    assert L.hxq_cuda_decompress_images(arr, 7, out.data_ptr(), offs_c, 0, None, conf.data_ptr(), None) == 0
+    assert L.hxq_cuda_stream_synchronize(None) == 0
+    cf = conf.cpu().numpy()
+    for i, d in enumerate(ds):
+        err, w_ref, c_ref = oracle.decompress(d)
+        got = out[int(offs[i]): int(offs[i]) + sizes[i]].cpu().numpy()
+        assert np.array_equal(_bits(got), _bits(w_ref)), i
+        _check_conf(float(cf[i]), c_ref, oracle.l2_exact(d))
+    for im in imgs:
+        L.hxq_cuda_image_destroy(im)

@@ -77,6 +77,13 @@ struct Scratch {
     float    *conf      = nullptr;   // kMaxJobs
 };
 
+// Resident CTAs per SM of the fast kernel: the scalar variant holds four
+// 16-byte index pieces per lane in flight and needs more registers.
+__host__ __device__ constexpr uint32_t ctas_per_sm(uint32_t kind)
+{
+    return kind == kKindVq12 ? 4u : 3u;
+}
+
 // Error bits written to the device error word.
 constexpr uint32_t kErrIndexOOB = 1u;
 
@@ -85,7 +92,7 @@ constexpr uint32_t kErrIndexOOB = 1u;
 cudaError_t configure_vq_kernels();
 cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
                            int check_k, cudaStream_t s);
-uint32_t    fast_grid(uint64_t total_chunks, int sms);
+uint32_t    fast_grid(uint64_t total_chunks, int sms, uint32_t kind);
 
 // Generic kernels (any shape/alignment; one image per launch).
 struct GenericJob {

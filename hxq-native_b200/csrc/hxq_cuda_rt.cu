@@ -54,7 +54,8 @@ struct hxq_cuda_image {
     SideEntry *d_ent = nullptr;
     uint32_t  n_chunks = 0;
     uint32_t  n_ent = 0;
-    double    sumsq = 0.0;
+    double    sumsq = 0.0;     // exact sum of squared in-range deltas
+    float     ref_l2 = 0.0f;   // sqrtf of the fp32 running sum in array order
 };
 
 namespace {
@@ -185,7 +186,7 @@ hxq_error_t get_scratch(int dev, cudaStream_t s, Scratch **out)
     DevCtx &d = g_dev[dev];
     auto it = d.scratch.find(s);
     if (it != d.scratch.end()) { *out = &it->second; return HXQ_OK; }
-    const uint32_t n_slots = (uint32_t)(kMaxJobs + 8u * (uint32_t)std::max(d.sms, 148) + 1024u);
+    const uint32_t n_slots = (uint32_t)(kMaxJobs + 4u * (uint32_t)std::max(d.sms, 148) + 1024u);
     const size_t bytes = 16 + kMaxJobs * 4 + kMaxJobs * 8 + kMaxJobs * 4 + (size_t)n_slots * 8;
     unsigned char *base = nullptr;
     cudaError_t e = cudaMalloc(&base, bytes);
@@ -212,10 +213,17 @@ struct HostEntry { uint64_t pos; float val; };
 
 // Sidecar entries of rows [r0, r1) that the reference would apply (r < out_f
 // and c < in_f, src/hxq.c:343), in array order, positions relative to r0.
+// Also returns, in *seq, the confidence exactly as the reference computes
+// it: a float running sum of v*v in array order (src/hxq.c:335-349).  That
+// order is inherently sequential, and over 1e5 terms its rounding drifts a
+// few 1e-5 from the true value, beyond reach of any parallel reduction; it
+// depends only on the loaded sidecar, so it is computed here once.
 void collect_sidecar(const hxq_tensor_t *t, uint32_t r0, uint32_t r1,
-                     std::vector<HostEntry> &ents, double &sumsq)
+                     std::vector<HostEntry> &ents, double &sumsq, float *seq)
 {
     sumsq = 0.0;
+    volatile float run = 0.0f;  // one rounded product, one rounded add per term
+    *seq = 0.0f;
     ents.clear();
     if (t->sidecar_nnz == 0 || !t->sidecar_rows || !t->sidecar_cols || !t->sidecar_vals) return;
     const uint32_t in_f = t->in_features, out_f = t->out_features;
@@ -225,7 +233,10 @@ void collect_sidecar(const hxq_tensor_t *t, uint32_t r0, uint32_t r1,
         const float v = t->sidecar_vals[i];
         ents.push_back({(uint64_t)(r - r0) * in_f + c, v});
         sumsq += (double)v * (double)v;
+        volatile float sq = v * v;
+        run = run + sq;
     }
+    *seq = sqrtf(run);
     bool sorted = true;
     for (size_t i = 1; i < ents.size() && sorted; ++i) sorted = ents[i - 1].pos <= ents[i].pos;
     if (!sorted)
@@ -321,7 +332,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
 
     std::vector<HostEntry> ents;
-    collect_sidecar(t, r0, r1, ents, img->sumsq);
+    collect_sidecar(t, r0, r1, ents, img->sumsq, &img->ref_l2);
     const bool fast = img->kind == kKindScalar || img->kind == kKindVq12;
     if (!fast && img->numel > 0xFFFFFFFFull) { delete img; return HXQ_ERR_INVALID_ARG; }
 
@@ -483,7 +494,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
     }
     p.n_jobs = (uint32_t)which.size();
     p.total_chunks = total;
-    p.grid = fast_grid(total, sms);
+    p.grid = fast_grid(total, sms, imgs[which[0]]->kind);
     uint32_t slot = 0;
     for (uint32_t n = 0; n < p.n_jobs; ++n) {
         VqJob &J = p.job[n];
@@ -640,7 +651,12 @@ hxq_error_t decompress_sync(hxq_tensor_t *t, void *d_out, int bf16, float *l2)
     const size_t off0 = 0;
     err = launch_images(&img, 1, d_out, &off0, bf16, sc->sumsq, sc->conf, dev, (cudaStream_t)0);
     if (err != HXQ_OK) return err;
-    return sync_and_check(dev, (cudaStream_t)0, l2);
+    float gpu_l2 = 0.0f;
+    if ((err = sync_and_check(dev, (cudaStream_t)0, &gpu_l2)) != HXQ_OK) return err;
+    // The drop-in API reports the reference's own value (see collect_sidecar);
+    // the kernel's fused fp64 reduction (gpu_l2) is the exact one.
+    *l2 = img->ref_l2;
+    return HXQ_OK;
 }
 
 }  // namespace
@@ -921,6 +937,8 @@ size_t hxq_cuda_image_numel(const hxq_cuda_image_t *img) { return img ? (size_t)
 size_t hxq_cuda_image_device_bytes(const hxq_cuda_image_t *img) { return img ? img->block_bytes : 0; }
 
 double hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img) { return img ? img->sumsq : 0.0; }
+
+float hxq_cuda_image_reference_confidence(const hxq_cuda_image_t *img) { return img ? img->ref_l2 : 0.0f; }
 
 hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n,
                                        void *d_out, const size_t *out_offsets,

@@ -99,28 +99,49 @@ __device__ __forceinline__ void load_codebook(unsigned char *cb_area,
     }
 }
 
+// Inputs of one chunk, loaded one chunk ahead of their use.
+template <uint32_t VPL>
+struct ChunkIn {
+    uint4     r[VPL];      // this lane's 16-byte pieces of the index bytes
+    uint32_t  e0, e1;      // sidecar entries [e0, e1) of the chunk
+    SideEntry ent;         // entry e0 + lane (if any)
+};
+
+template <uint32_t VPL>
+__device__ __forceinline__ void prefetch_chunk(const VqJob &J, uint32_t c, uint32_t lane,
+                                               ChunkIn<VPL> &in)
+{
+    const uint4 *src = J.idx + (size_t)c * (VPL * 32u);
+#pragma unroll
+    for (uint32_t q = 0; q < VPL; ++q) in.r[q] = ld_stream_v4(src + q * 32u + lane);
+    in.e0 = __ldg(J.chunk_ptr + c);
+    in.e1 = __ldg(J.chunk_ptr + c + 1);
+}
+
+template <uint32_t VPL>
+__device__ __forceinline__ void prefetch_entry(const VqJob &J, uint32_t lane, ChunkIn<VPL> &in)
+{
+    in.ent = SideEntry{0u, 0u};
+    if (in.e0 + lane < in.e1) in.ent = ld_entry(J.ent + in.e0 + lane);
+}
+
+template <uint32_t VPL>
+__device__ __forceinline__ void stage_chunk(const ChunkIn<VPL> &in, uint4 *stage, uint32_t lane)
+{
+    __syncwarp();  // previous chunk's readers of `stage` are done
+#pragma unroll
+    for (uint32_t q = 0; q < VPL; ++q) stage[q * 32u + lane] = in.r[q];
+    __syncwarp();
+}
+
 // One 12-bit chunk (512 triples, 2048 weights).
 template <bool BF16, bool CHECK_K>
-__device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c,
-                                           const unsigned char *cb_area,
-                                           uint4 *stage, uint32_t lane,
-                                           double &acc, uint32_t &errflag)
+__device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c, const ChunkIn<3> &in,
+                                           const unsigned char *cb_area, uint4 *stage,
+                                           uint32_t lane, double &acc, uint32_t &errflag)
 {
-    const uint4 *src = J.idx + (size_t)c * (kChunkBytes12 / 16u);
-    const uint4 r0 = ld_stream_v4(src + lane);
-    const uint4 r1 = ld_stream_v4(src + 32 + lane);
-    const uint4 r2 = ld_stream_v4(src + 64 + lane);
-    const uint32_t e0 = __ldg(J.chunk_ptr + c);
-    const uint32_t e1 = __ldg(J.chunk_ptr + c + 1);
-    SideEntry ent{0u, 0u};
-    if (e0 + lane < e1) ent = ld_entry(J.ent + e0 + lane);
-
-    __syncwarp();  // previous chunk's readers of `stage` are done
-    stage[lane] = r0;
-    stage[32 + lane] = r1;
-    stage[64 + lane] = r2;
-    __syncwarp();
-
+    stage_chunk<3>(in, stage, lane);
+    const uint32_t e0 = in.e0, e1 = in.e1;
     const uint64_t w0 = (uint64_t)c * kChunkW;
     const uint64_t left = J.numel - w0;
     const uint32_t ntrip = (left >= kChunkW ? kChunkW : (uint32_t)left) >> 2;
@@ -151,7 +172,7 @@ __device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c,
     for (uint32_t base = e0; base < e1; base += 32u) {
         const uint32_t e = base + lane;
         if (e >= e1) continue;
-        const SideEntry en = (base == e0) ? ent : ld_entry(J.ent + e);
+        const SideEntry en = (base == e0) ? in.ent : ld_entry(J.ent + e);
         const float v = __uint_as_float(en.y);
         acc += (double)v * (double)v;
         const uint32_t run = en.x >> 16;
@@ -177,28 +198,13 @@ __device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c,
 
 // One scalar chunk (2048 uint8 indices, 2048 weights).
 template <bool BF16>
-__device__ __forceinline__ void chunk_scalar(const VqJob &J, uint32_t c,
-                                             const unsigned char *cb_area,
-                                             uint4 *stage, uint32_t lane,
-                                             double &acc)
+__device__ __forceinline__ void chunk_scalar(const VqJob &J, uint32_t c, const ChunkIn<4> &in,
+                                             const unsigned char *cb_area, uint4 *stage,
+                                             uint32_t lane, double &acc)
 {
-    const uint4 *src = J.idx + (size_t)c * (kChunkBytes8 / 16u);
-    const uint4 r0 = ld_stream_v4(src + lane);
-    const uint4 r1 = ld_stream_v4(src + 32 + lane);
-    const uint4 r2 = ld_stream_v4(src + 64 + lane);
-    const uint4 r3 = ld_stream_v4(src + 96 + lane);
-    const uint32_t e0 = __ldg(J.chunk_ptr + c);
-    const uint32_t e1 = __ldg(J.chunk_ptr + c + 1);
-    SideEntry ent{0u, 0u};
-    if (e0 + lane < e1) ent = ld_entry(J.ent + e0 + lane);
-
-    __syncwarp();
-    stage[lane] = r0;
-    stage[32 + lane] = r1;
-    stage[64 + lane] = r2;
-    stage[96 + lane] = r3;
-    __syncwarp();
-
+    stage_chunk<4>(in, stage, lane);
+    const uint32_t e0 = in.e0, e1 = in.e1;
+    const SideEntry ent = in.ent;
     const uint64_t w0 = (uint64_t)c * kChunkW;
     const uint64_t left = J.numel - w0;
     const uint32_t nw = left >= kChunkW ? kChunkW : (uint32_t)left;
@@ -267,7 +273,7 @@ __host__ __device__ constexpr uint32_t fast_smem_bytes()
 }
 
 template <uint32_t KIND, bool BF16, bool CHECK_K>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, ctas_per_sm(KIND))
 vq_fast_kernel(const __grid_constant__ VqLaunch p)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -295,12 +301,28 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
         __syncthreads();
 
         double acc = 0.0;
-        for (uint64_t ch = pos + warp; ch < seg_end; ch += kWarps) {
+        // software pipeline: chunk ch+kWarps's index bytes and entry range are
+        // in flight while chunk ch is processed; its first sidecar entry is
+        // requested once that range has arrived, a whole chunk before use.
+        constexpr uint32_t VPL = (KIND == kKindVq12) ? 3u : 4u;
+        ChunkIn<VPL> cur, nxt;
+        uint64_t ch = pos + warp;
+        if (ch < seg_end) {
+            prefetch_chunk<VPL>(J, (uint32_t)(ch - J.chunk_begin), lane, cur);
+            prefetch_entry<VPL>(J, lane, cur);
+        }
+        for (; ch < seg_end; ch += kWarps) {
             const uint32_t c = (uint32_t)(ch - J.chunk_begin);
-            if (KIND == kKindVq12)
-                chunk_vq12<BF16, CHECK_K>(J, c, cb_area, stage, lane, acc, errflag);
+            const bool more = ch + kWarps < seg_end;
+            if (more) prefetch_chunk<VPL>(J, c + kWarps, lane, nxt);
+            if constexpr (KIND == kKindVq12)
+                chunk_vq12<BF16, CHECK_K>(J, c, cur, cb_area, stage, lane, acc, errflag);
             else
-                chunk_scalar<BF16>(J, c, cb_area, stage, lane, acc);
+                chunk_scalar<BF16>(J, c, cur, cb_area, stage, lane, acc);
+            if (more) {
+                prefetch_entry<VPL>(J, lane, nxt);
+                cur = nxt;
+            }
         }
 
         acc = warp_sum(acc);
@@ -509,9 +531,9 @@ cudaError_t configure_vq_kernels()
     return configure_one<kKindScalar, true, false>();
 }
 
-uint32_t fast_grid(uint64_t total_chunks, int sms)
+uint32_t fast_grid(uint64_t total_chunks, int sms, uint32_t kind)
 {
-    uint64_t g = (uint64_t)(sms > 0 ? sms : 148) * 4u;
+    uint64_t g = (uint64_t)(sms > 0 ? sms : 148) * ctas_per_sm(kind);
     if (g > total_chunks) g = total_chunks;
     return (uint32_t)(g == 0 ? 1 : g);
 }

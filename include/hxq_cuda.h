@@ -91,6 +91,13 @@ size_t      hxq_cuda_image_device_bytes(const hxq_cuda_image_t *img);
  * host at creation (double); the shards of one tensor add up to the
  * tensor's, and sqrt of the total is its confidence. */
 double      hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img);
+/* The confidence as the reference library reports it for these rows:
+ * sqrtf of a float running sum of squares in the sidecar's array order.
+ * hxq_dequant and hxq_tensor_decompress return this value, bit-identical
+ * to the reference; over ~1e5 entries it differs from the exact value
+ * (sqrt of hxq_cuda_image_sidecar_sumsq, and the d_conf output of
+ * hxq_cuda_decompress_images) by the reference's own fp32 rounding. */
+float       hxq_cuda_image_reference_confidence(const hxq_cuda_image_t *img);
 
 /* Streamed image: the same preprocessed block, kept in pinned host memory
  * instead of HBM, for weights that live on the host and cross PCIe each

@@ -1,0 +1,153 @@
+"""Affine group-quantized matmul on the GPU against the reference.
+
+Tolerance (stated by the north star: rel 1e-5 for fp32 paths, 1e-2 for bf16
+paths) is applied per output as |y - y_ref| / sum_i |x_i * w_i|: the
+natural scale of an fp32 dot product's rounding error (a plain relative
+error is ill-posed for outputs near zero).  Both the fp32- and the
+bf16-activation entry points are held to 1e-5 here, since bf16
+activations times integer codes are exact products.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import golden_names, load_golden
+from hxq_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _scale(oracle, x, d):
+    W = oracle.affine_decompress(d).reshape(d["out_f"], d["in_f"]).astype(np.float64)
+    return np.abs(x.astype(np.float64)) @ np.abs(W).T
+
+
+def _check(y, y_ref, scale, tol=TOL):
+    err = np.abs(y.astype(np.float64) - y_ref.astype(np.float64)) / np.maximum(scale, 1e-30)
+    assert float(err.max()) <= tol, float(err.max())
+
+
+class Dev:
+    def __init__(self, torch, d, bias=None):
+        self.torch = torch
+        self.codes = torch.from_numpy(np.ascontiguousarray(d["codes"])).cuda()
+        self.scales = torch.from_numpy(np.ascontiguousarray(d["scales"])).cuda()
+        self.offsets = torch.from_numpy(np.ascontiguousarray(d["offsets"])).cuda()
+        self.bias = None if bias is None else torch.from_numpy(np.ascontiguousarray(bias)).cuda()
+        self.d = d
+
+    def tensor(self, H):
+        return H.AffineTensor(self.codes.data_ptr(), self.scales.data_ptr(), self.offsets.data_ptr(),
+                              None if self.bias is None else self.bias.data_ptr(),
+                              self.d["out_f"], self.d["in_f"], self.d["gs"])
+
+
+def _run_f32(torch, H, L, dev, x, api="struct"):
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    y = torch.full((x.shape[0], dev.d["out_f"]), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    if api == "struct":
+        t = dev.tensor(H)
+        assert L.hxq_affine_group_matmul(xd.data_ptr(), C.byref(t), y.data_ptr(), x.shape[0]) == 0
+    else:
+        d = dev.d
+        assert L.hxq_affine_matmul_flat(xd.data_ptr(), dev.codes.data_ptr(), dev.scales.data_ptr(),
+                                        dev.offsets.data_ptr(), None if dev.bias is None else dev.bias.data_ptr(),
+                                        y.data_ptr(), x.shape[0], d["in_f"], d["out_f"], d["gs"]) == 0
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def _run_bf16(torch, H, L, dev, xh):
+    xd = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+    y = torch.full((xh.shape[0], dev.d["out_f"]), float("nan"), dtype=torch.float32, device="cuda")
+    t = dev.tensor(H)
+    torch.cuda.synchronize()
+    assert L.hxq_affine_group_matmul_bf16(xd.data_ptr(), C.byref(t), y.data_ptr(), xh.shape[0], None) == 0
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", golden_names("affine_mm"))
+@pytest.mark.parametrize("api", ["struct", "flat"])
+def test_golden(H, L, oracle, cuda, name, api):
+    g = load_golden(name)
+    dev = Dev(cuda, g, g.get("bias"))
+    y = _run_f32(cuda, H, L, dev, g["x"], api)
+    _check(y, g["expect_y"], _scale(oracle, g["x"], g))
+
+
+@pytest.mark.parametrize("N", [1, 2, 5, 8, 16, 64])
+def test_c3_4096_small_batches(H, L, oracle, cuda, N):
+    d = synth.affine(4096, 4096, 128, synth.SEED_C3, bias=(N == 5))
+    xh, x = synth.activations(N, 4096, synth.SEED_C3 + N)
+    dev = Dev(cuda, d, d["bias"])
+    ref = oracle.affine_matmul(x, d, bias=d["bias"])
+    sc = _scale(oracle, x, d)
+    _check(_run_bf16(cuda, H, L, dev, xh), ref, sc)
+    _check(_run_f32(cuda, H, L, dev, x), ref, sc)
+
+
+@pytest.mark.parametrize("N", [512, 4096])
+def test_c3_4096_large_batches_sampled(H, L, oracle, cuda, N):
+    d = synth.affine(4096, 4096, 128, synth.SEED_C3)
+    xh, x = synth.activations(N, 4096, synth.SEED_C3 + N)
+    dev = Dev(cuda, d)
+    yb = _run_bf16(cuda, H, L, dev, xh)
+    yf = _run_f32(cuda, H, L, dev, x)
+    rows = sorted({0, 1, N // 3, N // 2, N - 2, N - 1})
+    for n in rows:
+        ref = oracle.affine_matmul(x, d, n0=n, n1=n + 1)
+        sc = _scale(oracle, x[n:n + 1], d)
+        _check(yb[n:n + 1], ref, sc)
+        _check(yf[n:n + 1], ref, sc)
+
+
+@pytest.mark.parametrize("O,I,gs,N", [(33, 96, 32, 3), (40, 120, 24, 2), (17, 256, 128, 9), (64, 1024, 256, 1)])
+def test_odd_shapes(H, L, oracle, cuda, O, I, gs, N):
+    d = synth.affine(O, I, gs, O + I, bias=True)
+    xh, x = synth.activations(N, I, gs)
+    dev = Dev(cuda, d, d["bias"])
+    ref = oracle.affine_matmul(x, d, bias=d["bias"])
+    sc = _scale(oracle, x, d)
+    _check(_run_f32(cuda, H, L, dev, x), ref, sc)
+    _check(_run_bf16(cuda, H, L, dev, xh), ref, sc)
+
+
+@pytest.mark.parametrize("shape", [(2048, 2048), (11008, 2048), (2048, 11008)])
+def test_reference_shapes_6bit_codes(H, L, oracle, cuda, shape):
+    # test/test_affine_cuda.cu:194-272 shapes at N=1 with 6-bit codes
+    O, I = shape
+    d = synth.affine(O, I, 128, O * 3 + I)
+    d["codes"] = (np.random.default_rng(O + I).integers(0, 64, O * I)).astype(np.uint8)
+    _, x = synth.activations(1, I, O)
+    dev = Dev(cuda, d)
+    y = _run_f32(cuda, H, L, dev, x)
+    ref = oracle.affine_matmul(x, d)
+    assert np.max(np.abs(y - ref)) < 1e-3
+    _check(y, ref, _scale(oracle, x, d))
+
+
+def test_bias_only(H, L, oracle, cuda):
+    # test/test_affine_cuda.cu:276-338: zero codes and x, output = bias
+    d = dict(codes=np.zeros(64 * 128, np.uint8), scales=np.ones(64, np.float32), offsets=np.zeros(64, np.float32),
+             out_f=64, in_f=128, gs=128)
+    bias = (np.arange(64, dtype=np.float32) + 1) * 10
+    dev = Dev(cuda, d, bias)
+    y = _run_f32(cuda, H, L, dev, np.zeros((1, 128), np.float32))
+    assert np.max(np.abs(y[0] - bias)) < 1e-5
+
+
+def test_invalid_arguments(H, L, cuda):
+    d = synth.affine(8, 128, 128, 1)
+    dev = Dev(cuda, d)
+    t = dev.tensor(H)
+    t.group_size = 0
+    x = cuda.zeros(128, device="cuda")
+    y = cuda.zeros(8, device="cuda")
+    assert L.hxq_affine_group_matmul(x.data_ptr(), C.byref(t), y.data_ptr(), 1) == -1
+    t.group_size = 96  # does not divide 128
+    assert L.hxq_affine_group_matmul(x.data_ptr(), C.byref(t), y.data_ptr(), 1) == -1
+    assert L.hxq_affine_group_matmul(x.data_ptr(), None, y.data_ptr(), 1) == -1

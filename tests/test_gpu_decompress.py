@@ -2,9 +2,14 @@
 reference library, and the oracle on seeded inputs at the benchmark sizes.
 
 Bar: weights bit-exact (fp32) or equal to round-to-nearest-even of the
-reference's fp32 value (bf16); status codes identical; confidence within
-relative 1e-5 of the reference's own sequential fp32 sum (the north-star
-tolerance) and within 1e-6 of the exactly computed value.
+reference's fp32 value (bf16); status codes identical.  Confidence:
+  * drop-in API (hxq_dequant, hxq_tensor_decompress, ...): bit-identical to
+    the reference's value, the float running sum in array order;
+  * batched/sharded API (GPU fused fp64 reduction): within 1e-6 of the
+    exactly computed value.  The reference's own running sum deviates from
+    the exact value by up to its a-priori rounding bound (n*2^-24 relative
+    on the sum, half that after the square root), a few 1e-5 at 1e5
+    entries -- checked here too, so the two definitions are tied together.
 All calls go through the C ABI of libhxq.so.
 """
 import ctypes as C
@@ -17,7 +22,6 @@ from hxq_b200 import synth
 
 pytestmark = pytest.mark.gpu
 
-CONF_REL_REF = 1e-5     # vs the reference's fp32 running sum
 CONF_REL_EXACT = 1e-6   # vs the sum computed in double
 
 
@@ -25,12 +29,20 @@ def _dev(torch, host: np.ndarray):
     return torch.from_numpy(np.ascontiguousarray(host)).cuda()
 
 
-def _check_conf(got, ref_conf, exact):
+def _check_conf(got, ref_conf, exact=None):
+    """Drop-in API: the reference's value, bit for bit."""
+    assert np.float32(got) == np.float32(ref_conf), (got, ref_conf)
+
+
+def _check_conf_exact(got, exact, ref_conf=None, nnz=0):
+    """Fused GPU reduction: the exact value; and the reference within its bound."""
     if exact == 0.0:
         assert got == 0.0
         return
-    assert abs(got - ref_conf) <= CONF_REL_REF * abs(ref_conf), (got, ref_conf)
     assert abs(got - exact) <= CONF_REL_EXACT * exact, (got, exact)
+    if ref_conf is not None:
+        bound = 0.5 * max(nnz - 1, 0) * 2.0 ** -24 * exact + 2.0 ** -23 * exact
+        assert abs(ref_conf - exact) <= bound, (ref_conf, exact, bound)
 
 
 def _bits(a):
@@ -194,7 +206,8 @@ def test_batched_images_mixed_kinds(H, L, oracle, cuda):
         exact = oracle.l2_exact(d)
         assert abs(ss[i] - exact * exact) <= 1e-12 + 1e-9 * exact * exact
         assert abs(L.hxq_cuda_image_sidecar_sumsq(imgs[i]) - exact * exact) <= 1e-9 * max(exact * exact, 1e-30)
-        _check_conf(float(cf[i]), c_ref, exact)
+        assert np.float32(L.hxq_cuda_image_reference_confidence(imgs[i])) == np.float32(c_ref)
+        _check_conf_exact(float(cf[i]), exact, c_ref, len(d["rows"]))
     for im in imgs:
         L.hxq_cuda_image_destroy(im)
 
@@ -214,7 +227,7 @@ def test_row_shards_reassemble(H, L, oracle, cuda):
     err, w_ref, c_ref = oracle.decompress(d)
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(w_ref))
     total = float(sumsq.sum().item())
-    _check_conf(float(np.float32(np.sqrt(total))), c_ref, oracle.l2_exact(d))
+    _check_conf_exact(float(np.sqrt(total)), oracle.l2_exact(d), c_ref, len(d["rows"]))
     for im in imgs:
         L.hxq_cuda_image_destroy(im)
 
@@ -272,7 +285,7 @@ def test_reference_gpu_launchers(H, L, oracle, cuda):
     conf = L.hxq_cuda_apply_sidecar(r.data_ptr(), c.data_ptr(), v.data_ptr(), out.data_ptr(), 256, len(d["rows"]))
     err, w_ref, c_ref = oracle.decompress(d)
     assert np.array_equal(_bits(out.cpu().numpy()), _bits(w_ref))
-    _check_conf(conf, c_ref, oracle.l2_exact(d))
+    _check_conf_exact(conf, oracle.l2_exact(d), c_ref, len(d["rows"]))
     s = synth.scalar(50, 70, 32)
     sn = dict(s, rows=None)
     cb2, ix = _dev(torch, s["codebook"]), _dev(torch, s["indices"])
@@ -301,6 +314,7 @@ def test_llama7b_layer0_batch(H, L, oracle, cuda):
         err, w_ref, c_ref = oracle.decompress(d)
         got = out[int(offs[i]): int(offs[i]) + sizes[i]].cpu().numpy()
         assert np.array_equal(_bits(got), _bits(w_ref)), i
-        _check_conf(float(cf[i]), c_ref, oracle.l2_exact(d))
+        _check_conf_exact(float(cf[i]), oracle.l2_exact(d), c_ref, len(d["rows"]))
+        assert np.float32(L.hxq_cuda_image_reference_confidence(imgs[i])) == np.float32(c_ref)
     for im in imgs:
         L.hxq_cuda_image_destroy(im)

@@ -37,6 +37,12 @@ enum ImageKind : uint32_t {
 //   generic kinds: x = flat position in the image; y = value bits.
 struct SideEntry { uint32_t x; uint32_t y; };
 
+// Work of the fast kernel is handed out dynamically in units of
+// kChunksPerWarp * kWarps chunks (chunk k*kWarps + w of a unit goes to warp
+// w); units never span two jobs.
+constexpr uint32_t kChunksPerWarp = 2;
+constexpr uint32_t kUnitChunks = kChunksPerWarp * kWarps;
+
 // One job of a launch of the fast kernel.
 struct VqJob {
     const uint4     *idx;        // chunk-padded index bytes
@@ -45,13 +51,10 @@ struct VqJob {
     const SideEntry *ent;        // sidecar entries
     void            *out;        // fp32 or bf16 output, 16-B aligned
     uint64_t         numel;      // weights in the job
-    uint64_t         chunk_begin;// first global chunk index of the job
     uint32_t         n_chunks;
     uint32_t         k;          // codebook entries (index bound)
-    uint32_t         slot_base;  // first reduction slot of the job
-    uint32_t         cta_lo;     // first CTA whose range meets the job
-    uint32_t         n_cta;      // CTAs whose range meets the job
-    uint32_t         pad_;
+    uint32_t         unit_begin; // first global unit of the job (also its first slot)
+    uint32_t         n_units;
     double          *sumsq;      // optional device output
     float           *conf;       // optional device output
 };
@@ -60,18 +63,22 @@ struct VqLaunch {
     VqJob     job[kMaxJobs];
     uint32_t  n_jobs;
     uint32_t  grid;
-    uint64_t  total_chunks;
-    double   *slots;             // reduction slots (scratch)
-    uint32_t *counters;          // per-job arrival counters (scratch, zero)
+    uint32_t  total_units;
+    uint32_t  pad_;
+    double   *slots;             // one partial sum per unit (scratch)
+    uint32_t *counters;          // per job: units finished (scratch, zero)
+    uint32_t *work;              // [0] next unit to hand out, [1] CTAs done (zero)
     uint32_t *err;               // device error word (scratch)
 };
 
 // Device scratch owned by the runtime, one per (device, stream).  The
 // decompress kernels leave `counters` at zero when they finish.
 struct Scratch {
+    void     *base      = nullptr;   // the allocation holding all of the below
     double   *slots     = nullptr;
     uint32_t  n_slots   = 0;
     uint32_t *counters  = nullptr;   // kMaxJobs
+    uint32_t *work      = nullptr;   // 2 words, zero between launches
     uint32_t *err       = nullptr;   // 1 word
     double   *sumsq     = nullptr;   // kMaxJobs results for internal calls
     float    *conf      = nullptr;   // kMaxJobs
@@ -79,9 +86,12 @@ struct Scratch {
 
 // Resident CTAs per SM of the fast kernel: the scalar variant holds four
 // 16-byte index pieces per lane in flight and needs more registers.
+#ifndef HXQ_VQ12_CTAS_PER_SM
+#define HXQ_VQ12_CTAS_PER_SM 3
+#endif
 __host__ __device__ constexpr uint32_t ctas_per_sm(uint32_t kind)
 {
-    return kind == kKindVq12 ? 4u : 3u;
+    return kind == kKindVq12 ? HXQ_VQ12_CTAS_PER_SM : 3u;
 }
 
 // Error bits written to the device error word.

@@ -179,25 +179,37 @@ hxq_error_t dev_ready(int dev)
 }
 
 // Scratch layout: [err u32 x 4][conf f32 x kMaxJobs][sumsq f64 x kMaxJobs]
-// [counters u32 x kMaxJobs][slots f64 x n_slots].  Zeroed once; kernels
-// leave counters at zero.  Caller holds g_mu.
-hxq_error_t get_scratch(int dev, cudaStream_t s, Scratch **out)
+// [counters u32 x kMaxJobs][work u32 x 4][slots f64 x n_slots].  Zeroed at
+// allocation; kernels leave counters and work at zero.  A stream's scratch
+// grows (reallocated, zeroed) when a launch needs more slots than it has,
+// which the first, uncaptured call of a workload on that stream does.
+// Caller holds g_mu.
+hxq_error_t get_scratch(int dev, cudaStream_t s, Scratch **out, uint32_t min_slots = 0)
 {
     DevCtx &d = g_dev[dev];
+    const uint32_t floor_slots = (uint32_t)(kMaxJobs + 8u * (uint32_t)std::max(d.sms, 148) + 1024u);
     auto it = d.scratch.find(s);
-    if (it != d.scratch.end()) { *out = &it->second; return HXQ_OK; }
-    const uint32_t n_slots = (uint32_t)(kMaxJobs + 4u * (uint32_t)std::max(d.sms, 148) + 1024u);
-    const size_t bytes = 16 + kMaxJobs * 4 + kMaxJobs * 8 + kMaxJobs * 4 + (size_t)n_slots * 8;
+    if (it != d.scratch.end() && it->second.n_slots >= min_slots) { *out = &it->second; return HXQ_OK; }
+    const uint32_t n_slots = std::max(floor_slots, min_slots + min_slots / 4u);
+    const size_t head = 16 + kMaxJobs * 4 + kMaxJobs * 8 + kMaxJobs * 4 + 16;
+    const size_t bytes = head + (size_t)n_slots * 8;
     unsigned char *base = nullptr;
     cudaError_t e = cudaMalloc(&base, bytes);
     if (e == cudaSuccess) e = cudaMemset(base, 0, bytes);
     if (e != cudaSuccess) { cudaGetLastError(); if (base) cudaFree(base); return map_cuda(e); }
+    if (it != d.scratch.end()) {  // replace a smaller one once its work is done
+        cudaStreamSynchronize(s);
+        cudaFree(it->second.base);
+        d.scratch.erase(it);
+    }
     Scratch sc;
+    sc.base = base;
     sc.err = reinterpret_cast<uint32_t *>(base);
     sc.conf = reinterpret_cast<float *>(base + 16);
     sc.sumsq = reinterpret_cast<double *>(base + 16 + kMaxJobs * 4);
     sc.counters = reinterpret_cast<uint32_t *>(base + 16 + kMaxJobs * 12);
-    sc.slots = reinterpret_cast<double *>(base + 16 + kMaxJobs * 16);
+    sc.work = reinterpret_cast<uint32_t *>(base + 16 + kMaxJobs * 16);
+    sc.slots = reinterpret_cast<double *>(base + head);
     sc.n_slots = n_slots;
     auto res = d.scratch.emplace(s, sc);
     *out = &res.first->second;
@@ -451,19 +463,7 @@ void destroy_image(hxq_cuda_image *img)
 
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
-// CTA c of a fast launch covers chunks [f(c), f(c+1)), f(c) = total*c/grid.
-uint64_t cta_begin(uint64_t total, uint32_t grid, uint32_t c) { return total * c / grid; }
-
-// First CTA whose range contains chunk `ch` (largest c with f(c) <= ch).
-uint32_t cta_of(uint64_t total, uint32_t grid, uint64_t ch)
-{
-    uint32_t lo = 0, hi = grid - 1;
-    while (lo < hi) {
-        const uint32_t mid = lo + (hi - lo + 1) / 2;
-        if (cta_begin(total, grid, mid) <= ch) lo = mid; else hi = mid - 1;
-    }
-    return lo;
-}
+uint32_t units_of(const hxq_cuda_image *im) { return (im->n_chunks + kUnitChunks - 1) / kUnitChunks; }
 
 hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
                               hxq_cuda_image *const *imgs, char *out_base,
@@ -474,7 +474,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
     if (which.empty()) return HXQ_OK;
     VqLaunch p;
     std::memset(&p, 0, sizeof(p));
-    uint64_t total = 0;
+    uint32_t units = 0;
     for (uint32_t n = 0; n < which.size(); ++n) {
         const uint32_t i = which[n];
         const hxq_cuda_image *im = imgs[i];
@@ -485,29 +485,21 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
         J.ent = im->d_ent;
         J.out = out_base + offs[i] * elem;
         J.numel = im->numel;
-        J.chunk_begin = total;
         J.n_chunks = im->n_chunks;
         J.k = im->k;
+        J.unit_begin = units;
+        J.n_units = units_of(im);
         J.sumsq = d_sumsq ? d_sumsq + i : nullptr;
         J.conf = d_conf ? d_conf + i : nullptr;
-        total += im->n_chunks;
+        units += J.n_units;
     }
+    if (units > sc.n_slots) return HXQ_ERR_INVALID_ARG;
     p.n_jobs = (uint32_t)which.size();
-    p.total_chunks = total;
-    p.grid = fast_grid(total, sms, imgs[which[0]]->kind);
-    uint32_t slot = 0;
-    for (uint32_t n = 0; n < p.n_jobs; ++n) {
-        VqJob &J = p.job[n];
-        const uint32_t c0 = cta_of(total, p.grid, J.chunk_begin);
-        const uint32_t c1 = cta_of(total, p.grid, J.chunk_begin + J.n_chunks - 1);
-        J.cta_lo = c0;
-        J.n_cta = c1 - c0 + 1u;
-        J.slot_base = slot;
-        slot += J.n_cta;
-    }
-    if (slot > sc.n_slots) return HXQ_ERR_INVALID_ARG;
+    p.total_units = units;
+    p.grid = fast_grid(units, sms, imgs[which[0]]->kind);
     p.slots = sc.slots;
     p.counters = sc.counters;
+    p.work = sc.work;
     p.err = sc.err;
     const hxq_cuda_image *first = imgs[which[0]];
     const cudaError_t e = launch_vq_fast(p, first->kind, bf16, first->check_k ? 1 : 0, s);
@@ -521,10 +513,13 @@ hxq_error_t launch_images(hxq_cuda_image *const *imgs, uint32_t n, void *d_out,
 {
     Scratch *sc = nullptr;
     hxq_error_t err;
+    uint32_t need = 0;
+    for (uint32_t i = 0; i < n; ++i)
+        if (imgs[i] && (imgs[i]->kind == kKindScalar || imgs[i]->kind == kKindVq12)) need += units_of(imgs[i]);
     {
         std::lock_guard<std::mutex> lk(g_mu);
         if ((err = dev_ready(dev)) != HXQ_OK) return err;
-        if ((err = get_scratch(dev, s, &sc)) != HXQ_OK) return err;
+        if ((err = get_scratch(dev, s, &sc, need)) != HXQ_OK) return err;
     }
     const int sms = g_dev[dev].sms;
     const size_t elem = bf16 ? 2u : 4u;

@@ -105,6 +105,7 @@ struct ChunkIn {
     uint4     r[VPL];      // this lane's 16-byte pieces of the index bytes
     uint32_t  e0, e1;      // sidecar entries [e0, e1) of the chunk
     SideEntry ent;         // entry e0 + lane (if any)
+    uint32_t  c;           // chunk index within its job
 };
 
 template <uint32_t VPL>
@@ -116,6 +117,7 @@ __device__ __forceinline__ void prefetch_chunk(const VqJob &J, uint32_t c, uint3
     for (uint32_t q = 0; q < VPL; ++q) in.r[q] = ld_stream_v4(src + q * 32u + lane);
     in.e0 = __ldg(J.chunk_ptr + c);
     in.e1 = __ldg(J.chunk_ptr + c + 1);
+    in.c = c;
 }
 
 template <uint32_t VPL>
@@ -134,20 +136,20 @@ __device__ __forceinline__ void stage_chunk(const ChunkIn<VPL> &in, uint4 *stage
     __syncwarp();
 }
 
-// One 12-bit chunk (512 triples, 2048 weights).
+// One 12-bit chunk (512 triples, 2048 weights) whose index bytes are already
+// staged in `stage` (stage_chunk).
 template <bool BF16, bool CHECK_K>
 __device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c, const ChunkIn<3> &in,
                                            const unsigned char *cb_area, uint4 *stage,
                                            uint32_t lane, double &acc, uint32_t &errflag)
 {
-    stage_chunk<3>(in, stage, lane);
     const uint32_t e0 = in.e0, e1 = in.e1;
     const uint64_t w0 = (uint64_t)c * kChunkW;
     const uint64_t left = J.numel - w0;
     const uint32_t ntrip = (left >= kChunkW ? kChunkW : (uint32_t)left) >> 2;
     const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);
 
-#pragma unroll 4
+#pragma unroll 2
     for (uint32_t m = 0; m < 16u; ++m) {
         const uint32_t jt = m * 32u + lane;
         if (jt < ntrip) {
@@ -196,13 +198,12 @@ __device__ __forceinline__ void chunk_vq12(const VqJob &J, uint32_t c, const Chu
     }
 }
 
-// One scalar chunk (2048 uint8 indices, 2048 weights).
+// One scalar chunk (2048 uint8 indices, 2048 weights), index bytes staged.
 template <bool BF16>
 __device__ __forceinline__ void chunk_scalar(const VqJob &J, uint32_t c, const ChunkIn<4> &in,
                                              const unsigned char *cb_area, uint4 *stage,
                                              uint32_t lane, double &acc)
 {
-    stage_chunk<4>(in, stage, lane);
     const uint32_t e0 = in.e0, e1 = in.e1;
     const SideEntry ent = in.ent;
     const uint64_t w0 = (uint64_t)c * kChunkW;
@@ -211,7 +212,7 @@ __device__ __forceinline__ void chunk_scalar(const VqJob &J, uint32_t c, const C
     const uint32_t *sw = reinterpret_cast<const uint32_t *>(stage);
     const float *cbr = reinterpret_cast<const float *>(cb_area);
 
-#pragma unroll 4
+#pragma unroll 2
     for (uint32_t p = 0; p < 16u; ++p) {
         const uint32_t w = p * 32u + lane;
         const uint32_t first = 4u * w;
@@ -269,7 +270,57 @@ __host__ __device__ constexpr uint32_t stage_bytes()
 template <uint32_t KIND>
 __host__ __device__ constexpr uint32_t fast_smem_bytes()
 {
-    return kCbBytes + kWarps * stage_bytes<KIND>() + kWarps * sizeof(double);
+    return kCbBytes + kWarps * stage_bytes<KIND>();
+}
+
+// First job whose unit range contains u, scanning forward from j (the units
+// a CTA receives only increase).
+__device__ __forceinline__ uint32_t job_of_unit(const VqLaunch &p, uint32_t j, uint32_t u)
+{
+    while (j + 1u < p.n_jobs && u >= p.job[j].unit_begin + p.job[j].n_units) ++j;
+    return j;
+}
+
+// Warp 0, after the CTA barrier that completed unit u: lane 0 adds the eight
+// warp partials in order into the unit's slot; the warp that finishes a
+// job's last unit adds the job's slots in a fixed order (per-lane strided
+// sums, then a fixed butterfly), so the result does not depend on which SM
+// ran what.
+__device__ __forceinline__ void finish_unit(const VqLaunch &p, uint32_t j, uint32_t u,
+                                            const double *red, uint32_t lane)
+{
+    const VqJob &J = p.job[j];
+    uint32_t last = 0;
+    if (lane == 0) {
+        double s = 0.0;
+#pragma unroll
+        for (uint32_t w = 0; w < kWarps; ++w) s += red[w];
+        p.slots[u] = s;
+        __threadfence();
+        last = (atomicAdd(p.counters + j, 1u) + 1u == J.n_units) ? 1u : 0u;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    // eight independent loads in flight per lane, then a fixed-order combine
+    double part[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) part[q] = 0.0;
+    const double *sl = p.slots + J.unit_begin;
+    for (uint32_t i0 = 0; i0 < J.n_units; i0 += 256u) {
+#pragma unroll
+        for (uint32_t q = 0; q < 8u; ++q) {
+            const uint32_t i = i0 + q * 32u + lane;
+            if (i < J.n_units) part[q] += __ldcg(sl + i);
+        }
+    }
+    double t = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+    t = warp_sum(t);
+    if (lane == 0) {
+        if (J.sumsq) *J.sumsq = t;
+        if (J.conf) *J.conf = (float)sqrt(t);
+        p.counters[j] = 0u;  // leave scratch zeroed for the next launch
+    }
 }
 
 template <uint32_t KIND, bool BF16, bool CHECK_K>
@@ -277,77 +328,96 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(KIND))
 vq_fast_kernel(const __grid_constant__ VqLaunch p)
 {
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ uint32_t s_unit[3];
+    __shared__ double s_red[2][kWarps];
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     unsigned char *cb_area = smem;
     uint4 *stage = reinterpret_cast<uint4 *>(smem + kCbBytes + warp * stage_bytes<KIND>());
-    double *red = reinterpret_cast<double *>(smem + kCbBytes + kWarps * stage_bytes<KIND>());
+    constexpr uint32_t VPL = (KIND == kKindVq12) ? 3u : 4u;
+    const uint32_t total = p.total_units;
 
-    const uint32_t cta = blockIdx.x;
-    const uint64_t lo = p.total_chunks * cta / p.grid;
-    const uint64_t hi = p.total_chunks * (cta + 1u) / p.grid;
+    // Units are handed out by an atomic counter, two ahead of use, so a
+    // warp knows its next chunk (and prefetches it) while it works on the
+    // current one, and faster SMs simply take more units.
+    if (tid == 0) {
+        s_unit[0] = atomicAdd(p.work, 1u);
+        s_unit[1] = s_unit[0] < total ? atomicAdd(p.work, 1u) : total;
+    }
+    __syncthreads();
 
-    uint32_t j = 0;
-    while (j + 1u < p.n_jobs && p.job[j].chunk_begin + p.job[j].n_chunks <= lo) ++j;
-
+    uint32_t u = s_unit[0];
+    uint32_t j = 0, cb_job = 0xFFFFFFFFu;
     uint32_t errflag = 0;
-    uint64_t pos = lo;
-    while (pos < hi && j < p.n_jobs) {
-        const VqJob &J = p.job[j];
-        const uint64_t jend = J.chunk_begin + J.n_chunks;
-        const uint64_t seg_end = hi < jend ? hi : jend;
-
-        __syncthreads();  // codebook and red[] of the previous segment released
-        load_codebook<KIND, BF16>(cb_area, J, tid);
-        __syncthreads();
-
-        double acc = 0.0;
-        // software pipeline: chunk ch+kWarps's index bytes and entry range are
-        // in flight while chunk ch is processed; its first sidecar entry is
-        // requested once that range has arrived, a whole chunk before use.
-        constexpr uint32_t VPL = (KIND == kKindVq12) ? 3u : 4u;
-        ChunkIn<VPL> cur, nxt;
-        uint64_t ch = pos + warp;
-        if (ch < seg_end) {
-            prefetch_chunk<VPL>(J, (uint32_t)(ch - J.chunk_begin), lane, cur);
-            prefetch_entry<VPL>(J, lane, cur);
+    ChunkIn<VPL> cur, nxt;
+    bool have_cur = false;
+    if (u < total) {
+        j = job_of_unit(p, 0, u);
+        const uint32_t c = (u - p.job[j].unit_begin) * kUnitChunks + warp;
+        if (c < p.job[j].n_chunks) {
+            prefetch_chunk<VPL>(p.job[j], c, lane, cur);
+            prefetch_entry<VPL>(p.job[j], lane, cur);
+            have_cur = true;
         }
-        for (; ch < seg_end; ch += kWarps) {
-            const uint32_t c = (uint32_t)(ch - J.chunk_begin);
-            const bool more = ch + kWarps < seg_end;
-            if (more) prefetch_chunk<VPL>(J, c + kWarps, lane, nxt);
-            if constexpr (KIND == kKindVq12)
-                chunk_vq12<BF16, CHECK_K>(J, c, cur, cb_area, stage, lane, acc, errflag);
-            else
-                chunk_scalar<BF16>(J, c, cur, cb_area, stage, lane, acc);
-            if (more) {
-                prefetch_entry<VPL>(J, lane, nxt);
+    }
+    for (uint32_t it = 0; u < total; ++it) {
+        if (j != cb_job) {  // every thread is past the previous unit (barrier below)
+            load_codebook<KIND, BF16>(cb_area, p.job[j], tid);
+            __syncthreads();
+            cb_job = j;
+        }
+        const uint32_t un = s_unit[(it + 1u) % 3u];
+        if (tid == 0) s_unit[(it + 2u) % 3u] = un < total ? atomicAdd(p.work, 1u) : total;
+        const uint32_t jn = un < total ? job_of_unit(p, j, un) : j;
+        const uint32_t ubase = (u - p.job[j].unit_begin) * kUnitChunks + warp;
+        double acc = 0.0;
+#pragma unroll 1
+        for (uint32_t k = 0; k < kChunksPerWarp; ++k) {
+            // stage this chunk first: its index registers are then free for the next one
+            if (have_cur) stage_chunk<VPL>(cur, stage, lane);
+            // this warp's next chunk: the unit's next one, else the first of unit un
+            bool have_nxt = false;
+            uint32_t jx = j;
+            if (k + 1u < kChunksPerWarp) {
+                const uint32_t c = ubase + (k + 1u) * kWarps;
+                if (c < p.job[j].n_chunks) {
+                    prefetch_chunk<VPL>(p.job[j], c, lane, nxt);
+                    have_nxt = true;
+                }
+            } else if (un < total) {
+                jx = jn;
+                const uint32_t c = (un - p.job[jn].unit_begin) * kUnitChunks + warp;
+                if (c < p.job[jn].n_chunks) {
+                    prefetch_chunk<VPL>(p.job[jn], c, lane, nxt);
+                    have_nxt = true;
+                }
+            }
+            if (have_cur) {
+                if constexpr (KIND == kKindVq12)
+                    chunk_vq12<BF16, CHECK_K>(p.job[j], cur.c, cur, cb_area, stage, lane, acc, errflag);
+                else
+                    chunk_scalar<BF16>(p.job[j], cur.c, cur, cb_area, stage, lane, acc);
+            }
+            if (have_nxt) {
+                prefetch_entry<VPL>(p.job[jx], lane, nxt);
                 cur = nxt;
             }
+            have_cur = have_nxt;
         }
-
         acc = warp_sum(acc);
-        if (lane == 0) red[warp] = acc;
-        __syncthreads();
-        if (tid == 0) {
-            double s = 0.0;
-#pragma unroll
-            for (uint32_t w = 0; w < kWarps; ++w) s += red[w];
-            p.slots[J.slot_base + (cta - J.cta_lo)] = s;
-            __threadfence();
-            const uint32_t prev = atomicAdd(p.counters + j, 1u);
-            if (prev + 1u == J.n_cta) {
-                __threadfence();
-                double tot = 0.0;
-                for (uint32_t i = 0; i < J.n_cta; ++i) tot += __ldcg(p.slots + J.slot_base + i);
-                if (J.sumsq) *J.sumsq = tot;
-                if (J.conf) *J.conf = (float)sqrt(tot);
-                p.counters[j] = 0u;  // leave scratch zeroed for the next launch
-            }
-        }
-        pos = seg_end;
-        ++j;
+        if (lane == 0) s_red[it & 1u][warp] = acc;
+        __syncthreads();  // s_red and s_unit[(it+2)%3] published; codebook free
+        if (warp == 0) finish_unit(p, j, u, s_red[it & 1u], lane);
+        u = un;
+        j = jn;
     }
     if (CHECK_K && errflag) atomicOr(p.err, errflag);
+    if (tid == 0) {  // the last CTA out leaves the work counters at zero
+        __threadfence();
+        if (atomicAdd(p.work + 1, 1u) + 1u == gridDim.x) {
+            p.work[0] = 0u;
+            p.work[1] = 0u;
+        }
+    }
 }
 
 template <uint32_t KIND, bool BF16, bool CHECK_K>
@@ -531,10 +601,10 @@ cudaError_t configure_vq_kernels()
     return configure_one<kKindScalar, true, false>();
 }
 
-uint32_t fast_grid(uint64_t total_chunks, int sms, uint32_t kind)
+uint32_t fast_grid(uint64_t total_units, int sms, uint32_t kind)
 {
     uint64_t g = (uint64_t)(sms > 0 ? sms : 148) * ctas_per_sm(kind);
-    if (g > total_chunks) g = total_chunks;
+    if (g > total_units) g = total_units;
     return (uint32_t)(g == 0 ? 1 : g);
 }
 

@@ -1107,3 +1107,133 @@ float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decompress without allocating.
+//
+// Some callers cannot let a library call cudaMalloc: inference engines that
+// reserve nearly all of HBM for weights and KV cache at start-up and hand
+// plugins pre-planned buffers (a cudaMalloc there can fail or fragment the
+// pool), and latency-critical serving loops, where cudaMalloc/cudaFree may
+// synchronise the device.  The regular batched entry point allocates its
+// reduction scratch per stream on first use (cudaMalloc) and a pinned
+// read-back buffer per device (cudaMallocHost).  This variant of the same
+// fused decompress launch instead takes its scratch from a fixed array in
+// the module's global memory, which every GPU that loads the library holds
+// until the process exits.
+
+namespace {
+
+constexpr uint32_t kNoAllocUnits = 8192;          // one fp64 slot per unit
+constexpr size_t   kNoAllocHead = 512;            // err | counters | work
+constexpr size_t   kNoAllocOffCounters = 16;
+constexpr size_t   kNoAllocOffWork = 16 + 4 * kMaxJobs;
+constexpr size_t   kNoAllocBytes = kNoAllocHead + (size_t)kNoAllocUnits * sizeof(double);
+
+// In host code this name is only a host-side stand-in for the array, not a
+// device address; the address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+struct NoAllocDev {
+    bool ready = false;
+    unsigned char *ptr = nullptr;   // device address of g_noalloc_scratch
+    int sms = 0;
+};
+NoAllocDev g_noalloc[kMaxDev];
+
+// Once per device, with that device current: look up the array's device
+// address and prepare the kernels (no allocation).  Caller holds g_mu.
+hxq_error_t noalloc_setup(int dev, NoAllocDev **out)
+{
+    NoAllocDev &d = g_noalloc[dev];
+    if (!d.ready) {
+        void *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        int sms = 0;
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess) e = configure_vq_kernels();
+        if (e != cudaSuccess) { cudaGetLastError(); return map_cuda(e); }
+        d.ptr = static_cast<unsigned char *>(ptr);
+        d.sms = sms;
+        d.ready = true;
+    }
+    *out = &d;
+    return HXQ_OK;
+}
+
+}  // namespace
+
+extern "C" hxq_error_t hxq_cuda_decompress_images_noalloc(hxq_cuda_image_t *const *imgs, uint32_t n,
+                                                          void *d_out, const size_t *out_offsets,
+                                                          hxq_out_dtype_t dtype, double *d_sumsq,
+                                                          float *d_conf, void *stream)
+{
+    if (n == 0) return HXQ_OK;
+    if (!imgs || !d_out || !out_offsets) return HXQ_ERR_NULL_PTR;
+    if (n > kMaxJobs) return HXQ_ERR_INVALID_ARG;
+    if (dtype != HXQ_OUT_F32 && dtype != HXQ_OUT_BF16) return HXQ_ERR_INVALID_ARG;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    NoAllocDev *na = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = noalloc_setup(dev, &na)) != HXQ_OK) return err;
+    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int bf16 = dtype == HXQ_OUT_BF16;
+    const size_t elem = bf16 ? 2u : 4u;
+    char *base = static_cast<char *>(d_out);
+
+    // Only images the fused kernel takes (12-bit with in_f % 4 == 0, or
+    // scalar; output slot 16-byte aligned) and at most kNoAllocUnits units
+    // per launch group; everything is checked before anything is enqueued.
+    std::vector<uint32_t> g_scalar, g_vq12, g_vq12k, empty;
+    uint32_t u_scalar = 0, u_vq12 = 0, u_vq12k = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const hxq_cuda_image *im = imgs[i];
+        if (!im) return HXQ_ERR_NULL_PTR;
+        if (im->device != dev || !im->d_block) return HXQ_ERR_INVALID_ARG;
+        if (im->numel == 0) { empty.push_back(i); continue; }
+        if (!aligned16(base + out_offsets[i] * elem)) return HXQ_ERR_INVALID_ARG;
+        if (im->kind == kKindScalar) { g_scalar.push_back(i); u_scalar += units_of(im); }
+        else if (im->kind == kKindVq12 && im->check_k) { g_vq12k.push_back(i); u_vq12k += units_of(im); }
+        else if (im->kind == kKindVq12) { g_vq12.push_back(i); u_vq12 += units_of(im); }
+        else return HXQ_ERR_INVALID_ARG;
+    }
+    if (u_scalar > kNoAllocUnits || u_vq12 > kNoAllocUnits || u_vq12k > kNoAllocUnits)
+        return HXQ_ERR_INVALID_ARG;
+
+    Scratch sc;
+    sc.base = na->ptr;
+    sc.err = reinterpret_cast<uint32_t *>(na->ptr);
+    sc.counters = reinterpret_cast<uint32_t *>(na->ptr + kNoAllocOffCounters);
+    sc.work = reinterpret_cast<uint32_t *>(na->ptr + kNoAllocOffWork);
+    sc.slots = reinterpret_cast<double *>(na->ptr + kNoAllocHead);
+    sc.n_slots = kNoAllocUnits;
+
+    // The array keeps whatever the last call left: clear the error word and
+    // the counters the kernel expects at zero.  (Unit slots are written
+    // before they are read.)
+    cudaError_t ce = cudaMemsetAsync(na->ptr, 0, kNoAllocHead, s);
+    for (uint32_t i : empty) {
+        if (ce == cudaSuccess && d_sumsq) ce = cudaMemsetAsync(d_sumsq + i, 0, sizeof(double), s);
+        if (ce == cudaSuccess && d_conf) ce = cudaMemsetAsync(d_conf + i, 0, sizeof(float), s);
+    }
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    const std::vector<uint32_t> *groups[3] = {&g_vq12, &g_vq12k, &g_scalar};
+    for (const std::vector<uint32_t> *g : groups) {
+        if (g->empty()) continue;
+        ce = cudaMemsetAsync(na->ptr + kNoAllocOffCounters, 0, kNoAllocHead - kNoAllocOffCounters, s);
+        if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+        if ((err = launch_fast_group(*g, imgs, base, out_offsets, elem, bf16, d_sumsq, d_conf, sc,
+                                     na->sms, s)) != HXQ_OK)
+            return err;
+    }
+    // Synchronous: wait for the work, then read the device error word.
+    uint32_t word = 0;
+    ce = cudaMemcpyAsync(&word, na->ptr, sizeof(word), cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    return (word & kErrIndexOOB) ? HXQ_ERR_INDEX_OOB : HXQ_OK;
+}

@@ -131,6 +131,34 @@ hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs,
  * recorded on the device. */
 hxq_error_t hxq_cuda_stream_synchronize(void *stream);
 
+/* The same batched decompress, for callers that must not have the library
+ * allocate memory: engines that reserve HBM up front and give plugins
+ * pre-planned buffers (a cudaMalloc can fail or fragment the pool there),
+ * or serving loops where cudaMalloc/cudaFree would stall the device.  No
+ * counterpart in the reference library.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or cudaMallocHost.  The
+ *     caller passes the images (created and, if streamed, uploaded
+ *     beforehand) and the output buffers, as for
+ *     hxq_cuda_decompress_images.  The kernels' scratch is a fixed
+ *     66,048-byte array in the library's global memory, which every GPU
+ *     that loads the library holds until the process exits.
+ *   - Limit: at most 8,192 work units (16 chunks of 2048 weights each, i.e.
+ *     268,435,456 weights) per kind of image (12-bit, 12-bit with k = 256,
+ *     scalar) in one call, and only images the fused kernel takes (12-bit
+ *     with in_features % 4 == 0, or scalar) with 16-byte aligned output
+ *     slots; otherwise HXQ_ERR_INVALID_ARG before anything is enqueued.
+ *   - Synchronous: returns once the work on `stream` is done, with
+ *     HXQ_ERR_INDEX_OOB if an index was >= k.
+ *   - The first call on a device looks up the array's address and prepares
+ *     the kernels; make that first call before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (other
+ *     streams, other threads) race and must be serialised by the caller. */
+hxq_error_t hxq_cuda_decompress_images_noalloc(hxq_cuda_image_t *const *imgs,
+                                               uint32_t n, void *d_out,
+                                               const size_t *out_offsets,
+                                               hxq_out_dtype_t dtype, double *d_sumsq,
+                                               float *d_conf, void *stream);
+
 /* -- The reference's GPU launchers (src/hxq_cuda.cu:209-288) -------------
  * Exported, undeclared in the reference; device pointers throughout.
  * Return 0 on success and -1 on error (the reference's convention). */

@@ -68,6 +68,24 @@ def algorithmic_bytes(rows: int, in_f: int, nnz: int) -> int:
     return rows * in_f * 3 // 4 + CB_BYTES + 12 * nnz + 4 * rows * in_f
 
 
+N1_LAYER_ALGO_BYTES = 973653900  # one layer launch at N=1 (algorithmic_bytes summed)
+
+
+def profiled_traffic(bytes_per_launch: float, world: int):
+    """DRAM bytes per launch from the committed ncu summary of one layer launch
+    at N=1 (dram__bytes_read.sum + dram__bytes_write.sum); for a row shard the
+    traffic scales with the shard's algorithmic bytes."""
+    path = os.path.join(HERE, "profiles", "vq_fast_kernel_llama7b_layer_n1.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                n1 = float(line.split(":")[1])
+                return n1 if world == 1 else n1 * bytes_per_launch / N1_LAYER_ALGO_BYTES
+    except OSError:
+        pass
+    return None
+
+
 # ---------------------------------------------------------------------------
 # synthetic matrices (generated on the GPU, sliced, handed to the C loaders)
 
@@ -421,16 +439,7 @@ def main():
     my_launch_ms = my_ms / (args.steps * launches_per_step)
     achieved = my_bytes / launches_per_step / (my_launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
-    traffic = None
-    tf = os.path.join(HERE, "profiles", "traffic.json")
-    if os.path.exists(tf):
-        try:
-            tj = json.load(open(tf))
-            key = f"llama7b_layer_launch_n{world}"
-            if key in tj:
-                traffic = tj[key]["dram_bytes_per_launch"]
-        except Exception:
-            traffic = None
+    traffic = profiled_traffic(my_bytes / launches_per_step, world)
 
     # end to end through the public API: host images streamed every step
     e2e = None

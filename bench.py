@@ -39,6 +39,8 @@ for p in (HERE, PKG):
 
 import numpy as np  # noqa: E402
 
+from hxq_b200.shard import shard_rows, slice_rows  # noqa: E402
+
 METRIC = "dequant weights/s (7B-shaped 12-bit 2D-VQ decompress, sidecar + confidence fused)"
 UNIT = "weights/s"
 SIDECAR_FRAC = 0.005
@@ -57,10 +59,6 @@ def measured_peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
-
-
-def shard_rows(out_f: int, rank: int, world: int) -> tuple[int, int]:
-    return out_f * rank // world, out_f * (rank + 1) // world
 
 
 def algorithmic_bytes(rows: int, in_f: int, nnz: int) -> int:
@@ -89,9 +87,11 @@ def profiled_traffic(bytes_per_launch: float, world: int):
 # ---------------------------------------------------------------------------
 # synthetic matrices (generated on the GPU, sliced, handed to the C loaders)
 
-def gen_matrix_slice(torch, seed: int, out_f: int, in_f: int, r0: int, r1: int):
-    """Full matrix drawn on the device from `seed`, rows [r0, r1) returned on
-    the host as a dict for hxq_b200.Tensor.load."""
+def gen_matrix(torch, seed: int, out_f: int, in_f: int) -> dict:
+    """One matrix drawn on the device from `seed` (codebook ~N(0,0.02),
+    uniform packed index bytes = uniform 12-bit indices, floor(0.5%) unique
+    sidecar positions sorted row-major, deltas ~N(0,0.005)), returned on the
+    host in the hxq_b200.synth dict layout."""
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     cb = (torch.randn(8192, generator=g, device="cuda") * 0.02).float()
@@ -101,15 +101,11 @@ def gen_matrix_slice(torch, seed: int, out_f: int, in_f: int, r0: int, r1: int):
     nnz = int(SIDECAR_FRAC * n)
     pos = torch.randperm(n, generator=g, device="cuda")[:nnz].sort().values
     vals = (torch.randn(nnz, generator=g, device="cuda") * 0.005).float()
-    lo, hi = r0 * in_f, r1 * in_f
-    sel = (pos >= lo) & (pos < hi)
-    p = pos[sel] - lo
-    rb = in_f * 3 // 4
-    return dict(mode=2, out_f=r1 - r0, in_f=in_f, k=4096, vdim=2, codebook=cb.cpu().numpy(),
-                packed=packed[r0 * rb: r1 * rb].cpu().numpy(),
-                rows=(p // in_f).to(torch.int32).cpu().numpy().astype(np.uint32),
-                cols=(p % in_f).to(torch.int32).cpu().numpy().astype(np.uint32),
-                vals=vals[sel].cpu().numpy()), nnz
+    return dict(mode=2, out_f=out_f, in_f=in_f, k=4096, vdim=2, codebook=cb.cpu().numpy(),
+                packed=packed.cpu().numpy(),
+                rows=(pos // in_f).to(torch.int32).cpu().numpy().astype(np.uint32),
+                cols=(pos % in_f).to(torch.int32).cpu().numpy().astype(np.uint32),
+                vals=vals.cpu().numpy())
 
 
 def build_images(torch, H, L, rank: int, world: int, layers: int):
@@ -120,7 +116,7 @@ def build_images(torch, H, L, rank: int, world: int, layers: int):
         li, lm = [], []
         for p, (_, o, i) in enumerate(synth.LLAMA7B_PROJ):
             r0, r1 = shard_rows(o, rank, world)
-            d, _ = gen_matrix_slice(torch, synth.llama7b_seed(layer, p), o, i, r0, r1)
+            d = slice_rows(gen_matrix(torch, synth.llama7b_seed(layer, p), o, i), r0, r1)
             t = H.Tensor().load(d)
             img = C.c_void_p()
             H.check(L.hxq_cuda_image_create_streamed(t.ref, 0, r1 - r0, C.byref(img)), "image")
@@ -202,18 +198,14 @@ def cpu_reference_runner(layer0: list[dict]):
         Lr = ref.L
         from oracle.oracle import _RefBuf, _RefResult
         for d in layer0:
-            o, i = d["out_f"], d["in_f"]
+            o = d["out_f"]
             step = max(1, o // max(1, cores // 2))
             for r0 in range(0, o, step):
                 r1 = min(o, r0 + step)
-                rb = i * 3 // 4
-                sel = (d["rows"] >= r0) & (d["rows"] < r1)
-                sl = dict(mode=2, out_f=r1 - r0, in_f=i, k=4096, vdim=2, codebook=d["codebook"],
-                          packed=d["packed"][r0 * rb: r1 * rb], rows=(d["rows"][sel] - r0).astype(np.uint32),
-                          cols=d["cols"][sel], vals=d["vals"][sel])
+                sl = slice_rows(d, r0, r1)
                 t = ref.tensor(sl)
                 buf = _RefBuf()
-                Lr.ref_hxq_shared_buffer_init(C.byref(buf), (r1 - r0) * i)
+                Lr.ref_hxq_shared_buffer_init(C.byref(buf), (r1 - r0) * d["in_f"])
                 res = _RefResult()
                 jobs.append((t, buf, res))
 
@@ -225,16 +217,12 @@ def cpu_reference_runner(layer0: list[dict]):
     else:
         orc = Oracle()
         for d in layer0:
-            o, i = d["out_f"], d["in_f"]
+            o = d["out_f"]
             step = max(1, o // max(1, cores // 2))
             for r0 in range(0, o, step):
                 r1 = min(o, r0 + step)
-                rb = i * 3 // 4
-                sel = (d["rows"] >= r0) & (d["rows"] < r1)
-                sl = dict(mode=2, out_f=r1 - r0, in_f=i, k=4096, vdim=2, codebook=d["codebook"],
-                          packed=np.ascontiguousarray(d["packed"][r0 * rb: r1 * rb]),
-                          rows=(d["rows"][sel] - r0).astype(np.uint32), cols=d["cols"][sel], vals=d["vals"][sel])
-                jobs.append((sl, np.zeros((r1 - r0) * i, np.float32)))
+                sl = slice_rows(d, r0, r1)
+                jobs.append((sl, np.zeros((r1 - r0) * d["in_f"], np.float32)))
 
         def one(job):
             sl, out = job
@@ -255,8 +243,7 @@ def layer0_host(torch, rank_world=(0, 1)):
     from hxq_b200 import synth
     out = []
     for p, (_, o, i) in enumerate(synth.LLAMA7B_PROJ):
-        d, _ = gen_matrix_slice(torch, synth.llama7b_seed(0, p), o, i, 0, o)
-        out.append(d)
+        out.append(gen_matrix(torch, synth.llama7b_seed(0, p), o, i))
     return out
 
 

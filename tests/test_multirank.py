@@ -1,0 +1,92 @@
+"""Row sharding across ranks, on CPU with world-size-2 gloo process groups.
+
+Each rank cuts its rows out of a tensor (hxq_b200.shard.slice_rows, the
+cut bench.py applies before building the rank's images), decompresses them
+with the oracle, and the ranks gather weights and sums of squared sidecar
+deltas.  Rank 0 checks the reassembled matrix is bit-identical to the
+whole-tensor result and that the combined confidence equals the exact one.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, kind: str, q):
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, repo)
+    sys.path.insert(0, os.path.join(repo, "hxq-native_b200"))
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from hxq_b200 import synth
+    from hxq_b200.shard import combine_confidence, shard_rows, slice_rows
+    from oracle.oracle import Oracle
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=timedelta(seconds=60))
+    try:
+        d = synth.vq12(1376 * 2 + 5, 256, 77, frac=0.02) if kind == "vq12" else \
+            synth.scalar(301, 96, 78, frac=0.05)
+        # a few entries the reference skips, to check the cut drops them too
+        d["rows"] = np.concatenate([d["rows"], np.array([d["out_f"], 3], np.uint32)])
+        d["cols"] = np.concatenate([d["cols"], np.array([1, d["in_f"] + 2], np.uint32)])
+        d["vals"] = np.concatenate([d["vals"], np.array([9.0, 9.0], np.float32)])
+        orc = Oracle()
+        r0, r1 = shard_rows(d["out_f"], rank, world)
+        part = slice_rows(d, r0, r1)
+        err, w, _ = orc.decompress(part)
+        ss = orc.l2_exact(part) ** 2
+        got_w = [None] * world
+        got_ss = [None] * world
+        dist.all_gather_object(got_w, (r0, r1, err, w))
+        dist.all_gather_object(got_ss, ss)
+        if rank == 0:
+            e_full, w_full, _ = orc.decompress(d)
+            pieces = sorted(got_w, key=lambda t: t[0])
+            assert pieces[0][0] == 0 and pieces[-1][1] == d["out_f"]
+            assert all(p[2] == 0 for p in pieces)
+            whole = np.concatenate([p[3] for p in pieces])
+            ok_w = np.array_equal(whole.view(np.uint32), w_full.view(np.uint32))
+            exact = orc.l2_exact(d)
+            conf = combine_confidence(got_ss)
+            ok_c = abs(conf - exact) <= 1e-6 * exact
+            q.put((ok_w, ok_c, conf, exact))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind", ["vq12", "scalar"])
+def test_row_shards_gloo_world2(kind):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, kind, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    ok_w, ok_c, conf, exact = q.get(timeout=10)
+    assert ok_w, "reassembled shards differ from the whole-tensor decompress"
+    assert ok_c, (conf, exact)
+
+
+def test_shard_rows_partition():
+    from hxq_b200.shard import shard_rows
+    for out_f in (1, 7, 4096, 11008):
+        for world in (1, 2, 3, 4, 8):
+            spans = [shard_rows(out_f, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == out_f
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))

@@ -66,6 +66,15 @@ def algorithmic_bytes(rows: int, in_f: int, nnz: int) -> int:
     return rows * in_f * 3 // 4 + CB_BYTES + 12 * nnz + 4 * rows * in_f
 
 
+def measured_tensor_peak() -> float:
+    """Dense bf16 TFLOP/s measured on this pool (burst), else the fallback."""
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 N1_LAYER_ALGO_BYTES = 973653900  # one layer launch at N=1 (algorithmic_bytes summed)
 
 
@@ -272,6 +281,152 @@ def run_reference_arm(args):
 
 
 # ---------------------------------------------------------------------------
+# auxiliary workloads: single-tensor decompress (c1, c2) and the affine sweep (c3)
+
+def _graph_time(torch, stream, launch, n_launch: int, warmup: int) -> float:
+    """Capture n_launch calls of launch(i) in a CUDA graph, replay it after
+    warm-up, return the device time of one replay in ms (CUDA events)."""
+    with torch.cuda.stream(stream):
+        for i in range(min(n_launch, 8)):
+            launch(i)
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(n_launch):
+            launch(i)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    del g
+    return ms
+
+
+def _decompress_case(torch, H, L, name: str, d: dict, dtype: int, algo_bytes: int, stream, args) -> dict:
+    """Replicas of one tensor (inputs + outputs > 4x L2) decompressed one per
+    launch, cycling, in a CUDA graph of --steps x 10 launches."""
+    n = d["out_f"] * d["in_f"]
+    elem = 4 if dtype == 0 else 2
+    reps = max(2, int(np.ceil(4 * 126e6 / (algo_bytes))))
+    t = H.Tensor().load(d)
+    imgs = []
+    for _ in range(reps):
+        img = C.c_void_p()
+        H.check(L.hxq_cuda_image_create(t.ref, 0, d["out_f"], C.byref(img)), "image")
+        imgs.append(img)
+    slot = (n + 63) // 64 * 64
+    out = torch.empty(slot * reps * elem, dtype=torch.uint8, device="cuda")
+    conf = torch.zeros(reps, dtype=torch.float32, device="cuda")
+    arrs = [(C.c_void_p * 1)(img.value) for img in imgs]
+    zero = (C.c_size_t * 1)(0)
+
+    def launch(i):
+        r = i % reps
+        e = L.hxq_cuda_decompress_images(arrs[r], 1, out.data_ptr() + r * slot * elem, zero, dtype, None,
+                                         conf.data_ptr() + 4 * r, stream.cuda_stream)
+        if e != 0:
+            raise RuntimeError(f"decompress failed {e}")
+    n_launch = args.steps * 10
+    ms = _graph_time(torch, stream, launch, n_launch, args.warmup)
+    H.check(L.hxq_cuda_stream_synchronize(C.c_void_p(stream.cuda_stream)), name)
+    per = ms / n_launch
+    # drop-in API, synchronous, device arena
+    arena = H.SharedBuffer()
+    H.check(L.hxq_cuda_arena_init(C.byref(arena), n), "arena")
+    r = H.Result()
+    lat = []
+    fn = L.hxq_dequant if dtype == 0 else None
+    for i in range(30):
+        t0 = time.perf_counter()
+        if dtype == 0:
+            H.check(fn(t.ref, C.byref(arena), H.HXQ_BACKEND_CUDA, C.byref(r)), "dequant")
+        else:
+            H.check(L.hxq_dequant_bf16(t.ref, C.byref(arena), C.byref(r)), "dequant_bf16")
+        lat.append(time.perf_counter() - t0)
+    L.hxq_shared_buffer_free(C.byref(arena))
+    for img in imgs:
+        L.hxq_cuda_image_destroy(img)
+    peak, kind = measured_peaks()
+    gbs = algo_bytes / (per / 1e3) / 1e9
+    return {"case": name, "dtype": "f32" if dtype == 0 else "bf16", "weights": n,
+            "us_per_launch": per * 1e3, "weights_per_s": n / (per / 1e3),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes_per_launch": algo_bytes, "peak_source": kind},
+            "replicas": reps, "launches": n_launch,
+            "dequant_api_sync_us_median": 1e6 * statistics.median(lat[5:])}
+
+
+def _affine_case(torch, H, L, N: int, stream, args) -> dict:
+    from hxq_b200 import synth
+    O = I = 4096
+    gs = 128
+    d = synth.affine(O, I, gs, synth.SEED_C3)
+    xh, _ = synth.activations(N, I, synth.SEED_C3 + N)
+    code_bytes = O * I
+    io_bytes = code_bytes + 2 * O * (I // gs) * 4 + 2 * N * I + 4 * N * O
+    reps = max(2, int(np.ceil(4 * 126e6 / io_bytes))) if N <= 64 else 2
+    codes = [torch.from_numpy(d["codes"]).cuda() for _ in range(reps)]
+    sc = torch.from_numpy(d["scales"]).cuda()
+    of = torch.from_numpy(d["offsets"]).cuda()
+    x = torch.from_numpy(xh.view(np.int16)).cuda()
+    y = torch.empty(N * O, dtype=torch.float32, device="cuda")
+    ts = [H.AffineTensor(c.data_ptr(), sc.data_ptr(), of.data_ptr(), None, O, I, gs) for c in codes]
+
+    def launch(i):
+        if L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(ts[i % reps]), y.data_ptr(), N,
+                                          stream.cuda_stream) != 0:
+            raise RuntimeError("affine matmul failed")
+    n_launch = max(4, args.steps * (10 if N <= 64 else 2))
+    ms = _graph_time(torch, stream, launch, n_launch, args.warmup)
+    per_s = ms / n_launch / 1e3
+    flops = 2.0 * N * O * I
+    tf_peak = measured_tensor_peak()
+    hbm, _ = measured_peaks()
+    gbs = io_bytes / per_s / 1e9
+    tfl = flops / per_s / 1e12
+    return {"case": f"affine 4096x4096 g128 N={N}", "us_per_call": per_s * 1e6, "tflops": tfl,
+            "gbs": gbs, "hbm_frac": gbs / hbm, "tensor_frac": tfl / tf_peak, "bytes_per_call": io_bytes,
+            "replicas": reps}
+
+
+def run_aux_workload(args):
+    import torch
+
+    import hxq_b200 as H
+    from hxq_b200 import synth
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    L = H.lib()
+    stream = torch.cuda.Stream()
+    results = []
+    if args.workload == "c1":
+        d = synth.vq12(2048, 2048, synth.SEED_C1)
+        nnz = len(d["rows"])
+        results.append(_decompress_case(torch, H, L, "c1 12-bit 2048x2048", d, 0,
+                                        2048 * 2048 * 3 // 4 + CB_BYTES + 12 * nnz + 4 * 2048 * 2048, stream, args))
+        results.append(_decompress_case(torch, H, L, "c1 12-bit 2048x2048", d, 1,
+                                        2048 * 2048 * 3 // 4 + CB_BYTES + 12 * nnz + 2 * 2048 * 2048, stream, args))
+    elif args.workload == "c2":
+        d = synth.scalar(4096, 4096, synth.SEED_C2)
+        nnz = len(d["rows"])
+        n = 4096 * 4096
+        results.append(_decompress_case(torch, H, L, "c2 scalar 4096x4096", d, 0, n + 1024 + 12 * nnz + 4 * n,
+                                        stream, args))
+        results.append(_decompress_case(torch, H, L, "c2 scalar 4096x4096", d, 1, n + 1024 + 12 * nnz + 2 * n,
+                                        stream, args))
+    else:
+        for N in (1, 8, 64, 512, 4096):
+            results.append(_affine_case(torch, H, L, N, stream, args))
+    print(json.dumps({"workload": args.workload, "data": "synthetic", "results": results}), flush=True)
+
+
+# ---------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -285,11 +440,17 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers to run (profiling aid; the workload is 32 layers)")
+    ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3"], default="llama7b",
+                    help="llama7b: the headline (default); c1/c2/c3: single-tensor decompress "
+                         "and the affine batch sweep, one JSON line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload != "llama7b":
+        run_aux_workload(args)
         return
 
     import torch
@@ -341,10 +502,26 @@ def main():
             off += align(b)
     torch.cuda.synchronize()
 
-    # the shared device arena: one layer's worth of fp32 weights
-    layer_numel = [sum(m["numel"] for m in lm) for lm in meta]
+    # The shared device arena.  Each launch decompresses a group of layers
+    # (as many as there are ranks, at most 8 = 56 matrices), so every launch
+    # carries about one full layer's weights whatever N is; the arena holds
+    # one group and is reused by all groups.
+    lpl = max(1, min(8, world, nl))
+    groups = [list(range(g, min(g + lpl, nl))) for g in range(0, nl, lpl)]
+    g_imgs, g_offs, g_numel = [], [], []
+    for grp in groups:
+        o, pos, gi = [], 0, []
+        for layer in grp:
+            for img, m in zip(imgs[layer], meta[layer]):
+                o.append(pos)
+                pos += m["numel"]
+                gi.append(img)
+        g_imgs.append((C.c_void_p * len(gi))(*[i.value for i in gi]))
+        g_offs.append((C.c_size_t * len(o))(*o))
+        g_numel.append(pos)
     arena = H.SharedBuffer()
-    H.check(L.hxq_cuda_arena_init(C.byref(arena), max(layer_numel)), "arena")
+    H.check(L.hxq_cuda_arena_init(C.byref(arena), max(g_numel)), "arena")
+    # per-layer views for the e2e path (one layer per launch)
     offs = []
     for lm in meta:
         o, pos = [], 0
@@ -359,10 +536,11 @@ def main():
     f32 = C.sizeof(C.c_float)
 
     def step(stream_ptr):
-        for layer in range(nl):
-            e = L.hxq_cuda_decompress_images(arrs[layer], 7, arena.data, offs[layer], 0,
-                                             sumsq.data_ptr() + 8 * 7 * layer,
-                                             conf.data_ptr() + f32 * 7 * layer, stream_ptr)
+        for gi, grp in enumerate(groups):
+            first = 7 * grp[0]
+            e = L.hxq_cuda_decompress_images(g_imgs[gi], 7 * len(grp), arena.data, g_offs[gi], 0,
+                                             sumsq.data_ptr() + 8 * first, conf.data_ptr() + f32 * first,
+                                             stream_ptr)
             if e != 0:
                 raise RuntimeError(f"decompress failed: {e}")
 
@@ -453,7 +631,7 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "llama7b-vq12-decompress", "layers": nl, "matrices": n_mat,
                        "weights": total_weights, "sidecar_frac": SIDECAR_FRAC, "shard": "rows by out_features",
-                       "launch": "one per layer (7 matrices)", "graph": graph is not None,
+                       "launch": f"one per {lpl} layer(s) ({7 * lpl} matrices)", "graph": graph is not None,
                        "l2": "no flush: 5.3 GB read + 25.9 GB written per step >> 126 MB L2",
                        "parallelism": f"row-shard x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

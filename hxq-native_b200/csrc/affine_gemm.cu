@@ -1,0 +1,450 @@
+// affine_gemm.cu -- tcgen05 dequant-GEMM for the affine group-quantized
+// matmul at batch sizes where it is a dense contraction (sm_100a).
+//
+//   Y[n, o] = sum_k x[n, k] * W[o, k] + bias[o],  W = code * scale + offset
+// (the reference's src/hxq_affine.c:23-66 algebra, evaluated as a GEMM).
+//
+// CTA tile: 128 output features (M, TMEM lanes) x BN tokens (N), K in steps
+// of 128.  Warp roles (320 threads):
+//   warps 0-7  converters: thread (warp w, lane l) owns output row
+//              32*(w%4) + l and half (w/4) of each 128-wide K step; it reads
+//              64 codes (4 x 128-bit loads), forms W = fma(code, s, off) in
+//              fp32, rounds to bf16 and writes the packed pairs straight into
+//              tensor memory (tcgen05.st), which is the MMA's A operand --
+//              no shared-memory staging or swizzle for the weights;
+//              at the end the same threads drain the accumulator
+//              (tcgen05.ld), add the bias and store coalesced rows of Y;
+//   warp 8     TMA producer: activation tiles [BN tokens x 64 K] bf16 with
+//              128-byte swizzle into a 3-4 stage shared-memory ring;
+//   warp 9     allocates tensor memory and issues tcgen05.mma
+//              (kind::f16, bf16 x bf16 -> fp32, M=128, N=BN, K=16) from one
+//              thread; tcgen05.commit frees A buffers and ring stages.
+// Tensor memory: accumulator [128 x BN] fp32 at column 0, two A buffers of
+// 64 columns (128 bf16 of K) at columns 256 and 320; 512 columns allocated.
+// Every mbarrier wait is bounded (about one second of clock); a wait that
+// runs out records an error word and the CTA unwinds, releasing its tensor
+// memory.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "hxq_cuda.h"
+
+namespace hxq {
+namespace gemm {
+
+constexpr uint32_t kBM = 128;
+constexpr uint32_t kBK = 128;            // K per pipeline step
+constexpr uint32_t kConvWarps = 8;
+constexpr uint32_t kThreads = (kConvWarps + 2) * 32;
+constexpr uint32_t kProducerWarp = 8;
+constexpr uint32_t kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 256;         // first column of the A buffers
+constexpr uint64_t kWaitCycles = 2000000000ull;  // ~1 s at 1.9 GHz
+constexpr uint32_t kErrTimeout = 2u;
+
+__device__ uint32_t g_gemm_err;          // device status word of this kernel
+
+__host__ __device__ constexpr uint32_t stages_for(uint32_t bn) { return bn >= 256 ? 3u : 4u; }
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
+// ring | barriers (full[S], empty[S], a_full[2], a_empty[2], d_full) | tmem addr | abort
+__host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn)
+{
+    return 1024u /* alignment slack */ + stages_for(bn) * stage_bytes(bn) + 256u;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false if it ran out or another thread already gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
+{
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = clock64();
+    while (true) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *abort = 1u;
+            atomicOr(&g_gemm_err, kErrTimeout);
+            return false;
+        }
+    }
+}
+
+// Teardown wait: bounded, but not cut short by the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity)
+{
+    const uint64_t t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_gemm_err, kErrTimeout);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
+                                            int32_t c1)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1 (sm100), base offset 0 (1024-B aligned).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
+{
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
+// K-major, N = bn, M = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t bn)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((bn >> 3) << 17) | ((kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+        "%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]));
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+        "[%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ float code_f32(uint32_t word, uint32_t i)
+{
+    return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u + i)) - 8388608.0f;
+}
+
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+struct Params {
+    const uint8_t *codes;     // [O, I]
+    const float *scales;      // [O, I/gs]
+    const float *offsets;     // [O, I/gs]
+    const float *bias;        // [O] or null
+    float *y;                 // [T, O]
+    uint32_t T, I, O, gs;
+};
+
+template <uint32_t BN>
+__global__ void __launch_bounds__(kThreads, 1)
+affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ Params p)
+{
+    constexpr uint32_t S = stages_for(BN);
+    constexpr uint32_t SB = stage_bytes(BN);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *ring = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + S * SB);
+    uint64_t *empty = full + S;
+    uint64_t *a_full = empty + S;
+    uint64_t *a_empty = a_full + 2;
+    uint64_t *d_full = a_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(d_full + 1);
+    volatile uint32_t *abort_flag = tmem_slot + 1;
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t o0 = blockIdx.x * kBM;
+    const uint32_t n0 = blockIdx.y * BN;
+    const uint32_t KT = p.I / kBK;   // K steps
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(a_full + b, kConvWarps * 32);
+            mbar_init(a_empty + b, 1);
+        }
+        mbar_init(d_full, 1);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    uint32_t issued = 0;  // producer: loads issued
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            for (uint32_t kt = 0; kt < KT; ++kt) {
+                const uint32_t s = kt % S;
+                if (kt >= S && !mbar_wait(empty + s, ((kt / S) - 1u) & 1u, abort_flag)) break;
+                mbar_expect_tx(full + s, SB);
+                unsigned char *dst = ring + s * SB;
+                tma_load_2d(dst, &xmap, full + s, (int32_t)(kt * kBK), (int32_t)n0);
+                tma_load_2d(dst + BN * 128u, &xmap, full + s, (int32_t)(kt * kBK + 64u), (int32_t)n0);
+                issued = kt + 1u;
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(BN);
+            for (uint32_t kt = 0; kt < KT; ++kt) {
+                const uint32_t s = kt % S, b = kt & 1u;
+                if (!mbar_wait(a_full + b, (kt >> 1) & 1u, abort_flag)) break;
+                if (!mbar_wait(full + s, (kt / S) & 1u, abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t bbase = smem_u32(ring + s * SB);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kBK / 16u; ++kk) {
+                    const uint64_t bd = smem_desc(bbase + (kk >> 2) * (BN * 128u) + (kk & 3u) * 32u);
+                    mma_ts(tmem, tmem + kTmemA + b * 64u + kk * 8u, bd, idesc, (kt | kk) != 0u ? 1u : 0u);
+                }
+                mma_commit(a_empty + b);
+                mma_commit(empty + s);
+            }
+            mma_commit(d_full);
+        }
+    } else {
+        // converters, then the epilogue
+        const uint32_t q = warp & 3u, h = warp >> 2;
+        const uint32_t row = q * 32u + lane;
+        const uint32_t o = o0 + row;
+        const bool valid = o < p.O;
+        const uint32_t ng = p.I / p.gs;
+        const uint8_t *crow = p.codes + (size_t)(valid ? o : 0u) * p.I;
+        const uint32_t lane_base = (q * 32u) << 16;
+        bool ok = true;
+        for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+            const uint32_t b = kt & 1u;
+            const uint32_t k0 = kt * kBK + h * 64u;
+            uint4 c[4];
+            float sc = 0.0f, of = 0.0f;
+            if (valid) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(crow + k0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) c[i] = __ldg(src + i);
+                const uint32_t g = k0 / p.gs;
+                sc = __ldg(p.scales + (size_t)o * ng + g);
+                of = __ldg(p.offsets + (size_t)o * ng + g);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) c[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            uint32_t v[32];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float f0 = fmaf(code_f32(w4[j], 0), sc, of);
+                    const float f1 = fmaf(code_f32(w4[j], 1), sc, of);
+                    const float f2 = fmaf(code_f32(w4[j], 2), sc, of);
+                    const float f3 = fmaf(code_f32(w4[j], 3), sc, of);
+                    v[8 * i + 2 * j] = bf16x2(f0, f1);
+                    v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
+                }
+            }
+            if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+            tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
+            asm volatile("tcgen05.wait::st.sync.aligned;");
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            mbar_arrive(a_full + b);
+        }
+        if (ok && mbar_wait(d_full, 0u, abort_flag)) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const float bo = (valid && p.bias) ? __ldg(p.bias + o) : 0.0f;
+            // this half's accumulator columns; a 32-column load may read past
+            // them (inside the allocation) when BN < 64: those are not stored
+            const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
+#pragma unroll 1
+            for (uint32_t c0 = cbeg; c0 < cend; c0 += 32u) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_base + c0, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;");
+                if (valid) {
+#pragma unroll
+                    for (uint32_t j = 0; j < 32u; ++j) {
+                        const uint32_t n = n0 + c0 + j;
+                        if (c0 + j < cend && n < p.T) p.y[(size_t)n * p.O + o] = __uint_as_float(v[j]) + bo;
+                    }
+                }
+            }
+        }
+    }
+    // Teardown: every issued MMA (the d_full commit follows the last one)
+    // and every issued activation load has landed before tensor memory and
+    // shared memory are released, also when a wait above gave up.
+    if (warp == kMmaWarp && lane == 0) mbar_drain(d_full, 0u);
+    if (warp == kProducerWarp && lane == 0) {
+        for (uint32_t kt = issued > S ? issued - S : 0u; kt < issued; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+template <uint32_t BN>
+int launch(const uint16_t *x, const Params &p, cudaStream_t s)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return -1;
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    const cuuint64_t dims[2] = {p.I, p.T};
+    const cuuint64_t strides[1] = {(cuuint64_t)p.I * 2u};
+    const cuuint32_t box[2] = {64u, BN};
+    const cuuint32_t estr[2] = {1u, 1u};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
+    auto kern = affine_gemm_kernel<BN>;
+    const uint32_t smem = smem_bytes(BN);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    dim3 grid((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN);
+    kern<<<grid, kThreads, smem, s>>>(map, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace gemm
+
+// Tensor-core path for bf16 activations.  Returns 1 when the shape is not
+// one it takes (the caller uses the GEMV), 0 on launch, -1 on error.
+int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
+                     const float *bias, float *y, uint32_t T, uint32_t I, uint32_t O, uint32_t gs,
+                     cudaStream_t s)
+{
+    if (T == 0 || O == 0) return 1;
+    if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return 1;
+    if (((uintptr_t)x & 15u) || ((uintptr_t)codes & 15u)) return 1;
+    if ((uint64_t)T * I >= (1ull << 40)) return 1;
+    gemm::Params p{codes, scales, offsets, bias, y, T, I, O, gs};
+    if (T <= 16) return gemm::launch<16>(x, p, s);
+    if (T <= 32) return gemm::launch<32>(x, p, s);
+    if (T <= 64) return gemm::launch<64>(x, p, s);
+    if (T <= 128) return gemm::launch<128>(x, p, s);
+    return gemm::launch<256>(x, p, s);
+}
+
+}  // namespace hxq
+
+extern "C" int hxq_cuda_affine_device_status(void)
+{
+    uint32_t v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (cudaMemcpyFromSymbol(&v, hxq::gemm::g_gemm_err, sizeof(v)) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (v) {
+        const uint32_t z = 0;
+        cudaMemcpyToSymbol(hxq::gemm::g_gemm_err, &z, sizeof(z));
+    }
+    return (int)v;
+}

@@ -21,9 +21,16 @@
 #include "hxq_cuda.h"
 
 namespace hxq {
+
+int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
+                     const float *bias, float *y, uint32_t T, uint32_t I, uint32_t O, uint32_t gs,
+                     cudaStream_t s);
+
 namespace {
 
 constexpr int kGemvTokens = 8;   // tokens per pass of the GEMV
+// From this many tokens on, bf16 activations go to the tcgen05 dequant-GEMM.
+constexpr uint32_t kGemmMinTokens = 16;
 
 __device__ __forceinline__ float code_to_float(uint32_t word, uint32_t i)
 {
@@ -172,6 +179,13 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
     if (in_f == 0) {  // empty reduction: bias only
         affine_generic_kernel<XT><<<1, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    }
+    if constexpr (sizeof(XT) == 2) {
+        if (N >= kGemmMinTokens) {
+            const int r = affine_gemm_bf16(reinterpret_cast<const uint16_t *>(x), codes, scales, offsets, bias,
+                                           y, N, in_f, out_f, gs, s);
+            if (r <= 0) return r;  // launched (0) or failed (-1); 1 = shape not taken
+        }
     }
     const bool fast = gs % 16u == 0 && in_f % 16u == 0 && aligned(x, 16) && aligned(codes, 16);
     if (fast) {

@@ -128,6 +128,7 @@ SIGNATURES = {
     "hxq_cuda_apply_sidecar": (C.c_float, [P, P, P, P, C.c_uint32, C.c_uint32]),
     "hxq_affine_group_matmul_bf16": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
     "hxq_affine_group_matmul_async": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
+    "hxq_cuda_affine_device_status": (C.c_int, []),
 }
 
 

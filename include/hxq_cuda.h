@@ -177,10 +177,20 @@ float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
 /* -- Affine matmul variants --------------------------------------------- */
 
 /* bf16 activations (uint16_t bit patterns, [N, in_f]); fp32 output.
- * Products of bf16 x and integer codes are exact, accumulation is fp32. */
+ * Up to 15 tokens: the streaming GEMV (exact products of bf16 x and integer
+ * codes, fp32 accumulation).  From 16 tokens, when in_f % 128 == 0 and the
+ * group size is a multiple of 64: the tcgen05 dequant-GEMM, which rounds
+ * W = code*scale + offset to bf16 before the tensor-core product (fp32
+ * accumulation): per output the error is at most 2^-9 of sum |x_i w_i|. */
 int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16,
                                  const hxq_affine_tensor_t *tensor,
                                  float *d_output, uint32_t N, void *stream);
+/* Waits for the device, then returns (and clears) the status word of the
+ * tcgen05 dequant-GEMM: 0 when every pipeline wait completed, nonzero if
+ * one ran out of time (the kernel then unwinds without writing results);
+ * -1 on a CUDA error. */
+int hxq_cuda_affine_device_status(void);
+
 /* fp32 activations on a caller stream. */
 int hxq_affine_group_matmul_async(const float *d_x,
                                   const hxq_affine_tensor_t *tensor,

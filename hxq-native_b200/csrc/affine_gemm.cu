@@ -30,6 +30,9 @@
 
 #include <cstdint>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "hxq_cuda.h"
 
@@ -42,14 +45,17 @@ constexpr uint32_t kConvWarps = 8;
 constexpr uint32_t kThreads = (kConvWarps + 2) * 32;
 constexpr uint32_t kProducerWarp = 8;
 constexpr uint32_t kMmaWarp = 9;
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemA = 256;         // first column of the A buffers
+// Tensor memory: the accumulator takes BN columns from 0, the two A buffers
+// 64 columns each right after it (rounded to 128); a tile of BN <= 128 fits
+// in 256 columns, so two CTAs can share an SM.
+__host__ __device__ constexpr uint32_t tmem_a_col(uint32_t bn) { return bn <= 128 ? 128u : 256u; }
+__host__ __device__ constexpr uint32_t tmem_cols(uint32_t bn) { return bn <= 128 ? 256u : 512u; }
 constexpr uint64_t kWaitCycles = 2000000000ull;  // ~1 s at 1.9 GHz
 constexpr uint32_t kErrTimeout = 2u;
 
 __device__ uint32_t g_gemm_err;          // device status word of this kernel
 
-__host__ __device__ constexpr uint32_t stages_for(uint32_t bn) { return bn >= 256 ? 3u : 4u; }
+__host__ __device__ constexpr uint32_t stages_for(uint32_t bn) { return bn >= 256 ? 3u : bn == 128 ? 3u : 4u; }
 __host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
 // ring | barriers (full[S], empty[S], a_full[2], a_empty[2], d_full) | tmem addr | abort
 __host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn)
@@ -203,16 +209,19 @@ struct Params {
     const float *scales;      // [O, I/gs]
     const float *offsets;     // [O, I/gs]
     const float *bias;        // [O] or null
-    float *y;                 // [T, O]
+    float *y;                 // [T, O], or [splits][T, O] partial sums when splits > 1
     uint32_t T, I, O, gs;
+    uint32_t splits;          // K ranges (gridDim.z); >1 writes partials, no bias
 };
 
 template <uint32_t BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
 affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ Params p)
 {
     constexpr uint32_t S = stages_for(BN);
     constexpr uint32_t SB = stage_bytes(BN);
+    constexpr uint32_t kTmemA = tmem_a_col(BN);
+    constexpr uint32_t kTmemCols = tmem_cols(BN);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *ring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
@@ -227,7 +236,9 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t o0 = blockIdx.x * kBM;
     const uint32_t n0 = blockIdx.y * BN;
-    const uint32_t KT = p.I / kBK;   // K steps
+    const uint32_t KT_all = p.I / kBK;                          // K steps of the matrix
+    const uint32_t kt_lo = (uint32_t)((uint64_t)KT_all * blockIdx.z / p.splits);
+    const uint32_t KT = (uint32_t)((uint64_t)KT_all * (blockIdx.z + 1u) / p.splits) - kt_lo;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -261,8 +272,9 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
                 if (kt >= S && !mbar_wait(empty + s, ((kt / S) - 1u) & 1u, abort_flag)) break;
                 mbar_expect_tx(full + s, SB);
                 unsigned char *dst = ring + s * SB;
-                tma_load_2d(dst, &xmap, full + s, (int32_t)(kt * kBK), (int32_t)n0);
-                tma_load_2d(dst + BN * 128u, &xmap, full + s, (int32_t)(kt * kBK + 64u), (int32_t)n0);
+                const uint32_t kg = (kt_lo + kt) * kBK;
+                tma_load_2d(dst, &xmap, full + s, (int32_t)kg, (int32_t)n0);
+                tma_load_2d(dst + BN * 128u, &xmap, full + s, (int32_t)(kg + 64u), (int32_t)n0);
                 issued = kt + 1u;
             }
         }
@@ -295,22 +307,32 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
         const uint8_t *crow = p.codes + (size_t)(valid ? o : 0u) * p.I;
         const uint32_t lane_base = (q * 32u) << 16;
         bool ok = true;
-        for (uint32_t kt = 0; kt < KT && ok; ++kt) {
-            const uint32_t b = kt & 1u;
-            const uint32_t k0 = kt * kBK + h * 64u;
-            uint4 c[4];
-            float sc = 0.0f, of = 0.0f;
+        // codes, scale and offset of the next K step are loaded while the
+        // current one is converted
+        uint4 cn[4];
+        float scn = 0.0f, ofn = 0.0f;
+        auto fetch = [&](uint32_t kt) {
+            const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
             if (valid) {
                 const uint4 *src = reinterpret_cast<const uint4 *>(crow + k0);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) c[i] = __ldg(src + i);
+                for (int i = 0; i < 4; ++i) cn[i] = __ldg(src + i);
                 const uint32_t g = k0 / p.gs;
-                sc = __ldg(p.scales + (size_t)o * ng + g);
-                of = __ldg(p.offsets + (size_t)o * ng + g);
+                scn = __ldg(p.scales + (size_t)o * ng + g);
+                ofn = __ldg(p.offsets + (size_t)o * ng + g);
             } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) c[i] = make_uint4(0u, 0u, 0u, 0u);
+                for (int i = 0; i < 4; ++i) cn[i] = make_uint4(0u, 0u, 0u, 0u);
             }
+        };
+        if (KT > 0) fetch(0);
+        for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+            const uint32_t b = kt & 1u;
+            uint4 c[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[i] = cn[i];
+            const float sc = scn, of = ofn;
+            if (kt + 1u < KT) fetch(kt + 1u);
             uint32_t v[32];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -333,7 +355,9 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
         }
         if (ok && mbar_wait(d_full, 0u, abort_flag)) {
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const float bo = (valid && p.bias) ? __ldg(p.bias + o) : 0.0f;
+            const bool partial = p.splits > 1u;
+            const float bo = (valid && p.bias && !partial) ? __ldg(p.bias + o) : 0.0f;
+            float *yo = p.y + (partial ? (size_t)blockIdx.z * p.T * p.O : 0u);
             // this half's accumulator columns; a 32-column load may read past
             // them (inside the allocation) when BN < 64: those are not stored
             const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
@@ -346,7 +370,7 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
 #pragma unroll
                     for (uint32_t j = 0; j < 32u; ++j) {
                         const uint32_t n = n0 + c0 + j;
-                        if (c0 + j < cend && n < p.T) p.y[(size_t)n * p.O + o] = __uint_as_float(v[j]) + bo;
+                        if (c0 + j < cend && n < p.T) yo[(size_t)n * p.O + o] = __uint_as_float(v[j]) + bo;
                     }
                 }
             }
@@ -364,6 +388,20 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// y[n, o] = sum over the K ranges, in order, of the partial sums + bias.
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, const float *__restrict__ bias,
+                                     float *__restrict__ y, uint32_t T, uint32_t O, uint32_t splits)
+{
+    const uint64_t total = (uint64_t)T * O;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (uint32_t k = 0; k < splits; ++k) acc += part[(size_t)k * total + i];
+        if (bias) acc += __ldg(bias + (uint32_t)(i % O));
+        y[i] = acc;
     }
 }
 
@@ -410,9 +448,31 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
         cudaGetLastError();
         return -1;
     }
-    dim3 grid((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN);
+    dim3 grid((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
     kern<<<grid, kThreads, smem, s>>>(map, p);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// Partial-sum buffer for split-K, one per (device, stream) so calls on
+// different streams never share it; grown on demand (the first call of a
+// shape on a stream allocates; later calls, e.g. under graph capture, reuse).
+float *splitk_buffer(size_t floats, cudaStream_t s)
+{
+    struct Buf { float *p = nullptr; size_t cap = 0; };
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, Buf> bufs;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    std::lock_guard<std::mutex> lk(mu);
+    Buf &b = bufs[{dev, s}];
+    if (b.cap < floats) {
+        if (b.p) { cudaStreamSynchronize(s); cudaFree(b.p); }
+        b.p = nullptr;
+        b.cap = 0;
+        if (cudaMalloc(&b.p, floats * sizeof(float)) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        b.cap = floats;
+    }
+    return b.p;
 }
 
 }  // namespace gemm
@@ -427,12 +487,41 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
     if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return 1;
     if (((uintptr_t)x & 15u) || ((uintptr_t)codes & 15u)) return 1;
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
-    gemm::Params p{codes, scales, offsets, bias, y, T, I, O, gs};
-    if (T <= 16) return gemm::launch<16>(x, p, s);
-    if (T <= 32) return gemm::launch<32>(x, p, s);
-    if (T <= 64) return gemm::launch<64>(x, p, s);
-    if (T <= 128) return gemm::launch<128>(x, p, s);
-    return gemm::launch<256>(x, p, s);
+    // Split K when the (rows x token) tiles alone would leave SMs idle.
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t bn = T <= 16 ? 16u : T <= 32 ? 32u : T <= 64 ? 64u : T <= 128 ? 128u : 256u;
+    const uint32_t tiles = ((O + gemm::kBM - 1) / gemm::kBM) * ((T + bn - 1) / bn);
+    const uint32_t KT = I / gemm::kBK;
+    const uint32_t resident = (uint32_t)sms * (bn <= 128 ? 2u : 1u);  // CTAs the GPU holds at once
+    uint32_t splits = 1;
+    if (tiles < resident) {
+        splits = (resident + tiles - 1) / tiles;
+        if (splits > KT / 2u) splits = KT / 2u;  // keep at least two K steps per CTA
+        if (splits > 16u) splits = 16u;
+        if (splits < 1u) splits = 1u;
+    }
+    float *part = nullptr;
+    if (splits > 1) {
+        part = gemm::splitk_buffer((size_t)splits * T * O, s);
+        if (!part) return -1;
+    }
+    gemm::Params p{codes, scales, offsets, bias, splits > 1 ? part : y, T, I, O, gs, splits};
+    int r;
+    switch (bn) {
+    case 16: r = gemm::launch<16>(x, p, s); break;
+    case 32: r = gemm::launch<32>(x, p, s); break;
+    case 64: r = gemm::launch<64>(x, p, s); break;
+    case 128: r = gemm::launch<128>(x, p, s); break;
+    default: r = gemm::launch<256>(x, p, s); break;
+    }
+    if (r != 0 || splits == 1) return r;
+    const uint64_t total = (uint64_t)T * O;
+    uint64_t blocks = (total + 255u) / 256u;
+    if (blocks > (uint64_t)sms * 8u) blocks = (uint64_t)sms * 8u;
+    gemm::splitk_reduce_kernel<<<(uint32_t)blocks, 256, 0, s>>>(part, bias, y, T, O, splits);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace hxq

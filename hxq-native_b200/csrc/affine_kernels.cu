@@ -29,8 +29,10 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
 namespace {
 
 constexpr int kGemvTokens = 8;   // tokens per pass of the GEMV
-// From this many tokens on, bf16 activations go to the tcgen05 dequant-GEMM.
-constexpr uint32_t kGemmMinTokens = 16;
+// From this many tokens on, bf16 activations go to the tcgen05 dequant-GEMM
+// (split over K when the tiles alone would not fill the GPU); one token
+// stays on the exact streaming GEMV.
+constexpr uint32_t kGemmMinTokens = 2;
 
 __device__ __forceinline__ float code_to_float(uint32_t word, uint32_t i)
 {
@@ -76,46 +78,80 @@ template <> __device__ __forceinline__ float xval<uint16_t>(const uint16_t *p)
 }
 
 // Requirements: group_size % 16 == 0, in_f % 16 == 0, x and codes 16-B aligned.
-template <typename XT, int NT>
+// One warp per output row.  A lane owns 16-code slices sl = lane + 32*i; all
+// SPL slices of a pass are loaded before any is used, so a warp keeps
+// SPL*512 bytes of codes in flight.  Activations come from shared memory
+// (staged once per block as fp32) when ntok*in_f floats fit in xs_floats,
+// else through L1.
+template <typename XT, int NT, int SPL>
 __global__ void __launch_bounds__(256)
 affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
                    const float *__restrict__ scales, const float *__restrict__ offsets,
                    const float *__restrict__ bias, float *__restrict__ y,
                    uint32_t n0, uint32_t ntok, uint32_t in_f, uint32_t out_f,
-                   uint32_t gs)
+                   uint32_t gs, uint32_t xs_floats)
 {
+    extern __shared__ float xs[];
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t ng = in_f / gs;
     const uint32_t slices = in_f / 16u;
+    const bool staged = (size_t)ntok * in_f <= xs_floats;
+    if (staged) {
+        for (uint32_t i = threadIdx.x; i < ntok * in_f; i += blockDim.x)
+            xs[i] = xval<XT>(x + (size_t)n0 * in_f + i);
+        __syncthreads();
+    }
     for (uint32_t o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_f; o += warps) {
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
         const uint4 *crow = reinterpret_cast<const uint4 *>(codes + (size_t)o * in_f);
-        for (uint32_t sl = lane; sl < slices; sl += 32u) {
-            const uint4 cw = __ldg(crow + sl);
-            float q[16];
-            const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+        for (uint32_t base = 0; base < slices; base += 32u * SPL) {
+            uint4 cw[SPL];
+            float sv[SPL], fv[SPL];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int i = 0; i < SPL; ++i) {
+                const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                if (sl < slices) {
+                    cw[i] = __ldg(crow + sl);
+                    const uint32_t g = (sl * 16u) / gs;
+                    sv[i] = __ldg(scales + (size_t)o * ng + g);
+                    fv[i] = __ldg(offsets + (size_t)o * ng + g);
+                }
+            }
 #pragma unroll
-                for (int b = 0; b < 4; ++b) q[4 * j + b] = code_to_float(w[j], (uint32_t)b);
-            const uint32_t g = (sl * 16u) / gs;
-            const float s = __ldg(scales + (size_t)o * ng + g);
-            const float f = __ldg(offsets + (size_t)o * ng + g);
+            for (int i = 0; i < SPL; ++i) {
+                const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                if (sl >= slices) continue;
+                float q[16];
+                const uint32_t w[4] = {cw[i].x, cw[i].y, cw[i].z, cw[i].w};
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if ((uint32_t)t < ntok) {
-                    float xv[16];
-                    XLoad<XT>::load16(x + (size_t)(n0 + t) * in_f + sl * 16u, xv);
-                    float dot = 0.0f, xs = 0.0f;
+                for (int j = 0; j < 4; ++j)
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        dot = fmaf(xv[i], q[i], dot);
-                        xs += xv[i];
+                    for (int b = 0; b < 4; ++b) q[4 * j + b] = code_to_float(w[j], (uint32_t)b);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if ((uint32_t)t < ntok) {
+                        float xv[16];
+                        if (staged) {
+                            const float4 *p4 = reinterpret_cast<const float4 *>(xs + (size_t)t * in_f + sl * 16u);
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const float4 v4 = p4[u];
+                                xv[4 * u] = v4.x; xv[4 * u + 1] = v4.y; xv[4 * u + 2] = v4.z; xv[4 * u + 3] = v4.w;
+                            }
+                        } else {
+                            XLoad<XT>::load16(x + (size_t)(n0 + t) * in_f + sl * 16u, xv);
+                        }
+                        float dot = 0.0f, xsum = 0.0f;
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            dot = fmaf(xv[u], q[u], dot);
+                            xsum += xv[u];
+                        }
+                        acc[t] = fmaf(sv[i], dot, fmaf(fv[i], xsum, acc[t]));
                     }
-                    acc[t] = fmaf(s, dot, fmaf(f, xs, acc[t]));
                 }
             }
         }
@@ -195,14 +231,18 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         uint32_t blocks = (out_f + 7u) / 8u;
         const uint32_t cap = (uint32_t)sms * 8u;
         if (blocks > cap) blocks = cap;
+        constexpr uint32_t kXsFloats = 12288;  // 48 KB of staged activations
         for (uint32_t n0 = 0; n0 < N; n0 += kGemvTokens) {
             const uint32_t nt = N - n0 < (uint32_t)kGemvTokens ? N - n0 : (uint32_t)kGemvTokens;
+            // one token: activations through L1 (staging would cost more than it saves)
+            const size_t smem = (nt > 1 && (size_t)nt * in_f <= kXsFloats) ? (size_t)nt * in_f * sizeof(float) : 0;
+            const uint32_t xs = smem ? kXsFloats : 0u;
             if (nt == 1)
-                affine_gemv_kernel<XT, 1><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+                affine_gemv_kernel<XT, 1, 8><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
             else if (nt <= 4)
-                affine_gemv_kernel<XT, 4><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+                affine_gemv_kernel<XT, 4, 4><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
             else
-                affine_gemv_kernel<XT, kGemvTokens><<<blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs);
+                affine_gemv_kernel<XT, kGemvTokens, 2><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
         }
     } else {
         uint64_t blocks = ((uint64_t)N * out_f + 255u) / 256u;

@@ -177,8 +177,8 @@ float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
 /* -- Affine matmul variants --------------------------------------------- */
 
 /* bf16 activations (uint16_t bit patterns, [N, in_f]); fp32 output.
- * Up to 15 tokens: the streaming GEMV (exact products of bf16 x and integer
- * codes, fp32 accumulation).  From 16 tokens, when in_f % 128 == 0 and the
+ * One token: the streaming GEMV (exact products of bf16 x and integer
+ * codes, fp32 accumulation).  From 2 tokens, when in_f % 128 == 0 and the
  * group size is a multiple of 64: the tcgen05 dequant-GEMM, which rounds
  * W = code*scale + offset to bf16 before the tensor-core product (fp32
  * accumulation): per output the error is at most 2^-9 of sum |x_i w_i|. */

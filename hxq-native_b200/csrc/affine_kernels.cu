@@ -10,7 +10,7 @@
 // byte permute into the mantissa of 2^23, token activations read through
 // L1, the group scale applied per 16-code slice and the offset term from
 // the slice's activation sum, one warp reduction per row, bias fused into
-// the store.  Larger token counts use the tcgen05 GEMM (affine_gemm.cu)
+// the store.  Larger token counts use the tcgen05 GEMM (dequant_gemm.cu)
 // when the shape allows it.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

@@ -1,33 +1,42 @@
-// affine_gemm.cu -- tcgen05 dequant-GEMM for the affine group-quantized
-// matmul at batch sizes where it is a dense contraction (sm_100a).
+// dequant_gemm.cu -- tcgen05 dequant-GEMM for the quantized matmuls at
+// batch sizes where they are dense contractions (sm_100a).
 //
-//   Y[n, o] = sum_k x[n, k] * W[o, k] + bias[o],  W = code * scale + offset
-// (the reference's src/hxq_affine.c:23-66 algebra, evaluated as a GEMM).
+//   Y[n, o] = sum_k x[n, k] * W[o, k] (+ bias[o])
+// with W decoded on the fly from either
+//   - affine group-quantized codes, W = code * scale + offset (the
+//     reference's src/hxq_affine.c:23-66 algebra, evaluated as a GEMM), or
+//   - a 12-bit 2D-VQ image, W = codebook[index] + sidecar deltas (the
+//     reference's src/hxq.c:239-350 decode), with no dense W in memory.
 //
 // CTA tile: 128 output features (M, TMEM lanes) x BN tokens (N), K in steps
 // of 128.  Warp roles (320 threads):
 //   warps 0-7  converters: thread (warp w, lane l) owns output row
-//              32*(w%4) + l and half (w/4) of each 128-wide K step; it reads
-//              64 codes (4 x 128-bit loads), forms W = fma(code, s, off) in
-//              fp32, rounds to bf16 and writes the packed pairs straight into
-//              tensor memory (tcgen05.st), which is the MMA's A operand --
-//              no shared-memory staging or swizzle for the weights;
+//              32*(w%4) + l and half (w/4) of each 128-wide K step.
+//              Affine: 64 codes (4 x 128-bit loads), W = fma(code, s, off)
+//              in fp32, rounded to bf16.  VQ: 48 index bytes (3 x 128-bit
+//              loads), one PRMT per byte triple, each 12-bit index gathers
+//              one bf16 pair from a shared-memory copy of the codebook;
+//              sidecar positions are recomputed in fp32 (codebook value +
+//              deltas in array order) and rounded once.  The packed pairs go
+//              straight into tensor memory (tcgen05.st) as the MMA's A
+//              operand -- no shared-memory staging or swizzle for weights;
 //              at the end the same threads drain the accumulator
 //              (tcgen05.ld), add the bias and store coalesced rows of Y;
 //   warp 8     TMA producer: activation tiles [BN tokens x 64 K] bf16 with
-//              128-byte swizzle into a 3-4 stage shared-memory ring;
+//              128-byte swizzle into a 2-4 stage shared-memory ring;
 //   warp 9     allocates tensor memory and issues tcgen05.mma
 //              (kind::f16, bf16 x bf16 -> fp32, M=128, N=BN, K=16) from one
 //              thread; tcgen05.commit frees A buffers and ring stages.
-// Tensor memory: accumulator [128 x BN] fp32 at column 0, two A buffers of
-// 64 columns (128 bf16 of K) at columns 256 and 320; 512 columns allocated.
-// Every mbarrier wait is bounded (about one second of clock); a wait that
-// runs out records an error word and the CTA unwinds, releasing its tensor
-// memory.
+// Tensor memory: accumulator [128 x BN] fp32 from column 0, two A buffers of
+// 64 columns (128 bf16 of K) after it; 256 columns for BN <= 128 (two CTAs
+// per SM), else 512.  Every mbarrier wait is bounded (about one second of
+// clock); a wait that runs out records an error word and the CTA unwinds,
+// releasing its tensor memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <map>
@@ -35,6 +44,7 @@
 #include <utility>
 
 #include "hxq_cuda.h"
+#include "hxq_cuda_internal.h"
 
 namespace hxq {
 namespace gemm {
@@ -55,12 +65,19 @@ constexpr uint32_t kErrTimeout = 2u;
 
 __device__ uint32_t g_gemm_err;          // device status word of this kernel
 
-__host__ __device__ constexpr uint32_t stages_for(uint32_t bn) { return bn >= 256 ? 3u : bn == 128 ? 3u : 4u; }
-__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
-// ring | barriers (full[S], empty[S], a_full[2], a_empty[2], d_full) | tmem addr | abort
-__host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn)
+// Ring depth: 3 stages for the large tiles, 4 for the small; the VQ tile of
+// 128 tokens keeps 2 so that two CTAs (with their 16 KB codebooks) share an SM.
+__host__ __device__ constexpr uint32_t stages_for(uint32_t bn, bool vq)
 {
-    return 1024u /* alignment slack */ + stages_for(bn) * stage_bytes(bn) + 256u;
+    return bn >= 256 ? 3u : bn == 128 ? (vq ? 2u : 3u) : 4u;
+}
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
+constexpr uint32_t kCodebookBytes = 4096u * 4u;   // VQ: 4096 bf16 pairs
+// ring | barriers (full[S], empty[S], a_full[2], a_empty[2], d_full) | tmem
+// addr | abort | (VQ) codebook
+__host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn, bool vq)
+{
+    return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn) + 256u + (vq ? kCodebookBytes : 0u);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -205,20 +222,40 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi)
 }
 
 struct Params {
+    // affine weights
     const uint8_t *codes;     // [O, I]
     const float *scales;      // [O, I/gs]
     const float *offsets;     // [O, I/gs]
     const float *bias;        // [O] or null
-    float *y;                 // [T, O], or [splits][T, O] partial sums when splits > 1
-    uint32_t T, I, O, gs;
+    // 12-bit VQ weights (an image with its matmul tables): rows of I*3/4
+    // packed bytes; bf16 codebook pairs; sidecar patches (col | bf16 << 16)
+    // of row o from rb[o], those of K step kt from offset kp[o*(I/128+1)+kt]
+    const uint8_t *vidx;
+    const uint32_t *cbh;
+    const uint32_t *rb;
+    const uint16_t *kp;
+    const uint32_t *e4;
+    float *y;                 // [T, ldy], or [splits][T, O] partial sums when splits > 1
+    uint32_t T, I, O, gs, ldy;
     uint32_t splits;          // K ranges (gridDim.z); >1 writes partials, no bias
 };
 
-template <uint32_t BN>
-__global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
-affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ Params p)
+// Replace the bf16 at position `local` (0..63) of a thread's 32 packed
+// pairs; the register array is indexed statically.
+__device__ __forceinline__ void patch_pair(uint32_t (&v)[32], uint32_t local, uint32_t nb)
 {
-    constexpr uint32_t S = stages_for(BN);
+    const uint32_t word = local >> 1;
+    const bool hi = (local & 1u) != 0u;
+#pragma unroll
+    for (uint32_t i = 0; i < 32u; ++i)
+        if (i == word) v[i] = hi ? ((v[i] & 0xFFFFu) | (nb << 16)) : ((v[i] & 0xFFFF0000u) | nb);
+}
+
+template <uint32_t BN, bool VQ>
+__global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
+dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ Params p)
+{
+    constexpr uint32_t S = stages_for(BN, VQ);
     constexpr uint32_t SB = stage_bytes(BN);
     constexpr uint32_t kTmemA = tmem_a_col(BN);
     constexpr uint32_t kTmemCols = tmem_cols(BN);
@@ -232,6 +269,7 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
     uint64_t *d_full = a_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(d_full + 1);
     volatile uint32_t *abort_flag = tmem_slot + 1;
+    uint32_t *cbh = reinterpret_cast<uint32_t *>(ring + S * SB + 256u);   // VQ: bf16 pairs
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t o0 = blockIdx.x * kBM;
@@ -303,61 +341,138 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
         const uint32_t row = q * 32u + lane;
         const uint32_t o = o0 + row;
         const bool valid = o < p.O;
-        const uint32_t ng = p.I / p.gs;
-        const uint8_t *crow = p.codes + (size_t)(valid ? o : 0u) * p.I;
         const uint32_t lane_base = (q * 32u) << 16;
         bool ok = true;
-        // codes, scale and offset of the next K step are loaded while the
-        // current one is converted
-        uint4 cn[4];
-        float scn = 0.0f, ofn = 0.0f;
-        auto fetch = [&](uint32_t kt) {
-            const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
-            if (valid) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(crow + k0);
+        if constexpr (!VQ) {
+            const uint32_t ng = p.I / p.gs;
+            const uint8_t *crow = p.codes + (size_t)(valid ? o : 0u) * p.I;
+            // codes, scale and offset of the next K step are loaded while the
+            // current one is converted
+            uint4 cn[4];
+            float scn = 0.0f, ofn = 0.0f;
+            auto fetch = [&](uint32_t kt) {
+                const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
+                if (valid) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(crow + k0);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) cn[i] = __ldg(src + i);
-                const uint32_t g = k0 / p.gs;
-                scn = __ldg(p.scales + (size_t)o * ng + g);
-                ofn = __ldg(p.offsets + (size_t)o * ng + g);
-            } else {
+                    for (int i = 0; i < 4; ++i) cn[i] = __ldg(src + i);
+                    const uint32_t g = k0 / p.gs;
+                    scn = __ldg(p.scales + (size_t)o * ng + g);
+                    ofn = __ldg(p.offsets + (size_t)o * ng + g);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) cn[i] = make_uint4(0u, 0u, 0u, 0u);
-            }
-        };
-        if (KT > 0) fetch(0);
-        for (uint32_t kt = 0; kt < KT && ok; ++kt) {
-            const uint32_t b = kt & 1u;
-            uint4 c[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) c[i] = cn[i];
-            const float sc = scn, of = ofn;
-            if (kt + 1u < KT) fetch(kt + 1u);
-            uint32_t v[32];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float f0 = fmaf(code_f32(w4[j], 0), sc, of);
-                    const float f1 = fmaf(code_f32(w4[j], 1), sc, of);
-                    const float f2 = fmaf(code_f32(w4[j], 2), sc, of);
-                    const float f3 = fmaf(code_f32(w4[j], 3), sc, of);
-                    v[8 * i + 2 * j] = bf16x2(f0, f1);
-                    v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
+                    for (int i = 0; i < 4; ++i) cn[i] = make_uint4(0u, 0u, 0u, 0u);
                 }
+            };
+            if (KT > 0) fetch(0);
+            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+                const uint32_t b = kt & 1u;
+                uint4 c[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) c[i] = cn[i];
+                const float sc = scn, of = ofn;
+                if (kt + 1u < KT) fetch(kt + 1u);
+                uint32_t v[32];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float f0 = fmaf(code_f32(w4[j], 0), sc, of);
+                        const float f1 = fmaf(code_f32(w4[j], 1), sc, of);
+                        const float f2 = fmaf(code_f32(w4[j], 2), sc, of);
+                        const float f3 = fmaf(code_f32(w4[j], 3), sc, of);
+                        v[8 * i + 2 * j] = bf16x2(f0, f1);
+                        v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
+                    }
+                }
+                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
+                asm volatile("tcgen05.wait::st.sync.aligned;");
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                mbar_arrive(a_full + b);
             }
-            if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
-            tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
-            asm volatile("tcgen05.wait::st.sync.aligned;");
-            asm volatile("tcgen05.fence::before_thread_sync;");
-            mbar_arrive(a_full + b);
+        } else {
+            // the image's bf16 codebook, one 32-bit pair per entry: an
+            // index gathers exactly one TMEM column (low half = even k)
+            for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
+                reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
+            const size_t row_bytes = (size_t)(p.I / 4u) * 3u;
+            const uint8_t *vrow = p.vidx + (size_t)(valid ? o : 0u) * row_bytes;
+            // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
+            // this row, from this CTA's first step); the offsets are read two
+            // steps ahead and the first four patches of a step one step ahead
+            const uint16_t *kpr = p.kp + (size_t)(valid ? o : 0u) * (KT_all + 1u) + kt_lo;
+            const uint32_t pb = valid ? __ldg(p.rb + o) : 0u;
+            uint32_t k_cur = valid && KT > 0 ? __ldg(kpr) : 0u;          // start of step kt
+            uint32_t k_nxt = valid && KT > 0 ? __ldg(kpr + 1) : 0u;      // start of step kt + 1
+            uint32_t k_nn = valid && KT > 1 ? __ldg(kpr + 2) : k_nxt;    // start of step kt + 2
+            uint32_t pc0 = 0, pc1 = 0, pc2 = 0, pc3 = 0;                 // patches of step kt
+            uint32_t pn0 = 0, pn1 = 0, pn2 = 0, pn3 = 0;                 // patches of step kt + 1
+            auto load4 = [&](uint32_t lo, uint32_t hi, uint32_t &q0, uint32_t &q1, uint32_t &q2, uint32_t &q3) {
+                const uint32_t *src = p.e4 + pb + lo;
+                const uint32_t n = hi - lo;
+                q0 = n > 0u ? __ldg(src) : 0u;
+                q1 = n > 1u ? __ldg(src + 1) : 0u;
+                q2 = n > 2u ? __ldg(src + 2) : 0u;
+                q3 = n > 3u ? __ldg(src + 3) : 0u;
+            };
+            if (KT > 0) load4(k_cur, k_nxt, pc0, pc1, pc2, pc3);
+            // 64 weights = 16 byte triples = 3 x 16 bytes per thread and step
+            uint4 cn[3];
+            auto fetch = [&](uint32_t kt) {
+                const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
+                const uint4 *src = reinterpret_cast<const uint4 *>(vrow + (size_t)(k0 / 4u) * 3u);
+#pragma unroll
+                for (int i = 0; i < 3; ++i) cn[i] = __ldg(src + i);
+            };
+            if (KT > 0) fetch(0);
+            asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+                const uint32_t b = kt & 1u;
+                const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
+                                        cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
+                const uint32_t n_cur = k_nxt - k_cur, lo_cur = k_cur;
+                if (kt + 1u < KT) {
+                    fetch(kt + 1u);
+                    load4(k_nxt, k_nn, pn0, pn1, pn2, pn3);
+                    k_cur = k_nxt;
+                    k_nxt = k_nn;
+                    k_nn = valid && kt + 3u <= KT ? __ldg(kpr + kt + 3u) : k_nn;
+                }
+                uint32_t v[32];
+#pragma unroll
+                for (uint32_t t = 0; t < 16u; ++t) {
+                    const uint32_t byte = 3u * t, wq = byte >> 2;
+                    const uint32_t B = __byte_perm(w[wq], w[wq + 1u < 12u ? wq + 1u : 11u], 0x3012u + (byte & 3u) * 0x1111u);
+                    v[2u * t] = cbh[(B >> 12) & 0xFFFu];
+                    v[2u * t + 1u] = cbh[B & 0xFFFu];
+                }
+                // sidecar: the patches of this half-step replace their weights
+                // with the reference's fp32 value rounded once to bf16
+                const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
+#pragma unroll 1
+                for (uint32_t i = 0; i < n_cur; ++i) {
+                    const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
+                    pc0 = pc1; pc1 = pc2; pc2 = pc3;
+                    const uint32_t local = (q & 0xFFFFu) - k0;
+                    if (local < 64u) patch_pair(v, local, q >> 16);
+                }
+                pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
+                __syncwarp();
+                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
+                asm volatile("tcgen05.wait::st.sync.aligned;");
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                mbar_arrive(a_full + b);
+            }
         }
         if (ok && mbar_wait(d_full, 0u, abort_flag)) {
             asm volatile("tcgen05.fence::after_thread_sync;");
             const bool partial = p.splits > 1u;
             const float bo = (valid && p.bias && !partial) ? __ldg(p.bias + o) : 0.0f;
             float *yo = p.y + (partial ? (size_t)blockIdx.z * p.T * p.O : 0u);
+            const uint32_t ld = partial ? p.O : p.ldy;
             // this half's accumulator columns; a 32-column load may read past
             // them (inside the allocation) when BN < 64: those are not stored
             const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
@@ -370,7 +485,7 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
 #pragma unroll
                     for (uint32_t j = 0; j < 32u; ++j) {
                         const uint32_t n = n0 + c0 + j;
-                        if (c0 + j < cend && n < p.T) yo[(size_t)n * p.O + o] = __uint_as_float(v[j]) + bo;
+                        if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
                     }
                 }
             }
@@ -393,15 +508,16 @@ affine_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
 
 // y[n, o] = sum over the K ranges, in order, of the partial sums + bias.
 __global__ void splitk_reduce_kernel(const float *__restrict__ part, const float *__restrict__ bias,
-                                     float *__restrict__ y, uint32_t T, uint32_t O, uint32_t splits)
+                                     float *__restrict__ y, uint32_t T, uint32_t O, uint32_t ldy, uint32_t splits)
 {
     const uint64_t total = (uint64_t)T * O;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (uint64_t)gridDim.x * blockDim.x) {
         float acc = 0.0f;
         for (uint32_t k = 0; k < splits; ++k) acc += part[(size_t)k * total + i];
-        if (bias) acc += __ldg(bias + (uint32_t)(i % O));
-        y[i] = acc;
+        const uint32_t o = (uint32_t)(i % O);
+        if (bias) acc += __ldg(bias + o);
+        y[(i / O) * ldy + o] = acc;
     }
 }
 
@@ -427,7 +543,7 @@ EncodeTiledFn encode_fn()
     return fn;
 }
 
-template <uint32_t BN>
+template <uint32_t BN, bool VQ>
 int launch(const uint16_t *x, const Params &p, cudaStream_t s)
 {
     EncodeTiledFn enc = encode_fn();
@@ -442,11 +558,19 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
-    auto kern = affine_gemm_kernel<BN>;
-    const uint32_t smem = smem_bytes(BN);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-        cudaGetLastError();
-        return -1;
+    auto kern = dequant_gemm_kernel<BN, VQ>;
+    const uint32_t smem = smem_bytes(BN, VQ);
+    // the shared-memory opt-in is made once per device and instantiation
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
+    const uint64_t bit = 1ull << dev;
+    if (!(configured.load(std::memory_order_acquire) & bit)) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        configured.fetch_or(bit, std::memory_order_acq_rel);
     }
     dim3 grid((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
     kern<<<grid, kThreads, smem, s>>>(map, p);
@@ -477,6 +601,54 @@ float *splitk_buffer(size_t floats, cudaStream_t s)
 
 }  // namespace gemm
 
+namespace {
+
+// Token tile, K split and launch for one matmul; p.splits and p.y are set
+// here.  0 on launch, -1 on error.
+template <bool VQ>
+int run(const uint16_t *x, gemm::Params p, float *y, cudaStream_t s)
+{
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t T = p.T, O = p.O;
+    const uint32_t bn = T <= 16 ? 16u : T <= 32 ? 32u : T <= 64 ? 64u : T <= 128 ? 128u : 256u;
+    // Split K when the (rows x token) tiles alone would leave SMs idle.
+    const uint32_t tiles = ((O + gemm::kBM - 1) / gemm::kBM) * ((T + bn - 1) / bn);
+    const uint32_t KT = p.I / gemm::kBK;
+    const uint32_t resident = (uint32_t)sms * (bn <= 128 ? 2u : 1u);  // CTAs the GPU holds at once
+    uint32_t splits = 1;
+    if (tiles < resident) {
+        splits = resident / tiles;                 // one wave: tiles * splits <= resident
+        if (splits > KT / 2u) splits = KT / 2u;  // keep at least two K steps per CTA
+        if (splits > 16u) splits = 16u;
+        if (splits < 1u) splits = 1u;
+    }
+    float *part = nullptr;
+    if (splits > 1) {
+        part = gemm::splitk_buffer((size_t)splits * T * O, s);
+        if (!part) return -1;
+    }
+    p.splits = splits;
+    p.y = splits > 1 ? part : y;
+    int r;
+    switch (bn) {
+    case 16: r = gemm::launch<16, VQ>(x, p, s); break;
+    case 32: r = gemm::launch<32, VQ>(x, p, s); break;
+    case 64: r = gemm::launch<64, VQ>(x, p, s); break;
+    case 128: r = gemm::launch<128, VQ>(x, p, s); break;
+    default: r = gemm::launch<256, VQ>(x, p, s); break;
+    }
+    if (r != 0 || splits == 1) return r;
+    const uint64_t total = (uint64_t)T * O;
+    uint64_t blocks = (total + 255u) / 256u;
+    if (blocks > (uint64_t)sms * 8u) blocks = (uint64_t)sms * 8u;
+    gemm::splitk_reduce_kernel<<<(uint32_t)blocks, 256, 0, s>>>(part, p.bias, y, T, O, p.ldy, splits);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+
 // Tensor-core path for bf16 activations.  Returns 1 when the shape is not
 // one it takes (the caller uses the GEMV), 0 on launch, -1 on error.
 int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
@@ -487,41 +659,27 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
     if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return 1;
     if (((uintptr_t)x & 15u) || ((uintptr_t)codes & 15u)) return 1;
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
-    // Split K when the (rows x token) tiles alone would leave SMs idle.
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint32_t bn = T <= 16 ? 16u : T <= 32 ? 32u : T <= 64 ? 64u : T <= 128 ? 128u : 256u;
-    const uint32_t tiles = ((O + gemm::kBM - 1) / gemm::kBM) * ((T + bn - 1) / bn);
-    const uint32_t KT = I / gemm::kBK;
-    const uint32_t resident = (uint32_t)sms * (bn <= 128 ? 2u : 1u);  // CTAs the GPU holds at once
-    uint32_t splits = 1;
-    if (tiles < resident) {
-        splits = (resident + tiles - 1) / tiles;
-        if (splits > KT / 2u) splits = KT / 2u;  // keep at least two K steps per CTA
-        if (splits > 16u) splits = 16u;
-        if (splits < 1u) splits = 1u;
-    }
-    float *part = nullptr;
-    if (splits > 1) {
-        part = gemm::splitk_buffer((size_t)splits * T * O, s);
-        if (!part) return -1;
-    }
-    gemm::Params p{codes, scales, offsets, bias, splits > 1 ? part : y, T, I, O, gs, splits};
-    int r;
-    switch (bn) {
-    case 16: r = gemm::launch<16>(x, p, s); break;
-    case 32: r = gemm::launch<32>(x, p, s); break;
-    case 64: r = gemm::launch<64>(x, p, s); break;
-    case 128: r = gemm::launch<128>(x, p, s); break;
-    default: r = gemm::launch<256>(x, p, s); break;
-    }
-    if (r != 0 || splits == 1) return r;
-    const uint64_t total = (uint64_t)T * O;
-    uint64_t blocks = (total + 255u) / 256u;
-    if (blocks > (uint64_t)sms * 8u) blocks = (uint64_t)sms * 8u;
-    gemm::splitk_reduce_kernel<<<(uint32_t)blocks, 256, 0, s>>>(part, bias, y, T, O, splits);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    gemm::Params p{};
+    p.codes = codes; p.scales = scales; p.offsets = offsets; p.bias = bias;
+    p.T = T; p.I = I; p.O = O; p.gs = gs; p.ldy = O;
+    return run<false>(x, p, y, s);
+}
+
+// Fused VQ-dequant GEMM on a 12-bit image with its matmul tables: x bf16
+// [T, I], y fp32 [T, ldy].  Returns 1 when the shape is not one it takes, 0
+// on launch, -1 on error.
+int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
+                 const uint16_t *kp, const uint32_t *e4, float *y, uint32_t T, uint32_t I, uint32_t O,
+                 uint32_t ldy, cudaStream_t s)
+{
+    if (T == 0 || O == 0) return 1;
+    if (I == 0 || I % gemm::kBK != 0 || ldy < O) return 1;
+    if (((uintptr_t)x & 15u) || ((uintptr_t)idx & 15u) || ((uintptr_t)cbh & 15u)) return 1;
+    if ((uint64_t)T * I >= (1ull << 40)) return 1;
+    gemm::Params p{};
+    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4;
+    p.T = T; p.I = I; p.O = O; p.gs = 0; p.ldy = ldy;
+    return run<true>(x, p, y, s);
 }
 
 }  // namespace hxq

@@ -56,6 +56,15 @@ struct hxq_cuda_image {
     uint32_t  n_ent = 0;
     double    sumsq = 0.0;     // exact sum of squared in-range deltas
     float     ref_l2 = 0.0f;   // sqrtf of the fp32 running sum in array order
+    // fused-matmul extras (12-bit, k = 4096, in_features % 128 == 0): bf16
+    // codebook pairs; per row the first patch; per (row, 128-wide K step)
+    // the 16-bit offset of its first patch from the row's; patches
+    // col | bf16(final weight) << 16, one per distinct sidecar position
+    bool      has_mm = false;
+    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0;
+    uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr;
+    uint16_t *d_kp = nullptr;
+    uint32_t  n_patch = 0;
 };
 
 namespace {
@@ -282,10 +291,68 @@ void bind_image(hxq_cuda_image *img, void *base)
     img->d_offsets = img->has_aff ? reinterpret_cast<float *>(b + img->o_of) : nullptr;
     img->d_chunk_ptr = img->has_cp ? reinterpret_cast<uint32_t *>(b + img->o_cp) : nullptr;
     img->d_ent = reinterpret_cast<SideEntry *>(b + img->o_en);
+    if (img->has_mm) {
+        img->d_cbh = reinterpret_cast<uint32_t *>(b + img->o_cbh);
+        img->d_rb = reinterpret_cast<uint32_t *>(b + img->o_rb);
+        img->d_kp = reinterpret_cast<uint16_t *>(b + img->o_kp);
+        img->d_e4 = reinterpret_cast<uint32_t *>(b + img->o_e4);
+    }
+}
+
+uint16_t bf16_rne(float f)
+{
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// Fused-matmul patch tables of a 12-bit image (see hxq_cuda_image).  Each
+// distinct sidecar position gets the weight the reference decoder produces
+// there -- codebook value, then the deltas added in array order in fp32
+// (src/hxq.c:343-346) -- rounded once to bf16.  False if a row has more
+// than 65535 patches (16-bit offsets); the image then has no tables.
+bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows, uint32_t in_f,
+                   const std::vector<HostEntry> &ents, std::vector<uint32_t> &cbh,
+                   std::vector<uint32_t> &rb, std::vector<uint16_t> &kp, std::vector<uint32_t> &e4)
+{
+    const uint32_t KT = in_f / 128u;
+    const size_t row_bytes = (size_t)(in_f / 4u) * 3u;
+    cbh.resize(4096);
+    for (uint32_t j = 0; j < 4096u; ++j)
+        cbh[j] = (uint32_t)bf16_rne(t->codebook[2u * j]) | ((uint32_t)bf16_rne(t->codebook[2u * j + 1u]) << 16);
+    std::vector<uint32_t> erow;
+    e4.clear();
+    for (size_t i = 0; i < ents.size();) {
+        const uint64_t pos = ents[i].pos;
+        const uint32_t r = (uint32_t)(pos / in_f), c = (uint32_t)(pos % in_f);
+        const uint8_t *b = idx_rows + (size_t)r * row_bytes + (size_t)(c / 4u) * 3u;
+        const uint32_t id = ((c / 2u) & 1u) ? (((uint32_t)(b[1] & 15u) << 8) | b[2])
+                                            : (((uint32_t)b[0] << 4) | (b[1] >> 4));
+        volatile float w = t->codebook[2u * id + (c & 1u)];
+        for (; i < ents.size() && ents[i].pos == pos; ++i) w = w + ents[i].val;
+        e4.push_back(c | ((uint32_t)bf16_rne(w) << 16));
+        erow.push_back(r);
+    }
+    rb.assign(rows, 0u);
+    kp.assign((size_t)rows * (KT + 1u), 0u);
+    size_t e = 0;
+    for (uint32_t r = 0; r < rows; ++r) {
+        while (e < e4.size() && erow[e] < r) ++e;
+        rb[r] = (uint32_t)e;
+        size_t f = e;
+        for (uint32_t kt = 0; kt <= KT; ++kt) {
+            while (f < e4.size() && erow[f] == r && (e4[f] & 0xFFFFu) < kt * 128u) ++f;
+            if (kt == KT)
+                while (f < e4.size() && erow[f] == r) ++f;
+            if (f - e > 0xFFFFu) return false;
+            kp[(size_t)r * (KT + 1u) + kt] = (uint16_t)(f - e);
+        }
+    }
+    return true;
 }
 
 hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev,
-                        bool streamed, hxq_cuda_image **out)
+                        bool streamed, bool matmul, hxq_cuda_image **out)
 {
     if (!t || !out) return HXQ_ERR_NULL_PTR;
     if (!t->indices_raw) return HXQ_ERR_NULL_PTR;
@@ -385,6 +452,14 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
     img->n_ent = (uint32_t)dev_ents.size();
 
+    std::vector<uint32_t> mm_cbh, mm_rb, mm_e4;
+    std::vector<uint16_t> mm_kp;
+    if (matmul && img->kind == kKindVq12 && !img->check_k && img->k == 4096u && img->in_f % 128u == 0u &&
+        img->in_f <= 65536u)
+        img->has_mm = build_patches(t, t->indices_raw + idx_off, img->rows, img->in_f, ents, mm_cbh, mm_rb,
+                                    mm_kp, mm_e4);
+    img->n_patch = (uint32_t)mm_e4.size();
+
     // one block: idx | cb | scales | offsets | chunk_ptr | entries
     const size_t chunk_bytes = img->kind == kKindVq12 ? kChunkBytes12 : kChunkBytes8;
     const size_t idx_alloc = fast ? (size_t)img->n_chunks * chunk_bytes + kIdxPad
@@ -399,6 +474,12 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     img->o_of = off;   off = align256(off + aff_floats * 4);
     img->o_cp = off;   off = align256(off + chunk_ptr.size() * 4);
     img->o_en = off;   off = align256(off + std::max<size_t>(dev_ents.size(), 1) * sizeof(SideEntry));
+    if (img->has_mm) {
+        img->o_cbh = off;  off = align256(off + mm_cbh.size() * 4);
+        img->o_rb = off;   off = align256(off + std::max<size_t>(mm_rb.size(), 1) * 4);
+        img->o_kp = off;   off = align256(off + mm_kp.size() * 2);
+        img->o_e4 = off;   off = align256(off + (mm_e4.size() + 4) * 4);   // + speculative-read slack
+    }
     img->block_bytes = off;
     img->has_cb = cb_floats > 0;
     img->has_aff = aff_floats > 0;
@@ -422,6 +503,12 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
     if (!chunk_ptr.empty()) std::memcpy(hb + img->o_cp, chunk_ptr.data(), chunk_ptr.size() * 4);
     if (!dev_ents.empty()) std::memcpy(hb + img->o_en, dev_ents.data(), dev_ents.size() * sizeof(SideEntry));
+    if (img->has_mm) {
+        std::memcpy(hb + img->o_cbh, mm_cbh.data(), mm_cbh.size() * 4);
+        if (!mm_rb.empty()) std::memcpy(hb + img->o_rb, mm_rb.data(), mm_rb.size() * 4);
+        std::memcpy(hb + img->o_kp, mm_kp.data(), mm_kp.size() * 2);
+        if (!mm_e4.empty()) std::memcpy(hb + img->o_e4, mm_e4.data(), mm_e4.size() * 4);
+    }
 
     if (streamed) {
         img->h_block = hb;
@@ -619,7 +706,7 @@ hxq_error_t tensor_image(const hxq_tensor_t *t, int dev, hxq_cuda_image **out)
     }
     destroy_image(stale);
     hxq_cuda_image *img = nullptr;
-    hxq_error_t err = build_image(t, 0, t->out_features, dev, false, &img);
+    hxq_error_t err = build_image(t, 0, t->out_features, dev, false, false, &img);
     if (err != HXQ_OK) return err;
     std::lock_guard<std::mutex> lk(g_mu);
     g_images[t] = Cached{now, img};
@@ -882,10 +969,11 @@ hxq_error_t hxq_dequant_bf16(hxq_tensor_t *t, hxq_shared_buffer_t *arena, hxq_re
 
 void hxq_cuda_tensor_invalidate(const hxq_tensor_t *t) { hxqi_cuda_forget_tensor(t); }
 
-hxq_error_t hxq_cuda_image_create(const hxq_tensor_t *t, uint32_t row_begin,
-                                  uint32_t row_end, hxq_cuda_image_t **img)
+hxq_error_t hxq_cuda_image_create_ex(const hxq_tensor_t *t, uint32_t row_begin, uint32_t row_end,
+                                     uint32_t flags, hxq_cuda_image_t **img)
 {
     if (!t || !img) return HXQ_ERR_NULL_PTR;
+    if (flags & ~(uint32_t)(HXQ_IMAGE_STREAMED | HXQ_IMAGE_MATMUL)) return HXQ_ERR_INVALID_ARG;
     int dev = 0;
     hxq_error_t err = current_device(&dev);
     if (err != HXQ_OK) return err;
@@ -893,22 +981,23 @@ hxq_error_t hxq_cuda_image_create(const hxq_tensor_t *t, uint32_t row_begin,
         std::lock_guard<std::mutex> lk(g_mu);
         if ((err = dev_ready(dev)) != HXQ_OK) return err;
     }
-    return build_image(t, row_begin, row_end, dev, false, img);
+    return build_image(t, row_begin, row_end, dev, (flags & HXQ_IMAGE_STREAMED) != 0,
+                       (flags & HXQ_IMAGE_MATMUL) != 0, img);
+}
+
+hxq_error_t hxq_cuda_image_create(const hxq_tensor_t *t, uint32_t row_begin,
+                                  uint32_t row_end, hxq_cuda_image_t **img)
+{
+    return hxq_cuda_image_create_ex(t, row_begin, row_end, 0u, img);
 }
 
 hxq_error_t hxq_cuda_image_create_streamed(const hxq_tensor_t *t, uint32_t row_begin,
                                            uint32_t row_end, hxq_cuda_image_t **img)
 {
-    if (!t || !img) return HXQ_ERR_NULL_PTR;
-    int dev = 0;
-    hxq_error_t err = current_device(&dev);
-    if (err != HXQ_OK) return err;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if ((err = dev_ready(dev)) != HXQ_OK) return err;
-    }
-    return build_image(t, row_begin, row_end, dev, true, img);
+    return hxq_cuda_image_create_ex(t, row_begin, row_end, HXQ_IMAGE_STREAMED, img);
 }
+
+int hxq_cuda_image_has_matmul_tables(const hxq_cuda_image_t *img) { return img && img->has_mm ? 1 : 0; }
 
 size_t hxq_cuda_image_block_bytes(const hxq_cuda_image_t *img) { return img ? img->block_bytes : 0; }
 
@@ -951,6 +1040,46 @@ hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n
     if (err != HXQ_OK) return err;
     return launch_images(imgs, n, d_out, out_offsets, dtype == HXQ_OUT_BF16, d_sumsq, d_conf,
                          dev, static_cast<cudaStream_t>(stream));
+}
+
+hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream)
+{
+    if (!img || !d_x_bf16 || !d_y) return HXQ_ERR_NULL_PTR;
+    if (img->kind != kKindVq12 || img->check_k || img->k != 4096u || img->in_f % 64u != 0u)
+        return HXQ_ERR_INVALID_ARG;
+    if (gemm && !img->has_mm) return HXQ_ERR_INVALID_ARG;
+    if (!img->d_block) return HXQ_ERR_INVALID_ARG;   // streamed image never uploaded
+    if (ldy < img->rows || !aligned16(d_x_bf16)) return HXQ_ERR_INVALID_ARG;
+    if (N == 0 || img->rows == 0) return HXQ_OK;
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    if (img->device != dev) return HXQ_ERR_INVALID_ARG;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (gemm) {
+        const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
+                                        d_y, N, img->in_f, img->rows, ldy, s);
+        if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
+    } else {
+        const cudaError_t e = hxq::launch_vq_gemv(img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent,
+                                                  img->n_chunks, img->rows, img->in_f, d_x_bf16, N, d_y, ldy,
+                                                  g_dev[dev].sms, s);
+        if (e != cudaSuccess) return map_cuda(e);
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return HXQ_OK;
+}
+
+hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                               uint32_t N, float *d_y, uint32_t ldy, void *stream)
+{
+    const bool gemm = img && N > HXQ_VQ_MATMUL_GEMV_MAX && img->has_mm;
+    return hxq_cuda_vq_matmul_path(img, d_x_bf16, N, d_y, ldy, gemm ? 1 : 0, stream);
 }
 
 hxq_error_t hxq_cuda_stream_synchronize(void *stream)

@@ -1,0 +1,275 @@
+// vq_matmul.cu -- fused VQ-dequant matmul for a few tokens (sm_100a).
+//
+//   y[n, o] = sum_k x[n, k] * W[o, k],  W = the image's decompressed weights
+// (codebook[index] + in-range sidecar deltas, the reference's src/hxq.c:
+// 239-350 decode), with W never written to memory.
+//
+// One warp per output row, rows handed out grid-stride.  The CTA stages the
+// fp32 codebook (32 KB) and the pass's activations (bf16) in shared memory
+// once.  A row's packed 12-bit indices arrive in pieces of 2048 weights
+// (1536 bytes) through a two-deep per-warp cp.async ring (coalesced 16-byte
+// copies, L1 bypassed); each lane takes 4 consecutive byte triples per step
+// (3 bank-conflict-free word reads, one PRMT per triple), gathers the 8 fp32
+// pairs from the codebook and meets the activations in fp32 FMAs.  The row's
+// sidecar entries are a sparse epilogue, y += delta * x[col]: their chunk
+// range is read when the row starts and each lane's first two entries when
+// its last piece starts, so the dependent loads overlap the streaming.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hxq_cuda_internal.h"
+
+namespace hxq {
+namespace {
+
+constexpr uint32_t kGvWarps = 8;
+constexpr uint32_t kGvThreads = kGvWarps * 32;
+constexpr uint32_t kGvStages = 2;
+constexpr uint32_t kPieceTrip = 512;                   // byte triples per piece
+constexpr uint32_t kPieceVec = kPieceTrip * 3u / 16u;  // 96 16-byte copies
+constexpr uint32_t kGvCbBytes = 4096u * 8u;
+constexpr uint32_t kGvRingBytes = kGvWarps * kGvStages * kPieceVec * 16u;
+constexpr uint32_t kGvXsBytesMax = 48u * 1024u;        // staged activations per pass
+
+struct GemvArgs {
+    const uint8_t *idx;          // packed rows, row_bytes apart, 16-B aligned
+    const float *cb;             // fp32 codebook, 4096 pairs
+    const uint32_t *chunk_ptr;   // first sidecar entry of each 2048-weight chunk
+    const SideEntry *ent;        // sidecar entries, sorted by position
+    const uint16_t *x;           // bf16 [ntok, in_f]
+    float *y;                    // [ntok, ldy]
+    uint32_t rows, in_f, ntok, ldy, n_chunks;
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// XS: activations staged in shared memory (else read through L1).
+template <int NT, bool XS>
+__global__ void __launch_bounds__(kGvThreads, 3)
+vq_gemv_kernel(const __grid_constant__ GemvArgs a)
+{
+    extern __shared__ __align__(16) unsigned char smem[];
+    float2 *cb = reinterpret_cast<float2 *>(smem);
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    uint4 *ring = reinterpret_cast<uint4 *>(smem + kGvCbBytes) + warp * kGvStages * kPieceVec;
+    const uint16_t *xs = XS ? reinterpret_cast<const uint16_t *>(smem + kGvCbBytes + kGvRingBytes) : a.x;
+
+    const uint32_t row_trip = a.in_f / 4u;             // in_f % 64 == 0: whole 16-B copies
+    const size_t row_bytes = (size_t)row_trip * 3u;
+    const uint32_t P = (row_trip + kPieceTrip - 1u) / kPieceTrip;
+    const uint32_t stride = gridDim.x * kGvWarps;
+    const uint32_t first = blockIdx.x * kGvWarps + warp;
+    const uint32_t my_rows = first < a.rows ? (a.rows - first + stride - 1u) / stride : 0u;
+    const uint32_t total = my_rows * P;
+
+    auto issue = [&](uint32_t s) {
+        if (s < total) {
+            const uint32_t o = first + (s / P) * stride, p0 = (s % P) * kPieceTrip;
+            const uint32_t nvec = min(kPieceTrip, row_trip - p0) * 3u / 16u;
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.idx + (size_t)o * row_bytes + (size_t)p0 * 3u);
+            uint4 *dst = ring + (s % kGvStages) * kPieceVec;
+#pragma unroll
+            for (uint32_t q = 0; q < 3u; ++q) {
+                const uint32_t v = q * 32u + lane;
+                if (v < nvec) cp_async16(dst + v, src + v);
+            }
+        }
+        cp_commit();
+    };
+    // the first piece is in flight while the codebook and activations are staged
+    issue(0);
+    for (uint32_t i = tid; i < kGvCbBytes / 16u; i += kGvThreads)
+        reinterpret_cast<uint4 *>(smem)[i] = __ldg(reinterpret_cast<const uint4 *>(a.cb) + i);
+    if constexpr (XS) {
+        const uint32_t nv = a.ntok * a.in_f / 8u;
+        uint4 *xd = reinterpret_cast<uint4 *>(smem + kGvCbBytes + kGvRingBytes);
+        for (uint32_t i = tid; i < nv; i += kGvThreads) xd[i] = __ldg(reinterpret_cast<const uint4 *>(a.x) + i);
+    }
+    __syncthreads();
+
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    // sidecar of the current row: chunks [ch0, ch0 + nc) hold its entries,
+    // lane i keeps chunk_ptr[ch0 + i] (i <= nc), the entry range is
+    // [e_lo, e_hi), and each lane prefetches the range's entries lane and
+    // lane + 32
+    uint32_t cpv = 0, nc = 0, e_lo = 0, e_hi = 0;
+    uint2 en0 = make_uint2(0u, 0u), en1 = make_uint2(0u, 0u);
+    for (uint32_t s = 0; s < total; ++s) {
+        issue(s + 1u);
+        const uint32_t o = first + (s / P) * stride, pc = s % P, p0 = pc * kPieceTrip;
+        const uint64_t f0 = (uint64_t)o * a.in_f;
+        const uint32_t ch0 = (uint32_t)(f0 / kChunkW);
+        if (pc == 0) {
+            uint32_t ch1 = (uint32_t)((f0 + a.in_f - 1u) / kChunkW) + 1u;
+            ch1 = ch1 < a.n_chunks ? ch1 : a.n_chunks;
+            nc = ch1 - ch0;
+            cpv = lane <= nc ? __ldg(a.chunk_ptr + ch0 + lane) : 0u;
+        }
+        if (pc + 1u == P) {
+            e_lo = __shfl_sync(0xffffffffu, cpv, 0);
+            e_hi = nc < 32u ? __shfl_sync(0xffffffffu, cpv, nc) : __ldg(a.chunk_ptr + ch0 + nc);
+            en0 = e_lo + lane < e_hi ? __ldg(reinterpret_cast<const uint2 *>(a.ent + e_lo + lane)) : make_uint2(0u, 0u);
+            en1 = e_lo + 32u + lane < e_hi ? __ldg(reinterpret_cast<const uint2 *>(a.ent + e_lo + 32u + lane))
+                                           : make_uint2(0u, 0u);
+        }
+        cp_wait<kGvStages - 1>();
+        __syncwarp();
+        const uint32_t ngrp = min(kPieceTrip, row_trip - p0) / 4u;
+        const uint32_t *sw = reinterpret_cast<const uint32_t *>(ring + (s % kGvStages) * kPieceVec);
+#pragma unroll
+        for (uint32_t m = 0; m < kPieceTrip / 128u; ++m) {
+            const uint32_t g = m * 32u + lane;
+            if (g < ngrp) {
+                const uint32_t w0 = sw[3u * g], w1 = sw[3u * g + 1u], w2 = sw[3u * g + 2u];
+                const uint32_t B0 = __byte_perm(w0, w1, 0x3012u), B1 = __byte_perm(w0, w1, 0x6345u);
+                const uint32_t B2 = __byte_perm(w1, w2, 0x5234u), B3 = __byte_perm(w2, w2, 0x4123u);
+                const float2 c0 = cb[(B0 >> 12) & 0xFFFu], c1 = cb[B0 & 0xFFFu];
+                const float2 c2 = cb[(B1 >> 12) & 0xFFFu], c3 = cb[B1 & 0xFFFu];
+                const float2 c4 = cb[(B2 >> 12) & 0xFFFu], c5 = cb[B2 & 0xFFFu];
+                const float2 c6 = cb[(B3 >> 12) & 0xFFFu], c7 = cb[B3 & 0xFFFu];
+                const size_t col = (size_t)p0 * 4u + 16u * g;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    if ((uint32_t)t < a.ntok) {
+                        const uint4 *xp = reinterpret_cast<const uint4 *>(xs + (size_t)t * a.in_f + col);
+                        const uint4 xa = XS ? xp[0] : __ldg(xp), xb = XS ? xp[1] : __ldg(xp + 1);
+                        float r = acc[t];
+                        r = fmaf(c0.x, lo_bf16(xa.x), r); r = fmaf(c0.y, hi_bf16(xa.x), r);
+                        r = fmaf(c1.x, lo_bf16(xa.y), r); r = fmaf(c1.y, hi_bf16(xa.y), r);
+                        r = fmaf(c2.x, lo_bf16(xa.z), r); r = fmaf(c2.y, hi_bf16(xa.z), r);
+                        r = fmaf(c3.x, lo_bf16(xa.w), r); r = fmaf(c3.y, hi_bf16(xa.w), r);
+                        r = fmaf(c4.x, lo_bf16(xb.x), r); r = fmaf(c4.y, hi_bf16(xb.x), r);
+                        r = fmaf(c5.x, lo_bf16(xb.y), r); r = fmaf(c5.y, hi_bf16(xb.y), r);
+                        r = fmaf(c6.x, lo_bf16(xb.z), r); r = fmaf(c6.y, hi_bf16(xb.z), r);
+                        r = fmaf(c7.x, lo_bf16(xb.w), r); r = fmaf(c7.y, hi_bf16(xb.w), r);
+                        acc[t] = r;
+                    }
+                }
+            }
+        }
+        if (pc + 1u == P) {
+            // sparse epilogue: the row's sidecar deltas times the activations
+            const uint32_t rounds = (e_hi - e_lo + 31u) / 32u;
+            for (uint32_t k = 0; k < rounds; ++k) {
+                const uint32_t e = e_lo + 32u * k + lane;
+                const uint2 en = k == 0 ? en0 : k == 1 ? en1
+                                 : (e < e_hi ? __ldg(reinterpret_cast<const uint2 *>(a.ent + e)) : make_uint2(0u, 0u));
+                // the entry's chunk: ch0 + the number of later chunk starts <= e
+                uint32_t c = ch0;
+                if (nc < 32u) {
+                    for (uint32_t i = 1; i < nc; ++i) c += __shfl_sync(0xffffffffu, cpv, i) <= e ? 1u : 0u;
+                } else {
+                    while (c + 1u < a.n_chunks && __ldg(a.chunk_ptr + c + 1u) <= e) ++c;
+                }
+                if (e >= e_hi) continue;
+                const uint64_t pos = (uint64_t)c * kChunkW + (en.x & 0xFFFFu);
+                if (pos < f0 || pos >= f0 + a.in_f) continue;
+                const size_t col = (size_t)(pos - f0);
+                const float v = __uint_as_float(en.y);
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    if ((uint32_t)t < a.ntok)
+                        acc[t] = fmaf(v, lo_bf16(XS ? xs[(size_t)t * a.in_f + col] : __ldg(xs + (size_t)t * a.in_f + col)),
+                                      acc[t]);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float v = acc[t];
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+                if (lane == 0 && (uint32_t)t < a.ntok) a.y[(size_t)t * a.ldy + o] = v;
+                acc[t] = 0.0f;
+            }
+        }
+        __syncwarp();   // the slot just read is the next issue's target
+    }
+    cp_wait<0>();
+}
+
+template <int NT, bool XS>
+cudaError_t configure_one(size_t smem)
+{
+    return cudaFuncSetAttribute(vq_gemv_kernel<NT, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+}  // namespace
+
+// Fused VQ GEMV: 12-bit images with k = 4096 and in_f % 64 == 0, 16-byte
+// aligned x and index rows; up to 8 tokens per pass, fewer when their
+// activations would not fit the staging budget.
+cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
+                           uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
+                           float *y, uint32_t ldy, int sms, cudaStream_t s)
+{
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const size_t base = kGvCbBytes + kGvRingBytes;
+    if (!configured[dev]) {
+        const size_t mx = base + kGvXsBytesMax;
+        e = configure_one<1, true>(mx);
+        if (e == cudaSuccess) e = configure_one<2, true>(mx);
+        if (e == cudaSuccess) e = configure_one<4, true>(mx);
+        if (e == cudaSuccess) e = configure_one<8, true>(mx);
+        if (e == cudaSuccess) e = configure_one<1, false>(base);
+        if (e == cudaSuccess) e = configure_one<2, false>(base);
+        if (e == cudaSuccess) e = configure_one<4, false>(base);
+        if (e == cudaSuccess) e = configure_one<8, false>(base);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    if (rows == 0 || ntok == 0) return cudaSuccess;
+    const size_t row_x = (size_t)in_f * 2u;
+    const uint32_t fit = (uint32_t)(kGvXsBytesMax / row_x);      // tokens whose activations fit
+    const bool xs = fit >= 1u;
+    const uint32_t per_pass = xs ? (fit < 8u ? fit : 8u) : 8u;
+    for (uint32_t n0 = 0; n0 < ntok; n0 += per_pass) {
+        const uint32_t nt = ntok - n0 < per_pass ? ntok - n0 : per_pass;
+        GemvArgs a;
+        a.idx = idx; a.cb = cb; a.chunk_ptr = chunk_ptr; a.ent = ent;
+        a.x = x + (size_t)n0 * in_f;
+        a.y = y + (size_t)n0 * ldy;
+        a.rows = rows; a.in_f = in_f; a.ntok = nt; a.ldy = ldy; a.n_chunks = n_chunks;
+        const size_t smem = base + (xs ? (size_t)nt * row_x : 0u);
+        // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA), at most 3
+        uint32_t per_sm = (uint32_t)(233472u / (smem + 1024u));
+        per_sm = per_sm > 3u ? 3u : per_sm < 1u ? 1u : per_sm;
+        uint32_t blocks = (rows + kGvWarps - 1u) / kGvWarps;
+        const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
+        if (blocks > cap) blocks = cap;
+#define HXQ_GEMV_LAUNCH(NTV)                                                                     \
+        if (xs) vq_gemv_kernel<NTV, true><<<blocks, kGvThreads, smem, s>>>(a);                  \
+        else vq_gemv_kernel<NTV, false><<<blocks, kGvThreads, smem, s>>>(a);
+        if (nt == 1) { HXQ_GEMV_LAUNCH(1) }
+        else if (nt == 2) { HXQ_GEMV_LAUNCH(2) }
+        else if (nt <= 4) { HXQ_GEMV_LAUNCH(4) }
+        else { HXQ_GEMV_LAUNCH(8) }
+#undef HXQ_GEMV_LAUNCH
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace hxq

@@ -36,6 +36,7 @@ HXQ_ERR_NCCL = 35
 HXQ_SCALAR_VQ, HXQ_VQ2D_8BIT, HXQ_VQ2D_12BIT, HXQ_AFFINE_G128 = 0, 1, 2, 3
 HXQ_BACKEND_AUTO, HXQ_BACKEND_CPU, HXQ_BACKEND_CUDA, HXQ_BACKEND_METAL, HXQ_BACKEND_VULKAN = range(5)
 HXQ_OUT_F32, HXQ_OUT_BF16 = 0, 1
+HXQ_IMAGE_STREAMED, HXQ_IMAGE_MATMUL = 1, 2
 MAX_BATCH = 64
 
 P = C.c_void_p
@@ -129,6 +130,10 @@ SIGNATURES = {
     "hxq_affine_group_matmul_bf16": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
     "hxq_affine_group_matmul_async": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
     "hxq_cuda_affine_device_status": (C.c_int, []),
+    "hxq_cuda_vq_matmul": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, P]),
+    "hxq_cuda_image_create_ex": (C.c_int, [TP, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(P)]),
+    "hxq_cuda_image_has_matmul_tables": (C.c_int, [P]),
+    "hxq_cuda_vq_matmul_path": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, C.c_int, P]),
 }
 
 

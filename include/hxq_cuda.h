@@ -111,6 +111,19 @@ hxq_error_t hxq_cuda_image_create_streamed(const hxq_tensor_t *t, uint32_t row_b
 size_t      hxq_cuda_image_block_bytes(const hxq_cuda_image_t *img);
 hxq_error_t hxq_cuda_image_upload(hxq_cuda_image_t *img, void *d_dst, void *stream);
 
+/* Image with options: HXQ_IMAGE_STREAMED (as hxq_cuda_image_create_streamed)
+ * and HXQ_IMAGE_MATMUL, which adds the tables the tensor-core path of
+ * hxq_cuda_vq_matmul reads (a bf16 codebook copy and per-row sidecar
+ * patches, about 5% of the index bytes) to 12-bit images with k = 4096 and
+ * in_features % 128 == 0; other images are built without them. */
+#define HXQ_IMAGE_STREAMED 1u
+#define HXQ_IMAGE_MATMUL   2u
+hxq_error_t hxq_cuda_image_create_ex(const hxq_tensor_t *t, uint32_t row_begin,
+                                     uint32_t row_end, uint32_t flags,
+                                     hxq_cuda_image_t **img);
+/* 1 if the image carries the fused-matmul tables. */
+int         hxq_cuda_image_has_matmul_tables(const hxq_cuda_image_t *img);
+
 /* Kernels this library has launched in this process (all devices). */
 unsigned long long hxq_cuda_launch_count(void);
 
@@ -190,6 +203,30 @@ int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16,
  * one ran out of time (the kernel then unwinds without writing results);
  * -1 on a CUDA error. */
 int hxq_cuda_affine_device_status(void);
+
+/* -- Fused VQ-dequant matmul -------------------------------------------
+ * No counterpart function in the reference library (its fused matmul is
+ * affine only); the result is that of decompressing the image with
+ * hxq_tensor_decompress and multiplying:
+ *     d_y[n * ldy + o] = sum_i x[n, i] * W[o, i],  n < N, o < image rows,
+ * W = codebook[index] + in-range sidecar deltas.  W is never written to
+ * memory.  Images: 12-bit 2D-VQ with k = 4096 and in_features % 64 == 0
+ * (HXQ_ERR_INVALID_ARG otherwise), resident or uploaded.  d_x: bf16 bit
+ * patterns [N, in_features], 16-byte aligned; d_y: fp32, ldy >= rows.
+ *   - Up to HXQ_VQ_MATMUL_GEMV_MAX tokens, or for images without the
+ *     matmul tables (HXQ_IMAGE_MATMUL): the fused GEMV, with exact fp32
+ *     weights and fp32 accumulation.
+ *   - More tokens on images with the tables: the tcgen05 dequant-GEMM,
+ *     which rounds each weight to bf16 (|error| <= 2^-9 sum_i |x_i w_i| per
+ *     output, fp32 accumulation).
+ * Stream-ordered on `stream` (0: the legacy default stream); no sync. */
+#define HXQ_VQ_MATMUL_GEMV_MAX 4
+hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                               uint32_t N, float *d_y, uint32_t ldy, void *stream);
+/* The same with the path chosen by the caller: gemm = 0 GEMV, 1 GEMM
+ * (HXQ_ERR_INVALID_ARG if the image has no matmul tables). */
+hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream);
 
 /* fp32 activations on a caller stream. */
 int hxq_affine_group_matmul_async(const float *d_x,

@@ -145,4 +145,5 @@ def test_cuda_entry_points_without_gpu(H, L):
     img = C.c_void_p()
     assert L.hxq_cuda_image_create(t.ref, 0, 2, C.byref(img)) == H.HXQ_ERR_BACKEND_UNAVAILABLE
     assert L.hxq_affine_matmul_flat(None, None, None, None, None, None, 1, 128, 1, 128) == -1
+    assert L.hxq_cuda_vq_matmul(None, None, 1, None, 1, None) == H.HXQ_ERR_NULL_PTR
     L.hxq_shared_buffer_free(C.byref(buf))

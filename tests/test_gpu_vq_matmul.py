@@ -1,0 +1,248 @@
+"""Fused VQ-dequant matmul on the GPU against the oracle.
+
+The reference library has no fused VQ matmul; its result is defined as the
+reference decompress (hxq.c, restated bit-exactly by the oracle) followed by
+the naive ordered fp32 matmul of test/test_affine.c:51-65 (oracle
+dense_matmul).  Errors are normalised per output by sum_i |x_i * w_i|, the
+natural scale of an fp32 dot product's rounding error:
+  * GEMV (few tokens): exact fp32 weights, tolerance 1e-5 (fp32 paths);
+  * tcgen05 GEMM: weights rounded to bf16, tolerance 2^-9 + 1e-5 (inside
+    the 1e-2 allowed for bf16 paths), and 1e-4 against a float64 product
+    with the kernel's own weights bf16(W) -- which pins the layout.
+All calls go through the C ABI of libhxq.so.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from hxq_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+GEMM_TOL = 2.0 ** -9 + 1e-5
+
+
+def _scale(x, W):
+    return np.abs(x.astype(np.float64)) @ np.abs(W.astype(np.float64)).T
+
+
+def _check(y, y_ref, scale, tol):
+    err = np.abs(y.astype(np.float64) - y_ref.astype(np.float64)) / np.maximum(scale, 1e-30)
+    assert float(err.max()) <= tol, float(err.max())
+
+
+def _image(H, L, t, r0, r1, matmul=True):
+    img = C.c_void_p()
+    flags = H.HXQ_IMAGE_MATMUL if matmul else 0
+    assert L.hxq_cuda_image_create_ex(t.ref, r0, r1, flags, C.byref(img)) == 0
+    return img
+
+
+def _run(torch, L, img, xh, rows, path=None, ldy=None, col0=0):
+    N = xh.shape[0]
+    ldy = rows if ldy is None else ldy
+    xd = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+    y = torch.full((N, ldy), float("nan"), dtype=torch.float32, device="cuda")
+    yp = y.data_ptr() + 4 * col0
+    torch.cuda.synchronize()
+    if path is None:
+        assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), N, yp, ldy, None) == 0
+    else:
+        assert L.hxq_cuda_vq_matmul_path(img, xd.data_ptr(), N, yp, ldy, path, None) == 0
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def _with_dups_and_oob(d, seed):
+    """Append repeated coordinates (summed in array order) and entries the
+    reference skips (row >= out_f or col >= in_f)."""
+    rng = np.random.default_rng(seed)
+    n = len(d["rows"])
+    pick = rng.integers(0, n, size=min(n, 8))
+    rows = np.concatenate([d["rows"], d["rows"][pick], np.array([d["out_f"], 0], np.uint32)])
+    cols = np.concatenate([d["cols"], d["cols"][pick], np.array([0, d["in_f"]], np.uint32)])
+    vals = np.concatenate([d["vals"], (rng.standard_normal(len(pick)) * 0.01).astype(np.float32),
+                           np.array([5.0, 5.0], np.float32)])
+    d = dict(d)
+    d["rows"], d["cols"], d["vals"] = rows.astype(np.uint32), cols.astype(np.uint32), vals.astype(np.float32)
+    return d
+
+
+def _case(oracle, out_f, in_f, N, seed, frac=0.005, dups=False):
+    d = synth.vq12(out_f, in_f, seed, frac=frac)
+    if dups:
+        d = _with_dups_and_oob(d, seed)
+    err, w, _ = oracle.decompress(d)
+    assert err == 0
+    W = w.reshape(out_f, in_f)
+    xh, x = synth.activations(N, in_f, seed + 1)
+    return d, W, xh, x
+
+
+@pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 1), (256, 512, 2), (300, 1024, 3), (37, 64, 4),
+                                          (100, 192, 16), (4096, 4096, 1), (11008, 4096, 1), (4096, 11008, 2),
+                                          (513, 2048, 8), (64, 4096, 5)])
+def test_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
+    d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 3 + in_f + N, dups=True)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, out_f)
+    try:
+        y = _run(cuda, L, img, xh, out_f, path=0)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    _check(y, oracle.dense_matmul(x, W), _scale(x, W), TOL)
+
+
+@pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 5), (129, 128, 16), (300, 1024, 33), (4096, 4096, 16),
+                                          (1024, 2048, 100), (256, 384, 257), (11008, 4096, 16),
+                                          (4096, 11008, 16), (200, 256, 2)])
+def test_gemm_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
+    d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 7 + in_f + N, dups=True)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, out_f)
+    try:
+        y = _run(cuda, L, img, xh, out_f, path=1)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    assert L.hxq_cuda_affine_device_status() == 0
+    sc = _scale(x, W)
+    _check(y, oracle.dense_matmul(x, W), sc, GEMM_TOL)
+    # the kernel's own weights: one rounding of the fp32 (sidecar-corrected) weight
+    Wb = synth.bf16_to_f32(synth.bf16_round(W)).reshape(out_f, in_f)
+    _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
+
+
+def test_c5_prefill_2048_sampled(H, L, oracle, cuda):
+    """The prefill batch of the fused-matmul sweep on a 4096 x 4096 layer
+    matrix; outputs checked for a seeded sample of tokens."""
+    d, W, xh, x = _case(oracle, 4096, 4096, 2048, synth.SEED_C5)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, 4096)
+    try:
+        y = _run(cuda, L, img, xh, 4096)          # default path: GEMM
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    assert L.hxq_cuda_affine_device_status() == 0
+    for n in sorted({0, 1, 777, 1024, 2046, 2047}):
+        ref = oracle.dense_matmul(x, W, n0=n, n1=n + 1)
+        _check(y[n:n + 1], ref, _scale(x[n:n + 1], W), GEMM_TOL)
+
+
+def test_default_path_choice(H, L, oracle, cuda):
+    """Few tokens take the exact GEMV: bit-identical to the explicit path."""
+    d, W, xh, x = _case(oracle, 512, 1024, 4, 99)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, 512)
+    try:
+        y_default = _run(cuda, L, img, xh, 512)
+        y_gemv = _run(cuda, L, img, xh, 512, path=0)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    assert np.array_equal(y_default.view(np.uint32), y_gemv.view(np.uint32))
+
+
+@pytest.mark.parametrize("path", [0, 1])
+def test_row_shards_into_column_slices(H, L, oracle, cuda, path):
+    """An image of rows [r0, r1) writes output columns r0..r1 of a wider
+    [N, ldy] matrix (the column-sharded layout); nothing else is touched."""
+    out_f, in_f, N = 1000, 1024, 6
+    d, W, xh, x = _case(oracle, out_f, in_f, N, 4242, dups=True)
+    t = H.Tensor().load(d)
+    ref = oracle.dense_matmul(x, W)
+    sc = _scale(x, W)
+    tol = TOL if path == 0 else GEMM_TOL
+    for r0, r1 in ((0, 250), (250, 600), (600, 1000), (999, 1000)):
+        img = _image(H, L, t, r0, r1)
+        try:
+            y = _run(cuda, L, img, xh, r1 - r0, path=path, ldy=out_f + 3, col0=r0)
+        finally:
+            L.hxq_cuda_image_destroy(img)
+        assert np.isnan(y[:, :r0]).all() and np.isnan(y[:, r1:]).all()
+        _check(y[:, r0:r1], ref[:, r0:r1], sc[:, r0:r1], tol)
+    assert L.hxq_cuda_affine_device_status() == 0
+
+
+@pytest.mark.parametrize("path", [0, 1])
+def test_dense_sidecar_rows(H, L, oracle, cuda, path):
+    """Rows with many patches in one K step (more than the four a converter
+    prefetches), repeated coordinates summed in array order, and a row whose
+    every weight is corrected."""
+    out_f, in_f, N = 256, 1024, 9
+    d = synth.vq12(out_f, in_f, 31, frac=0.002)
+    rng = np.random.default_rng(3)
+    extra_r = np.concatenate([np.full(40, 5), np.full(in_f, 130), np.full(12, 255)]).astype(np.uint32)
+    extra_c = np.concatenate([np.arange(40) * 3, np.arange(in_f), rng.integers(0, 64, 12)]).astype(np.uint32)
+    extra_v = (rng.standard_normal(len(extra_r)) * 0.01).astype(np.float32)
+    d["rows"] = np.concatenate([d["rows"], extra_r, extra_r[:40]])
+    d["cols"] = np.concatenate([d["cols"], extra_c, extra_c[:40]])
+    d["vals"] = np.concatenate([d["vals"], extra_v, extra_v[:40] * np.float32(-0.5)])
+    err, w, _ = oracle.decompress(d)
+    assert err == 0
+    W = w.reshape(out_f, in_f)
+    xh, x = synth.activations(N, in_f, 8)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, out_f)
+    try:
+        assert L.hxq_cuda_image_has_matmul_tables(img) == 1
+        y = _run(cuda, L, img, xh, out_f, path=path)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    sc = _scale(x, W)
+    _check(y, oracle.dense_matmul(x, W), sc, TOL if path == 0 else GEMM_TOL)
+    if path == 1:
+        Wb = synth.bf16_to_f32(synth.bf16_round(W)).reshape(out_f, in_f)
+        _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
+
+
+def test_no_sidecar_and_zero_tokens(H, L, oracle, cuda):
+    d, W, xh, x = _case(oracle, 128, 256, 3, 7, frac=0.0)
+    assert len(d["rows"]) == 0
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, 128)
+    try:
+        for path in (0, 1):
+            _check(_run(cuda, L, img, xh, 128, path=path), oracle.dense_matmul(x, W), _scale(x, W),
+                   TOL if path == 0 else GEMM_TOL)
+        y = cuda.full((1, 128), 7.0, device="cuda")
+        xd = cuda.zeros((1, 256), dtype=cuda.int16, device="cuda")
+        assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), 0, y.data_ptr(), 128, None) == 0
+        cuda.cuda.synchronize()
+        assert bool((y == 7.0).all())
+    finally:
+        L.hxq_cuda_image_destroy(img)
+
+
+def test_invalid_images_and_arguments(H, L, cuda):
+    xd = cuda.zeros((4, 4096), dtype=cuda.int16, device="cuda")
+    y = cuda.zeros((4, 4096), dtype=cuda.float32, device="cuda")
+    cases = [synth.scalar(64, 128, 1),          # not 12-bit VQ
+             synth.vq12(64, 128, 2, k=256),     # k != 4096
+             synth.vq12(64, 96, 3)]             # in_f % 64 != 0
+    for d in cases:
+        t = H.Tensor().load(d)
+        img = _image(H, L, t, 0, d["out_f"])
+        try:
+            assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), 1, y.data_ptr(), 4096, None) == H.HXQ_ERR_INVALID_ARG
+        finally:
+            L.hxq_cuda_image_destroy(img)
+    d = synth.vq12(64, 192, 4)                  # in_f % 128 != 0: no matmul tables, GEMV only
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, 64)
+    plain = _image(H, L, H.Tensor().load(synth.vq12(64, 256, 5)), 0, 64, matmul=False)
+    try:
+        assert L.hxq_cuda_image_has_matmul_tables(img) == 0
+        assert L.hxq_cuda_image_has_matmul_tables(plain) == 0
+        assert L.hxq_cuda_vq_matmul_path(img, xd.data_ptr(), 8, y.data_ptr(), 64, 1, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul_path(plain, xd.data_ptr(), 8, y.data_ptr(), 64, 1, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul(plain, xd.data_ptr(), 8, y.data_ptr(), 64, None) == 0   # takes the GEMV
+        assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), 8, y.data_ptr(), 63, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul(img, xd.data_ptr() + 2, 1, y.data_ptr(), 64, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul(img, None, 1, y.data_ptr(), 64, None) == H.HXQ_ERR_NULL_PTR
+        assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), 8, y.data_ptr(), 64, None) == 0
+    finally:
+        L.hxq_cuda_image_destroy(img)
+        L.hxq_cuda_image_destroy(plain)
+    cuda.cuda.synchronize()
+    bad = C.c_void_p()
+    assert L.hxq_cuda_image_create_ex(t.ref, 0, 64, 8, C.byref(bad)) == H.HXQ_ERR_INVALID_ARG

@@ -5,13 +5,20 @@
 // (reference hxq-native src/hxq_affine.c:23-66; GPU entry points replace
 // src/hxq_affine_cuda.cu:184-294).
 //
-// Streaming dequant-GEMV for small token counts: one warp per output row,
-// 16 codes per lane per 128-bit load, codes widened to fp32 exactly with a
-// byte permute into the mantissa of 2^23, token activations read through
-// L1, the group scale applied per 16-code slice and the offset term from
-// the slice's activation sum, one warp reduction per row, bias fused into
-// the store.  Larger token counts use the tcgen05 GEMM (dequant_gemm.cu)
-// when the shape allows it.
+// Streaming dequant-GEMV for small token counts: one warp per output row
+// (a one-token launch holds 32 warps per SM, so a 4096-row matrix runs in
+// a single round), the warp's rows of codes first sent to L2 by bulk
+// prefetch so the copy engine streams them from DRAM, then 16 codes per
+// lane per 128-bit load, codes widened to fp32 exactly with a byte permute
+// into the mantissa of 2^23, the pass's group scales and offsets loaded one
+// per lane and handed out by shuffles, token activations read through L1,
+// the group scale applied per 16-code slice and the offset term from the
+// slice's activation sum, one warp reduction per row, bias fused into the
+// store.  Launched with programmatic stream serialization: the codes do not
+// depend on the kernel before it on the stream, so their loads start early
+// and the kernel waits (griddepcontrol.wait) only before the activations.
+// Larger token counts use the tcgen05 GEMM (dequant_gemm.cu) when the
+// shape allows it.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -77,6 +84,12 @@ template <> __device__ __forceinline__ float xval<uint16_t>(const uint16_t *p)
     return __uint_as_float((uint32_t)*p << 16);
 }
 
+// Group of 16-code slice sl: (16 sl) / gs, a shift when gs is a power of two.
+__device__ __forceinline__ uint32_t group_of(uint32_t sl, uint32_t gs, uint32_t gs_shift)
+{
+    return gs_shift < 32u ? (sl * 16u) >> gs_shift : (sl * 16u) / gs;
+}
+
 // Requirements: group_size % 16 == 0, in_f % 16 == 0, x and codes 16-B aligned.
 // One warp per output row.  A lane owns 16-code slices sl = lane + 32*i; all
 // SPL slices of a pass are loaded before any is used, so a warp keeps
@@ -84,12 +97,12 @@ template <> __device__ __forceinline__ float xval<uint16_t>(const uint16_t *p)
 // (staged once per block as fp32) when ntok*in_f floats fit in xs_floats,
 // else through L1.
 template <typename XT, int NT, int SPL>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, NT == 1 ? 4 : 1)
 affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
                    const float *__restrict__ scales, const float *__restrict__ offsets,
                    const float *__restrict__ bias, float *__restrict__ y,
                    uint32_t n0, uint32_t ntok, uint32_t in_f, uint32_t out_f,
-                   uint32_t gs, uint32_t xs_floats)
+                   uint32_t gs, uint32_t gs_shift, uint32_t xs_floats)
 {
     extern __shared__ float xs[];
     const uint32_t lane = threadIdx.x & 31u;
@@ -97,7 +110,18 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
     const uint32_t ng = in_f / gs;
     const uint32_t slices = in_f / 16u;
     const bool staged = (size_t)ntok * in_f <= xs_floats;
+    // the next kernel on the stream may start loading its weights now; this
+    // one reads activations and writes outputs only after the kernel before
+    // it has finished (griddepcontrol.wait)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // this warp's rows of codes go to L2 by bulk prefetch (the copy engine
+    // streams them from DRAM); the loads below then mostly hit L2
+    if (lane == 0 && (in_f & 15u) == 0)
+        for (uint32_t o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_f; o += warps)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(codes + (size_t)o * in_f), "r"(in_f)
+                         : "memory");
     if (staged) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         for (uint32_t i = threadIdx.x; i < ntok * in_f; i += blockDim.x)
             xs[i] = xval<XT>(x + (size_t)n0 * in_f + i);
         __syncthreads();
@@ -109,20 +133,34 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
         const uint4 *crow = reinterpret_cast<const uint4 *>(codes + (size_t)o * in_f);
         for (uint32_t base = 0; base < slices; base += 32u * SPL) {
             uint4 cw[SPL];
-            float sv[SPL], fv[SPL];
 #pragma unroll
             for (int i = 0; i < SPL; ++i) {
                 const uint32_t sl = base + (uint32_t)i * 32u + lane;
-                if (sl < slices) {
-                    cw[i] = __ldg(crow + sl);
-                    const uint32_t g = (sl * 16u) / gs;
-                    sv[i] = __ldg(scales + (size_t)o * ng + g);
-                    fv[i] = __ldg(offsets + (size_t)o * ng + g);
-                }
+                if (sl < slices) cw[i] = __ldg(crow + sl);
             }
+            // the pass's scales and offsets: one group per lane when the pass
+            // spans at most 32 groups (then handed out by shuffles)
+            const uint32_t g0 = group_of(base, gs, gs_shift);
+            const uint32_t g1 = group_of(min(base + 32u * SPL, slices) - 1u, gs, gs_shift) + 1u;
+            const bool by_lane = g1 - g0 <= 32u;
+            float s_l = 0.0f, f_l = 0.0f;
+            if (by_lane && g0 + lane < g1) {
+                s_l = __ldg(scales + (size_t)o * ng + g0 + lane);
+                f_l = __ldg(offsets + (size_t)o * ng + g0 + lane);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll
             for (int i = 0; i < SPL; ++i) {
                 const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                const uint32_t g = group_of(sl < slices ? sl : slices - 1u, gs, gs_shift);
+                float sv_i, fv_i;
+                if (by_lane) {
+                    sv_i = __shfl_sync(0xffffffffu, s_l, (g - g0) & 31u);
+                    fv_i = __shfl_sync(0xffffffffu, f_l, (g - g0) & 31u);
+                } else {
+                    sv_i = __ldg(scales + (size_t)o * ng + g);
+                    fv_i = __ldg(offsets + (size_t)o * ng + g);
+                }
                 if (sl >= slices) continue;
                 float q[16];
                 const uint32_t w[4] = {cw[i].x, cw[i].y, cw[i].z, cw[i].w};
@@ -150,7 +188,7 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
                             dot = fmaf(xv[u], q[u], dot);
                             xsum += xv[u];
                         }
-                        acc[t] = fmaf(sv[i], dot, fmaf(fv[i], xsum, acc[t]));
+                        acc[t] = fmaf(sv_i, dot, fmaf(fv_i, xsum, acc[t]));
                     }
                 }
             }
@@ -232,17 +270,30 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         const uint32_t cap = (uint32_t)sms * 8u;
         if (blocks > cap) blocks = cap;
         constexpr uint32_t kXsFloats = 12288;  // 48 KB of staged activations
+        const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
         for (uint32_t n0 = 0; n0 < N; n0 += kGemvTokens) {
             const uint32_t nt = N - n0 < (uint32_t)kGemvTokens ? N - n0 : (uint32_t)kGemvTokens;
             // one token: activations through L1 (staging would cost more than it saves)
             const size_t smem = (nt > 1 && (size_t)nt * in_f <= kXsFloats) ? (size_t)nt * in_f * sizeof(float) : 0;
             const uint32_t xs = smem ? kXsFloats : 0u;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(blocks);
+            cfg.blockDim = dim3(256);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e;
             if (nt == 1)
-                affine_gemv_kernel<XT, 1, 8><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 1, 8>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
             else if (nt <= 4)
-                affine_gemv_kernel<XT, 4, 4><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 4, 4>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
             else
-                affine_gemv_kernel<XT, kGemvTokens, 2><<<blocks, 256, smem, s>>>(x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, kGemvTokens, 2>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
+            if (e != cudaSuccess) { cudaGetLastError(); return -1; }
         }
     } else {
         uint64_t blocks = ((uint64_t)N * out_f + 255u) / 256u;

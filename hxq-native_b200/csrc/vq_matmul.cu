@@ -14,6 +14,9 @@
 // sidecar entries are a sparse epilogue, y += delta * x[col]: their chunk
 // range is read when the row starts and each lane's first two entries when
 // its last piece starts, so the dependent loads overlap the streaming.
+// Each warp first sends its rows of indices to L2 by bulk prefetch, and the
+// kernel is launched with programmatic stream serialization (the weights do
+// not depend on the kernel before it; the activations do).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -93,10 +96,19 @@ vq_gemv_kernel(const __grid_constant__ GemvArgs a)
         }
         cp_commit();
     };
+    // the next kernel on the stream may start now; this one waits for the
+    // kernel before it (griddepcontrol.wait) only before it reads the
+    // activations.  The warp's rows of indices go to L2 by bulk prefetch.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (lane == 0)
+        for (uint32_t r = 0; r < my_rows; ++r)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                         ::"l"(a.idx + (size_t)(first + r * stride) * row_bytes), "r"((uint32_t)row_bytes) : "memory");
     // the first piece is in flight while the codebook and activations are staged
     issue(0);
     for (uint32_t i = tid; i < kGvCbBytes / 16u; i += kGvThreads)
         reinterpret_cast<uint4 *>(smem)[i] = __ldg(reinterpret_cast<const uint4 *>(a.cb) + i);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if constexpr (XS) {
         const uint32_t nv = a.ntok * a.in_f / 8u;
         uint4 *xd = reinterpret_cast<uint4 *>(smem + kGvCbBytes + kGvRingBytes);
@@ -258,16 +270,23 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
         uint32_t blocks = (rows + kGvWarps - 1u) / kGvWarps;
         const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
         if (blocks > cap) blocks = cap;
-#define HXQ_GEMV_LAUNCH(NTV)                                                                     \
-        if (xs) vq_gemv_kernel<NTV, true><<<blocks, kGvThreads, smem, s>>>(a);                  \
-        else vq_gemv_kernel<NTV, false><<<blocks, kGvThreads, smem, s>>>(a);
-        if (nt == 1) { HXQ_GEMV_LAUNCH(1) }
-        else if (nt == 2) { HXQ_GEMV_LAUNCH(2) }
-        else if (nt <= 4) { HXQ_GEMV_LAUNCH(4) }
-        else { HXQ_GEMV_LAUNCH(8) }
-#undef HXQ_GEMV_LAUNCH
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(blocks);
+        cfg.blockDim = dim3(kGvThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        void (*kern)(GemvArgs) = nullptr;
+        if (nt == 1) kern = xs ? vq_gemv_kernel<1, true> : vq_gemv_kernel<1, false>;
+        else if (nt == 2) kern = xs ? vq_gemv_kernel<2, true> : vq_gemv_kernel<2, false>;
+        else if (nt <= 4) kern = xs ? vq_gemv_kernel<4, true> : vq_gemv_kernel<4, false>;
+        else kern = xs ? vq_gemv_kernel<8, true> : vq_gemv_kernel<8, false>;
+        e = cudaLaunchKernelEx(&cfg, kern, a);
+        if (e != cudaSuccess) { cudaGetLastError(); return e; }
     }
     return cudaSuccess;
 }

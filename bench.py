@@ -426,6 +426,169 @@ def run_aux_workload(args):
     print(json.dumps({"workload": args.workload, "data": "synthetic", "results": results}), flush=True)
 
 
+def run_fused_matmul_workload(args):
+    """The fused dequant-matmul sweep on one 7B layer (q, k, v, o, gate, up,
+    down): the same matrices as 12-bit 2D-VQ images (codebook gather +
+    sidecar, no dense weights) and as affine 4-bit codes in groups of 128,
+    bf16 activations at 1, 16 and 2048 tokens.  Output features are split
+    across the ranks (each rank holds the rows of its shard); with more than
+    one rank every matrix's output shard is all-gathered over NCCL into
+    [ranks, tokens, rows].  One step = the 7 matrices (+ gathers), captured
+    in a CUDA graph; device time, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import hxq_b200 as H
+    from hxq_b200 import synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    L = H.lib()
+    stream = torch.cuda.Stream()
+    hbm, peak_kind = measured_peaks()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # this rank's rows of every matrix, both formats
+    mats = []
+    vq_bytes = aff_bytes = 0
+    for p, (name, O, I) in enumerate(synth.LLAMA7B_PROJ):
+        r0, r1 = shard_rows(O, rank, world)
+        d = synth.vq12(O, I, synth.llama7b_seed(0, p))
+        t = H.Tensor().load(d)
+        img = C.c_void_p()
+        H.check(L.hxq_cuda_image_create_ex(t.ref, r0, r1, H.HXQ_IMAGE_MATMUL, C.byref(img)), "image")
+        assert L.hxq_cuda_image_has_matmul_tables(img) == 1
+        nnz = int(np.count_nonzero((d["rows"] >= r0) & (d["rows"] < r1)))
+        vq_bytes += (r1 - r0) * I * 3 // 4 + CB_BYTES + 12 * nnz
+        da = synth.affine(O, I, 128, synth.llama7b_seed(0, p) + 1000)
+        ng = I // 128
+        codes = torch.from_numpy(np.ascontiguousarray(da["codes"].reshape(O, I)[r0:r1])).cuda()
+        scales = torch.from_numpy(np.ascontiguousarray(da["scales"].reshape(O, ng)[r0:r1])).cuda()
+        offs = torch.from_numpy(np.ascontiguousarray(da["offsets"].reshape(O, ng)[r0:r1])).cuda()
+        at = H.AffineTensor(codes.data_ptr(), scales.data_ptr(), offs.data_ptr(), None, r1 - r0, I, 128)
+        aff_bytes += (r1 - r0) * I + 2 * (r1 - r0) * ng * 4
+        mats.append(dict(name=name, O=O, I=I, rows=r1 - r0, img=img, tensor=t, aff=at,
+                         keep=(codes, scales, offs)))
+    weights = 2.0 * sum(m["O"] * m["I"] for m in mats)   # flops per token per layer
+    results = []
+    for fmt in ("vq12", "affine"):
+        for N in (1, 16, 2048):
+            xh4, _ = synth.activations(N, 4096, synth.SEED_C5 + N)
+            xh11, _ = synth.activations(N, 11008, synth.SEED_C5 + N + 1)
+            x4 = torch.from_numpy(xh4.view(np.int16)).cuda()
+            x11 = torch.from_numpy(xh11.view(np.int16)).cuda()
+            ys = [torch.empty((N, m["rows"]), dtype=torch.float32, device="cuda") for m in mats]
+            # [ranks * tokens, rows]: rank r's shard at rows r*N .. r*N + N - 1
+            gathered = [torch.empty((world * N, m["rows"]), dtype=torch.float32, device="cuda") for m in mats]
+
+            def step():
+                for m, y, g in zip(mats, ys, gathered):
+                    x = x11 if m["I"] == 11008 else x4
+                    if fmt == "vq12":
+                        H.check(L.hxq_cuda_vq_matmul(m["img"], x.data_ptr(), N, y.data_ptr(), m["rows"],
+                                                     C.c_void_p(stream.cuda_stream)), "vq matmul")
+                    elif L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(m["aff"]), y.data_ptr(), N,
+                                                        C.c_void_p(stream.cuda_stream)) != 0:
+                        raise RuntimeError("affine matmul failed")
+                    if world > 1:
+                        dist.all_gather_into_tensor(g, y)
+
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    step()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(args.steps):
+                    step()
+            with torch.cuda.stream(stream):
+                for _ in range(max(1, args.warmup // 3)):
+                    graph.replay()
+            stream.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            with torch.cuda.stream(stream):
+                graph.replay()
+            e1.record(stream)
+            e1.synchronize()
+            ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+            del graph
+            if fmt == "vq12":
+                assert L.hxq_cuda_affine_device_status() == 0
+            wbytes = vq_bytes if fmt == "vq12" else aff_bytes
+            per_rank_gbs = wbytes / (ms * 1e-3) / 1e9
+            gather_bytes = sum(N * m["O"] * 4 for m in mats) if world > 1 else 0
+            results.append({"case": f"{fmt} 7B layer N={N}", "format": fmt, "tokens": N,
+                            "us_per_layer": ms * 1e3, "tflops": weights * N / (ms * 1e-3) / 1e12,
+                            "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
+                            "hbm_frac_per_rank": per_rank_gbs / hbm, "gather_bytes_per_layer": gather_bytes,
+                            "path": ("GEMV" if N <= 4 else "tcgen05 GEMM")})
+            del x4, x11, ys, gathered
+    for m in mats:
+        L.hxq_cuda_image_destroy(m["img"])
+    if rank == 0:
+        print(json.dumps({"workload": "c5", "data": "synthetic", "n_gpus": world,
+                          "parallelism": f"output features split x{world}" + (", NCCL all-gather" if world > 1 else ""),
+                          "peak": {"hbm_gbs": hbm, "kind": peak_kind}, "results": results}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_kernel_cases(args):
+    """One call each of the matmul kernels on a 4096 x 4096 matrix, for
+    profiling: affine GEMV (1 token), VQ GEMV (1 token), VQ tcgen05 GEMM
+    (2048 tokens), affine tcgen05 GEMM (4096 tokens); bf16 activations.
+    Prints each call's device time (CUDA events, cold start)."""
+    import torch
+
+    import hxq_b200 as H
+    from hxq_b200 import synth
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    L = H.lib()
+    da = synth.affine(4096, 4096, 128, synth.SEED_C3)
+    codes = torch.from_numpy(da["codes"]).cuda()
+    sc = torch.from_numpy(da["scales"]).cuda()
+    of = torch.from_numpy(da["offsets"]).cuda()
+    at = H.AffineTensor(codes.data_ptr(), sc.data_ptr(), of.data_ptr(), None, 4096, 4096, 128)
+    dv = synth.vq12(4096, 4096, synth.SEED_C5)
+    t = H.Tensor().load(dv)
+    img = C.c_void_p()
+    H.check(L.hxq_cuda_image_create_ex(t.ref, 0, 4096, H.HXQ_IMAGE_MATMUL, C.byref(img)), "image")
+    xs = {n: torch.from_numpy(synth.activations(n, 4096, 11 + n)[0].view(np.int16)).cuda() for n in (1, 2048, 4096)}
+    y = torch.empty(4096 * 4096, dtype=torch.float32, device="cuda")
+    cases = [("affine GEMV N=1", lambda: L.hxq_affine_group_matmul_bf16(xs[1].data_ptr(), C.byref(at), y.data_ptr(), 1, None)),
+             ("vq12 GEMV N=1", lambda: L.hxq_cuda_vq_matmul(img, xs[1].data_ptr(), 1, y.data_ptr(), 4096, None)),
+             ("vq12 GEMM N=2048", lambda: L.hxq_cuda_vq_matmul(img, xs[2048].data_ptr(), 2048, y.data_ptr(), 4096, None)),
+             ("affine GEMM N=4096", lambda: L.hxq_affine_group_matmul_bf16(xs[4096].data_ptr(), C.byref(at), y.data_ptr(), 4096, None))]
+    out = []
+    for name, fn in cases:
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if fn() != 0:
+            raise RuntimeError(name)
+        e1.record()
+        e1.synchronize()
+        out.append({"case": name, "ms": e0.elapsed_time(e1)})
+    if L.hxq_cuda_affine_device_status() != 0:
+        raise RuntimeError("tcgen05 GEMM reported a timeout")
+    L.hxq_cuda_image_destroy(img)
+    print(json.dumps({"workload": "kernels", "data": "synthetic", "results": out}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 
 def main():
@@ -440,14 +603,22 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers to run (profiling aid; the workload is 32 layers)")
-    ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3"], default="llama7b",
+    ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3", "c5", "kernels"], default="llama7b",
                     help="llama7b: the headline (default); c1/c2/c3: single-tensor decompress "
-                         "and the affine batch sweep, one JSON line each")
+                         "and the affine batch sweep; c5: the fused dequant-matmul sweep on a 7B "
+                         "layer (column-split over the ranks); kernels: one call of each matmul "
+                         "kernel (for profiling); one JSON line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload == "c5":
+        run_fused_matmul_workload(args)
+        return
+    if args.workload == "kernels":
+        run_kernel_cases(args)
         return
     if args.workload != "llama7b":
         run_aux_workload(args)

@@ -90,3 +90,59 @@ def test_shard_rows_partition():
             spans = [shard_rows(out_f, r, world) for r in range(world)]
             assert spans[0][0] == 0 and spans[-1][1] == out_f
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+
+
+def _matmul_worker(rank: int, world: int, port: int, q):
+    """Column-split fused matmul: each rank owns the output features of its
+    row shard, computes them with the oracle (the reference decompress of its
+    rows, then the ordered matmul) and the ranks all-gather [ranks, N, rows];
+    rank 0 checks the permuted result is bit-identical to the whole-tensor
+    product."""
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, repo)
+    sys.path.insert(0, os.path.join(repo, "hxq-native_b200"))
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from hxq_b200 import synth
+    from hxq_b200.shard import shard_rows, slice_rows
+    from oracle.oracle import Oracle
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=timedelta(seconds=60))
+    try:
+        out_f, in_f, N = 1376 * 2, 256, 3        # an even split, as the 7B shapes are
+        d = synth.vq12(out_f, in_f, 91, frac=0.02)
+        _, x = synth.activations(N, in_f, 92)
+        orc = Oracle()
+        r0, r1 = shard_rows(out_f, rank, world)
+        part = slice_rows(d, r0, r1)
+        err, w, _ = orc.decompress(part)
+        y = torch.from_numpy(orc.dense_matmul(x, w.reshape(r1 - r0, in_f)))
+        g = torch.empty((world * N, r1 - r0), dtype=torch.float32)
+        dist.all_gather_into_tensor(g, y)
+        if rank == 0:
+            whole = g.view(world, N, r1 - r0).permute(1, 0, 2).reshape(N, out_f).numpy()
+            e_full, w_full, _ = orc.decompress(d)
+            ref = orc.dense_matmul(x, w_full.reshape(out_f, in_f))
+            q.put((err == 0 and e_full == 0, bool(np.array_equal(whole.view(np.uint32), ref.view(np.uint32)))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_split_matmul_gloo_world2():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_matmul_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    ok_err, ok_y = q.get(timeout=10)
+    assert ok_err
+    assert ok_y, "gathered output shards differ from the whole-matrix product"

@@ -431,10 +431,17 @@ def run_fused_matmul_workload(args):
     down): the same matrices as 12-bit 2D-VQ images (codebook gather +
     sidecar, no dense weights) and as affine 4-bit codes in groups of 128,
     bf16 activations at 1, 16 and 2048 tokens.  Output features are split
-    across the ranks (each rank holds the rows of its shard); with more than
-    one rank every matrix's output shard is all-gathered over NCCL into
-    [ranks, tokens, rows].  One step = the 7 matrices (+ gathers), captured
-    in a CUDA graph; device time, max over ranks."""
+    across the ranks (each rank holds the rows of its shard).  With more
+    than one rank two ways of assembling the full outputs are timed:
+      nccl: each matrix's output shard is all-gathered over NCCL into
+            [ranks * tokens, rows];
+      p2p:  every rank's [tokens, out_features] output buffer is mapped into
+            every other rank (CUDA IPC) and the matmul stores each output
+            element into all of them over NVLink; after the layer's seven
+            matmuls one flag kernel tells the peers, one wait kernel waits
+            for them.  Two buffers alternate by step parity.
+    One step = the 7 matrices (+ assembly), captured in a CUDA graph; device
+    time, max over ranks."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -450,6 +457,7 @@ def run_fused_matmul_workload(args):
     L = H.lib()
     stream = torch.cuda.Stream()
     hbm, peak_kind = measured_peaks()
+    steps = args.steps + (args.steps % 2)          # even: the p2p buffers alternate by parity
 
     def max_over_ranks(x: float) -> float:
         if world == 1:
@@ -477,12 +485,83 @@ def run_fused_matmul_workload(args):
         offs = torch.from_numpy(np.ascontiguousarray(da["offsets"].reshape(O, ng)[r0:r1])).cuda()
         at = H.AffineTensor(codes.data_ptr(), scales.data_ptr(), offs.data_ptr(), None, r1 - r0, I, 128)
         aff_bytes += (r1 - r0) * I + 2 * (r1 - r0) * ng * 4
-        mats.append(dict(name=name, O=O, I=I, rows=r1 - r0, img=img, tensor=t, aff=at,
+        mats.append(dict(name=name, O=O, I=I, r0=r0, rows=r1 - r0, img=img, tensor=t, aff=at,
                          keep=(codes, scales, offs)))
     weights = 2.0 * sum(m["O"] * m["I"] for m in mats)   # flops per token per layer
+    Ns = (1, 16, 2048)
+
+    # p2p: per matrix and parity an IPC output buffer [max tokens, O] on every
+    # rank, mapped into every other rank; one flag array per rank
+    p2p = None
+    if world > 1:
+        nmax = max(Ns)
+        handle = lambda: (C.c_char * 64)()  # noqa: E731
+        own, hnd = [], []
+        for m in mats:
+            for q in range(2):
+                ptr, h = C.c_void_p(), handle()
+                H.check(L.hxq_cuda_ipc_alloc(nmax * m["O"] * 4, C.byref(ptr), h), "ipc alloc")
+                own.append(ptr)
+                hnd.append(bytes(h))
+        fptr, fh = C.c_void_p(), handle()
+        H.check(L.hxq_cuda_ipc_alloc(256, C.byref(fptr), fh), "ipc alloc")
+        all_h = [None] * world
+        dist.all_gather_object(all_h, (hnd, bytes(fh)))
+        opened = []
+        bufs = [[None] * world for _ in range(2 * len(mats))]    # [matrix*2 + parity][rank]
+        flag_ptrs = [None] * world
+        for pr in range(world):
+            for j in range(2 * len(mats)):
+                if pr == rank:
+                    bufs[j][pr] = own[j].value
+                else:
+                    dp = C.c_void_p()
+                    H.check(L.hxq_cuda_ipc_open((C.c_char * 64).from_buffer_copy(all_h[pr][0][j]), C.byref(dp)),
+                            "ipc open")
+                    opened.append(dp)
+                    bufs[j][pr] = dp.value
+            if pr == rank:
+                flag_ptrs[pr] = fptr.value
+            else:
+                dp = C.c_void_p()
+                H.check(L.hxq_cuda_ipc_open((C.c_char * 64).from_buffer_copy(all_h[pr][1]), C.byref(dp)), "ipc open")
+                opened.append(dp)
+                flag_ptrs[pr] = dp.value
+        counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        p2p = dict(own=own, fptr=fptr, opened=opened, bufs=bufs,
+                   flags=(C.c_void_p * world)(*flag_ptrs), counter=counter, status=status)
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    def time_graph(step):
+        with torch.cuda.stream(stream):
+            for k in range(2):
+                step(k)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for k in range(steps):
+                step(k)
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup // 3)):
+                graph.replay()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        e1.record(stream)
+        e1.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        del graph
+        return ms
+
     results = []
     for fmt in ("vq12", "affine"):
-        for N in (1, 16, 2048):
+        for N in Ns:
             xh4, _ = synth.activations(N, 4096, synth.SEED_C5 + N)
             xh11, _ = synth.activations(N, 11008, synth.SEED_C5 + N + 1)
             x4 = torch.from_numpy(xh4.view(np.int16)).cuda()
@@ -491,56 +570,81 @@ def run_fused_matmul_workload(args):
             # [ranks * tokens, rows]: rank r's shard at rows r*N .. r*N + N - 1
             gathered = [torch.empty((world * N, m["rows"]), dtype=torch.float32, device="cuda") for m in mats]
 
-            def step():
+            def matmul(m, outs, ldy):
+                x = x11 if m["I"] == 11008 else x4
+                n_out = len(outs)
+                arr = (C.c_void_p * n_out)(*outs)
+                if fmt == "vq12":
+                    H.check(L.hxq_cuda_vq_matmul_multi(m["img"], x.data_ptr(), N, arr, n_out, ldy,
+                                                       C.c_void_p(stream.cuda_stream)), "vq matmul")
+                elif L.hxq_affine_group_matmul_bf16_multi(x.data_ptr(), C.byref(m["aff"]), arr, n_out, ldy, N,
+                                                          C.c_void_p(stream.cuda_stream)) != 0:
+                    raise RuntimeError("affine matmul failed")
+
+            def step_nccl(k):
                 for m, y, g in zip(mats, ys, gathered):
-                    x = x11 if m["I"] == 11008 else x4
-                    if fmt == "vq12":
-                        H.check(L.hxq_cuda_vq_matmul(m["img"], x.data_ptr(), N, y.data_ptr(), m["rows"],
-                                                     C.c_void_p(stream.cuda_stream)), "vq matmul")
-                    elif L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(m["aff"]), y.data_ptr(), N,
-                                                        C.c_void_p(stream.cuda_stream)) != 0:
-                        raise RuntimeError("affine matmul failed")
+                    matmul(m, [y.data_ptr()], m["rows"])
                     if world > 1:
                         dist.all_gather_into_tensor(g, y)
 
-            with torch.cuda.stream(stream):
-                for _ in range(2):
-                    step()
-            stream.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for _ in range(args.steps):
-                    step()
-            with torch.cuda.stream(stream):
-                for _ in range(max(1, args.warmup // 3)):
-                    graph.replay()
-            stream.synchronize()
-            if world > 1:
-                dist.barrier()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            with torch.cuda.stream(stream):
-                graph.replay()
-            e1.record(stream)
-            e1.synchronize()
-            ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
-            del graph
-            if fmt == "vq12":
-                assert L.hxq_cuda_affine_device_status() == 0
-            wbytes = vq_bytes if fmt == "vq12" else aff_bytes
-            per_rank_gbs = wbytes / (ms * 1e-3) / 1e9
-            gather_bytes = sum(N * m["O"] * 4 for m in mats) if world > 1 else 0
-            results.append({"case": f"{fmt} 7B layer N={N}", "format": fmt, "tokens": N,
-                            "us_per_layer": ms * 1e3, "tflops": weights * N / (ms * 1e-3) / 1e12,
-                            "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
-                            "hbm_frac_per_rank": per_rank_gbs / hbm, "gather_bytes_per_layer": gather_bytes,
-                            "path": ("GEMV" if N <= 4 else "tcgen05 GEMM")})
+            def step_p2p(k):
+                for j, m in enumerate(mats):
+                    targets = [b + 4 * m["r0"] for b in p2p["bufs"][2 * j + (k & 1)]]
+                    matmul(m, targets, m["O"])
+                H.check(L.hxq_cuda_peer_signal(p2p["flags"], world, rank, p2p["counter"].data_ptr(),
+                                               C.c_void_p(stream.cuda_stream)), "peer signal")
+                H.check(L.hxq_cuda_peer_wait(p2p["flags"][rank], world, p2p["counter"].data_ptr(),
+                                             p2p["status"].data_ptr(), C.c_void_p(stream.cuda_stream)), "peer wait")
+
+            modes = [("nccl" if world > 1 else "local", step_nccl)]
+            if p2p is not None:
+                modes.append(("p2p", step_p2p))
+            for mode, step in modes:
+                ms = time_graph(step)
+                if fmt == "vq12":
+                    assert L.hxq_cuda_affine_device_status() == 0
+                wbytes = vq_bytes if fmt == "vq12" else aff_bytes
+                per_rank_gbs = wbytes / (ms * 1e-3) / 1e9
+                res = {"case": f"{fmt} 7B layer N={N} {mode}", "format": fmt, "tokens": N, "assembly": mode,
+                       "us_per_layer": ms * 1e3, "tflops": weights * N / (ms * 1e-3) / 1e12,
+                       "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
+                       "hbm_frac_per_rank": per_rank_gbs / hbm,
+                       "output_bytes_per_layer": sum(N * m["O"] * 4 for m in mats),
+                       "path": ("GEMV" if N <= 4 else "tcgen05 GEMM")}
+                if mode == "p2p":
+                    # one step outside the graph: the assembled outputs must equal
+                    # the NCCL-gathered shards, bit for bit
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    with torch.cuda.stream(stream):
+                        step_nccl(0)
+                        step_p2p(0)
+                    stream.synchronize()
+                    same = True
+                    for j, (m, g) in enumerate(zip(mats, gathered)):
+                        full = H.device_view(torch, p2p["own"][2 * j].value, N * m["O"]).view(N, m["O"])
+                        ref = g.view(world, N, m["rows"]).permute(1, 0, 2).reshape(N, m["O"])
+                        same = same and bool(torch.equal(full.view(torch.int32), ref.contiguous().view(torch.int32)))
+                    t = torch.tensor([1.0 if same else 0.0], dtype=torch.float64, device="cuda")
+                    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+                    res["p2p_equals_nccl"] = bool(t.item() == 1.0)
+                    res["peer_wait_status"] = int(p2p["status"].item())
+                results.append(res)
             del x4, x11, ys, gathered
+    if p2p is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        for dp in p2p["opened"]:
+            L.hxq_cuda_ipc_close(dp)
+        torch.cuda.synchronize()
+        dist.barrier()
+        for ptr in p2p["own"] + [p2p["fptr"]]:
+            L.hxq_cuda_ipc_free(ptr)
     for m in mats:
         L.hxq_cuda_image_destroy(m["img"])
     if rank == 0:
         print(json.dumps({"workload": "c5", "data": "synthetic", "n_gpus": world,
-                          "parallelism": f"output features split x{world}" + (", NCCL all-gather" if world > 1 else ""),
+                          "parallelism": f"output features split x{world}",
                           "peak": {"hbm_gbs": hbm, "kind": peak_kind}, "results": results}), flush=True)
     if world > 1:
         dist.barrier()

@@ -26,12 +26,10 @@
 
 #include "hxq_affine.h"
 #include "hxq_cuda.h"
+#include "hxq_cuda_internal.h"
 
 namespace hxq {
 
-int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
-                     const float *bias, float *y, uint32_t T, uint32_t I, uint32_t O, uint32_t gs,
-                     cudaStream_t s);
 
 namespace {
 
@@ -100,7 +98,7 @@ template <typename XT, int NT, int SPL>
 __global__ void __launch_bounds__(256, NT == 1 ? 4 : 1)
 affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
                    const float *__restrict__ scales, const float *__restrict__ offsets,
-                   const float *__restrict__ bias, float *__restrict__ y,
+                   const float *__restrict__ bias, const __grid_constant__ OutPtrs out, uint32_t ldy,
                    uint32_t n0, uint32_t ntok, uint32_t in_f, uint32_t out_f,
                    uint32_t gs, uint32_t gs_shift, uint32_t xs_floats)
 {
@@ -204,7 +202,8 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
             const float bo = bias ? __ldg(bias + o) : 0.0f;
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                if ((uint32_t)t < ntok) y[(size_t)(n0 + t) * out_f + o] = acc[t] + bo;
+                if ((uint32_t)t < ntok)
+                    for (uint32_t k = 0; k < out.n; ++k) out.y[k][(size_t)(n0 + t) * ldy + o] = acc[t] + bo;
         }
     }
 }
@@ -242,22 +241,30 @@ __global__ void affine_generic_kernel(const XT *__restrict__ x, const uint8_t *_
 
 bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
+// out: the outputs, each [N, ldy] (a single [N, out_f] buffer for the
+// reference entry points).  Several outputs or ldy != out_f need the GEMV or
+// GEMM paths (group size and in_f multiples of 16, 16-B aligned x and codes).
 template <typename XT>
 int run_affine(const XT *x, const uint8_t *codes, const float *scales, const float *offsets,
-               const float *bias, float *y, uint32_t N, uint32_t in_f, uint32_t out_f,
+               const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t N, uint32_t in_f, uint32_t out_f,
                uint32_t gs, cudaStream_t s)
 {
-    if (!x || !codes || !scales || !offsets || !y) return -1;
-    if (gs == 0 || in_f % gs != 0) return -1;
+    if (!x || !codes || !scales || !offsets || out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return -1;
+    for (uint32_t k = 0; k < out.n; ++k)
+        if (!out.y[k]) return -1;
+    if (gs == 0 || in_f % gs != 0 || ldy < out_f) return -1;
     if (N == 0 || out_f == 0) return 0;
+    const bool plain = out.n == 1 && ldy == out_f;
+    float *y = out.y[0];
     if (in_f == 0) {  // empty reduction: bias only
+        if (!plain) return -1;
         affine_generic_kernel<XT><<<1, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
     if constexpr (sizeof(XT) == 2) {
         if (N >= kGemmMinTokens) {
             const int r = affine_gemm_bf16(reinterpret_cast<const uint16_t *>(x), codes, scales, offsets, bias,
-                                           y, N, in_f, out_f, gs, s);
+                                           out, ldy, N, in_f, out_f, gs, s);
             if (r <= 0) return r;  // launched (0) or failed (-1); 1 = shape not taken
         }
     }
@@ -288,14 +295,15 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
             cfg.numAttrs = 1;
             cudaError_t e;
             if (nt == 1)
-                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 1, 8>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 1, 8>, x, codes, scales, offsets, bias, out, ldy, n0, nt, in_f, out_f, gs, gs_shift, xs);
             else if (nt <= 4)
-                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 4, 4>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, 4, 4>, x, codes, scales, offsets, bias, out, ldy, n0, nt, in_f, out_f, gs, gs_shift, xs);
             else
-                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, kGemvTokens, 2>, x, codes, scales, offsets, bias, y, n0, nt, in_f, out_f, gs, gs_shift, xs);
+                e = cudaLaunchKernelEx(&cfg, affine_gemv_kernel<XT, kGemvTokens, 2>, x, codes, scales, offsets, bias, out, ldy, n0, nt, in_f, out_f, gs, gs_shift, xs);
             if (e != cudaSuccess) { cudaGetLastError(); return -1; }
         }
     } else {
+        if (!plain) return -1;
         uint64_t blocks = ((uint64_t)N * out_f + 255u) / 256u;
         if (blocks > 148u * 32u) blocks = 148u * 32u;
         affine_generic_kernel<XT><<<(uint32_t)blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
@@ -306,39 +314,63 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
 }  // namespace
 }  // namespace hxq
 
+namespace {
+hxq::OutPtrs one_out(float *y)
+{
+    hxq::OutPtrs o{};
+    o.y[0] = y;
+    o.n = y ? 1u : 0u;
+    return o;
+}
+}  // namespace
+
 extern "C" {
 
 int hxq_affine_group_matmul(const float *d_x, const hxq_affine_tensor_t *t, float *d_output,
                             uint32_t N)
 {
     if (!t) return -1;
-    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, d_output, N,
-                                  t->in_features, t->out_features, t->group_size, (cudaStream_t)0);
+    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, one_out(d_output),
+                                  t->out_features, N, t->in_features, t->out_features, t->group_size,
+                                  (cudaStream_t)0);
 }
 
 int hxq_affine_matmul_flat(const float *d_x, const uint8_t *d_indices, const float *d_scales,
                            const float *d_offsets, const float *d_bias, float *d_output,
                            uint32_t N, uint32_t in_f, uint32_t out_f, uint32_t group_size)
 {
-    return hxq::run_affine<float>(d_x, d_indices, d_scales, d_offsets, d_bias, d_output, N, in_f,
-                                  out_f, group_size, (cudaStream_t)0);
+    return hxq::run_affine<float>(d_x, d_indices, d_scales, d_offsets, d_bias, one_out(d_output), out_f, N,
+                                  in_f, out_f, group_size, (cudaStream_t)0);
 }
 
 int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t,
                                  float *d_output, uint32_t N, void *stream)
 {
     if (!t) return -1;
-    return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias,
-                                     d_output, N, t->in_features, t->out_features,
-                                     t->group_size, static_cast<cudaStream_t>(stream));
+    return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias, one_out(d_output),
+                                     t->out_features, N, t->in_features, t->out_features, t->group_size,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t,
+                                       float *const *d_ys, uint32_t n_out, uint32_t ldy, uint32_t N,
+                                       void *stream)
+{
+    if (!t || !d_ys || n_out == 0 || n_out > HXQ_CUDA_MAX_PEERS) return -1;
+    hxq::OutPtrs o{};
+    for (uint32_t k = 0; k < n_out; ++k) o.y[k] = d_ys[k];
+    o.n = n_out;
+    return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias, o, ldy, N,
+                                     t->in_features, t->out_features, t->group_size,
+                                     static_cast<cudaStream_t>(stream));
 }
 
 int hxq_affine_group_matmul_async(const float *d_x, const hxq_affine_tensor_t *t,
                                   float *d_output, uint32_t N, void *stream)
 {
     if (!t) return -1;
-    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, d_output, N,
-                                  t->in_features, t->out_features, t->group_size,
+    return hxq::run_affine<float>(d_x, t->indices, t->scales, t->offsets, t->bias, one_out(d_output),
+                                  t->out_features, N, t->in_features, t->out_features, t->group_size,
                                   static_cast<cudaStream_t>(stream));
 }
 

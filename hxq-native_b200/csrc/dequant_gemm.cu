@@ -235,7 +235,8 @@ struct Params {
     const uint32_t *rb;
     const uint16_t *kp;
     const uint32_t *e4;
-    float *y;                 // [T, ldy], or [splits][T, O] partial sums when splits > 1
+    OutPtrs out;              // the [T, ldy] outputs (all get the same values)
+    float *part;              // [splits][T, O] partial sums when splits > 1
     uint32_t T, I, O, gs, ldy;
     uint32_t splits;          // K ranges (gridDim.z); >1 writes partials, no bias
 };
@@ -471,7 +472,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             asm volatile("tcgen05.fence::after_thread_sync;");
             const bool partial = p.splits > 1u;
             const float bo = (valid && p.bias && !partial) ? __ldg(p.bias + o) : 0.0f;
-            float *yo = p.y + (partial ? (size_t)blockIdx.z * p.T * p.O : 0u);
+            const uint32_t nout = partial ? 1u : p.out.n;
             const uint32_t ld = partial ? p.O : p.ldy;
             // this half's accumulator columns; a 32-column load may read past
             // them (inside the allocation) when BN < 64: those are not stored
@@ -482,10 +483,13 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 tmem_ld32(tmem + lane_base + c0, v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;");
                 if (valid) {
+                    for (uint32_t k = 0; k < nout; ++k) {
+                        float *yo = partial ? p.part + (size_t)blockIdx.z * p.T * p.O : p.out.y[k];
 #pragma unroll
-                    for (uint32_t j = 0; j < 32u; ++j) {
-                        const uint32_t n = n0 + c0 + j;
-                        if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
+                        for (uint32_t j = 0; j < 32u; ++j) {
+                            const uint32_t n = n0 + c0 + j;
+                            if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
+                        }
                     }
                 }
             }
@@ -506,9 +510,11 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     }
 }
 
-// y[n, o] = sum over the K ranges, in order, of the partial sums + bias.
+// y[n, o] = sum over the K ranges, in order, of the partial sums + bias,
+// stored into every output.
 __global__ void splitk_reduce_kernel(const float *__restrict__ part, const float *__restrict__ bias,
-                                     float *__restrict__ y, uint32_t T, uint32_t O, uint32_t ldy, uint32_t splits)
+                                     const __grid_constant__ OutPtrs out, uint32_t T, uint32_t O, uint32_t ldy,
+                                     uint32_t splits)
 {
     const uint64_t total = (uint64_t)T * O;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -517,7 +523,7 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ part, const float
         for (uint32_t k = 0; k < splits; ++k) acc += part[(size_t)k * total + i];
         const uint32_t o = (uint32_t)(i % O);
         if (bias) acc += __ldg(bias + o);
-        y[(i / O) * ldy + o] = acc;
+        for (uint32_t k = 0; k < out.n; ++k) out.y[k][(i / O) * ldy + o] = acc;
     }
 }
 
@@ -603,10 +609,10 @@ float *splitk_buffer(size_t floats, cudaStream_t s)
 
 namespace {
 
-// Token tile, K split and launch for one matmul; p.splits and p.y are set
+// Token tile, K split and launch for one matmul; p.splits, p.out and p.part are set
 // here.  0 on launch, -1 on error.
 template <bool VQ>
-int run(const uint16_t *x, gemm::Params p, float *y, cudaStream_t s)
+int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
 {
     int sms = 148, dev = 0;
     cudaGetDevice(&dev);
@@ -630,7 +636,8 @@ int run(const uint16_t *x, gemm::Params p, float *y, cudaStream_t s)
         if (!part) return -1;
     }
     p.splits = splits;
-    p.y = splits > 1 ? part : y;
+    p.out = out;
+    p.part = part;
     int r;
     switch (bn) {
     case 16: r = gemm::launch<16, VQ>(x, p, s); break;
@@ -643,7 +650,7 @@ int run(const uint16_t *x, gemm::Params p, float *y, cudaStream_t s)
     const uint64_t total = (uint64_t)T * O;
     uint64_t blocks = (total + 255u) / 256u;
     if (blocks > (uint64_t)sms * 8u) blocks = (uint64_t)sms * 8u;
-    gemm::splitk_reduce_kernel<<<(uint32_t)blocks, 256, 0, s>>>(part, p.bias, y, T, O, p.ldy, splits);
+    gemm::splitk_reduce_kernel<<<(uint32_t)blocks, 256, 0, s>>>(part, p.bias, out, T, O, p.ldy, splits);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -652,8 +659,8 @@ int run(const uint16_t *x, gemm::Params p, float *y, cudaStream_t s)
 // Tensor-core path for bf16 activations.  Returns 1 when the shape is not
 // one it takes (the caller uses the GEMV), 0 on launch, -1 on error.
 int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
-                     const float *bias, float *y, uint32_t T, uint32_t I, uint32_t O, uint32_t gs,
-                     cudaStream_t s)
+                     const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t T, uint32_t I, uint32_t O,
+                     uint32_t gs, cudaStream_t s)
 {
     if (T == 0 || O == 0) return 1;
     if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return 1;
@@ -661,15 +668,16 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
     gemm::Params p{};
     p.codes = codes; p.scales = scales; p.offsets = offsets; p.bias = bias;
-    p.T = T; p.I = I; p.O = O; p.gs = gs; p.ldy = O;
-    return run<false>(x, p, y, s);
+    if (ldy < O || out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
+    p.T = T; p.I = I; p.O = O; p.gs = gs; p.ldy = ldy;
+    return run<false>(x, p, out, s);
 }
 
 // Fused VQ-dequant GEMM on a 12-bit image with its matmul tables: x bf16
 // [T, I], y fp32 [T, ldy].  Returns 1 when the shape is not one it takes, 0
 // on launch, -1 on error.
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
-                 const uint16_t *kp, const uint32_t *e4, float *y, uint32_t T, uint32_t I, uint32_t O,
+                 const uint16_t *kp, const uint32_t *e4, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O,
                  uint32_t ldy, cudaStream_t s)
 {
     if (T == 0 || O == 0) return 1;
@@ -678,8 +686,9 @@ int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, con
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
     gemm::Params p{};
     p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4;
+    if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
     p.T = T; p.I = I; p.O = O; p.gs = 0; p.ldy = ldy;
-    return run<true>(x, p, y, s);
+    return run<true>(x, p, out, s);
 }
 
 }  // namespace hxq

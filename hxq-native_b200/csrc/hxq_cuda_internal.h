@@ -126,13 +126,23 @@ struct GenericJob {
 cudaError_t launch_generic(const GenericJob &j, const Scratch &sc,
                            cudaStream_t s);
 
+// Output buffers of a matmul: the same [tokens, ldy] result stored into each
+// (local or peer-mapped).
+struct OutPtrs {
+    float *y[HXQ_CUDA_MAX_PEERS];
+    uint32_t n;
+};
+
 // Fused VQ-dequant matmul on 12-bit images with k = 4096 (vq_matmul.cu,
-// dequant_gemm.cu).  x bf16 [ntok, in_f]; y fp32 [ntok, ldy].
+// dequant_gemm.cu).  x bf16 [ntok, in_f]; outputs fp32 [ntok, ldy].
 cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
                            uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
-                           float *y, uint32_t ldy, int sms, cudaStream_t s);
+                           const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s);
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
-                 const uint16_t *kp, const uint32_t *e4, float *y, uint32_t T, uint32_t I, uint32_t O,
+                 const uint16_t *kp, const uint32_t *e4, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O,
                  uint32_t ldy, cudaStream_t s);
+int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
+                     const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t T, uint32_t I, uint32_t O,
+                     uint32_t gs, cudaStream_t s);
 
 }  // namespace hxq

@@ -1042,10 +1042,15 @@ hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n
                          dev, static_cast<cudaStream_t>(stream));
 }
 
-hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
-                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream)
+namespace {
+
+hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uint32_t N, const hxq::OutPtrs &out,
+                      uint32_t ldy, int gemm, void *stream)
 {
-    if (!img || !d_x_bf16 || !d_y) return HXQ_ERR_NULL_PTR;
+    if (!img || !d_x_bf16) return HXQ_ERR_NULL_PTR;
+    if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return HXQ_ERR_INVALID_ARG;
+    for (uint32_t k = 0; k < out.n; ++k)
+        if (!out.y[k]) return HXQ_ERR_NULL_PTR;
     if (img->kind != kKindVq12 || img->check_k || img->k != 4096u || img->in_f % 64u != 0u)
         return HXQ_ERR_INVALID_ARG;
     if (gemm && !img->has_mm) return HXQ_ERR_INVALID_ARG;
@@ -1063,11 +1068,11 @@ hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (gemm) {
         const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
-                                        d_y, N, img->in_f, img->rows, ldy, s);
+                                        out, N, img->in_f, img->rows, ldy, s);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else {
         const cudaError_t e = hxq::launch_vq_gemv(img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent,
-                                                  img->n_chunks, img->rows, img->in_f, d_x_bf16, N, d_y, ldy,
+                                                  img->n_chunks, img->rows, img->in_f, d_x_bf16, N, out, ldy,
                                                   g_dev[dev].sms, s);
         if (e != cudaSuccess) return map_cuda(e);
     }
@@ -1075,11 +1080,36 @@ hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t 
     return HXQ_OK;
 }
 
+}  // namespace
+
+hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream)
+{
+    if (!d_y) return HXQ_ERR_NULL_PTR;
+    hxq::OutPtrs o{};
+    o.y[0] = d_y;
+    o.n = 1;
+    return vq_matmul(img, d_x_bf16, N, o, ldy, gemm, stream);
+}
+
 hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                uint32_t N, float *d_y, uint32_t ldy, void *stream)
 {
     const bool gemm = img && N > HXQ_VQ_MATMUL_GEMV_MAX && img->has_mm;
     return hxq_cuda_vq_matmul_path(img, d_x_bf16, N, d_y, ldy, gemm ? 1 : 0, stream);
+}
+
+hxq_error_t hxq_cuda_vq_matmul_multi(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                                     uint32_t N, float *const *d_ys, uint32_t n_out,
+                                     uint32_t ldy, void *stream)
+{
+    if (!d_ys) return HXQ_ERR_NULL_PTR;
+    if (n_out == 0 || n_out > HXQ_CUDA_MAX_PEERS) return HXQ_ERR_INVALID_ARG;
+    hxq::OutPtrs o{};
+    for (uint32_t k = 0; k < n_out; ++k) o.y[k] = d_ys[k];
+    o.n = n_out;
+    const bool gemm = img && N > HXQ_VQ_MATMUL_GEMV_MAX && img->has_mm;
+    return vq_matmul(img, d_x_bf16, N, o, ldy, gemm ? 1 : 0, stream);
 }
 
 hxq_error_t hxq_cuda_stream_synchronize(void *stream)

@@ -41,7 +41,7 @@ struct GemvArgs {
     const uint32_t *chunk_ptr;   // first sidecar entry of each 2048-weight chunk
     const SideEntry *ent;        // sidecar entries, sorted by position
     const uint16_t *x;           // bf16 [ntok, in_f]
-    float *y;                    // [ntok, ldy]
+    OutPtrs out;                 // [ntok, ldy] each
     uint32_t rows, in_f, ntok, ldy, n_chunks;
 };
 
@@ -208,7 +208,8 @@ vq_gemv_kernel(const __grid_constant__ GemvArgs a)
                 float v = acc[t];
 #pragma unroll
                 for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-                if (lane == 0 && (uint32_t)t < a.ntok) a.y[(size_t)t * a.ldy + o] = v;
+                if (lane == 0 && (uint32_t)t < a.ntok)
+                    for (uint32_t k = 0; k < a.out.n; ++k) a.out.y[k][(size_t)t * a.ldy + o] = v;
                 acc[t] = 0.0f;
             }
         }
@@ -230,7 +231,7 @@ cudaError_t configure_one(size_t smem)
 // activations would not fit the staging budget.
 cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
                            uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
-                           float *y, uint32_t ldy, int sms, cudaStream_t s)
+                           const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s)
 {
     static bool configured[64] = {};
     int dev = 0;
@@ -261,7 +262,8 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
         GemvArgs a;
         a.idx = idx; a.cb = cb; a.chunk_ptr = chunk_ptr; a.ent = ent;
         a.x = x + (size_t)n0 * in_f;
-        a.y = y + (size_t)n0 * ldy;
+        a.out = out;
+        for (uint32_t k = 0; k < out.n; ++k) a.out.y[k] = out.y[k] + (size_t)n0 * ldy;
         a.rows = rows; a.in_f = in_f; a.ntok = nt; a.ldy = ldy; a.n_chunks = n_chunks;
         const size_t smem = base + (xs ? (size_t)nt * row_x : 0u);
         // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA), at most 3

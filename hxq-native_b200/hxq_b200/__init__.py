@@ -132,6 +132,15 @@ SIGNATURES = {
     "hxq_cuda_affine_device_status": (C.c_int, []),
     "hxq_cuda_vq_matmul": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, P]),
     "hxq_cuda_image_create_ex": (C.c_int, [TP, C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(P)]),
+    "hxq_cuda_vq_matmul_multi": (C.c_int, [P, P, C.c_uint32, C.POINTER(P), C.c_uint32, C.c_uint32, P]),
+    "hxq_affine_group_matmul_bf16_multi": (C.c_int, [P, C.POINTER(AffineTensor), C.POINTER(P), C.c_uint32,
+                                                     C.c_uint32, C.c_uint32, P]),
+    "hxq_cuda_ipc_alloc": (C.c_int, [C.c_size_t, C.POINTER(P), P]),
+    "hxq_cuda_ipc_open": (C.c_int, [P, C.POINTER(P)]),
+    "hxq_cuda_ipc_close": (C.c_int, [P]),
+    "hxq_cuda_ipc_free": (C.c_int, [P]),
+    "hxq_cuda_peer_signal": (C.c_int, [C.POINTER(P), C.c_uint32, C.c_uint32, P, P]),
+    "hxq_cuda_peer_wait": (C.c_int, [P, C.c_uint32, P, P, P]),
     "hxq_cuda_image_has_matmul_tables": (C.c_int, [P]),
     "hxq_cuda_vq_matmul_path": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, C.c_int, P]),
 }

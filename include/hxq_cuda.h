@@ -228,6 +228,46 @@ hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_
 hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                     uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream);
 
+/* -- Outputs shared across the GPUs of one node ---------------------------
+ * For a matmul whose output features are split over the ranks of one node:
+ * every rank's output buffer is mapped into every other rank (CUDA IPC), the
+ * matmul stores each output element into all of them (the *_multi entry
+ * points), and a step's flags tell each rank when all peers' shards have
+ * landed.  No reference counterpart (the reference has no multi-GPU code).
+ *   hxq_cuda_ipc_alloc: cudaMalloc + zero fill + IPC handle (64 bytes);
+ *   hxq_cuda_ipc_open / _close: map / unmap a peer's allocation;
+ *   hxq_cuda_peer_signal: after this step's matmuls on `stream`, add one to
+ *     *d_counter (this rank's step count, device memory) and store it, after
+ *     a system-scope fence, into slot `rank` of every rank's flag array
+ *     (peer_flags[p] = rank p's flags, mapped here; host array of world
+ *     device pointers);
+ *   hxq_cuda_peer_wait: on `stream`, wait until every slot of this rank's
+ *     flags has reached *d_counter; bounded (about two seconds), then sets
+ *     *d_status nonzero and returns.
+ * Use two output buffers alternately (by step parity) so a rank never
+ * overwrites outputs a peer may still be reading. */
+#define HXQ_CUDA_MAX_PEERS 8
+hxq_error_t hxq_cuda_ipc_alloc(size_t bytes, void **d_ptr, void *handle);
+hxq_error_t hxq_cuda_ipc_open(const void *handle, void **d_peer);
+hxq_error_t hxq_cuda_ipc_close(void *d_peer);
+hxq_error_t hxq_cuda_ipc_free(void *d_ptr);
+hxq_error_t hxq_cuda_peer_signal(uint32_t *const *peer_flags, uint32_t world, uint32_t rank,
+                                 uint32_t *d_counter, void *stream);
+hxq_error_t hxq_cuda_peer_wait(const uint32_t *d_flags, uint32_t world, const uint32_t *d_counter,
+                               uint32_t *d_status, void *stream);
+
+/* The fused matmuls with the same result stored into n_out buffers
+ * (n_out <= HXQ_CUDA_MAX_PEERS; d_ys is a host array of device pointers,
+ * local or peer-mapped), each [N, ldy]: output o of token n at
+ * d_ys[k][n * ldy + o]. */
+hxq_error_t hxq_cuda_vq_matmul_multi(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
+                                     uint32_t N, float *const *d_ys, uint32_t n_out,
+                                     uint32_t ldy, void *stream);
+int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
+                                       const hxq_affine_tensor_t *tensor,
+                                       float *const *d_ys, uint32_t n_out,
+                                       uint32_t ldy, uint32_t N, void *stream);
+
 /* fp32 activations on a caller stream. */
 int hxq_affine_group_matmul_async(const float *d_x,
                                   const hxq_affine_tensor_t *tensor,

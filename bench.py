@@ -581,16 +581,34 @@ def run_fused_matmul_workload(args):
                                                           C.c_void_p(stream.cuda_stream)) != 0:
                     raise RuntimeError("affine matmul failed")
 
+            aff_tensors = (H.AffineTensor * len(mats))(*[m["aff"] for m in mats])
+            vq_imgs = (C.c_void_p * len(mats))(*[m["img"].value for m in mats])
+            aff_xs = (C.c_void_p * len(mats))(*[(x11 if m["I"] == 11008 else x4).data_ptr() for m in mats])
+
+            def matmuls(outs_per_matrix, ldys):
+                """The layer's seven matmuls as one batch call."""
+                n_out = len(outs_per_matrix[0])
+                if fmt == "vq12":
+                    Y = (C.c_void_p * (len(mats) * n_out))(*[p for outs in outs_per_matrix for p in outs])
+                    LD = (C.c_uint32 * len(mats))(*ldys)
+                    H.check(L.hxq_cuda_vq_matmul_batch(len(mats), vq_imgs, aff_xs, Y, n_out, LD, N,
+                                                       C.c_void_p(stream.cuda_stream)), "vq matmul batch")
+                    return
+                Y = (C.c_void_p * (len(mats) * n_out))(*[p for outs in outs_per_matrix for p in outs])
+                LD = (C.c_uint32 * len(mats))(*ldys)
+                if L.hxq_affine_group_matmul_bf16_batch(len(mats), aff_tensors, aff_xs, Y, n_out, LD, N,
+                                                        C.c_void_p(stream.cuda_stream)) != 0:
+                    raise RuntimeError("affine matmul batch failed")
+
             def step_nccl(k):
-                for m, y, g in zip(mats, ys, gathered):
-                    matmul(m, [y.data_ptr()], m["rows"])
-                    if world > 1:
+                matmuls([[y.data_ptr()] for y in ys], [m["rows"] for m in mats])
+                if world > 1:
+                    for y, g in zip(ys, gathered):
                         dist.all_gather_into_tensor(g, y)
 
             def step_p2p(k):
-                for j, m in enumerate(mats):
-                    targets = [b + 4 * m["r0"] for b in p2p["bufs"][2 * j + (k & 1)]]
-                    matmul(m, targets, m["O"])
+                matmuls([[b + 4 * m["r0"] for b in p2p["bufs"][2 * j + (k & 1)]] for j, m in enumerate(mats)],
+                        [m["O"] for m in mats])
                 H.check(L.hxq_cuda_peer_signal(p2p["flags"], world, rank, p2p["counter"].data_ptr(),
                                                C.c_void_p(stream.cuda_stream)), "peer signal")
                 H.check(L.hxq_cuda_peer_wait(p2p["flags"][rank], world, p2p["counter"].data_ptr(),

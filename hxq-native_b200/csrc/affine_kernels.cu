@@ -208,6 +208,140 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
     }
 }
 
+// One-token GEMV over a batch of matrices (a layer's projections, or one
+// matrix): the rows of all jobs form one sequence that the warps take
+// grid-stride (one row per warp at a time, the 4 KB passes as above), so a
+// launch carries every matrix of the batch and its fixed costs (launch,
+// ramp-up, tail) are paid once.  Each warp keeps the next two of its rows in
+// flight to L2 by bulk prefetch, a window that stays far below L2 whatever
+// the batch size.  Same arithmetic, order and results as the one-token path
+// of affine_gemv_kernel.
+constexpr uint32_t kMaxGemvJobs = 8;
+
+struct GemvJob {
+    const void *x;              // activations of this matrix, one token
+    const uint8_t *codes;       // [out_f, in_f]
+    const float *scales, *offsets, *bias;
+    OutPtrs out;                // each output: o at out.y[k][o]
+    uint32_t in_f, out_f, gs, gs_shift, ng;
+    uint32_t row_begin;         // first row of the job in the batch's sequence
+};
+
+struct GemvJobs {
+    GemvJob job[kMaxGemvJobs];
+    uint32_t n, total_rows;
+};
+
+template <typename XT>
+__global__ void __launch_bounds__(256, 4)
+affine_gemv_jobs_kernel(const __grid_constant__ GemvJobs J)
+{
+    constexpr int SPL = 8;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    auto job_of = [&](uint32_t r) {
+        uint32_t j = 0;
+        while (j + 1u < J.n && r >= J.job[j + 1u].row_begin) ++j;
+        return j;
+    };
+    auto prefetch = [&](uint32_t r) {
+        if (lane == 0 && r < J.total_rows) {
+            const GemvJob &b = J.job[job_of(r)];
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                         ::"l"(b.codes + (size_t)(r - b.row_begin) * b.in_f), "r"(b.in_f) : "memory");
+        }
+    };
+    prefetch(gw);
+    prefetch(gw + warps);
+    bool waited = false;
+    for (uint32_t r = gw; r < J.total_rows; r += warps) {
+        prefetch(r + 2u * warps);
+        const GemvJob &b = J.job[job_of(r)];
+        const uint32_t o = r - b.row_begin;
+        const uint32_t in_f = b.in_f, gs = b.gs, gs_shift = b.gs_shift, ng = b.ng;
+        const uint32_t slices = in_f / 16u;
+        const uint4 *crow = reinterpret_cast<const uint4 *>(b.codes + (size_t)o * in_f);
+        const XT *x = static_cast<const XT *>(b.x);
+        float acc = 0.0f;
+        for (uint32_t base = 0; base < slices; base += 32u * SPL) {
+            uint4 cw[SPL];
+#pragma unroll
+            for (int i = 0; i < SPL; ++i) {
+                const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                if (sl < slices) cw[i] = __ldg(crow + sl);
+            }
+            const uint32_t g0 = group_of(base, gs, gs_shift);
+            const uint32_t g1 = group_of(min(base + 32u * SPL, slices) - 1u, gs, gs_shift) + 1u;
+            const bool by_lane = g1 - g0 <= 32u;
+            float s_l = 0.0f, f_l = 0.0f;
+            if (by_lane && g0 + lane < g1) {
+                s_l = __ldg(b.scales + (size_t)o * ng + g0 + lane);
+                f_l = __ldg(b.offsets + (size_t)o * ng + g0 + lane);
+            }
+            if (!waited) {   // activations and outputs follow the kernel before this one
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                waited = true;
+            }
+#pragma unroll
+            for (int i = 0; i < SPL; ++i) {
+                const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                const uint32_t g = group_of(sl < slices ? sl : slices - 1u, gs, gs_shift);
+                float sv_i, fv_i;
+                if (by_lane) {
+                    sv_i = __shfl_sync(0xffffffffu, s_l, (g - g0) & 31u);
+                    fv_i = __shfl_sync(0xffffffffu, f_l, (g - g0) & 31u);
+                } else {
+                    sv_i = __ldg(b.scales + (size_t)o * ng + g);
+                    fv_i = __ldg(b.offsets + (size_t)o * ng + g);
+                }
+                if (sl >= slices) continue;
+                const uint32_t w[4] = {cw[i].x, cw[i].y, cw[i].z, cw[i].w};
+                float xv[16];
+                XLoad<XT>::load16(x + (size_t)sl * 16u, xv);
+                float dot = 0.0f, xsum = 0.0f;
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        dot = fmaf(xv[4 * m + c], code_to_float(w[m], (uint32_t)c), dot);
+                        xsum += xv[4 * m + c];
+                    }
+                acc = fmaf(sv_i, dot, fmaf(fv_i, xsum, acc));
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+        if (lane == 0) {
+            const float bo = b.bias ? __ldg(b.bias + o) : 0.0f;
+            for (uint32_t k = 0; k < b.out.n; ++k) b.out.y[k][o] = acc + bo;
+        }
+    }
+    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename XT>
+int launch_gemv_jobs(const GemvJobs &J, int sms, cudaStream_t s)
+{
+    if (J.n == 0 || J.total_rows == 0) return 0;
+    uint32_t blocks = (J.total_rows + 7u) / 8u;
+    const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * 4u;
+    if (blocks > cap) blocks = cap;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, affine_gemv_jobs_kernel<XT>, J) != cudaSuccess) { cudaGetLastError(); return -1; }
+    return 0;
+}
+
 // Any shape: one thread per output, the reference's loop order.
 template <typename XT>
 __global__ void affine_generic_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
@@ -278,6 +412,13 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         if (blocks > cap) blocks = cap;
         constexpr uint32_t kXsFloats = 12288;  // 48 KB of staged activations
         const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
+        if (N == 1) {
+            GemvJobs J{};
+            J.job[0] = GemvJob{x, codes, scales, offsets, bias, out, in_f, out_f, gs, gs_shift, in_f / gs, 0u};
+            J.n = 1;
+            J.total_rows = out_f;
+            return launch_gemv_jobs<XT>(J, sms, s);
+        }
         for (uint32_t n0 = 0; n0 < N; n0 += kGemvTokens) {
             const uint32_t nt = N - n0 < (uint32_t)kGemvTokens ? N - n0 : (uint32_t)kGemvTokens;
             // one token: activations through L1 (staging would cost more than it saves)
@@ -363,6 +504,64 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16, const hxq_affin
     return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias, o, ldy, N,
                                      t->in_features, t->out_features, t->group_size,
                                      static_cast<cudaStream_t>(stream));
+}
+
+int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *tensors,
+                                       const uint16_t *const *d_xs, float *const *d_ys, uint32_t n_out,
+                                       const uint32_t *ldys, uint32_t N, void *stream)
+{
+    if (n == 0 || N == 0) return 0;
+    if (!tensors || !d_xs || !d_ys || !ldys || n_out == 0 || n_out > HXQ_CUDA_MAX_PEERS) return -1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    auto outs_of = [&](uint32_t i, hxq::OutPtrs &o) {
+        o = hxq::OutPtrs{};
+        for (uint32_t k = 0; k < n_out; ++k) {
+            o.y[k] = d_ys[(size_t)i * n_out + k];
+            if (!o.y[k]) return false;
+        }
+        o.n = n_out;
+        return true;
+    };
+    // one token: every matrix whose shape suits the batched GEMV goes into
+    // launches of up to 8 matrices; the rest one call each
+    bool all_fast = N == 1;
+    for (uint32_t i = 0; i < n && all_fast; ++i) {
+        const hxq_affine_tensor_t &t = tensors[i];
+        all_fast = t.indices && t.scales && t.offsets && d_xs[i] && t.group_size && t.in_features &&
+                   t.group_size % 16u == 0 && t.in_features % t.group_size == 0 && t.in_features % 16u == 0 &&
+                   ldys[i] >= t.out_features && hxq::aligned(d_xs[i], 16) && hxq::aligned(t.indices, 16);
+    }
+    if (all_fast) {
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxGemvJobs) {
+            hxq::GemvJobs J{};
+            uint32_t rows = 0;
+            for (uint32_t i = i0; i < n && J.n < hxq::kMaxGemvJobs; ++i) {
+                const hxq_affine_tensor_t &t = tensors[i];
+                hxq::OutPtrs o;
+                if (!outs_of(i, o)) return -1;
+                const uint32_t gs = t.group_size;
+                const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
+                J.job[J.n++] = hxq::GemvJob{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, t.in_features,
+                                            t.out_features, gs, gs_shift, t.in_features / gs, rows};
+                rows += t.out_features;
+            }
+            J.total_rows = rows;
+            if (hxq::launch_gemv_jobs<uint16_t>(J, sms, s) != 0) return -1;
+        }
+        return 0;
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        const hxq_affine_tensor_t &t = tensors[i];
+        hxq::OutPtrs o;
+        if (!outs_of(i, o)) return -1;
+        const int r = hxq::run_affine<uint16_t>(d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, ldys[i], N,
+                                                t.in_features, t.out_features, t.group_size, s);
+        if (r != 0) return r;
+    }
+    return 0;
 }
 
 int hxq_affine_group_matmul_async(const float *d_x, const hxq_affine_tensor_t *t,

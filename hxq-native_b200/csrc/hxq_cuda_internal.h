@@ -135,6 +135,17 @@ struct OutPtrs {
 
 // Fused VQ-dequant matmul on 12-bit images with k = 4096 (vq_matmul.cu,
 // dequant_gemm.cu).  x bf16 [ntok, in_f]; outputs fp32 [ntok, ldy].
+struct VqGemvJob {
+    const uint8_t *idx;
+    const float *cb;
+    const uint32_t *chunk_ptr;
+    const SideEntry *ent;
+    uint32_t n_chunks, rows, in_f;
+    const uint16_t *x;
+    OutPtrs out;
+    uint32_t ldy;
+};
+cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t ntok, int sms, cudaStream_t s);
 cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
                            uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
                            const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s);

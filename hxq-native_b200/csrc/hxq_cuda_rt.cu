@@ -1112,6 +1112,63 @@ hxq_error_t hxq_cuda_vq_matmul_multi(const hxq_cuda_image_t *img, const uint16_t
     return vq_matmul(img, d_x_bf16, N, o, ldy, gemm ? 1 : 0, stream);
 }
 
+hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, const uint16_t *const *d_xs,
+                                     float *const *d_ys, uint32_t n_out, const uint32_t *ldys, uint32_t N,
+                                     void *stream)
+{
+    if (n == 0 || N == 0) return HXQ_OK;
+    if (!imgs || !d_xs || !d_ys || !ldys) return HXQ_ERR_NULL_PTR;
+    if (n_out == 0 || n_out > HXQ_CUDA_MAX_PEERS) return HXQ_ERR_INVALID_ARG;
+    auto outs_of = [&](uint32_t i, hxq::OutPtrs &o) -> hxq_error_t {
+        o = hxq::OutPtrs{};
+        for (uint32_t k = 0; k < n_out; ++k) {
+            o.y[k] = d_ys[(size_t)i * n_out + k];
+            if (!o.y[k]) return HXQ_ERR_NULL_PTR;
+        }
+        o.n = n_out;
+        return HXQ_OK;
+    };
+    if (N > HXQ_VQ_MATMUL_GEMV_MAX) {
+        for (uint32_t i = 0; i < n; ++i) {
+            hxq::OutPtrs o;
+            hxq_error_t err = outs_of(i, o);
+            if (err != HXQ_OK) return err;
+            err = vq_matmul(imgs[i], d_xs[i], N, o, ldys[i], imgs[i] && imgs[i]->has_mm ? 1 : 0, stream);
+            if (err != HXQ_OK) return err;
+        }
+        return HXQ_OK;
+    }
+    int dev = 0;
+    hxq_error_t err = current_device(&dev);
+    if (err != HXQ_OK) return err;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if ((err = dev_ready(dev)) != HXQ_OK) return err;
+    }
+    std::vector<hxq::VqGemvJob> jobs;
+    jobs.reserve(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const hxq_cuda_image_t *img = imgs[i];
+        if (!img || !d_xs[i]) return HXQ_ERR_NULL_PTR;
+        if (img->kind != kKindVq12 || img->check_k || img->k != 4096u || img->in_f % 64u != 0u || !img->d_block ||
+            img->device != dev || ldys[i] < img->rows || !aligned16(d_xs[i]))
+            return HXQ_ERR_INVALID_ARG;
+        hxq::OutPtrs o;
+        if ((err = outs_of(i, o)) != HXQ_OK) return err;
+        if (img->rows == 0) continue;
+        jobs.push_back(hxq::VqGemvJob{img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent, img->n_chunks, img->rows,
+                                      img->in_f, d_xs[i], o, ldys[i]});
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (size_t j0 = 0; j0 < jobs.size(); j0 += 8) {
+        const uint32_t cnt = (uint32_t)std::min<size_t>(8, jobs.size() - j0);
+        const cudaError_t e = hxq::launch_vq_gemv_batch(cnt, jobs.data() + j0, N, g_dev[dev].sms, s);
+        if (e != cudaSuccess) return map_cuda(e);
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    return HXQ_OK;
+}
+
 hxq_error_t hxq_cuda_stream_synchronize(void *stream)
 {
     int dev = 0;

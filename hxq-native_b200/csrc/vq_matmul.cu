@@ -19,6 +19,7 @@
 // not depend on the kernel before it; the activations do).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "hxq_cuda_internal.h"
@@ -43,6 +44,15 @@ struct GemvArgs {
     const uint16_t *x;           // bf16 [ntok, in_f]
     OutPtrs out;                 // [ntok, ldy] each
     uint32_t rows, in_f, ntok, ldy, n_chunks;
+    uint32_t cta_begin, n_ctas;  // the CTAs of the launch that serve this matrix
+};
+
+// A launch covers up to kMaxVqJobs matrices; each CTA serves one of them
+// (a contiguous range of its rows), so it stages one codebook.
+constexpr uint32_t kMaxVqJobs = 8;
+struct GemvBatch {
+    GemvArgs job[kMaxVqJobs];
+    uint32_t n;
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p)
@@ -66,9 +76,12 @@ __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w 
 // XS: activations staged in shared memory (else read through L1).
 template <int NT, bool XS>
 __global__ void __launch_bounds__(kGvThreads, 3)
-vq_gemv_kernel(const __grid_constant__ GemvArgs a)
+vq_gemv_kernel(const __grid_constant__ GemvBatch B)
 {
     extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t jb = 0;
+    while (jb + 1u < B.n && blockIdx.x >= B.job[jb + 1u].cta_begin) ++jb;
+    const GemvArgs &a = B.job[jb];
     float2 *cb = reinterpret_cast<float2 *>(smem);
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     uint4 *ring = reinterpret_cast<uint4 *>(smem + kGvCbBytes) + warp * kGvStages * kPieceVec;
@@ -77,9 +90,13 @@ vq_gemv_kernel(const __grid_constant__ GemvArgs a)
     const uint32_t row_trip = a.in_f / 4u;             // in_f % 64 == 0: whole 16-B copies
     const size_t row_bytes = (size_t)row_trip * 3u;
     const uint32_t P = (row_trip + kPieceTrip - 1u) / kPieceTrip;
-    const uint32_t stride = gridDim.x * kGvWarps;
-    const uint32_t first = blockIdx.x * kGvWarps + warp;
-    const uint32_t my_rows = first < a.rows ? (a.rows - first + stride - 1u) / stride : 0u;
+    // this CTA's rows of the matrix, taken by its warps in turn
+    const uint32_t cb_i = blockIdx.x - a.cta_begin;
+    const uint32_t r_lo = (uint32_t)((uint64_t)a.rows * cb_i / a.n_ctas);
+    const uint32_t r_hi = (uint32_t)((uint64_t)a.rows * (cb_i + 1u) / a.n_ctas);
+    const uint32_t stride = kGvWarps;
+    const uint32_t first = r_lo + warp;
+    const uint32_t my_rows = first < r_hi ? (r_hi - first + stride - 1u) / stride : 0u;
     const uint32_t total = my_rows * P;
 
     auto issue = [&](uint32_t s) {
@@ -98,12 +115,16 @@ vq_gemv_kernel(const __grid_constant__ GemvArgs a)
     };
     // the next kernel on the stream may start now; this one waits for the
     // kernel before it (griddepcontrol.wait) only before it reads the
-    // activations.  The warp's rows of indices go to L2 by bulk prefetch.
+    // activations.  The warp's next two rows of indices go to L2 by bulk
+    // prefetch (a window that stays far below L2 for any batch).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (lane == 0)
-        for (uint32_t r = 0; r < my_rows; ++r)
+    auto prefetch_row = [&](uint32_t r) {
+        if (lane == 0 && r < my_rows)
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
                          ::"l"(a.idx + (size_t)(first + r * stride) * row_bytes), "r"((uint32_t)row_bytes) : "memory");
+    };
+    prefetch_row(0);
+    prefetch_row(1);
     // the first piece is in flight while the codebook and activations are staged
     issue(0);
     for (uint32_t i = tid; i < kGvCbBytes / 16u; i += kGvThreads)
@@ -131,6 +152,7 @@ vq_gemv_kernel(const __grid_constant__ GemvArgs a)
         const uint64_t f0 = (uint64_t)o * a.in_f;
         const uint32_t ch0 = (uint32_t)(f0 / kChunkW);
         if (pc == 0) {
+            prefetch_row(s / P + 2u);
             uint32_t ch1 = (uint32_t)((f0 + a.in_f - 1u) / kChunkW) + 1u;
             ch1 = ch1 < a.n_chunks ? ch1 : a.n_chunks;
             nc = ch1 - ch0;
@@ -226,20 +248,21 @@ cudaError_t configure_one(size_t smem)
 
 }  // namespace
 
-// Fused VQ GEMV: 12-bit images with k = 4096 and in_f % 64 == 0, 16-byte
-// aligned x and index rows; up to 8 tokens per pass, fewer when their
-// activations would not fit the staging budget.
-cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
-                           uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
-                           const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s)
+// Fused VQ GEMV over a batch of 12-bit images (k = 4096, in_f % 64 == 0,
+// 16-byte aligned x and index rows); up to 8 tokens per pass, fewer when
+// their activations would not fit the staging budget.  The launch's CTAs
+// are shared out over the images in proportion to their index bytes.
+cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t ntok, int sms, cudaStream_t s)
 {
-    static bool configured[64] = {};
+    static std::atomic<uint64_t> configured{0};   // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (n == 0 || ntok == 0) return cudaSuccess;
+    if (n > kMaxVqJobs) return cudaErrorInvalidValue;
     const size_t base = kGvCbBytes + kGvRingBytes;
-    if (!configured[dev]) {
+    if (!(configured.load(std::memory_order_acquire) & (1ull << dev))) {
         const size_t mx = base + kGvXsBytesMax;
         e = configure_one<1, true>(mx);
         if (e == cudaSuccess) e = configure_one<2, true>(mx);
@@ -250,30 +273,46 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
         if (e == cudaSuccess) e = configure_one<4, false>(base);
         if (e == cudaSuccess) e = configure_one<8, false>(base);
         if (e != cudaSuccess) return e;
-        configured[dev] = true;
+        configured.fetch_or(1ull << dev, std::memory_order_acq_rel);
     }
-    if (rows == 0 || ntok == 0) return cudaSuccess;
-    const size_t row_x = (size_t)in_f * 2u;
+    uint32_t max_in = 0;
+    double total_bytes = 0.0;
+    for (uint32_t i = 0; i < n; ++i) {
+        max_in = jobs[i].in_f > max_in ? jobs[i].in_f : max_in;
+        total_bytes += (double)jobs[i].rows * jobs[i].in_f;
+    }
+    const size_t row_x = (size_t)max_in * 2u;
     const uint32_t fit = (uint32_t)(kGvXsBytesMax / row_x);      // tokens whose activations fit
     const bool xs = fit >= 1u;
     const uint32_t per_pass = xs ? (fit < 8u ? fit : 8u) : 8u;
     for (uint32_t n0 = 0; n0 < ntok; n0 += per_pass) {
         const uint32_t nt = ntok - n0 < per_pass ? ntok - n0 : per_pass;
-        GemvArgs a;
-        a.idx = idx; a.cb = cb; a.chunk_ptr = chunk_ptr; a.ent = ent;
-        a.x = x + (size_t)n0 * in_f;
-        a.out = out;
-        for (uint32_t k = 0; k < out.n; ++k) a.out.y[k] = out.y[k] + (size_t)n0 * ldy;
-        a.rows = rows; a.in_f = in_f; a.ntok = nt; a.ldy = ldy; a.n_chunks = n_chunks;
         const size_t smem = base + (xs ? (size_t)nt * row_x : 0u);
         // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA), at most 3
         uint32_t per_sm = (uint32_t)(233472u / (smem + 1024u));
         per_sm = per_sm > 3u ? 3u : per_sm < 1u ? 1u : per_sm;
-        uint32_t blocks = (rows + kGvWarps - 1u) / kGvWarps;
-        const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
-        if (blocks > cap) blocks = cap;
+        const uint32_t G = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
+        GemvBatch B{};
+        B.n = n;
+        uint32_t cta = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+            const VqGemvJob &j = jobs[i];
+            GemvArgs &a = B.job[i];
+            a.idx = j.idx; a.cb = j.cb; a.chunk_ptr = j.chunk_ptr; a.ent = j.ent;
+            a.x = j.x + (size_t)n0 * j.in_f;
+            a.out = j.out;
+            for (uint32_t k = 0; k < j.out.n; ++k) a.out.y[k] = j.out.y[k] + (size_t)n0 * j.ldy;
+            a.rows = j.rows; a.in_f = j.in_f; a.ntok = nt; a.ldy = j.ldy; a.n_chunks = j.n_chunks;
+            // CTAs in proportion to the matrix's bytes, at least one, at most one per 8 rows
+            uint32_t c = (uint32_t)((double)G * ((double)j.rows * j.in_f) / total_bytes + 0.5);
+            const uint32_t cmax = (j.rows + kGvWarps - 1u) / kGvWarps;
+            c = c < 1u ? 1u : c > cmax ? cmax : c;
+            a.cta_begin = cta;
+            a.n_ctas = c;
+            cta += c;
+        }
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(blocks);
+        cfg.gridDim = dim3(cta);
         cfg.blockDim = dim3(kGvThreads);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = s;
@@ -282,15 +321,23 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        void (*kern)(GemvArgs) = nullptr;
+        void (*kern)(GemvBatch) = nullptr;
         if (nt == 1) kern = xs ? vq_gemv_kernel<1, true> : vq_gemv_kernel<1, false>;
         else if (nt == 2) kern = xs ? vq_gemv_kernel<2, true> : vq_gemv_kernel<2, false>;
         else if (nt <= 4) kern = xs ? vq_gemv_kernel<4, true> : vq_gemv_kernel<4, false>;
         else kern = xs ? vq_gemv_kernel<8, true> : vq_gemv_kernel<8, false>;
-        e = cudaLaunchKernelEx(&cfg, kern, a);
+        e = cudaLaunchKernelEx(&cfg, kern, B);
         if (e != cudaSuccess) { cudaGetLastError(); return e; }
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
+                           uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
+                           const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s)
+{
+    VqGemvJob j{idx, cb, chunk_ptr, ent, n_chunks, rows, in_f, x, out, ldy};
+    return launch_vq_gemv_batch(1, &j, ntok, sms, s);
 }
 
 }  // namespace hxq

@@ -135,6 +135,10 @@ SIGNATURES = {
     "hxq_cuda_vq_matmul_multi": (C.c_int, [P, P, C.c_uint32, C.POINTER(P), C.c_uint32, C.c_uint32, P]),
     "hxq_affine_group_matmul_bf16_multi": (C.c_int, [P, C.POINTER(AffineTensor), C.POINTER(P), C.c_uint32,
                                                      C.c_uint32, C.c_uint32, P]),
+    "hxq_cuda_vq_matmul_batch": (C.c_int, [C.c_uint32, C.POINTER(P), C.POINTER(P), C.POINTER(P), C.c_uint32,
+                                           C.POINTER(C.c_uint32), C.c_uint32, P]),
+    "hxq_affine_group_matmul_bf16_batch": (C.c_int, [C.c_uint32, C.POINTER(AffineTensor), C.POINTER(P), C.POINTER(P),
+                                                     C.c_uint32, C.POINTER(C.c_uint32), C.c_uint32, P]),
     "hxq_cuda_ipc_alloc": (C.c_int, [C.c_size_t, C.POINTER(P), P]),
     "hxq_cuda_ipc_open": (C.c_int, [P, C.POINTER(P)]),
     "hxq_cuda_ipc_close": (C.c_int, [P]),

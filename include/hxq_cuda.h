@@ -267,6 +267,24 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
                                        const hxq_affine_tensor_t *tensor,
                                        float *const *d_ys, uint32_t n_out,
                                        uint32_t ldy, uint32_t N, void *stream);
+/* A batch of n affine matmuls (e.g. a layer's projections) with bf16
+ * activations d_xs[i] ([N, in_features of tensor i]) and outputs
+ * d_ys[i * n_out + k] ([N, ldys[i]], k < n_out).  At one token, matrices
+ * whose shapes suit the streaming GEMV share launches (up to 8 per launch),
+ * which pays the per-launch costs once for the batch; otherwise one call
+ * per matrix.  Returns 0, or -1 on an error. */
+/* A batch of n fused VQ matmuls (e.g. a layer's projections), outputs as
+ * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_GEMV_MAX
+ * tokens the GEMV shares launches (up to 8 images per launch); more tokens
+ * run one call per image (the GEMM for images with matmul tables). */
+hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs,
+                                     const uint16_t *const *d_xs, float *const *d_ys,
+                                     uint32_t n_out, const uint32_t *ldys, uint32_t N,
+                                     void *stream);
+int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *tensors,
+                                       const uint16_t *const *d_xs, float *const *d_ys,
+                                       uint32_t n_out, const uint32_t *ldys, uint32_t N,
+                                       void *stream);
 
 /* fp32 activations on a caller stream. */
 int hxq_affine_group_matmul_async(const float *d_x,

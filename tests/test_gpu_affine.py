@@ -190,3 +190,34 @@ def test_invalid_arguments(H, L, cuda):
     t.group_size = 96  # does not divide 128
     assert L.hxq_affine_group_matmul(x.data_ptr(), C.byref(t), y.data_ptr(), 1) == -1
     assert L.hxq_affine_group_matmul(x.data_ptr(), None, y.data_ptr(), 1) == -1
+
+
+@pytest.mark.parametrize("N", [1, 5])
+def test_batch_of_layer_projections(H, L, cuda, N):
+    """A layer's projections in one batch call (shared launches at one
+    token), two outputs each at a column offset: bit-identical to one call
+    per matrix."""
+    torch = cuda
+    shapes = [(512, 4096), (256, 4096), (256, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
+    devs, xs, refs, outs, ts = [], [], [], [], []
+    for i, (O, I) in enumerate(shapes):
+        d = synth.affine(O, I, 128, 100 + i, bias=(i % 2 == 0))
+        dev = Dev(torch, d, d["bias"])
+        xh, _ = synth.activations(N, I, 200 + i)
+        x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+        ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+        assert L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(dev.tensor(H)), ref.data_ptr(), N, None) == 0
+        devs.append(dev); xs.append(x); refs.append(ref); ts.append(dev.tensor(H))
+        outs.append([torch.full((N, O + 64), float("nan"), dtype=torch.float32, device="cuda") for _ in range(2)])
+    n = len(shapes)
+    T = (H.AffineTensor * n)(*ts)
+    X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+    Y = (C.c_void_p * (2 * n))(*[o.data_ptr() + 4 * 32 for pair in outs for o in pair])
+    LD = (C.c_uint32 * n)(*[O + 64 for O, _ in shapes])
+    assert L.hxq_affine_group_matmul_bf16_batch(n, T, X, Y, 2, LD, N, None) == 0
+    torch.cuda.synchronize()
+    for (O, _), ref, pair in zip(shapes, refs, outs):
+        for o in pair:
+            assert torch.equal(o[:, 32:32 + O].contiguous().view(torch.int32), ref.view(torch.int32))
+            assert bool(torch.isnan(o[:, :32]).all()) and bool(torch.isnan(o[:, 32 + O:]).all())
+    assert L.hxq_cuda_affine_device_status() == 0

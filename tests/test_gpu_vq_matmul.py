@@ -246,3 +246,39 @@ def test_invalid_images_and_arguments(H, L, cuda):
     cuda.cuda.synchronize()
     bad = C.c_void_p()
     assert L.hxq_cuda_image_create_ex(t.ref, 0, 64, 8, C.byref(bad)) == H.HXQ_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("N", [1, 3, 16])
+def test_batch_of_layer_projections(H, L, oracle, cuda, N):
+    """A layer's projections (row shards of 7B shapes) in one batch call, two
+    outputs each at a column offset: bit-identical to one call per image."""
+    torch = cuda
+    shapes = [(512, 4096), (256, 4096), (384, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
+    imgs, xs, refs, outs = [], [], [], []
+    try:
+        for i, (O, I) in enumerate(shapes):
+            d = _with_dups_and_oob(synth.vq12(O, I, 300 + i), 300 + i)
+            t = H.Tensor().load(d)
+            img = _image(H, L, t, 0, O)
+            imgs.append((img, t))
+            xh, _ = synth.activations(N, I, 400 + i)
+            x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+            ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+            assert L.hxq_cuda_vq_matmul(img, x.data_ptr(), N, ref.data_ptr(), O, None) == 0
+            xs.append(x); refs.append(ref)
+            outs.append([torch.full((N, O + 32), float("nan"), dtype=torch.float32, device="cuda") for _ in range(2)])
+        n = len(shapes)
+        IM = (C.c_void_p * n)(*[im.value for im, _ in imgs])
+        X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+        Y = (C.c_void_p * (2 * n))(*[o.data_ptr() + 4 * 16 for pair in outs for o in pair])
+        LD = (C.c_uint32 * n)(*[O + 32 for O, _ in shapes])
+        assert L.hxq_cuda_vq_matmul_batch(n, IM, X, Y, 2, LD, N, None) == 0
+        torch.cuda.synchronize()
+        for (O, _), ref, pair in zip(shapes, refs, outs):
+            for o in pair:
+                assert torch.equal(o[:, 16:16 + O].contiguous().view(torch.int32), ref.view(torch.int32))
+                assert bool(torch.isnan(o[:, :16]).all()) and bool(torch.isnan(o[:, 16 + O:]).all())
+        assert L.hxq_cuda_affine_device_status() == 0
+    finally:
+        for im, _ in imgs:
+            L.hxq_cuda_image_destroy(im)

@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "hxq_affine.h"
@@ -209,14 +210,19 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
 }
 
 // One-token GEMV over a batch of matrices (a layer's projections, or one
-// matrix): the rows of all jobs form one sequence that the warps take
-// grid-stride (one row per warp at a time, the 4 KB passes as above), so a
-// launch carries every matrix of the batch and its fixed costs (launch,
-// ramp-up, tail) are paid once.  Each warp keeps the next two of its rows in
-// flight to L2 by bulk prefetch, a window that stays far below L2 whatever
-// the batch size.  Same arithmetic, order and results as the one-token path
-// of affine_gemv_kernel.
+// matrix).  The rows of all jobs form one sequence; each CTA owns a
+// contiguous range of it holding an equal share of the codes (so at most a
+// few jobs), stages the job's
+// activations once in shared memory as fp32 planes laid out for
+// conflict-free 16-byte reads, with the sum of every 16-activation slice,
+// and its warps take the range's rows in turn: 16 codes per lane per 128-bit
+// load, a row's 4 KB pass in flight at once, the next two of the warp's rows
+// sent to L2 by bulk prefetch.  Per slice: 16 byte-permute code widenings,
+// 16 fp32 FMAs against the staged activations, the group scale times the
+// dot and the group offset times the slice sum.  A launch carries every
+// matrix of the batch, so launch, ramp-up and tail are paid once.
 constexpr uint32_t kMaxGemvJobs = 8;
+constexpr size_t kGemvStageMax = 200u * 1024u;   // staged activations + slice sums
 
 struct GemvJob {
     const void *x;              // activations of this matrix, one token
@@ -225,98 +231,129 @@ struct GemvJob {
     OutPtrs out;                // each output: o at out.y[k][o]
     uint32_t in_f, out_f, gs, gs_shift, ng;
     uint32_t row_begin;         // first row of the job in the batch's sequence
+    uint64_t code_begin;        // codes of the jobs before this one
 };
 
 struct GemvJobs {
     GemvJob job[kMaxGemvJobs];
     uint32_t n, total_rows;
+    uint64_t total_codes;
 };
+
+// First row of the batch sequence that starts at or after code position w.
+__device__ __forceinline__ uint32_t row_at(const GemvJobs &J, uint64_t w)
+{
+    if (w >= J.total_codes) return J.total_rows;
+    uint32_t j = 0;
+    while (j + 1u < J.n && w >= J.job[j + 1u].code_begin) ++j;
+    const GemvJob &b = J.job[j];
+    const uint64_t rows_in = (w - b.code_begin + b.in_f - 1u) / b.in_f;
+    return b.row_begin + (uint32_t)(rows_in < b.out_f ? rows_in : b.out_f);
+}
 
 template <typename XT>
 __global__ void __launch_bounds__(256, 4)
 affine_gemv_jobs_kernel(const __grid_constant__ GemvJobs J)
 {
     constexpr int SPL = 8;
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
-    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    extern __shared__ __align__(16) float xsm[];   // planes [4][slices] float4, then slice sums [slices]
+    const uint32_t lane = threadIdx.x & 31u, wib = threadIdx.x >> 5;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    auto job_of = [&](uint32_t r) {
-        uint32_t j = 0;
-        while (j + 1u < J.n && r >= J.job[j + 1u].row_begin) ++j;
-        return j;
-    };
-    auto prefetch = [&](uint32_t r) {
-        if (lane == 0 && r < J.total_rows) {
-            const GemvJob &b = J.job[job_of(r)];
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                         ::"l"(b.codes + (size_t)(r - b.row_begin) * b.in_f), "r"(b.in_f) : "memory");
-        }
-    };
-    prefetch(gw);
-    prefetch(gw + warps);
+    // this CTA's rows: an equal share of the batch's codes, cut at whole rows
+    const uint32_t r0 = row_at(J, J.total_codes * blockIdx.x / gridDim.x);
+    const uint32_t r1 = row_at(J, J.total_codes * (blockIdx.x + 1u) / gridDim.x);
+    uint32_t j = 0;
+    while (j + 1u < J.n && r0 >= J.job[j + 1u].row_begin) ++j;
     bool waited = false;
-    for (uint32_t r = gw; r < J.total_rows; r += warps) {
-        prefetch(r + 2u * warps);
-        const GemvJob &b = J.job[job_of(r)];
-        const uint32_t o = r - b.row_begin;
+    for (uint32_t seg = r0; seg < r1; ++j) {
+        const GemvJob &b = J.job[j];
+        const uint32_t seg_end = min(r1, b.row_begin + b.out_f);
         const uint32_t in_f = b.in_f, gs = b.gs, gs_shift = b.gs_shift, ng = b.ng;
         const uint32_t slices = in_f / 16u;
-        const uint4 *crow = reinterpret_cast<const uint4 *>(b.codes + (size_t)o * in_f);
-        const XT *x = static_cast<const XT *>(b.x);
-        float acc = 0.0f;
-        for (uint32_t base = 0; base < slices; base += 32u * SPL) {
-            uint4 cw[SPL];
+        const uint32_t first = seg + wib;
+        // the warp's rows of this job: first, first + 8, ... < seg_end
+        auto prefetch = [&](uint32_t r) {
+            if (lane == 0 && r < seg_end)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                             ::"l"(b.codes + (size_t)(r - b.row_begin) * in_f), "r"(in_f) : "memory");
+        };
+        prefetch(first);
+        prefetch(first + 8u);
+        // stage this job's activations (the previous kernel's output)
+        if (!waited) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            waited = true;
+        }
+        __syncthreads();    // the previous job's activations are no longer read
+        float4 *planes = reinterpret_cast<float4 *>(xsm);   // 4 * slices float4 = in_f floats
+        float *ssum = xsm + in_f;                            // slices floats
+        for (uint32_t sl = threadIdx.x; sl < slices; sl += blockDim.x) {
+            float v[16];
+            XLoad<XT>::load16(static_cast<const XT *>(b.x) + (size_t)sl * 16u, v);
+            float sum = 0.0f;
 #pragma unroll
-            for (int i = 0; i < SPL; ++i) {
-                const uint32_t sl = base + (uint32_t)i * 32u + lane;
-                if (sl < slices) cw[i] = __ldg(crow + sl);
+            for (int u = 0; u < 4; ++u) {
+                planes[(size_t)u * slices + sl] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                sum += (v[4 * u] + v[4 * u + 1]) + (v[4 * u + 2] + v[4 * u + 3]);
             }
-            const uint32_t g0 = group_of(base, gs, gs_shift);
-            const uint32_t g1 = group_of(min(base + 32u * SPL, slices) - 1u, gs, gs_shift) + 1u;
-            const bool by_lane = g1 - g0 <= 32u;
-            float s_l = 0.0f, f_l = 0.0f;
-            if (by_lane && g0 + lane < g1) {
-                s_l = __ldg(b.scales + (size_t)o * ng + g0 + lane);
-                f_l = __ldg(b.offsets + (size_t)o * ng + g0 + lane);
-            }
-            if (!waited) {   // activations and outputs follow the kernel before this one
-                asm volatile("griddepcontrol.wait;" ::: "memory");
-                waited = true;
-            }
+            ssum[sl] = sum;
+        }
+        __syncthreads();
+        for (uint32_t r = first; r < seg_end; r += 8u) {
+            prefetch(r + 16u);
+            const uint32_t o = r - b.row_begin;
+            const uint4 *crow = reinterpret_cast<const uint4 *>(b.codes + (size_t)o * in_f);
+            float acc = 0.0f;
+            for (uint32_t base = 0; base < slices; base += 32u * SPL) {
+                uint4 cw[SPL];
 #pragma unroll
-            for (int i = 0; i < SPL; ++i) {
-                const uint32_t sl = base + (uint32_t)i * 32u + lane;
-                const uint32_t g = group_of(sl < slices ? sl : slices - 1u, gs, gs_shift);
-                float sv_i, fv_i;
-                if (by_lane) {
-                    sv_i = __shfl_sync(0xffffffffu, s_l, (g - g0) & 31u);
-                    fv_i = __shfl_sync(0xffffffffu, f_l, (g - g0) & 31u);
-                } else {
-                    sv_i = __ldg(b.scales + (size_t)o * ng + g);
-                    fv_i = __ldg(b.offsets + (size_t)o * ng + g);
+                for (int i = 0; i < SPL; ++i) {
+                    const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                    if (sl < slices) cw[i] = __ldg(crow + sl);
                 }
-                if (sl >= slices) continue;
-                const uint32_t w[4] = {cw[i].x, cw[i].y, cw[i].z, cw[i].w};
-                float xv[16];
-                XLoad<XT>::load16(x + (size_t)sl * 16u, xv);
-                float dot = 0.0f, xsum = 0.0f;
+                const uint32_t g0 = group_of(base, gs, gs_shift);
+                const uint32_t g1 = group_of(min(base + 32u * SPL, slices) - 1u, gs, gs_shift) + 1u;
+                const bool by_lane = g1 - g0 <= 32u;
+                float s_l = 0.0f, f_l = 0.0f;
+                if (by_lane && g0 + lane < g1) {
+                    s_l = __ldg(b.scales + (size_t)o * ng + g0 + lane);
+                    f_l = __ldg(b.offsets + (size_t)o * ng + g0 + lane);
+                }
 #pragma unroll
-                for (int m = 0; m < 4; ++m)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        dot = fmaf(xv[4 * m + c], code_to_float(w[m], (uint32_t)c), dot);
-                        xsum += xv[4 * m + c];
+                for (int i = 0; i < SPL; ++i) {
+                    const uint32_t sl = base + (uint32_t)i * 32u + lane;
+                    const uint32_t slc = sl < slices ? sl : slices - 1u;
+                    const uint32_t g = group_of(slc, gs, gs_shift);
+                    float sv_i, fv_i;
+                    if (by_lane) {
+                        sv_i = __shfl_sync(0xffffffffu, s_l, (g - g0) & 31u);
+                        fv_i = __shfl_sync(0xffffffffu, f_l, (g - g0) & 31u);
+                    } else {
+                        sv_i = __ldg(b.scales + (size_t)o * ng + g);
+                        fv_i = __ldg(b.offsets + (size_t)o * ng + g);
                     }
-                acc = fmaf(sv_i, dot, fmaf(fv_i, xsum, acc));
+                    if (sl >= slices) continue;
+                    const uint32_t w[4] = {cw[i].x, cw[i].y, cw[i].z, cw[i].w};
+                    float d[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 xv = planes[(size_t)u * slices + sl];
+                        float t = xv.x * code_to_float(w[u], 0);
+                        t = fmaf(xv.y, code_to_float(w[u], 1), t);
+                        t = fmaf(xv.z, code_to_float(w[u], 2), t);
+                        d[u] = fmaf(xv.w, code_to_float(w[u], 3), t);
+                    }
+                    acc = fmaf(sv_i, (d[0] + d[1]) + (d[2] + d[3]), fmaf(fv_i, ssum[sl], acc));
+                }
+            }
+#pragma unroll
+            for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, dd);
+            if (lane == 0) {
+                const float bo = b.bias ? __ldg(b.bias + o) : 0.0f;
+                for (uint32_t k = 0; k < b.out.n; ++k) b.out.y[k][o] = acc + bo;
             }
         }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-        if (lane == 0) {
-            const float bo = b.bias ? __ldg(b.bias + o) : 0.0f;
-            for (uint32_t k = 0; k < b.out.n; ++k) b.out.y[k][o] = acc + bo;
-        }
+        seg = seg_end;
     }
     if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
@@ -325,13 +362,28 @@ template <typename XT>
 int launch_gemv_jobs(const GemvJobs &J, int sms, cudaStream_t s)
 {
     if (J.n == 0 || J.total_rows == 0) return 0;
+    uint32_t max_in = 0;
+    for (uint32_t i = 0; i < J.n; ++i) max_in = J.job[i].in_f > max_in ? J.job[i].in_f : max_in;
+    const size_t smem = (size_t)max_in * 4u + (size_t)(max_in / 16u) * 4u;   // fp32 planes + slice sums
+    if (smem > kGemvStageMax) return 1;
+    static std::atomic<uint64_t> configured{0};   // one bit per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
+    if (!(configured.load(std::memory_order_acquire) & (1ull << dev))) {
+        if (cudaFuncSetAttribute(affine_gemv_jobs_kernel<XT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kGemvStageMax) != cudaSuccess) { cudaGetLastError(); return -1; }
+        configured.fetch_or(1ull << dev, std::memory_order_acq_rel);
+    }
+    // CTAs resident per SM: shared memory (228 KB, 1 KB reserved each) and 4 by registers
+    uint32_t per_sm = (uint32_t)(233472u / (smem + 1024u));
+    per_sm = per_sm > 4u ? 4u : per_sm < 1u ? 1u : per_sm;
     uint32_t blocks = (J.total_rows + 7u) / 8u;
-    const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * 4u;
+    const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
     if (blocks > cap) blocks = cap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -414,10 +466,12 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
         if (N == 1) {
             GemvJobs J{};
-            J.job[0] = GemvJob{x, codes, scales, offsets, bias, out, in_f, out_f, gs, gs_shift, in_f / gs, 0u};
+            J.job[0] = GemvJob{x, codes, scales, offsets, bias, out, in_f, out_f, gs, gs_shift, in_f / gs, 0u, 0u};
             J.n = 1;
             J.total_rows = out_f;
-            return launch_gemv_jobs<XT>(J, sms, s);
+            J.total_codes = (uint64_t)out_f * in_f;
+            const int r = launch_gemv_jobs<XT>(J, sms, s);
+            if (r <= 0) return r;   // 1: activations too long to stage; the kernel below takes it
         }
         for (uint32_t n0 = 0; n0 < N; n0 += kGemvTokens) {
             const uint32_t nt = N - n0 < (uint32_t)kGemvTokens ? N - n0 : (uint32_t)kGemvTokens;
@@ -529,7 +583,8 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
         const hxq_affine_tensor_t &t = tensors[i];
         all_fast = t.indices && t.scales && t.offsets && d_xs[i] && t.group_size && t.in_features &&
                    t.group_size % 16u == 0 && t.in_features % t.group_size == 0 && t.in_features % 16u == 0 &&
-                   ldys[i] >= t.out_features && hxq::aligned(d_xs[i], 16) && hxq::aligned(t.indices, 16);
+                   ldys[i] >= t.out_features && hxq::aligned(d_xs[i], 16) && hxq::aligned(t.indices, 16) &&
+                   (size_t)t.in_features * 4u + (size_t)(t.in_features / 16u) * 4u <= hxq::kGemvStageMax;
     }
     if (all_fast) {
         int sms = 148, dev = 0;
@@ -538,6 +593,7 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
         for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxGemvJobs) {
             hxq::GemvJobs J{};
             uint32_t rows = 0;
+            uint64_t ncodes = 0;
             for (uint32_t i = i0; i < n && J.n < hxq::kMaxGemvJobs; ++i) {
                 const hxq_affine_tensor_t &t = tensors[i];
                 hxq::OutPtrs o;
@@ -545,10 +601,12 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
                 const uint32_t gs = t.group_size;
                 const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
                 J.job[J.n++] = hxq::GemvJob{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, t.in_features,
-                                            t.out_features, gs, gs_shift, t.in_features / gs, rows};
+                                            t.out_features, gs, gs_shift, t.in_features / gs, rows, ncodes};
                 rows += t.out_features;
+                ncodes += (uint64_t)t.out_features * t.in_features;
             }
             J.total_rows = rows;
+            J.total_codes = ncodes;
             if (hxq::launch_gemv_jobs<uint16_t>(J, sms, s) != 0) return -1;
         }
         return 0;

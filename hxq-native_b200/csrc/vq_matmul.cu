@@ -250,8 +250,9 @@ cudaError_t configure_one(size_t smem)
 
 // Fused VQ GEMV over a batch of 12-bit images (k = 4096, in_f % 64 == 0,
 // 16-byte aligned x and index rows); up to 8 tokens per pass, fewer when
-// their activations would not fit the staging budget.  The launch's CTAs
-// are shared out over the images in proportion to their index bytes.
+// their activations would not fit the staging budget.  Each image gets the
+// CTAs a launch of it alone would have (one per 8 rows, at most a full
+// grid), so a batch runs like back-to-back launches without their gaps.
 cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t ntok, int sms, cudaStream_t s)
 {
     static std::atomic<uint64_t> configured{0};   // one bit per device
@@ -276,11 +277,7 @@ cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t nto
         configured.fetch_or(1ull << dev, std::memory_order_acq_rel);
     }
     uint32_t max_in = 0;
-    double total_bytes = 0.0;
-    for (uint32_t i = 0; i < n; ++i) {
-        max_in = jobs[i].in_f > max_in ? jobs[i].in_f : max_in;
-        total_bytes += (double)jobs[i].rows * jobs[i].in_f;
-    }
+    for (uint32_t i = 0; i < n; ++i) max_in = jobs[i].in_f > max_in ? jobs[i].in_f : max_in;
     const size_t row_x = (size_t)max_in * 2u;
     const uint32_t fit = (uint32_t)(kGvXsBytesMax / row_x);      // tokens whose activations fit
     const bool xs = fit >= 1u;
@@ -303,10 +300,10 @@ cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t nto
             a.out = j.out;
             for (uint32_t k = 0; k < j.out.n; ++k) a.out.y[k] = j.out.y[k] + (size_t)n0 * j.ldy;
             a.rows = j.rows; a.in_f = j.in_f; a.ntok = nt; a.ldy = j.ldy; a.n_chunks = j.n_chunks;
-            // CTAs in proportion to the matrix's bytes, at least one, at most one per 8 rows
-            uint32_t c = (uint32_t)((double)G * ((double)j.rows * j.in_f) / total_bytes + 0.5);
+            // as many CTAs as a launch of this matrix alone would have: one
+            // per 8 rows, at most a full grid
             const uint32_t cmax = (j.rows + kGvWarps - 1u) / kGvWarps;
-            c = c < 1u ? 1u : c > cmax ? cmax : c;
+            const uint32_t c = cmax < G ? cmax : G;
             a.cta_begin = cta;
             a.n_ctas = c;
             cta += c;

@@ -4,9 +4,11 @@
 // (codebook[index] + in-range sidecar deltas, the reference's src/hxq.c:
 // 239-350 decode), with W never written to memory.
 //
-// One warp per output row, rows handed out grid-stride.  The CTA stages the
-// fp32 codebook (32 KB) and the pass's activations (bf16) in shared memory
-// once.  A row's packed 12-bit indices arrive in pieces of 2048 weights
+// One warp per output row, 16 warps per CTA (two CTAs per SM), so one staged
+// codebook serves many warps.  The CTA stages the fp32 codebook (32 KB) and
+// the pass's activations (bf16) in shared memory once; each CTA serves one
+// image of the batch (a contiguous range of its rows).  A row's packed
+// 12-bit indices arrive in pieces of 2048 weights
 // (1536 bytes) through a two-deep per-warp cp.async ring (coalesced 16-byte
 // copies, L1 bypassed); each lane takes 4 consecutive byte triples per step
 // (3 bank-conflict-free word reads, one PRMT per triple), gathers the 8 fp32
@@ -14,9 +16,10 @@
 // sidecar entries are a sparse epilogue, y += delta * x[col]: their chunk
 // range is read when the row starts and each lane's first two entries when
 // its last piece starts, so the dependent loads overlap the streaming.
-// Each warp first sends its rows of indices to L2 by bulk prefetch, and the
-// kernel is launched with programmatic stream serialization (the weights do
-// not depend on the kernel before it; the activations do).
+// Each warp keeps its next two rows of indices on their way to L2 by bulk
+// prefetch, and the kernel is launched with programmatic stream
+// serialization (the weights do not depend on the kernel before it; the
+// activations do).
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -27,7 +30,7 @@
 namespace hxq {
 namespace {
 
-constexpr uint32_t kGvWarps = 8;
+constexpr uint32_t kGvWarps = 16;
 constexpr uint32_t kGvThreads = kGvWarps * 32;
 constexpr uint32_t kGvStages = 2;
 constexpr uint32_t kPieceTrip = 512;                   // byte triples per piece
@@ -75,7 +78,7 @@ __device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w 
 
 // XS: activations staged in shared memory (else read through L1).
 template <int NT, bool XS>
-__global__ void __launch_bounds__(kGvThreads, 3)
+__global__ void __launch_bounds__(kGvThreads, 2)
 vq_gemv_kernel(const __grid_constant__ GemvBatch B)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -285,9 +288,9 @@ cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t nto
     for (uint32_t n0 = 0; n0 < ntok; n0 += per_pass) {
         const uint32_t nt = ntok - n0 < per_pass ? ntok - n0 : per_pass;
         const size_t smem = base + (xs ? (size_t)nt * row_x : 0u);
-        // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA), at most 3
+        // resident CTAs per SM: shared memory (228 KB, 1 KB reserved per CTA), at most 2
         uint32_t per_sm = (uint32_t)(233472u / (smem + 1024u));
-        per_sm = per_sm > 3u ? 3u : per_sm < 1u ? 1u : per_sm;
+        per_sm = per_sm > 2u ? 2u : per_sm < 1u ? 1u : per_sm;
         const uint32_t G = (uint32_t)(sms > 0 ? sms : 148) * per_sm;
         GemvBatch B{};
         B.n = n;

@@ -138,3 +138,19 @@ class HxqLinear(torch.nn.Module):
             except Exception:
                 pass
             self._img = C.c_void_p()
+
+
+def load_linears(path: str, shard: tuple[int, int] = (0, 1)) -> dict[str, HxqLinear]:
+    """HxqLinear layers for every compressed module of a helix-substrate
+    safetensors or GGUF file (hxq_b200.container), keyed by module prefix.
+    shard=(rank, world) keeps this rank's contiguous share of each module's
+    output features: rows [rank*O//world, (rank+1)*O//world)."""
+    from .container import load_modules
+    rank, world = shard
+    if not 0 <= rank < world:
+        raise ValueError("shard must be (rank, world) with 0 <= rank < world")
+    out = {}
+    for name, d in load_modules(path).items():
+        O = d["out_f"]
+        out[name] = HxqLinear(d, rank * O // world, (rank + 1) * O // world)
+    return out

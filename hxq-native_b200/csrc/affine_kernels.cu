@@ -17,8 +17,10 @@
 // store.  Launched with programmatic stream serialization: the codes do not
 // depend on the kernel before it on the stream, so their loads start early
 // and the kernel waits (griddepcontrol.wait) only before the activations.
-// Larger token counts use the tcgen05 GEMM (dequant_gemm.cu) when the
-// shape allows it.
+// With bf16 activations, 1..8 tokens go to the tensor-core GEMV
+// (affine_tc_gemv.cu) and larger token counts to the tcgen05 GEMM
+// (dequant_gemm.cu) when the shape allows it; this file's GEMVs take fp32
+// activations and the shapes those kernels do not.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -35,10 +37,11 @@ namespace hxq {
 namespace {
 
 constexpr int kGemvTokens = 8;   // tokens per pass of the GEMV
-// From this many tokens on, bf16 activations go to the tcgen05 dequant-GEMM
-// (split over K when the tiles alone would not fill the GPU); one token
-// stays on the exact streaming GEMV.
-constexpr uint32_t kGemmMinTokens = 2;
+// Up to this many bf16 tokens the tensor-core GEMV (exact products, fp32
+// accumulation; it takes up to 16 when asked for by path); from there on the
+// tcgen05 dequant-GEMM (split over K when the tiles alone would not fill the
+// GPU), which is faster from about 9 tokens on a 4096 x 4096 matrix.
+constexpr uint32_t kTcGemvMaxTokens = 8;
 
 __device__ __forceinline__ float code_to_float(uint32_t word, uint32_t i)
 {
@@ -430,10 +433,20 @@ bool aligned(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0;
 // out: the outputs, each [N, ldy] (a single [N, out_f] buffer for the
 // reference entry points).  Several outputs or ldy != out_f need the GEMV or
 // GEMM paths (group size and in_f multiples of 16, 16-B aligned x and codes).
+int sm_count()
+{
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+// path: HXQ_AFFINE_PATH_* (auto, CUDA-core GEMV, tensor-core GEMV, tcgen05
+// GEMM); a forced path that cannot take the shape returns -1.
 template <typename XT>
 int run_affine(const XT *x, const uint8_t *codes, const float *scales, const float *offsets,
                const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t N, uint32_t in_f, uint32_t out_f,
-               uint32_t gs, cudaStream_t s)
+               uint32_t gs, cudaStream_t s, int path = HXQ_AFFINE_PATH_AUTO)
 {
     if (!x || !codes || !scales || !offsets || out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return -1;
     for (uint32_t k = 0; k < out.n; ++k)
@@ -447,18 +460,26 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         affine_generic_kernel<XT><<<1, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
+    if (path < HXQ_AFFINE_PATH_AUTO || path > HXQ_AFFINE_PATH_GEMM) return -1;
     if constexpr (sizeof(XT) == 2) {
-        if (N >= kGemmMinTokens) {
-            const int r = affine_gemm_bf16(reinterpret_cast<const uint16_t *>(x), codes, scales, offsets, bias,
-                                           out, ldy, N, in_f, out_f, gs, s);
+        const uint16_t *xb = reinterpret_cast<const uint16_t *>(x);
+        if ((path == HXQ_AFFINE_PATH_AUTO && N <= kTcGemvMaxTokens) || path == HXQ_AFFINE_PATH_TC_GEMV) {
+            const TcMatrix m{xb, codes, scales, offsets, bias, out, ldy, in_f, out_f, gs};
+            const int r = launch_tc_gemv(1, &m, N, sm_count(), s);
             if (r <= 0) return r;  // launched (0) or failed (-1); 1 = shape not taken
+            if (path == HXQ_AFFINE_PATH_TC_GEMV) return -1;
         }
+        if ((path == HXQ_AFFINE_PATH_AUTO && N >= 2u) || path == HXQ_AFFINE_PATH_GEMM) {
+            const int r = affine_gemm_bf16(xb, codes, scales, offsets, bias, out, ldy, N, in_f, out_f, gs, s);
+            if (r <= 0) return r;
+            if (path == HXQ_AFFINE_PATH_GEMM) return -1;
+        }
+    } else {
+        if (path == HXQ_AFFINE_PATH_TC_GEMV || path == HXQ_AFFINE_PATH_GEMM) return -1;
     }
     const bool fast = gs % 16u == 0 && in_f % 16u == 0 && aligned(x, 16) && aligned(codes, 16);
     if (fast) {
-        int sms = 148, dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int sms = sm_count();
         uint32_t blocks = (out_f + 7u) / 8u;
         const uint32_t cap = (uint32_t)sms * 8u;
         if (blocks > cap) blocks = cap;
@@ -498,7 +519,7 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
             if (e != cudaSuccess) { cudaGetLastError(); return -1; }
         }
     } else {
-        if (!plain) return -1;
+        if (!plain || path != HXQ_AFFINE_PATH_AUTO) return -1;
         uint64_t blocks = ((uint64_t)N * out_f + 255u) / 256u;
         if (blocks > 148u * 32u) blocks = 148u * 32u;
         affine_generic_kernel<XT><<<(uint32_t)blocks, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
@@ -547,6 +568,27 @@ int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16, const hxq_affine_tens
                                      static_cast<cudaStream_t>(stream));
 }
 
+int hxq_affine_group_matmul_bf16_path(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t,
+                                      float *d_output, uint32_t N, int path, void *stream)
+{
+    if (!t) return -1;
+    return hxq::run_affine<uint16_t>(d_x_bf16, t->indices, t->scales, t->offsets, t->bias, one_out(d_output),
+                                     t->out_features, N, t->in_features, t->out_features, t->group_size,
+                                     static_cast<cudaStream_t>(stream), path);
+}
+
+int hxq_affine_group_matmul_bf16_auto_path(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t, uint32_t N)
+{
+    if (!t || N == 0) return -1;
+    if (N <= hxq::kTcGemvMaxTokens &&
+        hxq::tc_gemv_fits(d_x_bf16, t->indices, t->scales, t->offsets, N, t->in_features, t->out_features,
+                          t->group_size))
+        return HXQ_AFFINE_PATH_TC_GEMV;
+    if (N >= 2u && hxq::affine_gemm_fits(d_x_bf16, t->indices, N, t->in_features, t->out_features, t->group_size))
+        return HXQ_AFFINE_PATH_GEMM;
+    return HXQ_AFFINE_PATH_GEMV;
+}
+
 int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16, const hxq_affine_tensor_t *t,
                                        float *const *d_ys, uint32_t n_out, uint32_t ldy, uint32_t N,
                                        void *stream)
@@ -576,6 +618,31 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
         o.n = n_out;
         return true;
     };
+    // up to 8 tokens: matrices that suit the tensor-core GEMV share
+    // launches of up to 8 matrices
+    bool all_tc = N <= hxq::kTcGemvMaxTokens;
+    for (uint32_t i = 0; i < n && all_tc; ++i) {
+        const hxq_affine_tensor_t &t = tensors[i];
+        all_tc = ldys[i] >= t.out_features &&
+                 hxq::tc_gemv_fits(d_xs[i], t.indices, t.scales, t.offsets, N, t.in_features, t.out_features,
+                                   t.group_size);
+    }
+    if (all_tc) {
+        const int sms = hxq::sm_count();
+        for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxTcJobs) {
+            hxq::TcMatrix m[hxq::kMaxTcJobs];
+            uint32_t k = 0;
+            for (uint32_t i = i0; i < n && k < hxq::kMaxTcJobs; ++i, ++k) {
+                const hxq_affine_tensor_t &t = tensors[i];
+                hxq::OutPtrs o;
+                if (!outs_of(i, o)) return -1;
+                m[k] = hxq::TcMatrix{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, ldys[i], t.in_features,
+                                     t.out_features, t.group_size};
+            }
+            if (hxq::launch_tc_gemv(k, m, N, sms, s) != 0) return -1;
+        }
+        return 0;
+    }
     // one token: every matrix whose shape suits the batched GEMV goes into
     // launches of up to 8 matrices; the rest one call each
     bool all_fast = N == 1;
@@ -587,9 +654,7 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
                    (size_t)t.in_features * 4u + (size_t)(t.in_features / 16u) * 4u <= hxq::kGemvStageMax;
     }
     if (all_fast) {
-        int sms = 148, dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int sms = hxq::sm_count();
         for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxGemvJobs) {
             hxq::GemvJobs J{};
             uint32_t rows = 0;

@@ -1,0 +1,711 @@
+// affine_tc_gemv.cu -- affine group-quantized matmul for 1..16 bf16 tokens
+// on the tensor cores, streaming the codes through shared memory.
+//
+//   Y[n,o] = sum_g ( s[o,g] * sum_{k in g} x[n,k]*q[o,k]
+//                  + off[o,g] * sum_{k in g} x[n,k] ) + bias[o]
+// (reference hxq-native src/hxq_affine.c:23-66).
+//
+// At a few tokens the matmul is a stream over the codes (one byte per
+// weight); the work per code must stay well under the issue budget that
+// HBM speed leaves (about 7 thread instructions per code on 148 SMs at
+// 1.9 GHz).  Here the per-code work is one byte permute and one packed f16
+// subtract per two codes, and m16n8k16 tensor-core products do the
+// multiply-adds:
+//   * codes: a producer thread copies each 16-row block of codes, 1024
+//     codes of K per stage, with two TMA tensor copies per stage (a 3-D view
+//     [rows][in_f / 128][128 B] of the matrix, box 16 rows x 4 x 128 B,
+//     128-byte swizzle, so the 128-bit fragment loads are free of bank
+//     conflicts; rows past the matrix read as zero) into a ring of
+//     shared-memory stages; each row block's scales and offsets come in with
+//     its first stage (cp.async.bulk) and are transposed once per row block
+//     so that a warp reads a row pair's scale and offset with one 64-bit load;
+//   * widening: [byte, 0x64] is the f16 1024 + byte, so a byte permute makes
+//     two f16 values and one f16x2 subtract of 1024 leaves the code itself,
+//     exactly, for every byte value;
+//   * activations: each warp stages, once per matrix, the activations of
+//     the K slices it owns (no cross-warp synchronisation), as f16: each
+//     64-value chunk of a token scaled by a power of two 2^e that brings its
+//     largest |x| into [2^14, 2^15), so every bf16 value converts exactly
+//     (apart from ones 2^28 below the chunk's largest, which lose low bits as
+//     f16 subnormals); 2^-e and the chunk's activation sum (fp32, unscaled)
+//     are kept per (token, chunk);
+//   * products: each consumer warp owns 128 codes of K of every stage (two
+//     64-code chunks) and runs, per chunk and 8 tokens, four m16n8k16
+//     products with fp32 accumulation in two independent chains, over a K
+//     permutation shared by the code and activation fragments so that both
+//     come from single 128-bit / 64-bit loads;
+//   * groups: the group size is a multiple of 64, so a 64-code chunk lies in
+//     one group; its fresh partial sums are scaled by 2^-e s[o,g] and it adds
+//     off[o,g] times its activation sum;
+//   * the 8 warps' partial sums of a row block are added in a fixed order,
+//     bias fused into the store (into every output buffer).
+// Products of f16 values are exact in fp32, so the only rounding is the
+// fp32 accumulation.  Launched with programmatic stream serialization: the
+// producer streams codes before the previous kernel has finished; the
+// consumers wait (griddepcontrol.wait) before reading the activations.
+// Every mbarrier wait is bounded (about one second of clock) and reports
+// through a status word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+
+#include "hxq_cuda.h"
+#include "hxq_cuda_internal.h"
+
+namespace hxq {
+namespace tcg {
+
+constexpr uint32_t kConsumers = 8;                      // consumer warps
+constexpr uint32_t kThreads = (kConsumers + 1u) * 32u;  // + one producer warp
+constexpr uint32_t kChunk = 64;                         // codes of K per MMA chunk
+constexpr uint32_t kWarpK = 2u * kChunk;                // codes of K per warp per stage
+constexpr uint32_t kKC = kWarpK * kConsumers;           // 1024 codes of K per stage
+constexpr uint32_t kRows = 16;                          // rows per block (MMA M)
+constexpr uint32_t kHalfBytes = kRows * 512u;           // one box: [16 rows][4][128 B], swizzled
+constexpr uint32_t kStageBytes = 2u * kHalfBytes;       // 16 KB
+constexpr uint32_t kMaxStages = 6;
+constexpr uint32_t kSfStride = 2u * kRows + 2u;         // floats per group in the transposed scales
+constexpr uint64_t kWaitCycles = 2000000000ull;          // ~1 s at 1.9 GHz
+constexpr uint32_t kErrTimeout = 4u;
+
+__device__ uint32_t g_tc_err;
+
+struct Layout {
+    uint32_t bars, abort, sbuf, sf, xh, xc, red, total;
+};
+
+// Shared memory (from a 1024-byte aligned base): stages [S][2 halves][16
+// rows][4][128 B] | barriers full[S], empty[S], sdone | abort | scales and
+// offsets as copied [2][16][ng] | transposed [ng][16 rows][s, off] (+2 pad) |
+// f16 activations [N][in_f + 4] | per (token, 64-value chunk) {2^-e, sum} |
+// reductions [2][8 warps][16][8 NT]
+constexpr uint32_t kAlignSlack = 1024;
+__host__ __device__ inline Layout layout(uint32_t S, uint32_t N, uint32_t nt, uint32_t ng, uint32_t in_f)
+{
+    Layout L;
+    uint32_t o = S * kStageBytes;
+    L.bars = o;   o += (2u * kMaxStages + 1u) * 8u;
+    L.abort = o;  o += 8u;
+    o = (o + 127u) & ~127u;
+    L.sbuf = o;   o += 2u * kRows * ng * 4u;
+    L.sf = o;     o += ng * kSfStride * 4u;
+    o = (o + 127u) & ~127u;
+    L.xh = o;     o += N * (in_f + 4u) * 2u;
+    o = (o + 15u) & ~15u;
+    L.xc = o;     o += N * (in_f / kChunk) * 8u;
+    L.red = o;    o += 2u * kConsumers * kRows * 8u * nt * 4u;
+    L.total = o + kAlignSlack;
+    return L;
+}
+
+struct Job {
+    CUtensorMap map;            // codes as [out_f][in_f / 128][128] bytes, box 16 x 4 x 128
+    const uint16_t *x;          // bf16 activations [N][in_f]
+    const uint8_t *codes;       // [out_f][in_f]
+    const float *scales, *offsets, *bias;
+    OutPtrs out;                // output o of token n at out.y[k][n * ldy + o]
+    uint32_t in_f, out_f, gs, gs_shift, ng, ldy;
+    uint32_t rb_begin;          // first row block of the job in the launch
+    uint64_t w_begin;           // code weight (16 * in_f per row block) of the jobs before
+};
+
+struct Jobs {
+    Job job[kMaxTcJobs];
+    uint32_t n, N, total_rb, ng_max, in_max, stages;
+    uint64_t total_w;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false if it ran out or another thread already gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
+{
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = clock64();
+    while (true) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *abort = 1u;
+            atomicOr(&g_tc_err, kErrTimeout);
+            return false;
+        }
+    }
+}
+
+// Warp-uniform bounded wait: every lane waits, the warp goes on only if all did.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
+{
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort)) != 0;
+}
+
+// Teardown wait: bounded, not cut short by the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity)
+{
+    const uint64_t t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_tc_err, kErrTimeout);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
+                                            int32_t c1, int32_t c2)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Bytes 2i and 2i+1 of w as exact f16 values (f16 1024 + b, minus 1024).
+template <int HI>
+__device__ __forceinline__ uint32_t codes_f16x2(uint32_t w)
+{
+    const uint32_t h = __byte_perm(w, 0x64646464u, HI ? 0x4342u : 0x4140u);
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64006400u));
+    return r;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t f16x2_of(float lo, float hi)
+{
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// First row block of the launch whose code weight starts at or after w.
+__device__ __forceinline__ uint32_t rb_at(const Jobs &J, uint64_t w)
+{
+    if (w >= J.total_w) return J.total_rb;
+    uint32_t j = 0;
+    while (j + 1u < J.n && w >= J.job[j + 1u].w_begin) ++j;
+    const Job &b = J.job[j];
+    const uint64_t per = (uint64_t)kRows * b.in_f;
+    const uint64_t r = (w - b.w_begin + per - 1u) / per;
+    const uint32_t nrb = (b.out_f + kRows - 1u) / kRows;
+    return b.rb_begin + (uint32_t)(r < nrb ? r : nrb);
+}
+
+__device__ __forceinline__ uint32_t group_of(uint32_t k, const Job &b)
+{
+    return b.gs_shift < 32u ? k >> b.gs_shift : k / b.gs;
+}
+
+// Stage, for one warp, the activations of the K slices it owns: chunks
+// k0 = 1024 st + 128 warp + 64 u (u = 0, 1) of every token.  A pass covers 4
+// chunks of one token, 8 lanes per chunk, one 128-bit load (8 values) per
+// lane; four passes are in flight at a time.  Per chunk: the largest |x|
+// and the sum over the 8 lanes (xor shuffles, a fixed tree), the power of
+// two 2^e, the f16 values x 2^e into the activation rows, {2^-e, sum} into
+// the chunk table.
+__device__ void stage_x_warp(const Job &b, uint32_t N, uint8_t *smem, const Layout &L, uint32_t warp,
+                             uint32_t lane)
+{
+    const uint32_t in_f = b.in_f, xs = in_f + 4u, nck = in_f / kChunk;
+    const uint32_t nch = 2u * ((in_f + kKC - 1u) / kKC);     // chunk slots of this warp
+    const uint32_t ncg = (nch + 3u) / 4u;                     // passes per token
+    const uint32_t total = N * ncg;
+    const uint32_t c8 = lane >> 3, j = lane & 7u;
+    uint16_t *xh = reinterpret_cast<uint16_t *>(smem + L.xh);
+    float2 *xc = reinterpret_cast<float2 *>(smem + L.xc);
+    for (uint32_t q0 = 0; q0 < total; q0 += 4u) {
+        uint4 v[4];
+        uint32_t nn[4], kk[4];
+        bool val[4];
+#pragma unroll
+        for (uint32_t r = 0; r < 4u; ++r) {
+            const uint32_t qq = q0 + r;
+            const uint32_t n = qq / ncg, c = 4u * (qq - n * ncg) + c8;
+            const uint32_t k0 = (c >> 1) * kKC + warp * kWarpK + (c & 1u) * kChunk;
+            nn[r] = n;
+            kk[r] = k0;
+            val[r] = qq < total && c < nch && k0 < in_f;
+            v[r] = val[r] ? __ldg(reinterpret_cast<const uint4 *>(b.x + (size_t)n * in_f + k0) + j)
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (uint32_t r = 0; r < 4u; ++r) {
+            const uint32_t w[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+            float sum = 0.0f;
+            uint32_t m = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                sum += __uint_as_float(w[e] << 16);
+                sum += __uint_as_float(w[e] & 0xFFFF0000u);
+                const uint32_t a = w[e] & 0x7FFF7FFFu;
+                m = max(m, max(a & 0xFFFFu, a >> 16));
+            }
+#pragma unroll
+            for (uint32_t o = 1; o < 8u; o <<= 1) {
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+            }
+            if (!val[r]) continue;
+            // 2^e brings the largest |x| (bf16 bits m, exponent field m >> 7) into [2^14, 2^15)
+            const uint32_t ef = m >> 7;                  // 0: zero or subnormal; 255: inf or NaN
+            int e = (ef == 0u || ef == 255u) ? (ef == 0u && m ? 126 : 0) : 14 - ((int)ef - 127);
+            e = e > 126 ? 126 : e < -126 ? -126 : e;
+            const float sc = __uint_as_float((uint32_t)(e + 127) << 23);
+            uint32_t o4[4];
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2)
+                o4[e2] = f16x2_of(__uint_as_float(w[e2] << 16) * sc, __uint_as_float(w[e2] & 0xFFFF0000u) * sc);
+            // a token row is (in_f + 4) halves: 8-byte aligned, not 16
+            uint2 *dst = reinterpret_cast<uint2 *>(xh + (size_t)nn[r] * xs + kk[r] + 8u * j);
+            dst[0] = make_uint2(o4[0], o4[1]);
+            dst[1] = make_uint2(o4[2], o4[3]);
+            if (j == 0)
+                xc[nn[r] * nck + kk[r] / kChunk] = make_float2(__uint_as_float((uint32_t)(127 - e) << 23), sum);
+        }
+    }
+    __syncwarp();
+}
+
+// One 64-code chunk of a warp: rows g and g+8 of the row block, its codes at
+// 16-byte unit `unit` of 128-byte lines `line` and line + 32 of the half
+// stage `hs`; activation fragments from xrow[t] (per token tile, NULL past
+// N).  Two independent accumulation chains, added at the end.
+template <int NT>
+__device__ __forceinline__ void chunk_mma(const uint8_t *hs, uint32_t line, uint32_t unit,
+                                         const uint16_t *const (&xr)[NT], uint32_t k0, float (&d)[NT][4])
+{
+    const uint8_t *p = hs + line * 128u + unit * 16u;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(p);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(p + 32u * 128u);
+    const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
+    const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
+    float e[NT][4];
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { d[tt][u] = 0.0f; e[tt][u] = 0.0f; }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const uint32_t a0 = codes_f16x2<0>(w0[jj]), a2 = codes_f16x2<1>(w0[jj]);
+        const uint32_t a1 = codes_f16x2<0>(w1[jj]), a3 = codes_f16x2<1>(w1[jj]);
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+            uint2 bb = make_uint2(0u, 0u);
+            if (xr[tt]) bb = *reinterpret_cast<const uint2 *>(xr[tt] + k0 + (uint32_t)jj * 4u);
+            if (jj & 1) mma16816(e[tt], a0, a1, a2, a3, bb.x, bb.y);
+            else mma16816(d[tt], a0, a1, a2, a3, bb.x, bb.y);
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d[tt][u] += e[tt][u];
+}
+
+// A chunk's partial sums into the row pair's accumulators: times 2^-e and
+// the group's scale, plus the group's offset times the chunk's activation
+// sum.
+template <int NT>
+__device__ __forceinline__ void chunk_apply(const float (&d)[NT][4], uint32_t k0, const Job &b, const float *sf,
+                                           const float2 *xc, uint32_t g, uint32_t t, uint32_t N,
+                                           float (&as)[NT][4], float (&af)[NT][4])
+{
+    const uint32_t gi = group_of(k0, b), kc = k0 / kChunk, nck = b.in_f / kChunk;
+    const float2 sf0 = *reinterpret_cast<const float2 *>(sf + gi * kSfStride + 2u * g);
+    const float2 sf1 = *reinterpret_cast<const float2 *>(sf + gi * kSfStride + 2u * (g + 8u));
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+        const uint32_t n0 = (uint32_t)tt * 8u + 2u * t, n1 = n0 + 1u;
+        const float2 c0 = n0 < N ? xc[n0 * nck + kc] : make_float2(0.0f, 0.0f);
+        const float2 c1 = n1 < N ? xc[n1 * nck + kc] : make_float2(0.0f, 0.0f);
+        as[tt][0] = fmaf(sf0.x, d[tt][0] * c0.x, as[tt][0]);
+        as[tt][1] = fmaf(sf0.x, d[tt][1] * c1.x, as[tt][1]);
+        as[tt][2] = fmaf(sf1.x, d[tt][2] * c0.x, as[tt][2]);
+        as[tt][3] = fmaf(sf1.x, d[tt][3] * c1.x, as[tt][3]);
+        af[tt][0] = fmaf(sf0.y, c0.y, af[tt][0]);
+        af[tt][1] = fmaf(sf0.y, c1.y, af[tt][1]);
+        af[tt][2] = fmaf(sf1.y, c0.y, af[tt][2]);
+        af[tt][3] = fmaf(sf1.y, c1.y, af[tt][3]);
+    }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // stages on a 1024-byte boundary: the 128-byte swizzle pattern repeats every 1024 bytes
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t S = J.stages;
+    const Layout L = layout(S, J.N, NT, J.ng_max, J.in_max);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *empty = full + kMaxStages;
+    uint64_t *sdone = empty + kMaxStages;
+    volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(smem + L.abort);
+    float *sbuf = reinterpret_cast<float *>(smem + L.sbuf);
+    const uint32_t sb_stride = kRows * J.ng_max;   // floats per array (scales, offsets)
+
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kConsumers);
+        }
+        mbar_init(sdone, kConsumers);
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const uint32_t rb0 = rb_at(J, J.total_w * blockIdx.x / gridDim.x);
+    const uint32_t rb1 = rb_at(J, J.total_w * (blockIdx.x + 1u) / gridDim.x);
+
+    if (warp == kConsumers) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0, slot = 0, ph = 0, j = 0, rbi = 0;
+            bool ok = true;
+            for (uint32_t rb = rb0; rb < rb1 && ok; ++rb, ++rbi) {
+                while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
+                const Job &b = J.job[j];
+                const uint32_t row0 = (rb - b.rb_begin) * kRows;
+                const uint32_t rv = min(kRows, b.out_f - row0);
+                const uint32_t nst = (b.in_f + kKC - 1u) / kKC;
+                for (uint32_t st = 0; st < nst; ++st, ++it) {
+                    if (it >= S && !mbar_wait(empty + slot, ph ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint32_t sbytes = 0;
+                    if (st == 0) {
+                        // the scales of the previous row block have been transposed
+                        if (rbi >= 1u && !mbar_wait(sdone, (rbi - 1u) & 1u, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        sbytes = (rv * b.ng * 4u) & ~15u;
+                    }
+                    // the full boxes count, including the zero fill past the matrix
+                    mbar_expect_tx(full + slot, kStageBytes + 2u * sbytes);
+                    uint8_t *dst = smem + slot * kStageBytes;
+                    tma_load_3d(dst, &b.map, full + slot, 0, (int32_t)(st * (kKC / 128u)), (int32_t)row0);
+                    tma_load_3d(dst + kHalfBytes, &b.map, full + slot, 0, (int32_t)(st * (kKC / 128u) + 4u),
+                                (int32_t)row0);
+                    if (sbytes) {
+                        bulk_g2s(sbuf, b.scales + (size_t)row0 * b.ng, sbytes, full + slot);
+                        bulk_g2s(sbuf + sb_stride, b.offsets + (size_t)row0 * b.ng, sbytes, full + slot);
+                    }
+                    if (++slot == S) { slot = 0; ph ^= 1u; }
+                }
+            }
+            // every issued copy has landed before shared memory is released
+            for (uint32_t kt = it > S ? it - S : 0u; kt < it; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t ct = threadIdx.x;        // 0..255
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t N = J.N;
+    const uint16_t *xh = reinterpret_cast<const uint16_t *>(smem + L.xh);
+    const float2 *xc = reinterpret_cast<const float2 *>(smem + L.xc);
+    float *sf = reinterpret_cast<float *>(smem + L.sf);
+    float *red = reinterpret_cast<float *>(smem + L.red);
+    constexpr uint32_t NTOK = 8u * NT;
+    // this warp's 128 codes of a stage: line (warp & 3) of half stage (warp >> 2)
+    const uint32_t half = warp >> 2, cl = warp & 3u;
+    const uint32_t line = g * 4u + cl;
+    const uint32_t unit0 = t ^ (line & 7u), unit1 = (4u + t) ^ (line & 7u);
+    uint32_t slot = 0, ph = 0, j = 0, rbi = 0, cur = 0xFFFFFFFFu;
+    bool ok = true;
+    for (uint32_t rb = rb0; rb < rb1; ++rb, ++rbi) {
+        while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
+        const Job &b = J.job[j];
+        if (j != cur) {
+            stage_x_warp(b, N, smem, L, warp, lane);   // this warp's K slices only
+            cur = j;
+        }
+        const uint32_t in_f = b.in_f, ng = b.ng;
+        const uint32_t row0 = (rb - b.rb_begin) * kRows;
+        const uint32_t rv = min(kRows, b.out_f - row0);
+        const uint32_t nst = (in_f + kKC - 1u) / kKC;
+        const uint16_t *xr[NT];
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+            const uint32_t n = (uint32_t)tt * 8u + g;
+            xr[tt] = n < N ? xh + (size_t)n * (in_f + 4u) + t * 16u : nullptr;
+        }
+        float as[NT][4], af[NT][4];
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) { as[tt][u] = 0.0f; af[tt][u] = 0.0f; }
+        for (uint32_t st = 0; st < nst; ++st) {
+            if (ok && !warp_wait(full + slot, ph, abort_flag)) ok = false;
+            if (st == 0) {
+                // scales and offsets of the row block, transposed to [group][row][s, off];
+                // rows past the copied bytes come from global memory, rows past the matrix are 0
+                const uint32_t sbytes = (rv * ng * 4u) & ~15u;
+                const float *gsc = b.scales + (size_t)row0 * ng, *gof = b.offsets + (size_t)row0 * ng;
+                for (uint32_t i = ct; i < kRows * ng; i += 256u) {
+                    const uint32_t r = i / ng, gg = i - r * ng;
+                    float sv = 0.0f, fv = 0.0f;
+                    if (ok && r < rv) {
+                        sv = i * 4u < sbytes ? sbuf[i] : __ldg(gsc + i);
+                        fv = i * 4u < sbytes ? sbuf[sb_stride + i] : __ldg(gof + i);
+                    }
+                    sf[gg * kSfStride + 2u * r] = sv;
+                    sf[gg * kSfStride + 2u * r + 1u] = fv;
+                }
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (ok && lane == 0) mbar_arrive(sdone);
+            }
+            const uint32_t kb = st * kKC + warp * kWarpK;
+            if (ok && kb < in_f) {
+                const uint8_t *hs = smem + slot * kStageBytes + half * kHalfBytes;
+                // in_f is a multiple of 128: both chunks of the warp are inside K
+                float d[NT][4];
+                chunk_mma<NT>(hs, line, unit0, xr, kb, d);
+                chunk_apply<NT>(d, kb, b, sf, xc, g, t, N, as, af);
+                chunk_mma<NT>(hs, line, unit1, xr, kb + kChunk, d);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
+                chunk_apply<NT>(d, kb + kChunk, b, sf, xc, g, t, N, as, af);
+            } else {
+                __syncwarp();
+                if (ok && lane == 0) mbar_arrive(empty + slot);
+            }
+            if (++slot == S) { slot = 0; ph ^= 1u; }
+        }
+        // the 8 warps' partial sums of this row block, added in warp order
+        float *rd = red + (size_t)(rbi & 1u) * kConsumers * kRows * NTOK;
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+            const uint32_t n0 = (uint32_t)tt * 8u + 2u * t;
+            rd[(warp * kRows + g) * NTOK + n0] = as[tt][0] + af[tt][0];
+            rd[(warp * kRows + g) * NTOK + n0 + 1u] = as[tt][1] + af[tt][1];
+            rd[(warp * kRows + g + 8u) * NTOK + n0] = as[tt][2] + af[tt][2];
+            rd[(warp * kRows + g + 8u) * NTOK + n0 + 1u] = as[tt][3] + af[tt][3];
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        for (uint32_t idx = ct; idx < kRows * NTOK; idx += 256u) {
+            const uint32_t row = idx / NTOK, n = idx - row * NTOK;
+            if (ok && row < rv && n < N) {
+                float v = 0.0f;
+#pragma unroll
+                for (uint32_t w = 0; w < kConsumers; ++w) v += rd[(w * kRows + row) * NTOK + n];
+                const uint32_t o = row0 + row;
+                if (b.bias) v += __ldg(b.bias + o);
+                for (uint32_t k = 0; k < b.out.n; ++k) b.out.y[k][(size_t)n * b.ldy + o] = v;
+            }
+        }
+    }
+}
+
+// Ring depth and CTAs per SM for a launch: the deepest ring (2..6 stages)
+// that keeps two CTAs on an SM (228 KB, 1 KB reserved per CTA), else one
+// CTA with the deepest ring that fits 227 KB.  0 stages: does not fit.
+struct Plan {
+    uint32_t stages, per_sm;
+    Layout L;
+};
+
+Plan plan_for(uint32_t N, uint32_t ng, uint32_t in_f)
+{
+    const uint32_t nt = N > 8u ? 2u : 1u;
+    Plan p{0u, 0u, {}};
+    for (uint32_t s = kMaxStages; s >= 2u; --s) {
+        const Layout L = layout(s, N, nt, ng, in_f);
+        if (2u * (L.total + 1024u) <= 233472u) return Plan{s, 2u, L};
+    }
+    for (uint32_t s = kMaxStages; s >= 2u; --s) {
+        const Layout L = layout(s, N, nt, ng, in_f);
+        if (L.total <= 227u * 1024u) return Plan{s, 1u, L};
+    }
+    return p;
+}
+
+}  // namespace tcg
+
+// Eligibility of one matrix for the tensor-core GEMV (host side).
+bool tc_gemv_fits(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
+                  uint32_t N, uint32_t in_f, uint32_t out_f, uint32_t gs)
+{
+    auto al = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    if (N == 0 || N > 16u || out_f == 0 || in_f == 0 || gs == 0) return false;
+    if (in_f % 128u != 0 || gs % tcg::kChunk != 0 || in_f % gs != 0) return false;
+    if (!x || !codes || !scales || !offsets || !al(x) || !al(codes) || !al(scales) || !al(offsets)) return false;
+    return tcg::plan_for(N, in_f / gs, in_f).stages != 0;
+}
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::atomic<bool> tried{false};
+    if (!tried.load(std::memory_order_acquire)) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+        else
+            cudaGetLastError();
+        tried.store(true, std::memory_order_release);
+    }
+    return fn;
+}
+
+// The codes of a matrix as [out_f][in_f / 128][128] bytes; a half stage is
+// the box of 16 rows x 4 lines x 128 bytes at (0, line, first row).
+bool encode_codes_map(CUtensorMap *map, const uint8_t *codes, uint32_t in_f, uint32_t out_f)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    std::memset(map, 0, sizeof(*map));
+    const cuuint64_t dims[3] = {128u, in_f / 128u, out_f};
+    const cuuint64_t strides[2] = {128u, in_f};
+    const cuuint32_t box[3] = {128u, 4u, tcg::kRows};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(codes), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// 0 launched, 1 a matrix does not fit this kernel, -1 CUDA error.
+int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStream_t s)
+{
+    using namespace tcg;
+    if (n == 0 || N == 0) return 0;
+    if (n > kMaxTcJobs) return 1;
+    tcg::Jobs J{};
+    uint32_t rb = 0;
+    uint64_t w = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const TcMatrix &a = m[i];
+        if (!tc_gemv_fits(a.x, a.codes, a.scales, a.offsets, N, a.in_f, a.out_f, a.gs)) return 1;
+        if (a.out.n == 0 || a.out.n > HXQ_CUDA_MAX_PEERS || a.ldy < a.out_f) return 1;
+        Job &b = J.job[i];
+        if (!encode_codes_map(&b.map, a.codes, a.in_f, a.out_f)) return 1;
+        b.x = a.x; b.codes = a.codes; b.scales = a.scales; b.offsets = a.offsets; b.bias = a.bias;
+        b.out = a.out; b.in_f = a.in_f; b.out_f = a.out_f; b.gs = a.gs; b.ng = a.in_f / a.gs; b.ldy = a.ldy;
+        b.gs_shift = (a.gs & (a.gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(a.gs) : 32u;
+        b.rb_begin = rb;
+        b.w_begin = w;
+        const uint32_t nrb = (a.out_f + kRows - 1u) / kRows;
+        rb += nrb;
+        w += (uint64_t)nrb * kRows * a.in_f;
+        J.ng_max = b.ng > J.ng_max ? b.ng : J.ng_max;
+        J.in_max = a.in_f > J.in_max ? a.in_f : J.in_max;
+    }
+    J.n = n;
+    J.N = N;
+    J.total_rb = rb;
+    J.total_w = w;
+    const Plan P = plan_for(N, J.ng_max, J.in_max);
+    if (P.stages == 0) return 1;
+    J.stages = P.stages;
+    const uint32_t nt = N > 8u ? 2u : 1u;
+    static std::atomic<uint64_t> configured[2];   // per NT: one bit per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
+    auto kern = nt == 1u ? affine_tc_gemv_kernel<1> : affine_tc_gemv_kernel<2>;
+    if (!(configured[nt - 1u].load(std::memory_order_acquire) & (1ull << dev))) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        configured[nt - 1u].fetch_or(1ull << dev, std::memory_order_acq_rel);
+    }
+    uint32_t grid = (uint32_t)(sms > 0 ? sms : 148) * P.per_sm;
+    if (grid > rb) grid = rb;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(tcg::kThreads);
+    cfg.dynamicSmemBytes = P.L.total;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, J) != cudaSuccess) { cudaGetLastError(); return -1; }
+    return 0;
+}
+
+uint32_t tc_gemv_status_take()
+{
+    uint32_t v = 0;
+    if (cudaMemcpyFromSymbol(&v, tcg::g_tc_err, sizeof(v)) != cudaSuccess) { cudaGetLastError(); return 0xFFFFFFFFu; }
+    if (v) {
+        const uint32_t z = 0;
+        cudaMemcpyToSymbol(tcg::g_tc_err, &z, sizeof(z));
+    }
+    return v;
+}
+
+}  // namespace hxq

@@ -656,16 +656,21 @@ int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
 
 }  // namespace
 
+bool affine_gemm_fits(const uint16_t *x, const uint8_t *codes, uint32_t T, uint32_t I, uint32_t O, uint32_t gs)
+{
+    if (T == 0 || O == 0) return false;
+    if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return false;
+    if (((uintptr_t)x & 15u) || ((uintptr_t)codes & 15u)) return false;
+    return (uint64_t)T * I < (1ull << 40);
+}
+
 // Tensor-core path for bf16 activations.  Returns 1 when the shape is not
 // one it takes (the caller uses the GEMV), 0 on launch, -1 on error.
 int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
                      const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t T, uint32_t I, uint32_t O,
                      uint32_t gs, cudaStream_t s)
 {
-    if (T == 0 || O == 0) return 1;
-    if (I == 0 || I % gemm::kBK != 0 || gs == 0 || gs % 64u != 0 || I % gs != 0) return 1;
-    if (((uintptr_t)x & 15u) || ((uintptr_t)codes & 15u)) return 1;
-    if ((uint64_t)T * I >= (1ull << 40)) return 1;
+    if (!affine_gemm_fits(x, codes, T, I, O, gs)) return 1;
     gemm::Params p{};
     p.codes = codes; p.scales = scales; p.offsets = offsets; p.bias = bias;
     if (ldy < O || out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
@@ -702,5 +707,7 @@ extern "C" int hxq_cuda_affine_device_status(void)
         const uint32_t z = 0;
         cudaMemcpyToSymbol(hxq::gemm::g_gemm_err, &z, sizeof(z));
     }
-    return (int)v;
+    const uint32_t tc = hxq::tc_gemv_status_take();
+    if (tc == 0xFFFFFFFFu) return -1;
+    return (int)(v | tc);
 }

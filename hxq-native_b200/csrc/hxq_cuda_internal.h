@@ -152,8 +152,27 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
                  const uint16_t *kp, const uint32_t *e4, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O,
                  uint32_t ldy, cudaStream_t s);
+bool affine_gemm_fits(const uint16_t *x, const uint8_t *codes, uint32_t T, uint32_t I, uint32_t O, uint32_t gs);
 int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
                      const float *bias, const OutPtrs &out, uint32_t ldy, uint32_t T, uint32_t I, uint32_t O,
                      uint32_t gs, cudaStream_t s);
+
+// One matrix of a tensor-core affine GEMV launch (affine_tc_gemv.cu).
+constexpr uint32_t kMaxTcJobs = 8;
+struct TcMatrix {
+    const uint16_t *x;                    // bf16 activations [N][in_f]
+    const uint8_t *codes;                 // [out_f][in_f]
+    const float *scales, *offsets, *bias;
+    OutPtrs out;
+    uint32_t ldy, in_f, out_f, gs;
+};
+// Shape, alignment and shared-memory test for the tensor-core GEMV:
+// 1 <= N <= 16, in_f and gs multiples of 64, 16-byte aligned operands.
+bool tc_gemv_fits(const uint16_t *x, const uint8_t *codes, const float *scales, const float *offsets,
+                  uint32_t N, uint32_t in_f, uint32_t out_f, uint32_t gs);
+// Up to kMaxTcJobs matrices in one launch: 0 launched, 1 not taken, -1 error.
+int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStream_t s);
+// Reads and clears the kernel's status word (nonzero: a wait ran out).
+uint32_t tc_gemv_status_take();
 
 }  // namespace hxq

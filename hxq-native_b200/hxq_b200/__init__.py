@@ -37,6 +37,7 @@ HXQ_SCALAR_VQ, HXQ_VQ2D_8BIT, HXQ_VQ2D_12BIT, HXQ_AFFINE_G128 = 0, 1, 2, 3
 HXQ_BACKEND_AUTO, HXQ_BACKEND_CPU, HXQ_BACKEND_CUDA, HXQ_BACKEND_METAL, HXQ_BACKEND_VULKAN = range(5)
 HXQ_OUT_F32, HXQ_OUT_BF16 = 0, 1
 HXQ_IMAGE_STREAMED, HXQ_IMAGE_MATMUL = 1, 2
+HXQ_AFFINE_PATH_AUTO, HXQ_AFFINE_PATH_GEMV, HXQ_AFFINE_PATH_TC_GEMV, HXQ_AFFINE_PATH_GEMM = 0, 1, 2, 3
 MAX_BATCH = 64
 
 P = C.c_void_p
@@ -128,6 +129,8 @@ SIGNATURES = {
     "hxq_cuda_decompress_vq2d_12bit": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32]),
     "hxq_cuda_apply_sidecar": (C.c_float, [P, P, P, P, C.c_uint32, C.c_uint32]),
     "hxq_affine_group_matmul_bf16": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
+    "hxq_affine_group_matmul_bf16_path": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, C.c_int, P]),
+    "hxq_affine_group_matmul_bf16_auto_path": (C.c_int, [P, C.POINTER(AffineTensor), C.c_uint32]),
     "hxq_affine_group_matmul_async": (C.c_int, [P, C.POINTER(AffineTensor), P, C.c_uint32, P]),
     "hxq_cuda_affine_device_status": (C.c_int, []),
     "hxq_cuda_vq_matmul": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, P]),

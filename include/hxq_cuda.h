@@ -190,18 +190,39 @@ float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
 /* -- Affine matmul variants --------------------------------------------- */
 
 /* bf16 activations (uint16_t bit patterns, [N, in_f]); fp32 output.
- * One token: the streaming GEMV (exact products of bf16 x and integer
- * codes, fp32 accumulation).  From 2 tokens, when in_f % 128 == 0 and the
- * group size is a multiple of 64: the tcgen05 dequant-GEMM, which rounds
- * W = code*scale + offset to bf16 before the tensor-core product (fp32
- * accumulation): per output the error is at most 2^-9 of sum |x_i w_i|. */
+ * Up to 8 tokens, when in_f is a multiple of 128, the group size a multiple
+ * of 64 and the operands 16-byte aligned: the tensor-core GEMV (codes and
+ * activations exact in f16, exact products, fp32 accumulation).  From 9
+ * tokens, when
+ * in_f % 128 == 0 and the group size is a multiple of 64: the tcgen05
+ * dequant-GEMM, which rounds W = code*scale + offset to bf16 before the
+ * tensor-core product (fp32 accumulation): per output the error is at most
+ * 2^-9 of sum |x_i w_i|.  Other shapes: the CUDA-core streaming GEMV (exact
+ * products, fp32 accumulation). */
 int hxq_affine_group_matmul_bf16(const uint16_t *d_x_bf16,
                                  const hxq_affine_tensor_t *tensor,
                                  float *d_output, uint32_t N, void *stream);
-/* Waits for the device, then returns (and clears) the status word of the
- * tcgen05 dequant-GEMM: 0 when every pipeline wait completed, nonzero if
- * one ran out of time (the kernel then unwinds without writing results);
- * -1 on a CUDA error. */
+/* The same with the kernel chosen by the caller; -1 if that kernel cannot
+ * take the shape or alignment (the tensor-core GEMV: more than 16 tokens,
+ * in_f not a multiple of 128 or group size of 64, activations too long to
+ * stage;
+ * the GEMM: in_f not a multiple of 128, group size not a multiple of 64). */
+#define HXQ_AFFINE_PATH_AUTO     0
+#define HXQ_AFFINE_PATH_GEMV     1   /* CUDA-core streaming GEMV */
+#define HXQ_AFFINE_PATH_TC_GEMV  2   /* tensor-core GEMV, 1..16 tokens (auto: up to 8) */
+#define HXQ_AFFINE_PATH_GEMM     3   /* tcgen05 dequant-GEMM */
+int hxq_affine_group_matmul_bf16_path(const uint16_t *d_x_bf16,
+                                      const hxq_affine_tensor_t *tensor,
+                                      float *d_output, uint32_t N, int path, void *stream);
+/* The kernel hxq_affine_group_matmul_bf16 takes for these operands
+ * (HXQ_AFFINE_PATH_GEMV, _TC_GEMV or _GEMM), which fixes its error bound;
+ * -1 on a NULL tensor or N == 0. */
+int hxq_affine_group_matmul_bf16_auto_path(const uint16_t *d_x_bf16,
+                                           const hxq_affine_tensor_t *tensor, uint32_t N);
+/* Waits for the device, then returns (and clears) the status words of the
+ * tcgen05 dequant-GEMM and the tensor-core GEMV: 0 when every pipeline wait
+ * completed, nonzero if one ran out of time (the kernel then unwinds
+ * without writing results); -1 on a CUDA error. */
 int hxq_cuda_affine_device_status(void);
 
 /* -- Fused VQ-dequant matmul -------------------------------------------
@@ -269,10 +290,11 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
                                        uint32_t ldy, uint32_t N, void *stream);
 /* A batch of n affine matmuls (e.g. a layer's projections) with bf16
  * activations d_xs[i] ([N, in_features of tensor i]) and outputs
- * d_ys[i * n_out + k] ([N, ldys[i]], k < n_out).  At one token, matrices
- * whose shapes suit the streaming GEMV share launches (up to 8 per launch),
- * which pays the per-launch costs once for the batch; otherwise one call
- * per matrix.  Returns 0, or -1 on an error. */
+ * d_ys[i * n_out + k] ([N, ldys[i]], k < n_out).  Up to 8 tokens, when
+ * every matrix suits the tensor-core GEMV, and at one token, when every
+ * matrix suits the streaming GEMV, the matrices share launches (up to 8 per
+ * launch), which pays the per-launch costs once for the batch; otherwise
+ * one call per matrix.  Returns 0, or -1 on an error. */
 /* A batch of n fused VQ matmuls (e.g. a layer's projections), outputs as
  * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_GEMV_MAX
  * tokens the GEMV shares launches (up to 8 images per launch); more tokens

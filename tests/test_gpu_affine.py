@@ -29,6 +29,15 @@ def _tol_bf16(N, d):
     return GEMM_TOL if gemm else TOL
 
 
+def _tol_path(H, L, dev, xd, N):
+    """Tolerance of the kernel the automatic choice takes for these operands:
+    the bf16-weight GEMM's bound, else the exact GEMVs' 1e-5."""
+    t = dev.tensor(H)
+    p = L.hxq_affine_group_matmul_bf16_auto_path(xd.data_ptr(), C.byref(t), N)
+    assert p in (H.HXQ_AFFINE_PATH_GEMV, H.HXQ_AFFINE_PATH_TC_GEMV, H.HXQ_AFFINE_PATH_GEMM)
+    return GEMM_TOL if p == H.HXQ_AFFINE_PATH_GEMM else TOL
+
+
 def _scale(oracle, x, d):
     W = oracle.affine_decompress(d).reshape(d["out_f"], d["in_f"]).astype(np.float64)
     return np.abs(x.astype(np.float64)) @ np.abs(W).T
@@ -70,12 +79,17 @@ def _run_f32(torch, H, L, dev, x, api="struct"):
     return y.cpu().numpy()
 
 
-def _run_bf16(torch, H, L, dev, xh):
+def _run_bf16(torch, H, L, dev, xh, path=None):
+    """bf16 matmul through the automatic entry point, or with `path` forced."""
     xd = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
     y = torch.full((xh.shape[0], dev.d["out_f"]), float("nan"), dtype=torch.float32, device="cuda")
     t = dev.tensor(H)
     torch.cuda.synchronize()
-    assert L.hxq_affine_group_matmul_bf16(xd.data_ptr(), C.byref(t), y.data_ptr(), xh.shape[0], None) == 0
+    if path is None:
+        assert L.hxq_affine_group_matmul_bf16(xd.data_ptr(), C.byref(t), y.data_ptr(), xh.shape[0], None) == 0
+    else:
+        assert L.hxq_affine_group_matmul_bf16_path(xd.data_ptr(), C.byref(t), y.data_ptr(), xh.shape[0], path,
+                                                   None) == 0
     torch.cuda.synchronize()
     return y.cpu().numpy()
 
@@ -96,7 +110,10 @@ def test_c3_4096_small_batches(H, L, oracle, cuda, N):
     dev = Dev(cuda, d, d["bias"])
     ref = oracle.affine_matmul(x, d, bias=d["bias"])
     sc = _scale(oracle, x, d)
-    _check(_run_bf16(cuda, H, L, dev, xh), ref, sc, _tol_bf16(N, d))
+    xd = cuda.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+    tol = _tol_path(H, L, dev, xd, N)
+    assert (tol == TOL) == (N <= 8)           # up to 8 tokens: an exact-product GEMV
+    _check(_run_bf16(cuda, H, L, dev, xh), ref, sc, tol)
     _check(_run_f32(cuda, H, L, dev, x), ref, sc)
     assert L.hxq_cuda_affine_device_status() == 0
 
@@ -139,7 +156,7 @@ def test_tcgen05_gemm_shapes(H, L, oracle, cuda, O, I, gs, N):
     dev = Dev(cuda, d, d["bias"])
     ref = oracle.affine_matmul(x, d, bias=d["bias"])
     sc = _scale(oracle, x, d)
-    y = _run_bf16(cuda, H, L, dev, xh)
+    y = _run_bf16(cuda, H, L, dev, xh, path=H.HXQ_AFFINE_PATH_GEMM)
     assert L.hxq_cuda_affine_device_status() == 0
     _check(y, ref, sc, GEMM_TOL)
     # layout check: the same contraction in float64 with the kernel's own
@@ -192,7 +209,66 @@ def test_invalid_arguments(H, L, cuda):
     assert L.hxq_affine_group_matmul(x.data_ptr(), None, y.data_ptr(), 1) == -1
 
 
-@pytest.mark.parametrize("N", [1, 5])
+@pytest.mark.parametrize("O,I,gs,N", [(1, 128, 64, 1), (17, 128, 64, 3), (100, 768, 192, 8), (4096, 4096, 128, 1),
+                                      (4096, 4096, 128, 16), (513, 2048, 256, 9), (11008, 4096, 128, 2),
+                                      (4096, 11008, 128, 4), (33, 11008, 128, 1), (256, 4096, 512, 12)])
+def test_tc_gemv_vs_oracle(H, L, oracle, cuda, O, I, gs, N):
+    """The tensor-core GEMV (forced): ragged row blocks (1, 17, 100, 513
+    rows), K not a multiple of the 512-code stage, group sizes 64..512,
+    1..16 tokens (one and two 8-token tiles), bias on odd token counts."""
+    d = synth.affine(O, I, gs, O * 5 + I + N, bias=(N % 2 == 1))
+    xh, x = synth.activations(N, I, O + 3 * N)
+    dev = Dev(cuda, d, d["bias"])
+    y = _run_bf16(cuda, H, L, dev, xh, path=H.HXQ_AFFINE_PATH_TC_GEMV)
+    assert L.hxq_cuda_affine_device_status() == 0
+    _check(y, oracle.affine_matmul(x, d, bias=d["bias"]), _scale(oracle, x, d))
+
+
+def test_tc_gemv_byte_codes_and_token_scales(H, L, oracle, cuda):
+    """Every byte value as a code (widened exactly), and tokens of very
+    different sizes (2^-120 .. 2^40, an all-zero token, values 2^-30 below
+    the token's largest): each token's power-of-two staging scale keeps the
+    products exact."""
+    O, I, gs, N = 96, 1024, 128, 6
+    d = synth.affine(O, I, gs, 77)
+    d["codes"] = np.random.default_rng(5).integers(0, 256, O * I).astype(np.uint8)
+    _, x = synth.activations(N, I, 78)
+    x = x * np.array([1.0, 2.0 ** -60, 2.0 ** 40, 0.0, 1.0, 2.0 ** -120], np.float32)[:, None]
+    x[4, ::7] *= np.float32(2.0 ** -30)
+    xh = synth.bf16_round(x.astype(np.float32)).reshape(N, I)
+    x = synth.bf16_to_f32(xh).reshape(N, I)
+    dev = Dev(cuda, d)
+    ref = oracle.affine_matmul(x, d)
+    sc = _scale(oracle, x, d)
+    for path in (H.HXQ_AFFINE_PATH_TC_GEMV, H.HXQ_AFFINE_PATH_AUTO):
+        y = _run_bf16(cuda, H, L, dev, xh, path=path)
+        _check(y, ref, sc)
+        assert not np.any(y[3])                 # the zero token: exactly zero
+    assert L.hxq_cuda_affine_device_status() == 0
+
+
+def test_path_selection(H, L, cuda):
+    d = synth.affine(256, 4096, 128, 3)
+    dev = Dev(cuda, d)
+    t = dev.tensor(H)
+    x = cuda.zeros(64 * 4096, dtype=cuda.int16, device="cuda")
+    y = cuda.zeros(64 * 256, dtype=cuda.float32, device="cuda")
+    auto = L.hxq_affine_group_matmul_bf16_auto_path
+    assert auto(x.data_ptr(), C.byref(t), 1) == H.HXQ_AFFINE_PATH_TC_GEMV
+    assert auto(x.data_ptr(), C.byref(t), 8) == H.HXQ_AFFINE_PATH_TC_GEMV
+    assert auto(x.data_ptr(), C.byref(t), 9) == H.HXQ_AFFINE_PATH_GEMM
+    assert auto(x.data_ptr() + 2, C.byref(t), 4) == H.HXQ_AFFINE_PATH_GEMV     # unaligned activations
+    assert auto(x.data_ptr(), None, 4) == -1
+    run = L.hxq_affine_group_matmul_bf16_path
+    assert run(x.data_ptr(), C.byref(t), y.data_ptr(), 17, H.HXQ_AFFINE_PATH_TC_GEMV, None) == -1
+    assert run(x.data_ptr(), C.byref(t), y.data_ptr(), 4, 9, None) == -1
+    for p in (H.HXQ_AFFINE_PATH_GEMV, H.HXQ_AFFINE_PATH_TC_GEMV, H.HXQ_AFFINE_PATH_GEMM):
+        assert run(x.data_ptr(), C.byref(t), y.data_ptr(), 4, p, None) == 0
+    cuda.cuda.synchronize()
+    assert L.hxq_cuda_affine_device_status() == 0
+
+
+@pytest.mark.parametrize("N", [1, 5, 16])
 def test_batch_of_layer_projections(H, L, cuda, N):
     """A layer's projections in one batch call (shared launches at one
     token), two outputs each at a column offset: bit-identical to one call

@@ -34,8 +34,8 @@
 //     products with fp32 accumulation in two independent chains, over a K
 //     permutation shared by the code and activation fragments so that both
 //     come from single 128-bit / 64-bit loads;
-//   * groups: the group size is a multiple of 64, so a 64-code chunk lies in
-//     one group; its fresh partial sums are scaled by 2^-e s[o,g] and it adds
+//   * groups: the group size is a power of two of at least 64, so a 64-code
+//     chunk lies in one group; its fresh partial sums are scaled by 2^-e s[o,g] and it adds
 //     off[o,g] times its activation sum;
 //   * the 8 warps' partial sums of a row block are added in a fixed order,
 //     bias fused into the store (into every output buffer).
@@ -249,12 +249,16 @@ __device__ __forceinline__ uint32_t group_of(uint32_t k, const Job &b)
 }
 
 // Stage, for one warp, the activations of the K slices it owns: chunks
-// k0 = 1024 st + 128 warp + 64 u (u = 0, 1) of every token.  A pass covers 4
+// k0 = 1024 st + 128 warp + 64 u (u = 0, 1) of every token.  MERGE: the two
+// chunks of a stage get one factor (the group size is a multiple of 128, so
+// they also share the group).  A pass covers 4
 // chunks of one token, 8 lanes per chunk, one 128-bit load (8 values) per
-// lane; four passes are in flight at a time.  Per chunk: the largest |x|
+// lane; eight passes are in flight at a time (one round trip for a token of
+// up to 16384 values).  Per chunk: the largest |x|
 // and the sum over the 8 lanes (xor shuffles, a fixed tree), the power of
 // two 2^e, the f16 values x 2^e into the activation rows, {2^-e, sum} into
 // the chunk table.
+template <bool MERGE>
 __device__ void stage_x_warp(const Job &b, uint32_t N, uint8_t *smem, const Layout &L, uint32_t warp,
                              uint32_t lane)
 {
@@ -297,6 +301,9 @@ __device__ void stage_x_warp(const Job &b, uint32_t N, uint8_t *smem, const Layo
                 sum += __shfl_xor_sync(0xffffffffu, sum, o);
                 m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
             }
+            // merged: the warp's two chunks of a stage (lanes 16i..16i+7 and
+            // 16i+8..16i+15) share one factor, from the larger of their maxima
+            if (MERGE) m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
             if (!val[r]) continue;
             // 2^e brings the largest |x| (bf16 bits m, exponent field m >> 7) into [2^14, 2^15)
             const uint32_t ef = m >> 7;                  // 0: zero or subnormal; 255: inf or NaN
@@ -318,17 +325,29 @@ __device__ void stage_x_warp(const Job &b, uint32_t N, uint8_t *smem, const Layo
     __syncwarp();
 }
 
-// One 64-code chunk of a warp: rows g and g+8 of the row block, its codes at
-// 16-byte unit `unit` of 128-byte lines `line` and line + 32 of the half
-// stage `hs`; activation fragments from xrow[t] (per token tile, NULL past
-// N).  Two independent accumulation chains, added at the end.
-template <int NT>
-__device__ __forceinline__ void chunk_mma(const uint8_t *hs, uint32_t line, uint32_t unit,
-                                         const uint16_t *const (&xr)[NT], uint32_t k0, float (&d)[NT][4])
+__device__ __forceinline__ uint4 lds128(uint32_t a)
 {
-    const uint8_t *p = hs + line * 128u + unit * 16u;
-    const uint4 q0 = *reinterpret_cast<const uint4 *>(p);
-    const uint4 q1 = *reinterpret_cast<const uint4 *>(p + 32u * 128u);
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t a)
+{
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+
+// One 64-code chunk of a warp: rows g and g+8 of the row block (their 16
+// codes at shared address ca and ca + 32 lines), the activation fragments of
+// each token tile at xa[tt] (the lane's token, its 16 values of the chunk).
+// Two independent accumulation chains, added at the end.
+template <int NT>
+__device__ __forceinline__ void chunk_mma(uint32_t ca, const uint32_t (&xa)[NT], float (&d)[NT][4])
+{
+    const uint4 q0 = lds128(ca);
+    const uint4 q1 = lds128(ca + 32u * 128u);
     const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
     const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
     float e[NT][4];
@@ -342,8 +361,7 @@ __device__ __forceinline__ void chunk_mma(const uint8_t *hs, uint32_t line, uint
         const uint32_t a1 = codes_f16x2<0>(w1[jj]), a3 = codes_f16x2<1>(w1[jj]);
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
-            uint2 bb = make_uint2(0u, 0u);
-            if (xr[tt]) bb = *reinterpret_cast<const uint2 *>(xr[tt] + k0 + (uint32_t)jj * 4u);
+            const uint2 bb = lds64(xa[tt] + 8u * (uint32_t)jj);
             if (jj & 1) mma16816(e[tt], a0, a1, a2, a3, bb.x, bb.y);
             else mma16816(d[tt], a0, a1, a2, a3, bb.x, bb.y);
         }
@@ -356,32 +374,97 @@ __device__ __forceinline__ void chunk_mma(const uint8_t *hs, uint32_t line, uint
 
 // A chunk's partial sums into the row pair's accumulators: times 2^-e and
 // the group's scale, plus the group's offset times the chunk's activation
-// sum.
+// sum.  sa: the {scale, offset} of row g for the chunk's group (row g + 8 is
+// 64 bytes on); ca0 / ca1[tt]: the {2^-e, sum} of the lane's two tokens for
+// the chunk.  Token columns past N read some valid token's values; those
+// columns are never stored.
 template <int NT>
-__device__ __forceinline__ void chunk_apply(const float (&d)[NT][4], uint32_t k0, const Job &b, const float *sf,
-                                           const float2 *xc, uint32_t g, uint32_t t, uint32_t N,
-                                           float (&as)[NT][4], float (&af)[NT][4])
+__device__ __forceinline__ void chunk_apply(const float (&d)[NT][4], uint32_t sa, const uint32_t (&ca0)[NT],
+                                           const uint32_t (&ca1)[NT], uint32_t kc, float (&as)[NT][4],
+                                           float (&af)[NT][4])
 {
-    const uint32_t gi = group_of(k0, b), kc = k0 / kChunk, nck = b.in_f / kChunk;
-    const float2 sf0 = *reinterpret_cast<const float2 *>(sf + gi * kSfStride + 2u * g);
-    const float2 sf1 = *reinterpret_cast<const float2 *>(sf + gi * kSfStride + 2u * (g + 8u));
+    const uint2 s0 = lds64(sa), s1 = lds64(sa + 64u);
+    const float sc0 = __uint_as_float(s0.x), of0 = __uint_as_float(s0.y);
+    const float sc1 = __uint_as_float(s1.x), of1 = __uint_as_float(s1.y);
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt) {
-        const uint32_t n0 = (uint32_t)tt * 8u + 2u * t, n1 = n0 + 1u;
-        const float2 c0 = n0 < N ? xc[n0 * nck + kc] : make_float2(0.0f, 0.0f);
-        const float2 c1 = n1 < N ? xc[n1 * nck + kc] : make_float2(0.0f, 0.0f);
-        as[tt][0] = fmaf(sf0.x, d[tt][0] * c0.x, as[tt][0]);
-        as[tt][1] = fmaf(sf0.x, d[tt][1] * c1.x, as[tt][1]);
-        as[tt][2] = fmaf(sf1.x, d[tt][2] * c0.x, as[tt][2]);
-        as[tt][3] = fmaf(sf1.x, d[tt][3] * c1.x, as[tt][3]);
-        af[tt][0] = fmaf(sf0.y, c0.y, af[tt][0]);
-        af[tt][1] = fmaf(sf0.y, c1.y, af[tt][1]);
-        af[tt][2] = fmaf(sf1.y, c0.y, af[tt][2]);
-        af[tt][3] = fmaf(sf1.y, c1.y, af[tt][3]);
+        const uint2 c0 = lds64(ca0[tt] + 8u * kc), c1 = lds64(ca1[tt] + 8u * kc);
+        const float f0 = __uint_as_float(c0.x), x0 = __uint_as_float(c0.y);
+        const float f1 = __uint_as_float(c1.x), x1 = __uint_as_float(c1.y);
+        as[tt][0] = fmaf(sc0, d[tt][0] * f0, as[tt][0]);
+        as[tt][1] = fmaf(sc0, d[tt][1] * f1, as[tt][1]);
+        as[tt][2] = fmaf(sc1, d[tt][2] * f0, as[tt][2]);
+        as[tt][3] = fmaf(sc1, d[tt][3] * f1, as[tt][3]);
+        af[tt][0] = fmaf(of0, x0, af[tt][0]);
+        af[tt][1] = fmaf(of0, x1, af[tt][1]);
+        af[tt][2] = fmaf(of1, x0, af[tt][2]);
+        af[tt][3] = fmaf(of1, x1, af[tt][3]);
     }
 }
 
+// Both 64-code chunks of a warp's stage into one set of accumulators (their
+// activations share a factor): codes at ca0 and ca1, activations from xa[tt]
+// (chunk 0) and xa[tt] + 128 bytes (chunk 1).
 template <int NT>
+__device__ __forceinline__ void pair_mma(uint32_t ca0, uint32_t ca1, const uint32_t (&xa)[NT], float (&d)[NT][4])
+{
+    float e[NT][4];
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { d[tt][u] = 0.0f; e[tt][u] = 0.0f; }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t ca = h ? ca1 : ca0;
+        const uint4 q0 = lds128(ca);
+        const uint4 q1 = lds128(ca + 32u * 128u);
+        const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
+        const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t a0 = codes_f16x2<0>(w0[jj]), a2 = codes_f16x2<1>(w0[jj]);
+            const uint32_t a1 = codes_f16x2<0>(w1[jj]), a3 = codes_f16x2<1>(w1[jj]);
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+                const uint2 bb = lds64(xa[tt] + 128u * (uint32_t)h + 8u * (uint32_t)jj);
+                if (jj & 1) mma16816(e[tt], a0, a1, a2, a3, bb.x, bb.y);
+                else mma16816(d[tt], a0, a1, a2, a3, bb.x, bb.y);
+            }
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d[tt][u] += e[tt][u];
+}
+
+// The stage's merged partial sums into the accumulators: one factor, one
+// group scale, the offset times the two chunks' activation sums.
+template <int NT>
+__device__ __forceinline__ void pair_apply(const float (&d)[NT][4], uint32_t sa, const uint32_t (&ca0)[NT],
+                                          const uint32_t (&ca1)[NT], uint32_t kc, float (&as)[NT][4],
+                                          float (&af)[NT][4])
+{
+    const uint2 s0 = lds64(sa), s1 = lds64(sa + 64u);
+    const float sc0 = __uint_as_float(s0.x), of0 = __uint_as_float(s0.y);
+    const float sc1 = __uint_as_float(s1.x), of1 = __uint_as_float(s1.y);
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+        const uint4 c0 = lds128(ca0[tt] + 8u * kc), c1 = lds128(ca1[tt] + 8u * kc);
+        const float f0 = __uint_as_float(c0.x), x0 = __uint_as_float(c0.y) + __uint_as_float(c0.w);
+        const float f1 = __uint_as_float(c1.x), x1 = __uint_as_float(c1.y) + __uint_as_float(c1.w);
+        as[tt][0] = fmaf(sc0, d[tt][0] * f0, as[tt][0]);
+        as[tt][1] = fmaf(sc0, d[tt][1] * f1, as[tt][1]);
+        as[tt][2] = fmaf(sc1, d[tt][2] * f0, as[tt][2]);
+        as[tt][3] = fmaf(sc1, d[tt][3] * f1, as[tt][3]);
+        af[tt][0] = fmaf(of0, x0, af[tt][0]);
+        af[tt][1] = fmaf(of0, x1, af[tt][1]);
+        af[tt][2] = fmaf(of1, x0, af[tt][2]);
+        af[tt][3] = fmaf(of1, x1, af[tt][3]);
+    }
+}
+
+template <int NT, bool MERGE>
 __global__ void __launch_bounds__(kThreads, 2)
 affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
 {
@@ -463,8 +546,8 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
     const uint32_t ct = threadIdx.x;        // 0..255
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t N = J.N;
-    const uint16_t *xh = reinterpret_cast<const uint16_t *>(smem + L.xh);
-    const float2 *xc = reinterpret_cast<const float2 *>(smem + L.xc);
+    const uint32_t xh_a = smem_u32(smem + L.xh), xc_a = smem_u32(smem + L.xc), sf_a = smem_u32(smem + L.sf);
+    const uint32_t stage_a = smem_u32(smem);
     float *sf = reinterpret_cast<float *>(smem + L.sf);
     float *red = reinterpret_cast<float *>(smem + L.red);
     constexpr uint32_t NTOK = 8u * NT;
@@ -472,25 +555,34 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
     const uint32_t half = warp >> 2, cl = warp & 3u;
     const uint32_t line = g * 4u + cl;
     const uint32_t unit0 = t ^ (line & 7u), unit1 = (4u + t) ^ (line & 7u);
+    const uint32_t coff0 = half * kHalfBytes + line * 128u + unit0 * 16u;
+    const uint32_t coff1 = half * kHalfBytes + line * 128u + unit1 * 16u;
     uint32_t slot = 0, ph = 0, j = 0, rbi = 0, cur = 0xFFFFFFFFu;
     bool ok = true;
     for (uint32_t rb = rb0; rb < rb1; ++rb, ++rbi) {
         while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
         const Job &b = J.job[j];
         if (j != cur) {
-            stage_x_warp(b, N, smem, L, warp, lane);   // this warp's K slices only
+            stage_x_warp<MERGE>(b, N, smem, L, warp, lane);   // this warp's K slices only
             cur = j;
         }
         const uint32_t in_f = b.in_f, ng = b.ng;
         const uint32_t row0 = (rb - b.rb_begin) * kRows;
         const uint32_t rv = min(kRows, b.out_f - row0);
         const uint32_t nst = (in_f + kKC - 1u) / kKC;
-        const uint16_t *xr[NT];
+        // 32-bit shared addresses of this lane's activation fragments and chunk
+        // factors (tokens past N clamped to N - 1: their columns are not stored)
+        const uint32_t nck = in_f / kChunk;
+        uint32_t xa0[NT], ca0[NT], ca1[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
-            const uint32_t n = (uint32_t)tt * 8u + g;
-            xr[tt] = n < N ? xh + (size_t)n * (in_f + 4u) + t * 16u : nullptr;
+            const uint32_t n = min((uint32_t)tt * 8u + g, N - 1u);
+            const uint32_t n0 = min((uint32_t)tt * 8u + 2u * t, N - 1u), n1 = min((uint32_t)tt * 8u + 2u * t + 1u, N - 1u);
+            xa0[tt] = xh_a + 2u * (n * (in_f + 4u) + t * 16u);
+            ca0[tt] = xc_a + 8u * n0 * nck;
+            ca1[tt] = xc_a + 8u * n1 * nck;
         }
+        const uint32_t gsh = b.gs_shift;
         float as[NT][4], af[NT][4];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt)
@@ -503,8 +595,9 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 // rows past the copied bytes come from global memory, rows past the matrix are 0
                 const uint32_t sbytes = (rv * ng * 4u) & ~15u;
                 const float *gsc = b.scales + (size_t)row0 * ng, *gof = b.offsets + (size_t)row0 * ng;
+                const uint32_t q256 = 256u / ng, r256 = 256u - q256 * ng;
+                uint32_t r = ct / ng, gg = ct - r * ng;
                 for (uint32_t i = ct; i < kRows * ng; i += 256u) {
-                    const uint32_t r = i / ng, gg = i - r * ng;
                     float sv = 0.0f, fv = 0.0f;
                     if (ok && r < rv) {
                         sv = i * 4u < sbytes ? sbuf[i] : __ldg(gsc + i);
@@ -512,21 +605,37 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     }
                     sf[gg * kSfStride + 2u * r] = sv;
                     sf[gg * kSfStride + 2u * r + 1u] = fv;
+                    gg += r256;
+                    r += q256;
+                    if (gg >= ng) { gg -= ng; ++r; }
                 }
                 asm volatile("bar.sync 1, 256;" ::: "memory");
                 if (ok && lane == 0) mbar_arrive(sdone);
             }
             const uint32_t kb = st * kKC + warp * kWarpK;
             if (ok && kb < in_f) {
-                const uint8_t *hs = smem + slot * kStageBytes + half * kHalfBytes;
                 // in_f is a multiple of 128: both chunks of the warp are inside K
+                const uint32_t sa = stage_a + slot * kStageBytes;
+                uint32_t xa[NT];
                 float d[NT][4];
-                chunk_mma<NT>(hs, line, unit0, xr, kb, d);
-                chunk_apply<NT>(d, kb, b, sf, xc, g, t, N, as, af);
-                chunk_mma<NT>(hs, line, unit1, xr, kb + kChunk, d);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
-                chunk_apply<NT>(d, kb + kChunk, b, sf, xc, g, t, N, as, af);
+#pragma unroll
+                for (int tt = 0; tt < NT; ++tt) xa[tt] = xa0[tt] + 2u * kb;
+                if constexpr (MERGE) {
+                    pair_mma<NT>(sa + coff0, sa + coff1, xa, d);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
+                    pair_apply<NT>(d, sf_a + (kb >> gsh) * (kSfStride * 4u) + 8u * g, ca0, ca1, kb >> 6, as, af);
+                } else {
+                    chunk_mma<NT>(sa + coff0, xa, d);
+                    chunk_apply<NT>(d, sf_a + (kb >> gsh) * (kSfStride * 4u) + 8u * g, ca0, ca1, kb >> 6, as, af);
+#pragma unroll
+                    for (int tt = 0; tt < NT; ++tt) xa[tt] += 2u * kChunk;
+                    chunk_mma<NT>(sa + coff1, xa, d);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
+                    const uint32_t k1 = kb + kChunk;
+                    chunk_apply<NT>(d, sf_a + (k1 >> gsh) * (kSfStride * 4u) + 8u * g, ca0, ca1, k1 >> 6, as, af);
+                }
             } else {
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(empty + slot);
@@ -589,7 +698,7 @@ bool tc_gemv_fits(const uint16_t *x, const uint8_t *codes, const float *scales, 
 {
     auto al = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
     if (N == 0 || N > 16u || out_f == 0 || in_f == 0 || gs == 0) return false;
-    if (in_f % 128u != 0 || gs % tcg::kChunk != 0 || in_f % gs != 0) return false;
+    if (in_f % 128u != 0 || gs < tcg::kChunk || (gs & (gs - 1u)) != 0 || in_f % gs != 0) return false;
     if (!x || !codes || !scales || !offsets || !al(x) || !al(codes) || !al(scales) || !al(offsets)) return false;
     return tcg::plan_for(N, in_f / gs, in_f).stages != 0;
 }
@@ -670,16 +779,22 @@ int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStrea
     if (P.stages == 0) return 1;
     J.stages = P.stages;
     const uint32_t nt = N > 8u ? 2u : 1u;
-    static std::atomic<uint64_t> configured[2];   // per NT: one bit per device
+    // one factor and one scale per warp stage when every group size is a multiple of 128
+    bool merge = true;
+    for (uint32_t i = 0; i < n; ++i) merge = merge && m[i].gs % 128u == 0;
+    const uint32_t variant = (nt - 1u) * 2u + (merge ? 1u : 0u);
+    static std::atomic<uint64_t> configured[4];   // per instantiation: one bit per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
-    auto kern = nt == 1u ? affine_tc_gemv_kernel<1> : affine_tc_gemv_kernel<2>;
-    if (!(configured[nt - 1u].load(std::memory_order_acquire) & (1ull << dev))) {
+    void (*kerns[4])(Jobs) = {affine_tc_gemv_kernel<1, false>, affine_tc_gemv_kernel<1, true>,
+                              affine_tc_gemv_kernel<2, false>, affine_tc_gemv_kernel<2, true>};
+    auto kern = kerns[variant];
+    if (!(configured[variant].load(std::memory_order_acquire) & (1ull << dev))) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
             cudaGetLastError();
             return -1;
         }
-        configured[nt - 1u].fetch_or(1ull << dev, std::memory_order_acq_rel);
+        configured[variant].fetch_or(1ull << dev, std::memory_order_acq_rel);
     }
     uint32_t grid = (uint32_t)(sms > 0 ? sms : 148) * P.per_sm;
     if (grid > rb) grid = rb;

@@ -209,7 +209,7 @@ def test_invalid_arguments(H, L, cuda):
     assert L.hxq_affine_group_matmul(x.data_ptr(), None, y.data_ptr(), 1) == -1
 
 
-@pytest.mark.parametrize("O,I,gs,N", [(1, 128, 64, 1), (17, 128, 64, 3), (100, 768, 192, 8), (4096, 4096, 128, 1),
+@pytest.mark.parametrize("O,I,gs,N", [(1, 128, 64, 1), (17, 128, 64, 3), (100, 768, 256, 8), (4096, 4096, 128, 1),
                                       (4096, 4096, 128, 16), (513, 2048, 256, 9), (11008, 4096, 128, 2),
                                       (4096, 11008, 128, 4), (33, 11008, 128, 1), (256, 4096, 512, 12)])
 def test_tc_gemv_vs_oracle(H, L, oracle, cuda, O, I, gs, N):

@@ -26,6 +26,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <vector>
 
 #include "hxq_affine.h"
 #include "hxq_cuda.h"
@@ -618,65 +619,71 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
         o.n = n_out;
         return true;
     };
-    // up to 8 tokens: matrices that suit the tensor-core GEMV share
-    // launches of up to 8 matrices
-    bool all_tc = N <= hxq::kTcGemvMaxTokens;
-    for (uint32_t i = 0; i < n && all_tc; ++i) {
-        const hxq_affine_tensor_t &t = tensors[i];
-        all_tc = ldys[i] >= t.out_features &&
-                 hxq::tc_gemv_fits(d_xs[i], t.indices, t.scales, t.offsets, N, t.in_features, t.out_features,
-                                   t.group_size);
-    }
-    if (all_tc) {
-        const int sms = hxq::sm_count();
-        for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxTcJobs) {
-            hxq::TcMatrix m[hxq::kMaxTcJobs];
-            uint32_t k = 0;
-            for (uint32_t i = i0; i < n && k < hxq::kMaxTcJobs; ++i, ++k) {
+    // The batch in three parts, each matrix in the first that takes it:
+    // up to 8 tokens, matrices that suit the tensor-core GEMV share launches
+    // of up to 8; at one token, the rest that suit the streaming GEMV share
+    // launches of up to 8; anything left runs one call per matrix.
+    std::vector<uint8_t> done(n, 0);
+    const int sms = hxq::sm_count();
+    if (N <= hxq::kTcGemvMaxTokens) {
+        hxq::TcMatrix m[hxq::kMaxTcJobs];
+        uint32_t k = 0;
+        for (uint32_t i = 0; i <= n; ++i) {
+            if (i < n) {
                 const hxq_affine_tensor_t &t = tensors[i];
+                if (ldys[i] < t.out_features ||
+                    !hxq::tc_gemv_fits(d_xs[i], t.indices, t.scales, t.offsets, N, t.in_features, t.out_features,
+                                       t.group_size))
+                    continue;
                 hxq::OutPtrs o;
                 if (!outs_of(i, o)) return -1;
-                m[k] = hxq::TcMatrix{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, ldys[i], t.in_features,
-                                     t.out_features, t.group_size};
+                m[k++] = hxq::TcMatrix{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, ldys[i], t.in_features,
+                                       t.out_features, t.group_size};
+                done[i] = 1;
             }
-            if (hxq::launch_tc_gemv(k, m, N, sms, s) != 0) return -1;
+            if (k == hxq::kMaxTcJobs || (i == n && k > 0)) {
+                if (hxq::launch_tc_gemv(k, m, N, sms, s) != 0) return -1;
+                k = 0;
+            }
         }
-        return 0;
     }
-    // one token: every matrix whose shape suits the batched GEMV goes into
-    // launches of up to 8 matrices; the rest one call each
-    bool all_fast = N == 1;
-    for (uint32_t i = 0; i < n && all_fast; ++i) {
-        const hxq_affine_tensor_t &t = tensors[i];
-        all_fast = t.indices && t.scales && t.offsets && d_xs[i] && t.group_size && t.in_features &&
-                   t.group_size % 16u == 0 && t.in_features % t.group_size == 0 && t.in_features % 16u == 0 &&
-                   ldys[i] >= t.out_features && hxq::aligned(d_xs[i], 16) && hxq::aligned(t.indices, 16) &&
-                   (size_t)t.in_features * 4u + (size_t)(t.in_features / 16u) * 4u <= hxq::kGemvStageMax;
-    }
-    if (all_fast) {
-        const int sms = hxq::sm_count();
-        for (uint32_t i0 = 0; i0 < n; i0 += hxq::kMaxGemvJobs) {
-            hxq::GemvJobs J{};
-            uint32_t rows = 0;
-            uint64_t ncodes = 0;
-            for (uint32_t i = i0; i < n && J.n < hxq::kMaxGemvJobs; ++i) {
+    if (N == 1) {
+        hxq::GemvJobs J{};
+        uint32_t rows = 0;
+        uint64_t ncodes = 0;
+        for (uint32_t i = 0; i <= n; ++i) {
+            if (i < n && !done[i]) {
                 const hxq_affine_tensor_t &t = tensors[i];
-                hxq::OutPtrs o;
-                if (!outs_of(i, o)) return -1;
-                const uint32_t gs = t.group_size;
-                const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
-                J.job[J.n++] = hxq::GemvJob{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, t.in_features,
-                                            t.out_features, gs, gs_shift, t.in_features / gs, rows, ncodes};
-                rows += t.out_features;
-                ncodes += (uint64_t)t.out_features * t.in_features;
+                const bool fits = t.indices && t.scales && t.offsets && d_xs[i] && t.group_size && t.in_features &&
+                                  t.group_size % 16u == 0 && t.in_features % t.group_size == 0 &&
+                                  t.in_features % 16u == 0 && ldys[i] >= t.out_features &&
+                                  hxq::aligned(d_xs[i], 16) && hxq::aligned(t.indices, 16) &&
+                                  (size_t)t.in_features * 4u + (size_t)(t.in_features / 16u) * 4u <=
+                                      hxq::kGemvStageMax;
+                if (fits) {
+                    hxq::OutPtrs o;
+                    if (!outs_of(i, o)) return -1;
+                    const uint32_t gs = t.group_size;
+                    const uint32_t gs_shift = (gs & (gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(gs) : 32u;
+                    J.job[J.n++] = hxq::GemvJob{d_xs[i], t.indices, t.scales, t.offsets, t.bias, o, t.in_features,
+                                                t.out_features, gs, gs_shift, t.in_features / gs, rows, ncodes};
+                    rows += t.out_features;
+                    ncodes += (uint64_t)t.out_features * t.in_features;
+                    done[i] = 1;
+                }
             }
-            J.total_rows = rows;
-            J.total_codes = ncodes;
-            if (hxq::launch_gemv_jobs<uint16_t>(J, sms, s) != 0) return -1;
+            if (J.n == hxq::kMaxGemvJobs || (i == n && J.n > 0)) {
+                J.total_rows = rows;
+                J.total_codes = ncodes;
+                if (hxq::launch_gemv_jobs<uint16_t>(J, sms, s) != 0) return -1;
+                J = hxq::GemvJobs{};
+                rows = 0;
+                ncodes = 0;
+            }
         }
-        return 0;
     }
     for (uint32_t i = 0; i < n; ++i) {
+        if (done[i]) continue;
         const hxq_affine_tensor_t &t = tensors[i];
         hxq::OutPtrs o;
         if (!outs_of(i, o)) return -1;

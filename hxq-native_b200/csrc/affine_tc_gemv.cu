@@ -59,13 +59,16 @@ namespace hxq {
 namespace tcg {
 
 constexpr uint32_t kConsumers = 8;                      // consumer warps
-constexpr uint32_t kThreads = (kConsumers + 1u) * 32u;  // + one producer warp
+constexpr uint32_t kCThreads = kConsumers * 32u;        // consumer threads
+constexpr uint32_t kThreads = kCThreads + 32u;          // + one producer warp
+constexpr uint32_t kCtasPerSm = 2;                      // resident CTAs per SM
+#define HXQ_TC_BAR_CONSUMERS "bar.sync 1, 256;"
 constexpr uint32_t kChunk = 64;                         // codes of K per MMA chunk
 constexpr uint32_t kWarpK = 2u * kChunk;                // codes of K per warp per stage
 constexpr uint32_t kKC = kWarpK * kConsumers;           // 1024 codes of K per stage
 constexpr uint32_t kRows = 16;                          // rows per block (MMA M)
 constexpr uint32_t kHalfBytes = kRows * 512u;           // one box: [16 rows][4][128 B], swizzled
-constexpr uint32_t kStageBytes = 2u * kHalfBytes;       // 16 KB
+constexpr uint32_t kStageBytes = kRows * kKC;           // kKC / 512 boxes
 constexpr uint32_t kMaxStages = 6;
 constexpr uint32_t kSfStride = 2u * kRows + 2u;         // floats per group in the transposed scales
 constexpr uint64_t kWaitCycles = 2000000000ull;          // ~1 s at 1.9 GHz
@@ -465,7 +468,7 @@ __device__ __forceinline__ void pair_apply(const float (&d)[NT][4], uint32_t sa,
 }
 
 template <int NT, bool MERGE>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -524,9 +527,10 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     // the full boxes count, including the zero fill past the matrix
                     mbar_expect_tx(full + slot, kStageBytes + 2u * sbytes);
                     uint8_t *dst = smem + slot * kStageBytes;
-                    tma_load_3d(dst, &b.map, full + slot, 0, (int32_t)(st * (kKC / 128u)), (int32_t)row0);
-                    tma_load_3d(dst + kHalfBytes, &b.map, full + slot, 0, (int32_t)(st * (kKC / 128u) + 4u),
-                                (int32_t)row0);
+#pragma unroll
+                    for (uint32_t h = 0; h < kKC / 512u; ++h)
+                        tma_load_3d(dst + h * kHalfBytes, &b.map, full + slot, 0,
+                                    (int32_t)(st * (kKC / 128u) + 4u * h), (int32_t)row0);
                     if (sbytes) {
                         bulk_g2s(sbuf, b.scales + (size_t)row0 * b.ng, sbytes, full + slot);
                         bulk_g2s(sbuf + sb_stride, b.offsets + (size_t)row0 * b.ng, sbytes, full + slot);
@@ -595,9 +599,9 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 // rows past the copied bytes come from global memory, rows past the matrix are 0
                 const uint32_t sbytes = (rv * ng * 4u) & ~15u;
                 const float *gsc = b.scales + (size_t)row0 * ng, *gof = b.offsets + (size_t)row0 * ng;
-                const uint32_t q256 = 256u / ng, r256 = 256u - q256 * ng;
+                const uint32_t qs = kCThreads / ng, rs = kCThreads - qs * ng;
                 uint32_t r = ct / ng, gg = ct - r * ng;
-                for (uint32_t i = ct; i < kRows * ng; i += 256u) {
+                for (uint32_t i = ct; i < kRows * ng; i += kCThreads) {
                     float sv = 0.0f, fv = 0.0f;
                     if (ok && r < rv) {
                         sv = i * 4u < sbytes ? sbuf[i] : __ldg(gsc + i);
@@ -605,11 +609,11 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     }
                     sf[gg * kSfStride + 2u * r] = sv;
                     sf[gg * kSfStride + 2u * r + 1u] = fv;
-                    gg += r256;
-                    r += q256;
+                    gg += rs;
+                    r += qs;
                     if (gg >= ng) { gg -= ng; ++r; }
                 }
-                asm volatile("bar.sync 1, 256;" ::: "memory");
+                asm volatile(HXQ_TC_BAR_CONSUMERS ::: "memory");
                 if (ok && lane == 0) mbar_arrive(sdone);
             }
             const uint32_t kb = st * kKC + warp * kWarpK;
@@ -652,8 +656,8 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
             rd[(warp * kRows + g + 8u) * NTOK + n0] = as[tt][2] + af[tt][2];
             rd[(warp * kRows + g + 8u) * NTOK + n0 + 1u] = as[tt][3] + af[tt][3];
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        for (uint32_t idx = ct; idx < kRows * NTOK; idx += 256u) {
+        asm volatile(HXQ_TC_BAR_CONSUMERS ::: "memory");
+        for (uint32_t idx = ct; idx < kRows * NTOK; idx += kCThreads) {
             const uint32_t row = idx / NTOK, n = idx - row * NTOK;
             if (ok && row < rv && n < N) {
                 float v = 0.0f;
@@ -681,7 +685,7 @@ Plan plan_for(uint32_t N, uint32_t ng, uint32_t in_f)
     Plan p{0u, 0u, {}};
     for (uint32_t s = kMaxStages; s >= 2u; --s) {
         const Layout L = layout(s, N, nt, ng, in_f);
-        if (2u * (L.total + 1024u) <= 233472u) return Plan{s, 2u, L};
+        if (kCtasPerSm == 2u && 2u * (L.total + 1024u) <= 233472u) return Plan{s, 2u, L};
     }
     for (uint32_t s = kMaxStages; s >= 2u; --s) {
         const Layout L = layout(s, N, nt, ng, in_f);

@@ -426,6 +426,119 @@ def run_aux_workload(args):
     print(json.dumps({"workload": args.workload, "data": "synthetic", "results": results}), flush=True)
 
 
+def _randf_stream(seed: int, n: int) -> np.ndarray:
+    """The reference Lloyd tests' generator (LCG, float(state >> 16) / 32768 - 1)."""
+    hi = np.empty(n, np.uint32)
+    s = seed
+    for i in range(n):
+        s = (s * 1103515245 + 12345) & 0xFFFFFFFF
+        hi[i] = s >> 16
+    return (hi.astype(np.float32) / np.float32(32768.0) - np.float32(1.0)).astype(np.float32)
+
+
+def _graph_ms(torch, stream, launch, n_launch: int, warmup: int) -> float:
+    """Device time of one of n_launch captured calls (CUDA graph, CUDA events)."""
+    with torch.cuda.stream(stream):
+        launch()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(n_launch):
+            launch()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / n_launch
+    del g
+    return ms
+
+
+def run_compression_workloads(args):
+    """The compression-side rows, one JSON line.
+      lloyd: one Lloyd iteration (assign, centroid update, dead-centroid
+             reinit) on the reference's benchmark inputs (test/test_lloyd.c:
+             590,000 vectors x k 256 x d 2 and 295,000 x 256 x 4, its LCG
+             generator), device arrays; vectors per second.
+      pq:    PolarQuant rotation of 1,048,576 KV-cache head vectors of 128
+             fp32 (512 MB) in place, Q from pq_generate_rotation(128, 42);
+             vectors per second and bytes (read + write) per second.
+    Each beside the reference compiled from its own sources (oracle/_ref) on
+    one host thread (its OpenMP is not available in this image): Lloyd on
+    the same input, the rotation on a 16,384-vector sample."""
+    import torch
+
+    import hxq_b200 as H
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    L = H.lib()
+    stream = torch.cuda.Stream()
+    hbm, peak_kind = measured_peaks()
+    results = []
+    if args.workload == "lloyd":
+        for n, k, d, seed in ((590000, 256, 2, 999), (295000, 256, 4, 777)):
+            r = _randf_stream(seed, n * d + k * d)
+            w, cb = r[:n * d].copy(), r[n * d:].copy()
+            dw = torch.from_numpy(w).cuda()
+            dcb = torch.from_numpy(cb.copy()).cuda()
+            didx = torch.zeros(n, dtype=torch.uint8, device="cuda")
+            dnd = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+            def launch():
+                if L.hxq_cuda_lloyd_reassign(dw.data_ptr(), dcb.data_ptr(), didx.data_ptr(), n, k, d, dnd.data_ptr(),
+                                             C.c_void_p(stream.cuda_stream)) != 0:
+                    raise RuntimeError("lloyd failed")
+            ms = _graph_ms(torch, stream, launch, max(4, args.steps), args.warmup)
+            res = {"case": f"lloyd n={n} k={k} d={d}", "ms_per_iteration": ms, "vectors_per_s": n / (ms * 1e-3)}
+            if not args.no_cpu_baseline:
+                from oracle.oracle import ReferenceLloyd
+                rl = ReferenceLloyd()
+                t0 = time.perf_counter()
+                rc, _, _, _ = rl.reassign(w, cb, k, d)
+                dt = time.perf_counter() - t0
+                res["cpu_baseline"] = {"value": n / dt, "unit": "vectors/s", "cores": 1, "kind": "reference",
+                                       "sample": "one iteration on the same input, oracle/_ref, one thread",
+                                       "ms_per_iteration": dt * 1e3}
+            results.append(res)
+    else:
+        nvec, hd = 1 << 20, 128
+        Q = np.zeros(hd * hd, np.float32)
+        if L.pq_generate_rotation(hd, 42, Q.ctypes.data) != 0:
+            raise RuntimeError("pq_generate_rotation failed")
+        rng = np.random.Generator(np.random.PCG64(0x5051))
+        x = torch.from_numpy(rng.standard_normal(nvec * hd, dtype=np.float32)).cuda()
+        dQ = torch.from_numpy(Q).cuda()
+        flip = [0]
+
+        def launch():
+            fn = L.hxq_cuda_pq_rotate if flip[0] % 2 == 0 else L.hxq_cuda_pq_unrotate
+            flip[0] += 1
+            H.check(fn(x.data_ptr(), dQ.data_ptr(), nvec, hd, C.c_void_p(stream.cuda_stream)), "pq")
+        ms = _graph_ms(torch, stream, launch, max(4, args.steps) // 2 * 2, args.warmup)
+        gbs = 2 * nvec * hd * 4 / (ms * 1e-3) / 1e9
+        res = {"case": f"pq rotate n={nvec} head_dim={hd}", "ms_per_call": ms, "vectors_per_s": nvec / (ms * 1e-3),
+               "gbs": gbs, "hbm_frac": gbs / hbm, "peak_source": peak_kind,
+               "fp32_ops_per_s": 2.0 * nvec * hd * hd / (ms * 1e-3),
+               "bound": "fp32 pipe (each output a sequential fp32 sum: one multiply and one add per term)"}
+        if not args.no_cpu_baseline:
+            from oracle.oracle import ReferencePolarQuant
+            rp = ReferencePolarQuant()
+            sample = 16384
+            xs = x[:sample * hd].cpu().numpy()
+            t0 = time.perf_counter()
+            rp.apply(xs, Q.reshape(hd, hd), hd, True)
+            dt = time.perf_counter() - t0
+            res["cpu_baseline"] = {"value": sample / dt, "unit": "vectors/s", "cores": 1, "kind": "reference",
+                                   "sample": f"{sample} vectors, oracle/_ref pq_rotate, one thread"}
+        results.append(res)
+    print(json.dumps({"workload": args.workload, "data": "synthetic", "results": results}), flush=True)
+
+
 def run_fused_matmul_workload(args):
     """The fused dequant-matmul sweep on one 7B layer (q, k, v, o, gate, up,
     down): the same matrices as 12-bit 2D-VQ images (codebook gather +
@@ -726,11 +839,13 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers to run (profiling aid; the workload is 32 layers)")
-    ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3", "c5", "kernels"], default="llama7b",
+    ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3", "c5", "kernels", "lloyd", "pq"],
+                    default="llama7b",
                     help="llama7b: the headline (default); c1/c2/c3: single-tensor decompress "
                          "and the affine batch sweep; c5: the fused dequant-matmul sweep on a 7B "
                          "layer (column-split over the ranks); kernels: one call of each matmul "
-                         "kernel (for profiling); one JSON line each")
+                         "kernel (for profiling); lloyd / pq: the compression-side rows (Lloyd "
+                         "iteration, PolarQuant rotation); one JSON line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -742,6 +857,9 @@ def main():
         return
     if args.workload == "kernels":
         run_kernel_cases(args)
+        return
+    if args.workload in ("lloyd", "pq"):
+        run_compression_workloads(args)
         return
     if args.workload != "llama7b":
         run_aux_workload(args)

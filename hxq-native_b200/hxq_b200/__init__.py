@@ -150,7 +150,29 @@ SIGNATURES = {
     "hxq_cuda_peer_wait": (C.c_int, [P, C.c_uint32, P, P, P]),
     "hxq_cuda_image_has_matmul_tables": (C.c_int, [P]),
     "hxq_cuda_vq_matmul_path": (C.c_int, [P, P, C.c_uint32, P, C.c_uint32, C.c_int, P]),
+    # Lloyd's algorithm (hxq_lloyd.h, hxq_cuda.h)
+    "hxq_lloyd_reassign": (C.c_int, [P, P, P, C.c_size_t, C.c_int, C.c_int, P]),
+    "hxq_lloyd_assign_only": (C.c_int, [P, P, P, C.c_size_t, C.c_int, C.c_int]),
+    "hxq_cuda_lloyd_assign": (C.c_int, [P, P, P, C.c_size_t, C.c_int, C.c_int, P]),
+    "hxq_cuda_lloyd_reassign": (C.c_int, [P, P, P, C.c_size_t, C.c_int, C.c_int, P, P]),
+    # PolarQuant (polarquant.h, hxq_cuda.h)
+    "pq_generate_rotation": (C.c_int, [C.c_uint32, C.c_uint32, P]),
+    "pq_rotate": (C.c_int, [P, P, C.c_uint32, C.c_uint32]),
+    "pq_unrotate": (C.c_int, [P, P, C.c_uint32, C.c_uint32]),
+    "pq_infer_head_geometry": (C.c_int, [C.c_uint32, C.c_uint32, P, P]),
+    "pq_layer_init": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "pq_layer_rotate": (C.c_int, [P, P]),
+    "pq_layer_unrotate": (C.c_int, [P, P]),
+    "pq_layer_free": (None, [P]),
+    "hxq_cuda_pq_rotate": (C.c_int, [P, P, C.c_uint64, C.c_uint32, P]),
+    "hxq_cuda_pq_unrotate": (C.c_int, [P, P, C.c_uint64, C.c_uint32, P]),
 }
+
+
+class PqLayer(C.Structure):
+    """pq_layer_t (polarquant.h)."""
+    _fields_ = [("Q", C.POINTER(C.c_float)), ("head_dim", C.c_uint32), ("n_heads", C.c_uint32),
+                ("seed", C.c_uint32), ("initialized", C.c_int)]
 
 
 def load(path: str = LIB_PATH) -> C.CDLL:
@@ -283,7 +305,7 @@ def header_functions(include_dir: str = INCLUDE_DIR) -> list[str]:
         src = open(os.path.join(include_dir, fn)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         src = re.sub(r"static inline[^{]*\{.*?\n\}", "", src, flags=re.S)
-        for m in re.finditer(r"\b(hxq_[a-z0-9_]+)\s*\(", src):
+        for m in re.finditer(r"\b((?:hxq|pq)_[a-z0-9_]+)\s*\(", src):
             name = m.group(1)
             start = src.rfind("\n", 0, m.start()) + 1
             line = src[start:m.start()]

@@ -313,6 +313,35 @@ int hxq_affine_group_matmul_async(const float *d_x,
                                   const hxq_affine_tensor_t *tensor,
                                   float *d_output, uint32_t N, void *stream);
 
+/* -- Lloyd's algorithm on the GPU (compression side) -------------------
+ * Device-pointer forms of hxq_lloyd_reassign / hxq_lloyd_assign_only
+ * (hxq_lloyd.h; reference src/hxq_lloyd.c:41-308), stream-ordered, no
+ * synchronisation: d_weights [n * d] fp32, d_codebook [k * d] fp32,
+ * d_indices [n] uint8; k in [1, 256], d in {1, 2, 4, 8}, n < 2^32.
+ * Assignment is bit-identical to the reference (fp32 in its order, first
+ * minimum wins).  Centroid sums are exact-order-independent 64-bit
+ * fixed-point sums (scale: a power of two from the largest |weight|), so
+ * the updated codebook is reproducible run to run and within about one fp32
+ * ulp of the reference's double sums (whose order depends on its thread
+ * count).  *d_n_dead (device int, may be NULL) receives the dead-centroid
+ * count.  Returns HXQ_LLOYD_* codes. */
+int hxq_cuda_lloyd_assign(const float *d_weights, const float *d_codebook, uint8_t *d_indices, size_t n, int k,
+                          int d, void *stream);
+int hxq_cuda_lloyd_reassign(const float *d_weights, float *d_codebook, uint8_t *d_indices, size_t n, int k, int d,
+                            int *d_n_dead, void *stream);
+
+/* -- PolarQuant rotation on the GPU ---------------------------------------
+ * In place on d_values [n_vectors * head_dim]: rotate = each vector times
+ * Q^T, unrotate = times Q (d_Q [head_dim * head_dim] row-major, device).
+ * Each output is the reference's sequential fp32 sum (reference
+ * src/polarquant.c:249-300), so results are bit-identical to it.
+ * Stream-ordered.  HXQ_OK, HXQ_ERR_NULL_PTR, HXQ_ERR_INVALID_ARG
+ * (head_dim == 0) or HXQ_ERR_CUDA. */
+hxq_error_t hxq_cuda_pq_rotate(float *d_values, const float *d_Q, uint64_t n_vectors, uint32_t head_dim,
+                               void *stream);
+hxq_error_t hxq_cuda_pq_unrotate(float *d_values, const float *d_Q, uint64_t n_vectors, uint32_t head_dim,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

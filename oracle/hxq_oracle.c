@@ -277,3 +277,102 @@ void orc_dense_matmul_rows_f64(const float *x, const float *W, double *out,
             out[(size_t)(n - n0) * out_f + o] = acc;
         }
 }
+
+/* ---- Lloyd's algorithm, src/hxq_lloyd.c:41-308 ------------------------- */
+
+/* Phase 1, src/hxq_lloyd.c:41-95: squared centroid norms, then per vector
+ * its squared norm, each centroid's dot product (sums in component order)
+ * and dist = w_sq + c_sq - 2 dot; the first strict minimum wins. */
+void orc_lloyd_assign(const float *w, const float *cb, uint8_t *idx, size_t n, int k, int d)
+{
+    float csq[256];
+    for (int j = 0; j < k; j++) {
+        float s = 0.0f;
+        for (int p = 0; p < d; p++) s += cb[j * d + p] * cb[j * d + p];
+        csq[j] = s;
+    }
+    for (size_t i = 0; i < n; i++) {
+        const float *wi = w + i * (size_t)d;
+        float wsq = 0.0f;
+        for (int p = 0; p < d; p++) wsq += wi[p] * wi[p];
+        float best = 3.402823466e38f;
+        int bj = 0;
+        for (int j = 0; j < k; j++) {
+            float dot = 0.0f;
+            for (int p = 0; p < d; p++) dot += wi[p] * cb[j * d + p];
+            float dist = wsq + csq[j] - 2.0f * dot;
+            if (dist < best) {
+                best = dist;
+                bj = j;
+            }
+        }
+        idx[i] = (uint8_t)bj;
+    }
+}
+
+/* Phases 1-3 (src/hxq_lloyd.c:100-260), one thread: centroid sums in
+ * double in vector order; mean = sum * (1 / count) rounded to float;
+ * every dead centroid -> the member of the largest cluster (first maximum
+ * count) farthest from its updated centroid (largest fp32 squared
+ * distance, first index on ties) times 1.001f.  Returns the dead count. */
+int orc_lloyd_reassign(const float *w, float *cb, uint8_t *idx, size_t n, int k, int d)
+{
+    double sums[256 * 8];
+    int counts[256];
+    orc_lloyd_assign(w, cb, idx, n, k, d);
+    for (int j = 0; j < k * d; j++) sums[j] = 0.0;
+    for (int j = 0; j < k; j++) counts[j] = 0;
+    for (size_t i = 0; i < n; i++) {
+        const int j = idx[i];
+        counts[j]++;
+        for (int p = 0; p < d; p++) sums[j * d + p] += (double)w[i * (size_t)d + p];
+    }
+    for (int j = 0; j < k; j++)
+        if (counts[j] > 0) {
+            const double inv = 1.0 / (double)counts[j];
+            for (int p = 0; p < d; p++) cb[j * d + p] = (float)(sums[j * d + p] * inv);
+        }
+    int dead = 0, largest = 0;
+    for (int j = 0; j < k; j++) {
+        if (counts[j] == 0) dead++;
+        if (counts[j] > counts[largest]) largest = j;
+    }
+    if (dead == 0) return 0;
+    const float *lc = cb + largest * d;
+    float maxd = -1.0f;
+    size_t far = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (idx[i] != (uint8_t)largest) continue;
+        float dist = 0.0f;
+        for (int p = 0; p < d; p++) {
+            const float diff = w[i * (size_t)d + p] - lc[p];
+            dist += diff * diff;
+        }
+        if (dist > maxd) {
+            maxd = dist;
+            far = i;
+        }
+    }
+    for (int j = 0; j < k; j++)
+        if (counts[j] == 0)
+            for (int p = 0; p < d; p++) cb[j * d + p] = w[far * (size_t)d + p] * 1.001f;
+    return dead;
+}
+
+/* ---- PolarQuant rotation, src/polarquant.c:249-300 --------------------- */
+
+/* In place: transpose != 0: head <- head Q^T (pq_rotate); else head <- head
+ * Q (pq_unrotate).  fp32 sums in k order from 0. */
+void orc_pq_apply(float *values, const float *Q, size_t nvec, uint32_t hd, int transpose, float *tmp)
+{
+    for (size_t v = 0; v < nvec; v++) {
+        float *head = values + v * hd;
+        for (uint32_t j = 0; j < hd; j++) {
+            float sum = 0.0f;
+            for (uint32_t k = 0; k < hd; k++)
+                sum += head[k] * (transpose ? Q[(size_t)j * hd + k] : Q[(size_t)k * hd + j]);
+            tmp[j] = sum;
+        }
+        for (uint32_t j = 0; j < hd; j++) head[j] = tmp[j];
+    }
+}

@@ -17,6 +17,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libhxqref.so")
+REF_LLOYD_SO = os.path.join(HERE, "_ref", "libhxqref_lloyd.so")
+REF_PQ_SO = os.path.join(HERE, "_ref", "libpqref.so")
 
 P = C.c_void_p
 
@@ -56,6 +58,12 @@ class Oracle:
         L.orc_unpack12.argtypes = [P, P, P]
         L.orc_pack_rows12.restype = C.c_size_t
         L.orc_pack_rows12.argtypes = [P, C.c_uint32, C.c_uint32, P]
+        L.orc_lloyd_assign.restype = None
+        L.orc_lloyd_assign.argtypes = [P, P, P, C.c_size_t, C.c_int, C.c_int]
+        L.orc_lloyd_reassign.restype = C.c_int
+        L.orc_lloyd_reassign.argtypes = [P, P, P, C.c_size_t, C.c_int, C.c_int]
+        L.orc_pq_apply.restype = None
+        L.orc_pq_apply.argtypes = [P, P, C.c_size_t, C.c_uint32, C.c_int, P]
 
     def decompress(self, d: dict, out: np.ndarray | None = None, k: int | None = None,
                    vdim: int | None = None, idx_len: int | None = None):
@@ -125,6 +133,31 @@ class Oracle:
         n1 = N if n1 is None else n1
         out = np.zeros((n1 - n0, out_f), np.float64)
         self.L.orc_dense_matmul_rows_f64(_p(x), _p(W), _p(out), n0, n1, in_f, out_f)
+        return out
+
+    def lloyd_assign(self, w: np.ndarray, cb: np.ndarray, k: int, d: int) -> np.ndarray:
+        w = np.ascontiguousarray(w, np.float32)
+        cb = np.ascontiguousarray(cb, np.float32)
+        n = w.size // d
+        idx = np.zeros(n, np.uint8)
+        self.L.orc_lloyd_assign(_p(w), _p(cb), _p(idx), n, k, d)
+        return idx
+
+    def lloyd_reassign(self, w: np.ndarray, cb: np.ndarray, k: int, d: int):
+        """(indices, updated codebook, dead count)."""
+        w = np.ascontiguousarray(w, np.float32)
+        cb = np.array(cb, np.float32, copy=True)
+        n = w.size // d
+        idx = np.zeros(n, np.uint8)
+        dead = self.L.orc_lloyd_reassign(_p(w), _p(cb), _p(idx), n, k, d)
+        return idx, cb, dead
+
+    def pq_apply(self, values: np.ndarray, Q: np.ndarray, head_dim: int, rotate: bool) -> np.ndarray:
+        """head @ Q^T (rotate) or head @ Q, for every head_dim-vector."""
+        out = np.array(values, np.float32, copy=True).reshape(-1)
+        Q = np.ascontiguousarray(Q, np.float32)
+        tmp = np.zeros(head_dim, np.float32)
+        self.L.orc_pq_apply(_p(out), _p(Q), out.size // head_dim, head_dim, 1 if rotate else 0, _p(tmp))
         return out
 
     def pack12(self, a: int, b: int) -> bytes:
@@ -249,4 +282,63 @@ class Reference:
         self.L.ref_hxq_affine_group_matmul_ref(x.ctypes.data, d["codes"].ctypes.data, d["scales"].ctypes.data,
                                                d["offsets"].ctypes.data, None if b is None else b.ctypes.data,
                                                out.ctypes.data, x.shape[0], d["in_f"], d["out_f"], d["gs"])
+        return out
+
+
+class ReferenceLloyd:
+    """The reference's Lloyd library compiled from its own source (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_LLOYD_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = self.L = C.CDLL(path)
+        L.ref_hxq_lloyd_reassign.restype = C.c_int
+        L.ref_hxq_lloyd_reassign.argtypes = [P, P, P, C.c_size_t, C.c_int, C.c_int, P]
+        L.ref_hxq_lloyd_assign_only.restype = C.c_int
+        L.ref_hxq_lloyd_assign_only.argtypes = [P, P, P, C.c_size_t, C.c_int, C.c_int]
+
+    def reassign(self, w: np.ndarray, cb: np.ndarray, k: int, d: int):
+        """(return code, indices, updated codebook, dead count)."""
+        w = np.ascontiguousarray(w, np.float32)
+        cb = np.array(cb, np.float32, copy=True)
+        n = w.size // d
+        idx = np.zeros(n, np.uint8)
+        dead = C.c_int(-1)
+        rc = self.L.ref_hxq_lloyd_reassign(_p(w), _p(cb), _p(idx), n, k, d, C.addressof(dead))
+        return rc, idx, cb, dead.value
+
+    def assign(self, w: np.ndarray, cb: np.ndarray, k: int, d: int):
+        w = np.ascontiguousarray(w, np.float32)
+        cb = np.ascontiguousarray(cb, np.float32)
+        idx = np.zeros(w.size // d, np.uint8)
+        rc = self.L.ref_hxq_lloyd_assign_only(_p(w), _p(cb), _p(idx), w.size // d, k, d)
+        return rc, idx
+
+
+class ReferencePolarQuant:
+    """The reference's PolarQuant library compiled from its own source (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_PQ_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = self.L = C.CDLL(path)
+        for name, res, args in [
+            ("ref_pq_generate_rotation", C.c_int, [C.c_uint32, C.c_uint32, P]),
+            ("ref_pq_rotate", C.c_int, [P, P, C.c_uint32, C.c_uint32]),
+            ("ref_pq_unrotate", C.c_int, [P, P, C.c_uint32, C.c_uint32]),
+        ]:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+
+    def rotation(self, dim: int, seed: int) -> np.ndarray:
+        Q = np.zeros(dim * dim, np.float32)
+        assert self.L.ref_pq_generate_rotation(dim, seed, _p(Q)) == 0
+        return Q.reshape(dim, dim)
+
+    def apply(self, values: np.ndarray, Q: np.ndarray, head_dim: int, rotate: bool) -> np.ndarray:
+        out = np.array(values, np.float32, copy=True).reshape(-1)
+        Q = np.ascontiguousarray(Q, np.float32)
+        fn = self.L.ref_pq_rotate if rotate else self.L.ref_pq_unrotate
+        assert fn(_p(out), _p(Q), out.size // head_dim, head_dim) == 0
         return out

@@ -741,8 +741,7 @@ def run_fused_matmul_workload(args):
                        "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
                        "hbm_frac_per_rank": per_rank_gbs / hbm,
                        "output_bytes_per_layer": sum(N * m["O"] * 4 for m in mats),
-                       "path": (("GEMV" if N <= 4 else "tcgen05 GEMM") if fmt == "vq12" else
-                                ("tensor-core GEMV" if N <= 8 else "tcgen05 GEMM"))}
+                       "path": "tensor-core GEMV" if N <= 8 else "tcgen05 GEMM"}
                 if mode == "p2p":
                     # one step outside the graph: the assembled outputs must equal
                     # the NCCL-gathered shards, bit for bit

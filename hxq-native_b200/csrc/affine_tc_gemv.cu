@@ -54,9 +54,12 @@
 
 #include "hxq_cuda.h"
 #include "hxq_cuda_internal.h"
+#include "tc_pipe.cuh"
 
 namespace hxq {
 namespace tcg {
+
+using namespace pipe;
 
 constexpr uint32_t kConsumers = 8;                      // consumer warps
 constexpr uint32_t kCThreads = kConsumers * 32u;        // consumer threads
@@ -71,8 +74,6 @@ constexpr uint32_t kHalfBytes = kRows * 512u;           // one box: [16 rows][4]
 constexpr uint32_t kStageBytes = kRows * kKC;           // kKC / 512 boxes
 constexpr uint32_t kMaxStages = 6;
 constexpr uint32_t kSfStride = 2u * kRows + 2u;         // floats per group in the transposed scales
-constexpr uint64_t kWaitCycles = 2000000000ull;          // ~1 s at 1.9 GHz
-constexpr uint32_t kErrTimeout = 4u;
 
 __device__ uint32_t g_tc_err;
 
@@ -121,91 +122,6 @@ struct Jobs {
     uint64_t total_w;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait; false if it ran out or another thread already gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
-{
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = clock64();
-    while (true) {
-        if (mbar_try(bar, parity)) return true;
-        if (*abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            *abort = 1u;
-            atomicOr(&g_tc_err, kErrTimeout);
-            return false;
-        }
-    }
-}
-
-// Warp-uniform bounded wait: every lane waits, the warp goes on only if all did.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort)
-{
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort)) != 0;
-}
-
-// Teardown wait: bounded, not cut short by the abort flag.
-__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity)
-{
-    const uint64_t t0 = clock64();
-    while (!mbar_try(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) {
-            atomicOr(&g_tc_err, kErrTimeout);
-            return;
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
-                                            int32_t c1, int32_t c2)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
 // Bytes 2i and 2i+1 of w as exact f16 values (f16 1024 + b, minus 1024).
 template <int HI>
 __device__ __forceinline__ uint32_t codes_f16x2(uint32_t w)
@@ -214,16 +130,6 @@ __device__ __forceinline__ uint32_t codes_f16x2(uint32_t w)
     uint32_t r;
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64006400u));
     return r;
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1)
-{
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t f16x2_of(float lo, float hi)
@@ -328,20 +234,6 @@ __device__ void stage_x_warp(const Job &b, uint32_t N, uint8_t *smem, const Layo
     __syncwarp();
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t a)
-{
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
-    return v;
-}
-
-__device__ __forceinline__ uint2 lds64(uint32_t a)
-{
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
-}
-
 // One 64-code chunk of a warp: rows g and g+8 of the row block (their 16
 // codes at shared address ca and ca + 32 lines), the activation fragments of
 // each token tile at xa[tt] (the lane's token, its 16 values of the chunk).
@@ -365,8 +257,8 @@ __device__ __forceinline__ void chunk_mma(uint32_t ca, const uint32_t (&xa)[NT],
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
             const uint2 bb = lds64(xa[tt] + 8u * (uint32_t)jj);
-            if (jj & 1) mma16816(e[tt], a0, a1, a2, a3, bb.x, bb.y);
-            else mma16816(d[tt], a0, a1, a2, a3, bb.x, bb.y);
+            if (jj & 1) mma16816_f16(e[tt], a0, a1, a2, a3, bb.x, bb.y);
+            else mma16816_f16(d[tt], a0, a1, a2, a3, bb.x, bb.y);
         }
     }
 #pragma unroll
@@ -430,8 +322,8 @@ __device__ __forceinline__ void pair_mma(uint32_t ca0, uint32_t ca1, const uint3
 #pragma unroll
             for (int tt = 0; tt < NT; ++tt) {
                 const uint2 bb = lds64(xa[tt] + 128u * (uint32_t)h + 8u * (uint32_t)jj);
-                if (jj & 1) mma16816(e[tt], a0, a1, a2, a3, bb.x, bb.y);
-                else mma16816(d[tt], a0, a1, a2, a3, bb.x, bb.y);
+                if (jj & 1) mma16816_f16(e[tt], a0, a1, a2, a3, bb.x, bb.y);
+                else mma16816_f16(d[tt], a0, a1, a2, a3, bb.x, bb.y);
             }
         }
     }
@@ -511,14 +403,14 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 const uint32_t rv = min(kRows, b.out_f - row0);
                 const uint32_t nst = (b.in_f + kKC - 1u) / kKC;
                 for (uint32_t st = 0; st < nst; ++st, ++it) {
-                    if (it >= S && !mbar_wait(empty + slot, ph ^ 1u, abort_flag)) {
+                    if (it >= S && !mbar_wait(empty + slot, ph ^ 1u, abort_flag, &g_tc_err)) {
                         ok = false;
                         break;
                     }
                     uint32_t sbytes = 0;
                     if (st == 0) {
                         // the scales of the previous row block have been transposed
-                        if (rbi >= 1u && !mbar_wait(sdone, (rbi - 1u) & 1u, abort_flag)) {
+                        if (rbi >= 1u && !mbar_wait(sdone, (rbi - 1u) & 1u, abort_flag, &g_tc_err)) {
                             ok = false;
                             break;
                         }
@@ -539,7 +431,7 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 }
             }
             // every issued copy has landed before shared memory is released
-            for (uint32_t kt = it > S ? it - S : 0u; kt < it; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u);
+            for (uint32_t kt = it > S ? it - S : 0u; kt < it; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u, &g_tc_err);
         }
         asm volatile("griddepcontrol.wait;" ::: "memory");
         return;
@@ -593,7 +485,7 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
 #pragma unroll
             for (int u = 0; u < 4; ++u) { as[tt][u] = 0.0f; af[tt][u] = 0.0f; }
         for (uint32_t st = 0; st < nst; ++st) {
-            if (ok && !warp_wait(full + slot, ph, abort_flag)) ok = false;
+            if (ok && !warp_wait(full + slot, ph, abort_flag, &g_tc_err)) ok = false;
             if (st == 0) {
                 // scales and offsets of the row block, transposed to [group][row][s, off];
                 // rows past the copied bytes come from global memory, rows past the matrix are 0
@@ -707,48 +599,6 @@ bool tc_gemv_fits(const uint16_t *x, const uint8_t *codes, const float *scales, 
     return tcg::plan_for(N, in_f / gs, in_f).stages != 0;
 }
 
-namespace {
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
-                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                  CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn()
-{
-    static EncodeTiledFn fn = nullptr;
-    static std::atomic<bool> tried{false};
-    if (!tried.load(std::memory_order_acquire)) {
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(f);
-        else
-            cudaGetLastError();
-        tried.store(true, std::memory_order_release);
-    }
-    return fn;
-}
-
-// The codes of a matrix as [out_f][in_f / 128][128] bytes; a half stage is
-// the box of 16 rows x 4 lines x 128 bytes at (0, line, first row).
-bool encode_codes_map(CUtensorMap *map, const uint8_t *codes, uint32_t in_f, uint32_t out_f)
-{
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    std::memset(map, 0, sizeof(*map));
-    const cuuint64_t dims[3] = {128u, in_f / 128u, out_f};
-    const cuuint64_t strides[2] = {128u, in_f};
-    const cuuint32_t box[3] = {128u, 4u, tcg::kRows};
-    const cuuint32_t estr[3] = {1u, 1u, 1u};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(codes), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-}  // namespace
-
 // 0 launched, 1 a matrix does not fit this kernel, -1 CUDA error.
 int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStream_t s)
 {
@@ -763,7 +613,9 @@ int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStrea
         if (!tc_gemv_fits(a.x, a.codes, a.scales, a.offsets, N, a.in_f, a.out_f, a.gs)) return 1;
         if (a.out.n == 0 || a.out.n > HXQ_CUDA_MAX_PEERS || a.ldy < a.out_f) return 1;
         Job &b = J.job[i];
-        if (!encode_codes_map(&b.map, a.codes, a.in_f, a.out_f)) return 1;
+        // the codes as [out_f][in_f / 128][128] bytes; a half stage is the box of 16 rows x 4 lines
+        std::memset(&b.map, 0, sizeof(b.map));
+        if (!pipe::encode_rows_map(&b.map, a.codes, a.in_f, a.out_f, 128u, 4u, kRows)) return 1;
         b.x = a.x; b.codes = a.codes; b.scales = a.scales; b.offsets = a.offsets; b.bias = a.bias;
         b.out = a.out; b.in_f = a.in_f; b.out_f = a.out_f; b.gs = a.gs; b.ng = a.in_f / a.gs; b.ldy = a.ldy;
         b.gs_shift = (a.gs & (a.gs - 1u)) == 0 ? (uint32_t)__builtin_ctz(a.gs) : 32u;

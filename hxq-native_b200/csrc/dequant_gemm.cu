@@ -707,7 +707,7 @@ extern "C" int hxq_cuda_affine_device_status(void)
         const uint32_t z = 0;
         cudaMemcpyToSymbol(hxq::gemm::g_gemm_err, &z, sizeof(z));
     }
-    const uint32_t tc = hxq::tc_gemv_status_take();
-    if (tc == 0xFFFFFFFFu) return -1;
-    return (int)(v | tc);
+    const uint32_t tc = hxq::tc_gemv_status_take(), vq = hxq::vq_tc_status_take();
+    if (tc == 0xFFFFFFFFu || vq == 0xFFFFFFFFu) return -1;
+    return (int)(v | tc | vq);
 }

@@ -175,4 +175,23 @@ int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStrea
 // Reads and clears the kernel's status word (nonzero: a wait ran out).
 uint32_t tc_gemv_status_take();
 
+// One image of a tensor-core VQ GEMV launch (vq_tc_gemv.cu): packed 12-bit
+// indices [rows][in_f * 3 / 4], the image's matmul tables (bf16x2 codebook,
+// first patch per row, patch columns, patch weight differences), bf16
+// activations [N][in_f].
+struct VqTcMatrix {
+    const uint8_t *idx;
+    const uint32_t *cbh, *rb, *e4;
+    const float *ed;
+    uint32_t n_patch;
+    const uint16_t *x;
+    OutPtrs out;
+    uint32_t ldy, rows, in_f;
+};
+// 1 <= N <= 8, in_f a multiple of 128 (at most 65536), x 16-byte aligned.
+bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f);
+// Up to kMaxTcJobs images in one launch: 0 launched, 1 not taken, -1 error.
+int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s);
+uint32_t vq_tc_status_take();
+
 }  // namespace hxq

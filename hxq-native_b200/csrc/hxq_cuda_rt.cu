@@ -60,10 +60,12 @@ struct hxq_cuda_image {
     // codebook pairs; per row the first patch; per (row, 128-wide K step)
     // the 16-bit offset of its first patch from the row's; patches
     // col | bf16(final weight) << 16, one per distinct sidecar position
+    // and per patch bf16(final weight) - bf16(codebook value) in fp32
     bool      has_mm = false;
-    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0;
+    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0;
     uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr;
     uint16_t *d_kp = nullptr;
+    float    *d_ed = nullptr;
     uint32_t  n_patch = 0;
 };
 
@@ -296,6 +298,7 @@ void bind_image(hxq_cuda_image *img, void *base)
         img->d_rb = reinterpret_cast<uint32_t *>(b + img->o_rb);
         img->d_kp = reinterpret_cast<uint16_t *>(b + img->o_kp);
         img->d_e4 = reinterpret_cast<uint32_t *>(b + img->o_e4);
+        img->d_ed = reinterpret_cast<float *>(b + img->o_ed);
     }
 }
 
@@ -311,9 +314,18 @@ uint16_t bf16_rne(float f)
 // there -- codebook value, then the deltas added in array order in fp32
 // (src/hxq.c:343-346) -- rounded once to bf16.  False if a row has more
 // than 65535 patches (16-bit offsets); the image then has no tables.
+float bf16_to_float(uint32_t h)
+{
+    const uint32_t u = (h & 0xFFFFu) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
 bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows, uint32_t in_f,
                    const std::vector<HostEntry> &ents, std::vector<uint32_t> &cbh,
-                   std::vector<uint32_t> &rb, std::vector<uint16_t> &kp, std::vector<uint32_t> &e4)
+                   std::vector<uint32_t> &rb, std::vector<uint16_t> &kp, std::vector<uint32_t> &e4,
+                   std::vector<float> &ed)
 {
     const uint32_t KT = in_f / 128u;
     const size_t row_bytes = (size_t)(in_f / 4u) * 3u;
@@ -322,6 +334,7 @@ bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows
         cbh[j] = (uint32_t)bf16_rne(t->codebook[2u * j]) | ((uint32_t)bf16_rne(t->codebook[2u * j + 1u]) << 16);
     std::vector<uint32_t> erow;
     e4.clear();
+    ed.clear();
     for (size_t i = 0; i < ents.size();) {
         const uint64_t pos = ents[i].pos;
         const uint32_t r = (uint32_t)(pos / in_f), c = (uint32_t)(pos % in_f);
@@ -330,7 +343,9 @@ bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows
                                             : (((uint32_t)b[0] << 4) | (b[1] >> 4));
         volatile float w = t->codebook[2u * id + (c & 1u)];
         for (; i < ents.size() && ents[i].pos == pos; ++i) w = w + ents[i].val;
-        e4.push_back(c | ((uint32_t)bf16_rne(w) << 16));
+        const uint16_t fw = bf16_rne(w);
+        e4.push_back(c | ((uint32_t)fw << 16));
+        ed.push_back(bf16_to_float(fw) - bf16_to_float(cbh[id] >> (16u * (c & 1u))));
         erow.push_back(r);
     }
     rb.assign(rows, 0u);
@@ -454,10 +469,11 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
 
     std::vector<uint32_t> mm_cbh, mm_rb, mm_e4;
     std::vector<uint16_t> mm_kp;
+    std::vector<float> mm_ed;
     if (matmul && img->kind == kKindVq12 && !img->check_k && img->k == 4096u && img->in_f % 128u == 0u &&
         img->in_f <= 65536u)
         img->has_mm = build_patches(t, t->indices_raw + idx_off, img->rows, img->in_f, ents, mm_cbh, mm_rb,
-                                    mm_kp, mm_e4);
+                                    mm_kp, mm_e4, mm_ed);
     img->n_patch = (uint32_t)mm_e4.size();
 
     // one block: idx | cb | scales | offsets | chunk_ptr | entries
@@ -479,6 +495,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         img->o_rb = off;   off = align256(off + std::max<size_t>(mm_rb.size(), 1) * 4);
         img->o_kp = off;   off = align256(off + mm_kp.size() * 2);
         img->o_e4 = off;   off = align256(off + (mm_e4.size() + 4) * 4);   // + speculative-read slack
+        img->o_ed = off;   off = align256(off + std::max<size_t>(mm_ed.size(), 1) * 4);
     }
     img->block_bytes = off;
     img->has_cb = cb_floats > 0;
@@ -508,6 +525,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         if (!mm_rb.empty()) std::memcpy(hb + img->o_rb, mm_rb.data(), mm_rb.size() * 4);
         std::memcpy(hb + img->o_kp, mm_kp.data(), mm_kp.size() * 2);
         if (!mm_e4.empty()) std::memcpy(hb + img->o_e4, mm_e4.data(), mm_e4.size() * 4);
+        if (!mm_ed.empty()) std::memcpy(hb + img->o_ed, mm_ed.data(), mm_ed.size() * 4);
     }
 
     if (streamed) {
@@ -1044,8 +1062,22 @@ hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n
 
 namespace {
 
+// path: 0 the exact fp32 GEMV, 1 the tcgen05 GEMM, 2 the tensor-core GEMV
+// (1 and 2 need the image's matmul tables).
+hxq::VqTcMatrix tc_matrix(const hxq_cuda_image_t *img, const uint16_t *x, const hxq::OutPtrs &out, uint32_t ldy)
+{
+    return hxq::VqTcMatrix{img->d_idx, img->d_cbh, img->d_rb, img->d_e4, img->d_ed, img->n_patch, x, out, ldy,
+                           img->rows, img->in_f};
+}
+
+int default_path(const hxq_cuda_image_t *img, const uint16_t *x, uint32_t N)
+{
+    if (!img || !img->has_mm) return 0;
+    return N <= HXQ_VQ_MATMUL_TC_MAX && hxq::vq_tc_fits(x, N, img->in_f) ? 2 : 1;
+}
+
 hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uint32_t N, const hxq::OutPtrs &out,
-                      uint32_t ldy, int gemm, void *stream)
+                      uint32_t ldy, int path, void *stream)
 {
     if (!img || !d_x_bf16) return HXQ_ERR_NULL_PTR;
     if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return HXQ_ERR_INVALID_ARG;
@@ -1053,7 +1085,7 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if (!out.y[k]) return HXQ_ERR_NULL_PTR;
     if (img->kind != kKindVq12 || img->check_k || img->k != 4096u || img->in_f % 64u != 0u)
         return HXQ_ERR_INVALID_ARG;
-    if (gemm && !img->has_mm) return HXQ_ERR_INVALID_ARG;
+    if (path < 0 || path > 2 || (path != 0 && !img->has_mm)) return HXQ_ERR_INVALID_ARG;
     if (!img->d_block) return HXQ_ERR_INVALID_ARG;   // streamed image never uploaded
     if (ldy < img->rows || !aligned16(d_x_bf16)) return HXQ_ERR_INVALID_ARG;
     if (N == 0 || img->rows == 0) return HXQ_OK;
@@ -1066,7 +1098,11 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if ((err = dev_ready(dev)) != HXQ_OK) return err;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (gemm) {
+    if (path == 2) {
+        const hxq::VqTcMatrix m = tc_matrix(img, d_x_bf16, out, ldy);
+        const int r = hxq::launch_vq_tc_gemv(1, &m, N, g_dev[dev].sms, s);
+        if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
+    } else if (path == 1) {
         const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
                                         out, N, img->in_f, img->rows, ldy, s);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
@@ -1083,20 +1119,19 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
 }  // namespace
 
 hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
-                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream)
+                                    uint32_t N, float *d_y, uint32_t ldy, int path, void *stream)
 {
     if (!d_y) return HXQ_ERR_NULL_PTR;
     hxq::OutPtrs o{};
     o.y[0] = d_y;
     o.n = 1;
-    return vq_matmul(img, d_x_bf16, N, o, ldy, gemm, stream);
+    return vq_matmul(img, d_x_bf16, N, o, ldy, path, stream);
 }
 
 hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                uint32_t N, float *d_y, uint32_t ldy, void *stream)
 {
-    const bool gemm = img && N > HXQ_VQ_MATMUL_GEMV_MAX && img->has_mm;
-    return hxq_cuda_vq_matmul_path(img, d_x_bf16, N, d_y, ldy, gemm ? 1 : 0, stream);
+    return hxq_cuda_vq_matmul_path(img, d_x_bf16, N, d_y, ldy, default_path(img, d_x_bf16, N), stream);
 }
 
 hxq_error_t hxq_cuda_vq_matmul_multi(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
@@ -1108,8 +1143,7 @@ hxq_error_t hxq_cuda_vq_matmul_multi(const hxq_cuda_image_t *img, const uint16_t
     hxq::OutPtrs o{};
     for (uint32_t k = 0; k < n_out; ++k) o.y[k] = d_ys[k];
     o.n = n_out;
-    const bool gemm = img && N > HXQ_VQ_MATMUL_GEMV_MAX && img->has_mm;
-    return vq_matmul(img, d_x_bf16, N, o, ldy, gemm ? 1 : 0, stream);
+    return vq_matmul(img, d_x_bf16, N, o, ldy, default_path(img, d_x_bf16, N), stream);
 }
 
 hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, const uint16_t *const *d_xs,
@@ -1128,16 +1162,6 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
         o.n = n_out;
         return HXQ_OK;
     };
-    if (N > HXQ_VQ_MATMUL_GEMV_MAX) {
-        for (uint32_t i = 0; i < n; ++i) {
-            hxq::OutPtrs o;
-            hxq_error_t err = outs_of(i, o);
-            if (err != HXQ_OK) return err;
-            err = vq_matmul(imgs[i], d_xs[i], N, o, ldys[i], imgs[i] && imgs[i]->has_mm ? 1 : 0, stream);
-            if (err != HXQ_OK) return err;
-        }
-        return HXQ_OK;
-    }
     int dev = 0;
     hxq_error_t err = current_device(&dev);
     if (err != HXQ_OK) return err;
@@ -1145,21 +1169,56 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
         std::lock_guard<std::mutex> lk(g_mu);
         if ((err = dev_ready(dev)) != HXQ_OK) return err;
     }
-    std::vector<hxq::VqGemvJob> jobs;
-    jobs.reserve(n);
     for (uint32_t i = 0; i < n; ++i) {
         const hxq_cuda_image_t *img = imgs[i];
         if (!img || !d_xs[i]) return HXQ_ERR_NULL_PTR;
         if (img->kind != kKindVq12 || img->check_k || img->k != 4096u || img->in_f % 64u != 0u || !img->d_block ||
             img->device != dev || ldys[i] < img->rows || !aligned16(d_xs[i]))
             return HXQ_ERR_INVALID_ARG;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The batch in three parts, each image in the first that takes it: up to
+    // HXQ_VQ_MATMUL_TC_MAX tokens, images with matmul tables share tensor-core
+    // GEMV launches (8 per launch); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the
+    // rest share exact-GEMV launches; anything left runs one call per image.
+    std::vector<uint8_t> done(n, 0);
+    std::vector<hxq::VqTcMatrix> tcs;
+    std::vector<uint32_t> tc_of;
+    for (uint32_t i = 0; i < n; ++i) {
         hxq::OutPtrs o;
         if ((err = outs_of(i, o)) != HXQ_OK) return err;
-        if (img->rows == 0) continue;
+        if (imgs[i]->rows == 0) { done[i] = 1; continue; }
+        if (default_path(imgs[i], d_xs[i], N) == 2) {
+            tcs.push_back(tc_matrix(imgs[i], d_xs[i], o, ldys[i]));
+            done[i] = 1;
+        }
+    }
+    for (size_t j0 = 0; j0 < tcs.size(); j0 += hxq::kMaxTcJobs) {
+        const uint32_t cnt = (uint32_t)std::min<size_t>(hxq::kMaxTcJobs, tcs.size() - j0);
+        const int r = hxq::launch_vq_tc_gemv(cnt, tcs.data() + j0, N, g_dev[dev].sms, s);
+        if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    if (N > HXQ_VQ_MATMUL_GEMV_MAX) {
+        for (uint32_t i = 0; i < n; ++i) {
+            if (done[i]) continue;
+            hxq::OutPtrs o;
+            if ((err = outs_of(i, o)) != HXQ_OK) return err;
+            err = vq_matmul(imgs[i], d_xs[i], N, o, ldys[i], default_path(imgs[i], d_xs[i], N), stream);
+            if (err != HXQ_OK) return err;
+        }
+        return HXQ_OK;
+    }
+    std::vector<hxq::VqGemvJob> jobs;
+    jobs.reserve(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (done[i]) continue;
+        const hxq_cuda_image_t *img = imgs[i];
+        hxq::OutPtrs o;
+        if ((err = outs_of(i, o)) != HXQ_OK) return err;
         jobs.push_back(hxq::VqGemvJob{img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent, img->n_chunks, img->rows,
                                       img->in_f, d_xs[i], o, ldys[i]});
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (size_t j0 = 0; j0 < jobs.size(); j0 += 8) {
         const uint32_t cnt = (uint32_t)std::min<size_t>(8, jobs.size() - j0);
         const cudaError_t e = hxq::launch_vq_gemv_batch(cnt, jobs.data() + j0, N, g_dev[dev].sms, s);

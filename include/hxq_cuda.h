@@ -220,7 +220,8 @@ int hxq_affine_group_matmul_bf16_path(const uint16_t *d_x_bf16,
 int hxq_affine_group_matmul_bf16_auto_path(const uint16_t *d_x_bf16,
                                            const hxq_affine_tensor_t *tensor, uint32_t N);
 /* Waits for the device, then returns (and clears) the status words of the
- * tcgen05 dequant-GEMM and the tensor-core GEMV: 0 when every pipeline wait
+ * tcgen05 dequant-GEMMs and the tensor-core GEMVs (affine and VQ): 0 when
+ * every pipeline wait
  * completed, nonzero if one ran out of time (the kernel then unwinds
  * without writing results); -1 on a CUDA error. */
 int hxq_cuda_affine_device_status(void);
@@ -234,20 +235,23 @@ int hxq_cuda_affine_device_status(void);
  * memory.  Images: 12-bit 2D-VQ with k = 4096 and in_features % 64 == 0
  * (HXQ_ERR_INVALID_ARG otherwise), resident or uploaded.  d_x: bf16 bit
  * patterns [N, in_features], 16-byte aligned; d_y: fp32, ldy >= rows.
- *   - Up to HXQ_VQ_MATMUL_GEMV_MAX tokens, or for images without the
- *     matmul tables (HXQ_IMAGE_MATMUL): the fused GEMV, with exact fp32
- *     weights and fp32 accumulation.
- *   - More tokens on images with the tables: the tcgen05 dequant-GEMM,
- *     which rounds each weight to bf16 (|error| <= 2^-9 sum_i |x_i w_i| per
- *     output, fp32 accumulation).
+ *   - Images with the matmul tables (HXQ_IMAGE_MATMUL), up to
+ *     HXQ_VQ_MATMUL_TC_MAX tokens: the tensor-core GEMV; more tokens: the
+ *     tcgen05 dequant-GEMM.  Both use each weight rounded to bf16 (the bf16
+ *     codebook pair, or bf16 of the sidecar-corrected weight):
+ *     |error| <= 2^-9 sum_i |x_i w_i| per output, fp32 accumulation.
+ *   - Images without the tables: the fused GEMV with exact fp32 weights
+ *     and fp32 accumulation.
  * Stream-ordered on `stream` (0: the legacy default stream); no sync. */
 #define HXQ_VQ_MATMUL_GEMV_MAX 4
+#define HXQ_VQ_MATMUL_TC_MAX 8
 hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                uint32_t N, float *d_y, uint32_t ldy, void *stream);
-/* The same with the path chosen by the caller: gemm = 0 GEMV, 1 GEMM
- * (HXQ_ERR_INVALID_ARG if the image has no matmul tables). */
+/* The same with the kernel chosen by the caller: path 0 the exact fp32
+ * GEMV, 1 the tcgen05 GEMM, 2 the tensor-core GEMV (1..8 tokens); 1 and 2
+ * need the image's matmul tables (HXQ_ERR_INVALID_ARG otherwise). */
 hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
-                                    uint32_t N, float *d_y, uint32_t ldy, int gemm, void *stream);
+                                    uint32_t N, float *d_y, uint32_t ldy, int path, void *stream);
 
 /* -- Outputs shared across the GPUs of one node ---------------------------
  * For a matmul whose output features are split over the ranks of one node:
@@ -296,9 +300,10 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
  * launch), which pays the per-launch costs once for the batch; any other
  * matrix runs one call of its own.  Returns 0, or -1 on an error. */
 /* A batch of n fused VQ matmuls (e.g. a layer's projections), outputs as
- * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_GEMV_MAX
- * tokens the GEMV shares launches (up to 8 images per launch); more tokens
- * run one call per image (the GEMM for images with matmul tables). */
+ * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_TC_MAX tokens
+ * the images with matmul tables share tensor-core GEMV launches (up to 8
+ * images per launch); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the others share
+ * exact-GEMV launches; anything else runs one call per image. */
 hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs,
                                      const uint16_t *const *d_xs, float *const *d_ys,
                                      uint32_t n_out, const uint32_t *ldys, uint32_t N,

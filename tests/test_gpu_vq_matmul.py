@@ -113,6 +113,28 @@ def test_gemm_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
     _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
 
 
+@pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 1), (256, 512, 2), (300, 1024, 3), (17, 128, 7), (4096, 4096, 1),
+                                          (11008, 4096, 1), (4096, 11008, 2), (513, 2048, 8), (64, 4096, 5)])
+def test_tc_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
+    """The tensor-core GEMV (path 2): ragged row blocks, K with 128- and
+    64-byte index lines (4096: 3072-byte rows; 11008: 8256), a partial last
+    stage, repeated and out-of-range sidecar entries; within the bf16-weight
+    bound of the oracle, and within 1e-4 of a float64 product with the
+    kernel's own weights (bf16 of each final weight)."""
+    d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 11 + in_f + N, dups=True)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, out_f)
+    try:
+        y = _run(cuda, L, img, xh, out_f, path=2)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    assert L.hxq_cuda_affine_device_status() == 0
+    sc = _scale(x, W)
+    _check(y, oracle.dense_matmul(x, W), sc, GEMM_TOL)
+    Wb = synth.bf16_to_f32(synth.bf16_round(W)).reshape(out_f, in_f)
+    _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
+
+
 def test_c5_prefill_2048_sampled(H, L, oracle, cuda):
     """The prefill batch of the fused-matmul sweep on a 4096 x 4096 layer
     matrix; outputs checked for a seeded sample of tokens."""
@@ -130,19 +152,27 @@ def test_c5_prefill_2048_sampled(H, L, oracle, cuda):
 
 
 def test_default_path_choice(H, L, oracle, cuda):
-    """Few tokens take the exact GEMV: bit-identical to the explicit path."""
-    d, W, xh, x = _case(oracle, 512, 1024, 4, 99)
+    """With matmul tables, up to 8 tokens take the tensor-core GEMV and more
+    the GEMM; without tables, the exact GEMV: each bit-identical to its
+    explicit path."""
+    d, W, xh, x = _case(oracle, 512, 1024, 9, 99)
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, 512)
+    plain = _image(H, L, t, 0, 512, matmul=False)
     try:
-        y_default = _run(cuda, L, img, xh, 512)
-        y_gemv = _run(cuda, L, img, xh, 512, path=0)
+        for n, path in ((4, 2), (8, 2), (9, 1)):
+            y_default = _run(cuda, L, img, xh[:n], 512)
+            y_path = _run(cuda, L, img, xh[:n], 512, path=path)
+            assert np.array_equal(y_default.view(np.uint32), y_path.view(np.uint32)), n
+        y_default = _run(cuda, L, plain, xh[:4], 512)
+        y_gemv = _run(cuda, L, plain, xh[:4], 512, path=0)
+        assert np.array_equal(y_default.view(np.uint32), y_gemv.view(np.uint32))
     finally:
         L.hxq_cuda_image_destroy(img)
-    assert np.array_equal(y_default.view(np.uint32), y_gemv.view(np.uint32))
+        L.hxq_cuda_image_destroy(plain)
 
 
-@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("path", [0, 1, 2])
 def test_row_shards_into_column_slices(H, L, oracle, cuda, path):
     """An image of rows [r0, r1) writes output columns r0..r1 of a wider
     [N, ldy] matrix (the column-sharded layout); nothing else is touched."""
@@ -163,12 +193,12 @@ def test_row_shards_into_column_slices(H, L, oracle, cuda, path):
     assert L.hxq_cuda_affine_device_status() == 0
 
 
-@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("path", [0, 1, 2])
 def test_dense_sidecar_rows(H, L, oracle, cuda, path):
     """Rows with many patches in one K step (more than the four a converter
     prefetches), repeated coordinates summed in array order, and a row whose
     every weight is corrected."""
-    out_f, in_f, N = 256, 1024, 9
+    out_f, in_f, N = 256, 1024, 8
     d = synth.vq12(out_f, in_f, 31, frac=0.002)
     rng = np.random.default_rng(3)
     extra_r = np.concatenate([np.full(40, 5), np.full(in_f, 130), np.full(12, 255)]).astype(np.uint32)
@@ -190,7 +220,7 @@ def test_dense_sidecar_rows(H, L, oracle, cuda, path):
         L.hxq_cuda_image_destroy(img)
     sc = _scale(x, W)
     _check(y, oracle.dense_matmul(x, W), sc, TOL if path == 0 else GEMM_TOL)
-    if path == 1:
+    if path != 0:
         Wb = synth.bf16_to_f32(synth.bf16_round(W)).reshape(out_f, in_f)
         _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
 
@@ -201,7 +231,7 @@ def test_no_sidecar_and_zero_tokens(H, L, oracle, cuda):
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, 128)
     try:
-        for path in (0, 1):
+        for path in (0, 1, 2):
             _check(_run(cuda, L, img, xh, 128, path=path), oracle.dense_matmul(x, W), _scale(x, W),
                    TOL if path == 0 else GEMM_TOL)
         y = cuda.full((1, 128), 7.0, device="cuda")
@@ -235,6 +265,8 @@ def test_invalid_images_and_arguments(H, L, cuda):
         assert L.hxq_cuda_image_has_matmul_tables(plain) == 0
         assert L.hxq_cuda_vq_matmul_path(img, xd.data_ptr(), 8, y.data_ptr(), 64, 1, None) == H.HXQ_ERR_INVALID_ARG
         assert L.hxq_cuda_vq_matmul_path(plain, xd.data_ptr(), 8, y.data_ptr(), 64, 1, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul_path(plain, xd.data_ptr(), 4, y.data_ptr(), 64, 2, None) == H.HXQ_ERR_INVALID_ARG
+        assert L.hxq_cuda_vq_matmul_path(plain, xd.data_ptr(), 4, y.data_ptr(), 64, 3, None) == H.HXQ_ERR_INVALID_ARG
         assert L.hxq_cuda_vq_matmul(plain, xd.data_ptr(), 8, y.data_ptr(), 64, None) == 0   # takes the GEMV
         assert L.hxq_cuda_vq_matmul(img, xd.data_ptr(), 8, y.data_ptr(), 63, None) == H.HXQ_ERR_INVALID_ARG
         assert L.hxq_cuda_vq_matmul(img, xd.data_ptr() + 2, 1, y.data_ptr(), 64, None) == H.HXQ_ERR_INVALID_ARG

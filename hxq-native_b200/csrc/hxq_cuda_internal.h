@@ -190,6 +190,9 @@ struct VqTcMatrix {
 };
 // 1 <= N <= 8, in_f a multiple of 128 (at most 65536), x 16-byte aligned.
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f);
+// How many of m[0..n) (at most kMaxTcJobs) share one launch without costing
+// the first ones residency (CTAs per SM).
+uint32_t vq_tc_group(uint32_t n, const VqTcMatrix *m, uint32_t N);
 // Up to kMaxTcJobs images in one launch: 0 launched, 1 not taken, -1 error.
 int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s);
 uint32_t vq_tc_status_take();

@@ -1183,7 +1183,6 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
     // rest share exact-GEMV launches; anything left runs one call per image.
     std::vector<uint8_t> done(n, 0);
     std::vector<hxq::VqTcMatrix> tcs;
-    std::vector<uint32_t> tc_of;
     for (uint32_t i = 0; i < n; ++i) {
         hxq::OutPtrs o;
         if ((err = outs_of(i, o)) != HXQ_OK) return err;
@@ -1193,9 +1192,14 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
             done[i] = 1;
         }
     }
-    for (size_t j0 = 0; j0 < tcs.size(); j0 += hxq::kMaxTcJobs) {
-        const uint32_t cnt = (uint32_t)std::min<size_t>(hxq::kMaxTcJobs, tcs.size() - j0);
+    // narrow matrices first, so that a wide one's activations do not cost
+    // the narrow ones stages or residency
+    std::stable_sort(tcs.begin(), tcs.end(),
+                     [](const hxq::VqTcMatrix &a, const hxq::VqTcMatrix &b) { return a.in_f < b.in_f; });
+    for (size_t j0 = 0; j0 < tcs.size();) {
+        const uint32_t cnt = hxq::vq_tc_group((uint32_t)(tcs.size() - j0), tcs.data() + j0, N);
         const int r = hxq::launch_vq_tc_gemv(cnt, tcs.data() + j0, N, g_dev[dev].sms, s);
+        j0 += cnt;
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
         g_launches.fetch_add(1, std::memory_order_relaxed);
     }

@@ -8,17 +8,25 @@
 // one row).  So a lane's A fragment is one 4-byte gather per register from a
 // 16 KB shared codebook, no conversion; the activations are bf16 already.
 //   * Index stream: a producer thread copies each 16-row block of packed
-//     indices, 1024 weights of K per stage (768 B per row), with one TMA
-//     tensor copy per stage: the rows as [rows][row_bytes / L][L] bytes with
-//     L = 128, 64 or 32 (the largest dividing the row; swizzle of L bytes),
-//     a box of 16 rows x 768 / L lines; rows past the image read as zero.
-//   * Fragments: a consumer warp owns 128 weights of K of every stage (two
-//     64-weight chunks); per chunk a lane reads its 8 pairs of rows g and
-//     g + 8 (12 bytes each: three 4-byte loads through the swizzle), unpacks
-//     the 8 indices and gathers their bf16x2 pairs; 4 products per chunk with
-//     fp32 accumulation in two chains, over the K permutation of the affine
-//     tensor-core GEMV (activation fragments: one 64-bit load of the
-//     lane's token, raw bf16 staged once per matrix).
+//     indices, 1024 weights of K per stage (768 B per row), as six TMA
+//     tensor copies of 128 bytes x 16 rows (128-byte swizzle: the 16-byte
+//     units of row r XOR r & 7); bytes past a row and rows past the image
+//     read as zero.
+//   * Fragments: a consumer warp owns a 128-weight window of K of every
+//     stage (two 64-weight chunks).  Lane (g, t) takes the window's pairs
+//     [16t, 16t + 16) of rows g and g + 8: 24 contiguous index bytes per row
+//     (three 64-bit loads through the swizzle), pairs [16t + 8u, +8) in
+//     chunk u.  Product jj of chunk u takes index triple jj of the lane's
+//     12 bytes: its even pair is the A register of MMA column pair t, its
+//     odd pair that of column pair t + 4 (the K permutation, shared with the
+//     activations).  A triple (b0, b1, b2) is turned into both codebook byte
+//     offsets by one byte permute and two shift-and-mask steps; the
+//     codebook is a static shared array, so its base is the loads' immediate.
+//   * Activations: raw bf16 staged once per matrix in fragment order (within
+//     each 128-weight window: chunk, then lane t, then its 16 weights; rows
+//     of in_f + 8 so that the 8 tokens' 16-byte loads fall in distinct
+//     banks); a lane's B fragments of a chunk are two 128-bit loads.  4
+//     products per chunk, fp32 accumulation in two chains.
 //   * Sidecar: the positions where the decoded weight differs from the
 //     codebook pair carry d = bf16(final weight) - bf16(codebook value)
 //     (image table, one entry per position, rows in order).  After a row
@@ -58,11 +66,13 @@ constexpr uint32_t kRowStageBytes = kKC / 4u * 3u;    // 768 B of indices per ro
 constexpr uint32_t kStageBytes = kRows * kRowStageBytes;   // 12 KB
 constexpr uint32_t kMaxStages = 8;
 constexpr uint32_t kCbBytes = 4096u * 4u;              // bf16x2 codebook
+constexpr uint32_t kXPad = 8;                          // activation row pitch: in_f + 8
 
 __device__ uint32_t g_vqtc_err;
+__shared__ __align__(16) uint32_t s_cb[4096];          // the matrix's bf16x2 codebook
 
 struct Job {
-    CUtensorMap map;            // indices [rows][row_bytes / line][line]
+    CUtensorMap map;            // indices [rows][row_bytes], boxes of 128 B x 16 rows
     const uint32_t *cbh;        // bf16x2 pairs [4096]
     const uint16_t *x;          // bf16 [N][in_f]
     const uint32_t *prow;       // sidecar: first entry of each row (null: none)
@@ -70,7 +80,7 @@ struct Job {
     const float *ed;            // sidecar weight differences
     uint32_t n_patch;
     OutPtrs out;
-    uint32_t ldy, rows, in_f, line;
+    uint32_t ldy, rows, in_f;
     uint32_t rb_begin;
     uint64_t w_begin;
 };
@@ -82,7 +92,7 @@ struct Jobs {
 };
 
 struct Layout {
-    uint32_t bars, abort, cb, xh, red, cs, total;
+    uint32_t bars, abort, xh, red, cs, total;
 };
 
 constexpr uint32_t kAlignSlack = 1024;
@@ -93,8 +103,7 @@ __host__ __device__ inline Layout layout(uint32_t S, uint32_t N, uint32_t in_f)
     L.bars = o;  o += 2u * kMaxStages * 8u;
     L.abort = o; o += 16u;
     o = (o + 127u) & ~127u;
-    L.cb = o;    o += kCbBytes;
-    L.xh = o;    o += N * (in_f + 4u) * 2u;
+    L.xh = o;    o += N * (in_f + kXPad) * 2u;
     o = (o + 15u) & ~15u;
     L.red = o;   o += 2u * kConsumers * kRows * 8u * 4u;
     L.cs = o;    o += 2u * kRows * 8u * 4u;
@@ -114,56 +123,124 @@ __device__ __forceinline__ uint32_t rb_at(const Jobs &J, uint64_t w)
     return b.rb_begin + (uint32_t)(r < nrb ? r : nrb);
 }
 
-// Shared-memory byte offset, within a stage, of byte o (a multiple of 4) of
-// the stage slice of row r: line r * (768 / L) + o / L, its 16-byte unit
-// XOR the swizzle bits 7.. of the line's address (128: line & 7; 64:
-// (line >> 1) & 3; 32: (line >> 2) & 1).
-__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t o, uint32_t L)
+// Shared-memory byte offset, within a stage, of byte o (a multiple of 8) of
+// the stage slice of row r: box o / 128 (2 KB each), line r, 16-byte unit
+// XOR r & 7.
+__device__ __forceinline__ uint32_t stage_off(uint32_t r, uint32_t o)
 {
-    const uint32_t line = r * (kRowStageBytes / L) + o / L, b = o % L;
-    const uint32_t x = L == 128u ? (line & 7u) : L == 64u ? ((line >> 1) & 3u) : ((line >> 2) & 1u);
-    return line * L + ((((b >> 4) ^ x) << 4) | (b & 15u));
+    const uint32_t b = o & 127u;
+    return (o >> 7) * 2048u + r * 128u + ((((b >> 4) ^ (r & 7u)) << 4) | (b & 15u));
 }
 
-// The 8 indices of 12 packed bytes (four byte triples, each two 12-bit
-// indices: a = b0 << 4 | b1 >> 4, b = (b1 & 15) << 8 | b2).
-__device__ __forceinline__ void unpack8(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t (&id)[8])
+// Codebook entry at byte offset o (a multiple of 4 below 16 KB).
+__device__ __forceinline__ uint32_t cb_at(uint32_t o)
 {
-    id[0] = ((w0 & 0xFFu) << 4) | ((w0 >> 12) & 0xFu);
-    id[1] = (w0 & 0xF00u) | ((w0 >> 16) & 0xFFu);
-    id[2] = ((w0 >> 24) << 4) | ((w1 >> 4) & 0xFu);
-    id[3] = ((w1 & 0xFu) << 8) | ((w1 >> 8) & 0xFFu);
-    id[4] = (((w1 >> 16) & 0xFFu) << 4) | (w1 >> 28);
-    id[5] = (((w1 >> 24) & 0xFu) << 8) | (w2 & 0xFFu);
-    id[6] = (((w2 >> 8) & 0xFFu) << 4) | ((w2 >> 20) & 0xFu);
-    id[7] = (((w2 >> 16) & 0xFu) << 8) | (w2 >> 24);
+    return *reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint8_t *>(s_cb) + o);
 }
 
-// One 64-weight chunk: rows g and g+8 (index words at shared addresses
-// a0 / a0 + 8 rows, +4, +8 through the swizzle), activation fragments from
-// xa[tt]; two accumulation chains.
+// Triple (b0, b1, b2) -> b1 | b0 << 8 | b2 << 16 | b1 << 24: bits 2..13 of
+// v >> 2 are 4 x the even index (b0 << 4 | b1 >> 4), bits 2..13 of v >> 14
+// are 4 x the odd index ((b1 & 15) << 8 | b2).
+__device__ __forceinline__ uint32_t even_off(uint32_t v) { return (v >> 2) & 0x3FFCu; }
+__device__ __forceinline__ uint32_t odd_off(uint32_t v) { return (v >> 14) & 0x3FFCu; }
+
+// One 64-weight chunk: w[0..2] / h[0..2] are the lane's 12 index bytes of
+// rows g / g + 8 (four triples), xb its 32 activation bytes per token tile
+// (four 8-byte B fragments); two accumulation chains.
 template <int NT>
-__device__ __forceinline__ void chunk(uint32_t w_g[3], uint32_t w_h[3], uint32_t cb_a, const uint32_t (&xa)[NT],
+__device__ __forceinline__ void chunk(const uint32_t *w, const uint32_t *h, const uint4 (&xb)[NT][2],
                                       float (&d)[NT][4], float (&e)[NT][4])
 {
-    uint32_t ig[8], ih[8];
-    unpack8(w_g[0], w_g[1], w_g[2], ig);
-    unpack8(w_h[0], w_h[1], w_h[2], ih);
+    uint32_t vg[4], vh[4];
+    vg[0] = __byte_perm(w[0], 0u, 0x1201u);
+    vg[1] = __byte_perm(w[0], w[1], 0x4534u);
+    vg[2] = __byte_perm(w[1], w[2], 0x3423u);
+    vg[3] = __byte_perm(w[2], 0u, 0x2312u);
+    vh[0] = __byte_perm(h[0], 0u, 0x1201u);
+    vh[1] = __byte_perm(h[0], h[1], 0x4534u);
+    vh[2] = __byte_perm(h[1], h[2], 0x3423u);
+    vh[3] = __byte_perm(h[2], 0u, 0x2312u);
     uint32_t ag[8], ah[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-        ag[m] = lds32(cb_a + 4u * ig[m]);
-        ah[m] = lds32(cb_a + 4u * ih[m]);
+    for (int jj = 0; jj < 4; ++jj) {
+        ag[2 * jj] = cb_at(even_off(vg[jj]));
+        ag[2 * jj + 1] = cb_at(odd_off(vg[jj]));
+        ah[2 * jj] = cb_at(even_off(vh[jj]));
+        ah[2 * jj + 1] = cb_at(odd_off(vh[jj]));
     }
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
-            const uint2 bb = lds64(xa[tt] + 8u * (uint32_t)jj);
-            if (jj & 1) mma16816_bf16(e[tt], ag[2 * jj], ah[2 * jj], ag[2 * jj + 1], ah[2 * jj + 1], bb.x, bb.y);
-            else mma16816_bf16(d[tt], ag[2 * jj], ah[2 * jj], ag[2 * jj + 1], ah[2 * jj + 1], bb.x, bb.y);
+            const uint4 &q = xb[tt][jj >> 1];
+            const uint32_t b0 = (jj & 1) ? q.z : q.x, b1 = (jj & 1) ? q.w : q.y;
+            if (jj & 1) mma16816_bf16(e[tt], ag[2 * jj], ah[2 * jj], ag[2 * jj + 1], ah[2 * jj + 1], b0, b1);
+            else mma16816_bf16(d[tt], ag[2 * jj], ah[2 * jj], ag[2 * jj + 1], ah[2 * jj + 1], b0, b1);
         }
     }
+}
+
+// Fragment-order position of activation column k: within its 128-weight
+// window, (chunk u, lane t, weight r) for k = 32t + 16u + r.
+__device__ __forceinline__ uint32_t xpos(uint32_t k)
+{
+    return (k & ~127u) | (((k >> 4) & 1u) << 6) | (((k >> 5) & 3u) << 4) | (k & 15u);
+}
+
+// Sidecar ranges of rows 2w, 2w + 1 of row block rb: entries [pr[0], pr[1])
+// and [pr[1], pr[2]) (rows past the image: empty; no sidecar: all zero).
+__device__ __forceinline__ void side_rows(const Jobs &J, uint32_t rb, uint32_t warp, uint32_t (&pr)[3])
+{
+    uint32_t j = 0;
+    while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
+    const Job &b = J.job[j];
+    pr[0] = pr[1] = pr[2] = 0u;
+    if (!b.prow) return;
+    const uint32_t r0 = (rb - b.rb_begin) * kRows + 2u * warp;
+#pragma unroll
+    for (int q = 0; q < 3; ++q) pr[q] = r0 + (uint32_t)q < b.rows ? ldg_pinned(b.prow + r0 + q) : b.n_patch;
+}
+
+// sn[n] += d x[n, col] for the tokens n < N (x: staged bf16 rows of ldx in
+// fragment order).
+__device__ __forceinline__ void side_add(float (&sn)[8], uint32_t e4, float dl, const uint16_t *xs, uint32_t ldx,
+                                         uint32_t N)
+{
+    const uint32_t col = xpos(e4 & 0xFFFFu);
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+        if ((uint32_t)n < N) sn[n] = fmaf(dl, __uint_as_float((uint32_t)xs[(size_t)n * ldx + col] << 16), sn[n]);
+}
+
+// Warp sum of sn[n] for n < N into out[n] (fixed order: deterministic).
+// N <= 2: a butterfly per token; else a transposed butterfly (9 shuffles for
+// the 8 sums: halves exchanged over lane bits 4, 3, 2, then bits 1, 0), the
+// sum of token n ending in lanes 4n .. 4n + 3.
+__device__ __forceinline__ void side_reduce(float (&sn)[8], uint32_t N, uint32_t lane, float *out)
+{
+    if (N <= 2u) {
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            if ((uint32_t)n < N) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sn[n] += __shfl_xor_sync(0xffffffffu, sn[n], o);
+                if (lane == 0) out[n] = sn[n];
+            }
+        }
+        return;
+    }
+    const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
+    float v4[4], v2[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        v4[i] = (b4 ? sn[i + 4] : sn[i]) + __shfl_xor_sync(0xffffffffu, b4 ? sn[i] : sn[i + 4], 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        v2[i] = (b3 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v4[i] : v4[i + 2], 8);
+    float v = (b2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? v2[0] : v2[1], 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    if ((lane & 3u) == 0 && (lane >> 2) < N) out[lane >> 2] = v;
 }
 
 template <int NT>
@@ -201,15 +278,15 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 const Job &b = J.job[j];
                 const uint32_t row0 = (rb - b.rb_begin) * kRows;
                 const uint32_t nst = (b.in_f + kKC - 1u) / kKC;
-                const uint32_t lines = kRowStageBytes / b.line;
                 for (uint32_t st = 0; st < nst; ++st, ++it) {
                     if (it >= S && !mbar_wait(empty + slot, ph ^ 1u, abort_flag, &g_vqtc_err)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(full + slot, kStageBytes);   // the full box, zero fill included
-                    tma_load_3d(smem + slot * kStageBytes, &b.map, full + slot, 0, (int32_t)(st * lines),
-                                (int32_t)row0);
+                    mbar_expect_tx(full + slot, kStageBytes);   // the full boxes, zero fill included
+                    for (uint32_t c = 0; c < kRowStageBytes / 128u; ++c)
+                        tma_load_2d(smem + slot * kStageBytes + c * 2048u, &b.map, full + slot,
+                                    (int32_t)(st * kRowStageBytes + c * 128u), (int32_t)row0);
                     if (++slot == S) { slot = 0; ph ^= 1u; }
                 }
             }
@@ -225,29 +302,33 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t N = J.N;
     constexpr uint32_t NTOK = 8u * NT;
-    const uint32_t stage_a = smem_u32(smem), cb_a = smem_u32(smem + L.cb), xh_a = smem_u32(smem + L.xh);
+    const uint32_t stage_a = smem_u32(smem), xh_a = smem_u32(smem + L.xh);
     float *red = reinterpret_cast<float *>(smem + L.red);
     float *csum = reinterpret_cast<float *>(smem + L.cs);
     const uint16_t *xs = reinterpret_cast<const uint16_t *>(smem + L.xh);
     uint32_t slot = 0, ph = 0, j = 0, rbi = 0, cur = 0xFFFFFFFFu;
     bool ok = true;
+    // Sidecar, software-pipelined over row blocks: the ranges of a block's
+    // rows are loaded during the block before, its first 64 entries per row
+    // at its start; both are used after its products.
+    uint32_t pr[3] = {0u, 0u, 0u};
+    if (rb0 < rb1) side_rows(J, rb0, warp, pr);
     for (uint32_t rb = rb0; rb < rb1; ++rb, ++rbi) {
         while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
         const Job &b = J.job[j];
         const uint32_t in_f = b.in_f;
         if (j != cur) {
-            // the matrix's codebook and activations (raw bf16, rows of in_f + 4)
+            // the matrix's codebook and activations (raw bf16 in fragment order,
+            // rows of in_f + 8)
             const uint4 *cs = reinterpret_cast<const uint4 *>(b.cbh);
-            uint4 *cd = reinterpret_cast<uint4 *>(smem + L.cb);
+            uint4 *cd = reinterpret_cast<uint4 *>(s_cb);
             for (uint32_t i = ct; i < kCbBytes / 16u; i += kConsumers * 32u) cd[i] = __ldg(cs + i);
             const uint32_t per_tok = in_f / 8u;
             uint16_t *xh = reinterpret_cast<uint16_t *>(smem + L.xh);
             for (uint32_t p = ct; p < N * per_tok; p += kConsumers * 32u) {
                 const uint32_t n = p / per_tok, k8 = p - n * per_tok;
                 const uint4 v = __ldg(reinterpret_cast<const uint4 *>(b.x + (size_t)n * in_f) + k8);
-                uint2 *dst = reinterpret_cast<uint2 *>(xh + (size_t)n * (in_f + 4u) + k8 * 8u);   // 8-byte aligned rows
-                dst[0] = make_uint2(v.x, v.y);
-                dst[1] = make_uint2(v.z, v.w);
+                *reinterpret_cast<uint4 *>(xh + (size_t)n * (in_f + kXPad) + xpos(k8 * 8u)) = v;
             }
             asm volatile("bar.sync 1, 256;" ::: "memory");
             cur = j;
@@ -255,28 +336,31 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         const uint32_t row0 = (rb - b.rb_begin) * kRows;
         const uint32_t rv = min(kRows, b.rows - row0);
         const uint32_t nst = (in_f + kKC - 1u) / kKC;
-        const uint32_t Lb = b.line;
-        // sidecar ranges of this warp's two rows (consumed after the products)
-        uint32_t pr[3] = {0u, 0u, 0u};
+        uint32_t pe[2][2] = {{0u, 0u}, {0u, 0u}};
+        float pd[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         if (b.prow) {
 #pragma unroll
-            for (int q = 0; q < 3; ++q) {
-                const uint32_t r = row0 + 2u * warp + (uint32_t)q;
-                pr[q] = r < b.rows ? __ldg(b.prow + r) : b.n_patch;
-            }
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+                for (int v = 0; v < 2; ++v) {
+                    const uint32_t p = pr[q] + lane + 32u * (uint32_t)v;
+                    if (p < pr[q + 1]) {
+                        pe[q][v] = ldg_pinned(b.e4 + p);
+                        pd[q][v] = ldg_pinned(b.ed + p);
+                    }
+                }
         }
-        // this lane's index words: chunk u, word i of row g (row g + 8: 8 * 768 B on)
-        uint32_t wo[2][3];
+        uint32_t pn[3] = {0u, 0u, 0u};
+        if (rb + 1u < rb1) side_rows(J, rb + 1u, warp, pn);
+        // this lane's index bytes: 8-byte piece i of its 24 of row g (row g + 8: 1 KB on)
+        uint32_t wo[3];
 #pragma unroll
-        for (int u = 0; u < 2; ++u)
-#pragma unroll
-            for (int i = 0; i < 3; ++i)
-                wo[u][i] = swz(g, warp * 96u + (uint32_t)u * 48u + t * 12u + (uint32_t)i * 4u, Lb);
+        for (int i = 0; i < 3; ++i) wo[i] = stage_off(g, warp * 96u + t * 24u + (uint32_t)i * 8u);
         uint32_t xa0[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
             const uint32_t n = min((uint32_t)tt * 8u + g, N - 1u);   // columns past N are not stored
-            xa0[tt] = xh_a + 2u * (n * (in_f + 4u) + t * 16u);
+            xa0[tt] = xh_a + 2u * (n * (in_f + kXPad) + warp * kWarpK + t * 16u);
         }
         float d[NT][4], e[NT][4];
 #pragma unroll
@@ -289,23 +373,26 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
             if (ok && kb < in_f) {
                 // in_f is a multiple of 128: both chunks of the warp are inside K
                 const uint32_t sa = stage_a + slot * kStageBytes;
-                uint32_t wg[2][3], wh[2][3];
+                uint32_t wg[6], wh[6];
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) {
-                        wg[u][i] = lds32(sa + wo[u][i]);
-                        wh[u][i] = lds32(sa + wo[u][i] + 8u * kRowStageBytes);
-                    }
+                for (int i = 0; i < 3; ++i) {
+                    const uint2 a = lds64(sa + wo[i]), c = lds64(sa + wo[i] + 1024u);
+                    wg[2 * i] = a.x; wg[2 * i + 1] = a.y;
+                    wh[2 * i] = c.x; wh[2 * i + 1] = c.y;
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + slot);   // the stage's indices are in registers
-                uint32_t xa[NT];
 #pragma unroll
-                for (int tt = 0; tt < NT; ++tt) xa[tt] = xa0[tt] + 2u * kb;
-                chunk<NT>(wg[0], wh[0], cb_a, xa, d, e);
+                for (int u = 0; u < 2; ++u) {
+                    uint4 xb[NT][2];
 #pragma unroll
-                for (int tt = 0; tt < NT; ++tt) xa[tt] += 2u * kChunk;
-                chunk<NT>(wg[1], wh[1], cb_a, xa, d, e);
+                    for (int tt = 0; tt < NT; ++tt) {
+                        const uint32_t xa = xa0[tt] + 2u * st * kKC + (uint32_t)u * 128u;
+                        xb[tt][0] = lds128(xa);
+                        xb[tt][1] = lds128(xa + 16u);
+                    }
+                    chunk<NT>(wg + 3 * u, wh + 3 * u, xb, d, e);
+                }
             } else {
                 __syncwarp();
                 if (ok && lane == 0) mbar_arrive(empty + slot);
@@ -319,24 +406,17 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 float sn[8];
 #pragma unroll
                 for (int n = 0; n < 8; ++n) sn[n] = 0.0f;
-                for (uint32_t p = pr[q] + lane; p < pr[q + 1]; p += 32u) {
-                    const uint32_t col = __ldg(b.e4 + p) & 0xFFFFu;
-                    const float dl = __ldg(b.ed + p);
 #pragma unroll
-                    for (int n = 0; n < 8; ++n)
-                        if ((uint32_t)n < N)
-                            sn[n] = fmaf(dl, __uint_as_float((uint32_t)xs[(size_t)n * (in_f + 4u) + col] << 16), sn[n]);
-                }
-#pragma unroll
-                for (int n = 0; n < 8; ++n) {
-                    if ((uint32_t)n < N) {
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) sn[n] += __shfl_xor_sync(0xffffffffu, sn[n], o);
-                        if (lane == 0) cw[(2u * warp + (uint32_t)q) * 8u + (uint32_t)n] = sn[n];
-                    }
-                }
+                for (int v = 0; v < 2; ++v)
+                    if (pr[q] + lane + 32u * (uint32_t)v < pr[q + 1])
+                        side_add(sn, pe[q][v], pd[q][v], xs, in_f + kXPad, N);
+                for (uint32_t p = pr[q] + 64u + lane; p < pr[q + 1]; p += 32u)
+                    side_add(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
+                side_reduce(sn, N, lane, cw + (2u * warp + (uint32_t)q) * 8u);
             }
         }
+#pragma unroll
+        for (int q = 0; q < 3; ++q) pr[q] = pn[q];
         float *rd = red + (size_t)(rbi & 1u) * kConsumers * kRows * NTOK;
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
@@ -370,11 +450,11 @@ Plan plan_for(uint32_t N, uint32_t in_f)
 {
     for (uint32_t s = kMaxStages; s >= 2u; --s) {
         const Layout L = layout(s, N, in_f);
-        if (2u * (L.total + 1024u) <= 233472u) return Plan{s, 2u, L};
+        if (2u * (L.total + kCbBytes + 1024u) <= 233472u) return Plan{s, 2u, L};
     }
     for (uint32_t s = kMaxStages; s >= 2u; --s) {
         const Layout L = layout(s, N, in_f);
-        if (L.total <= 227u * 1024u) return Plan{s, 1u, L};
+        if (L.total + kCbBytes <= 227u * 1024u) return Plan{s, 1u, L};
     }
     return Plan{0u, 0u, {}};
 }
@@ -385,6 +465,21 @@ bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f)
 {
     if (N == 0 || N > 8u || in_f == 0 || in_f % 128u != 0 || in_f > 65536u || ((uintptr_t)x & 15u)) return false;
     return vqtc::plan_for(N, in_f).stages != 0;
+}
+
+uint32_t vq_tc_group(uint32_t n, const VqTcMatrix *m, uint32_t N)
+{
+    if (n == 0) return 0;
+    uint32_t in_max = m[0].in_f, k = 1;
+    vqtc::Plan P = vqtc::plan_for(N, in_max);
+    for (; k < n && k < kMaxTcJobs; ++k) {
+        const uint32_t in2 = m[k].in_f > in_max ? m[k].in_f : in_max;
+        const vqtc::Plan Q = vqtc::plan_for(N, in2);
+        if (Q.per_sm < P.per_sm) break;   // a second launch costs less than half the CTAs
+        in_max = in2;
+        P = Q;
+    }
+    return k;
 }
 
 int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s)
@@ -399,11 +494,10 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
         const VqTcMatrix &a = m[i];
         if (!vq_tc_fits(a.x, N, a.in_f) || a.out.n == 0 || a.out.n > HXQ_CUDA_MAX_PEERS || a.ldy < a.rows) return 1;
         const uint64_t row_bytes = (uint64_t)a.in_f / 4u * 3u;
-        const uint32_t line = row_bytes % 128u == 0 ? 128u : row_bytes % 64u == 0 ? 64u : 32u;
         Job &b = J.job[i];
         std::memset(&b.map, 0, sizeof(b.map));
-        if (!pipe::encode_rows_map(&b.map, a.idx, row_bytes, a.rows, line, kRowStageBytes / line, kRows)) return 1;
-        b.cbh = a.cbh; b.x = a.x; b.out = a.out; b.ldy = a.ldy; b.rows = a.rows; b.in_f = a.in_f; b.line = line;
+        if (!pipe::encode_bytes_2d(&b.map, a.idx, row_bytes, a.rows, kRows)) return 1;
+        b.cbh = a.cbh; b.x = a.x; b.out = a.out; b.ldy = a.ldy; b.rows = a.rows; b.in_f = a.in_f;
         if (a.n_patch) {
             if (!a.rb || !a.e4 || !a.ed) return 1;
             b.prow = a.rb; b.e4 = a.e4; b.ed = a.ed; b.n_patch = a.n_patch;
@@ -430,7 +524,8 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
     if (!(configured.load(std::memory_order_acquire) & (1ull << dev))) {
-        if (cudaFuncSetAttribute(vq_tc_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+        if (cudaFuncSetAttribute(vq_tc_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(227u * 1024u - kCbBytes)) !=
             cudaSuccess) {
             cudaGetLastError();
             return -1;

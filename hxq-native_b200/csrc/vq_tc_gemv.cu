@@ -300,6 +300,10 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t ct = threadIdx.x;
     const uint32_t g = lane >> 2, t = lane & 3u;
+    // MMA rows g and g + 8 are rows gr and gr + 8 of the block: the four
+    // rows of a half-warp then have box lines with swizzle phases 0, 2, 4, 6
+    // (or 1, 3, 5, 7), and the 64-bit index loads are free of bank conflicts
+    const uint32_t gr = 2u * (g & 3u) + (g >> 2);
     const uint32_t N = J.N;
     constexpr uint32_t NTOK = 8u * NT;
     const uint32_t stage_a = smem_u32(smem), xh_a = smem_u32(smem + L.xh);
@@ -352,10 +356,10 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         }
         uint32_t pn[3] = {0u, 0u, 0u};
         if (rb + 1u < rb1) side_rows(J, rb + 1u, warp, pn);
-        // this lane's index bytes: 8-byte piece i of its 24 of row g (row g + 8: 1 KB on)
+        // this lane's index bytes: 8-byte piece i of its 24 of row gr (row gr + 8: 1 KB on)
         uint32_t wo[3];
 #pragma unroll
-        for (int i = 0; i < 3; ++i) wo[i] = stage_off(g, warp * 96u + t * 24u + (uint32_t)i * 8u);
+        for (int i = 0; i < 3; ++i) wo[i] = stage_off(gr, warp * 96u + t * 24u + (uint32_t)i * 8u);
         uint32_t xa0[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
@@ -421,10 +425,10 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
             const uint32_t n0 = (uint32_t)tt * 8u + 2u * t;
-            rd[(warp * kRows + g) * NTOK + n0] = d[tt][0] + e[tt][0];
-            rd[(warp * kRows + g) * NTOK + n0 + 1u] = d[tt][1] + e[tt][1];
-            rd[(warp * kRows + g + 8u) * NTOK + n0] = d[tt][2] + e[tt][2];
-            rd[(warp * kRows + g + 8u) * NTOK + n0 + 1u] = d[tt][3] + e[tt][3];
+            rd[(warp * kRows + gr) * NTOK + n0] = d[tt][0] + e[tt][0];
+            rd[(warp * kRows + gr) * NTOK + n0 + 1u] = d[tt][1] + e[tt][1];
+            rd[(warp * kRows + gr + 8u) * NTOK + n0] = d[tt][2] + e[tt][2];
+            rd[(warp * kRows + gr + 8u) * NTOK + n0 + 1u] = d[tt][3] + e[tt][3];
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         for (uint32_t idx = ct; idx < kRows * NTOK; idx += kConsumers * 32u) {

@@ -201,49 +201,57 @@ __device__ __forceinline__ void side_rows(const Jobs &J, uint32_t rb, uint32_t w
     for (int q = 0; q < 3; ++q) pr[q] = r0 + (uint32_t)q < b.rows ? ldg_pinned(b.prow + r0 + q) : b.n_patch;
 }
 
-// sn[n] += d x[n, col] for the tokens n < N (x: staged bf16 rows of ldx in
-// fragment order).
-__device__ __forceinline__ void side_add(float (&sn)[8], uint32_t e4, float dl, const uint16_t *xs, uint32_t ldx,
+// sn[n] += d x[n, col] for the tokens n < N <= NC (x: staged bf16 rows of
+// ldx in fragment order).
+template <int NC>
+__device__ __forceinline__ void side_add(float (&sn)[NC], uint32_t e4, float dl, const uint16_t *xs, uint32_t ldx,
                                          uint32_t N)
 {
-    const uint32_t col = xpos(e4 & 0xFFFFu);
+    const uint16_t *xc = xs + xpos(e4 & 0xFFFFu);
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
-        if ((uint32_t)n < N) sn[n] = fmaf(dl, __uint_as_float((uint32_t)xs[(size_t)n * ldx + col] << 16), sn[n]);
+    for (int n = 0; n < NC; ++n)
+        if (NC == 1 || (uint32_t)n < N)
+            sn[n] = fmaf(dl, __uint_as_float((uint32_t)xc[(uint32_t)n * ldx] << 16), sn[n]);
 }
 
-// Warp sum of sn[n] for n < N into out[n] (fixed order: deterministic).
-// N <= 2: a butterfly per token; else a transposed butterfly (9 shuffles for
-// the 8 sums: halves exchanged over lane bits 4, 3, 2, then bits 1, 0), the
-// sum of token n ending in lanes 4n .. 4n + 3.
-__device__ __forceinline__ void side_reduce(float (&sn)[8], uint32_t N, uint32_t lane, float *out)
+// Warp sum of sn[n] for n < N <= NC into out[n] (fixed order:
+// deterministic).  NC <= 2: a butterfly per token; else a transposed
+// butterfly (9 shuffles for 8 sums: halves exchanged over lane bits 4, 3, 2,
+// then bits 1, 0), the sum of token n ending in lanes 4n .. 4n + 3.
+template <int NC>
+__device__ __forceinline__ void side_reduce(float (&sn)[NC], uint32_t N, uint32_t lane, float *out)
 {
-    if (N <= 2u) {
+    if constexpr (NC <= 2) {
 #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-            if ((uint32_t)n < N) {
+        for (int n = 0; n < NC; ++n) {
+            if (NC == 1 || (uint32_t)n < N) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) sn[n] += __shfl_xor_sync(0xffffffffu, sn[n], o);
                 if (lane == 0) out[n] = sn[n];
             }
         }
-        return;
+    } else {
+        float s8[8];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) s8[n] = n < NC ? sn[n < NC ? n : 0] : 0.0f;
+        const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
+        float v4[4], v2[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            v4[i] = (b4 ? s8[i + 4] : s8[i]) + __shfl_xor_sync(0xffffffffu, b4 ? s8[i] : s8[i + 4], 16);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+            v2[i] = (b3 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v4[i] : v4[i + 2], 8);
+        float v = (b2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? v2[0] : v2[1], 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if ((lane & 3u) == 0 && (lane >> 2) < N) out[lane >> 2] = v;
     }
-    const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
-    float v4[4], v2[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        v4[i] = (b4 ? sn[i + 4] : sn[i]) + __shfl_xor_sync(0xffffffffu, b4 ? sn[i] : sn[i + 4], 16);
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-        v2[i] = (b3 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v4[i] : v4[i + 2], 8);
-    float v = (b2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? v2[0] : v2[1], 4);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    if ((lane & 3u) == 0 && (lane >> 2) < N) out[lane >> 2] = v;
 }
 
-template <int NT>
+// NT token tiles of 8 (always 1: up to 8 tokens); NC >= N bounds the
+// sidecar's per-token loops.
+template <int NT, int NC>
 __global__ void __launch_bounds__(kThreads, 2)
 vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 {
@@ -407,16 +415,16 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         if (b.prow) {
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-                float sn[8];
+                float sn[NC];
 #pragma unroll
-                for (int n = 0; n < 8; ++n) sn[n] = 0.0f;
+                for (int n = 0; n < NC; ++n) sn[n] = 0.0f;
 #pragma unroll
                 for (int v = 0; v < 2; ++v)
                     if (pr[q] + lane + 32u * (uint32_t)v < pr[q + 1])
-                        side_add(sn, pe[q][v], pd[q][v], xs, in_f + kXPad, N);
+                        side_add<NC>(sn, pe[q][v], pd[q][v], xs, in_f + kXPad, N);
                 for (uint32_t p = pr[q] + 64u + lane; p < pr[q + 1]; p += 32u)
-                    side_add(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
-                side_reduce(sn, N, lane, cw + (2u * warp + (uint32_t)q) * 8u);
+                    side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
+                side_reduce<NC>(sn, N, lane, cw + (2u * warp + (uint32_t)q) * 8u);
             }
         }
 #pragma unroll
@@ -524,17 +532,20 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    static std::atomic<uint64_t> configured{0};   // one bit per device
+    using KernelFn = void (*)(Jobs);
+    static const KernelFn kernels[4] = {vq_tc_gemv_kernel<1, 1>, vq_tc_gemv_kernel<1, 2>, vq_tc_gemv_kernel<1, 4>,
+                                        vq_tc_gemv_kernel<1, 8>};
+    const int kv = N <= 1u ? 0 : N <= 2u ? 1 : N <= 4u ? 2 : 3;
+    static std::atomic<uint64_t> configured[4];   // one bit per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
-    if (!(configured.load(std::memory_order_acquire) & (1ull << dev))) {
-        if (cudaFuncSetAttribute(vq_tc_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(227u * 1024u - kCbBytes)) !=
-            cudaSuccess) {
+    if (!(configured[kv].load(std::memory_order_acquire) & (1ull << dev))) {
+        if (cudaFuncSetAttribute(kernels[kv], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(227u * 1024u - kCbBytes)) != cudaSuccess) {
             cudaGetLastError();
             return -1;
         }
-        configured.fetch_or(1ull << dev, std::memory_order_acq_rel);
+        configured[kv].fetch_or(1ull << dev, std::memory_order_acq_rel);
     }
     uint32_t grid = (uint32_t)(sms > 0 ? sms : 148) * P.per_sm;
     if (grid > rb) grid = rb;
@@ -545,7 +556,7 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, vq_tc_gemv_kernel<1>, J) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (cudaLaunchKernelEx(&cfg, kernels[kv], J) != cudaSuccess) { cudaGetLastError(); return -1; }
     return 0;
 }
 

@@ -194,12 +194,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference library on the host cores
 
-def cpu_reference_runner(layer0: list[dict]):
-    """Returns (run_once() -> seconds, cores, kind, weights) for layer 0 on all host threads."""
+def cpu_reference_runner(layer0: list[dict], threads: int | None = None):
+    """Returns (run_once() -> seconds, cores, kind, weights) for layer 0 on
+    `threads` host threads (default: all), each running the unchanged
+    reference function on a slice of rows."""
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle.oracle import Oracle, Reference, ref_available
-    cores = os.cpu_count() or 1
+    cores = threads or os.cpu_count() or 1
     kind = "reference" if ref_available() else "port"
     jobs = []  # (callable) per row slice
     if kind == "reference":
@@ -1034,6 +1036,10 @@ def main():
         cpu = {"value": weights / statistics.median(times), "unit": UNIT, "cores": cores, "kind": kind,
                "sample": f"layer 0 (7 matrices, {weights} weights) per rep, {len(times)} reps, "
                          f"median, {cores} host threads"}
+        # the reference is single-threaded: its own speed, one core
+        run1, _, _, _ = cpu_reference_runner(layer0, threads=1)
+        t1 = [run1() for _ in range(3)]
+        cpu["value_1core"] = weights / statistics.median(t1)
 
     if rank == 0:
         line = {

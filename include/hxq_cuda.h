@@ -294,7 +294,7 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
                                        uint32_t ldy, uint32_t N, void *stream);
 /* A batch of n affine matmuls (e.g. a layer's projections) with bf16
  * activations d_xs[i] ([N, in_features of tensor i]) and outputs
- * d_ys[i * n_out + k] ([N, ldys[i]], k < n_out).  Up to 8 tokens the
+ * d_ys[i * n_out + k] ([N, ldys[i]], k < n_out).  Up to 16 tokens the
  * matrices that suit the tensor-core GEMV, and at one token the remaining
  * ones that suit the streaming GEMV, share launches (up to 8 matrices per
  * launch), which pays the per-launch costs once for the batch; any other

@@ -270,9 +270,10 @@ def test_path_selection(H, L, cuda):
 
 @pytest.mark.parametrize("N", [1, 5, 16])
 def test_batch_of_layer_projections(H, L, cuda, N):
-    """A layer's projections in one batch call (shared launches at one
-    token), two outputs each at a column offset: bit-identical to one call
-    per matrix."""
+    """A layer's projections in one batch call (shared launches), two
+    outputs each at a column offset: bit-identical to one call per matrix on
+    the same path (up to 16 tokens the batch takes the tensor-core GEMV for
+    every matrix it suits, one call only up to 8)."""
     torch = cuda
     shapes = [(512, 4096), (256, 4096), (256, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
     devs, xs, refs, outs, ts = [], [], [], [], []
@@ -282,7 +283,10 @@ def test_batch_of_layer_projections(H, L, cuda, N):
         xh, _ = synth.activations(N, I, 200 + i)
         x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
         ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
-        assert L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(dev.tensor(H)), ref.data_ptr(), N, None) == 0
+        t = dev.tensor(H)
+        if N > 16 or L.hxq_affine_group_matmul_bf16_path(x.data_ptr(), C.byref(t), ref.data_ptr(), N,
+                                                         H.HXQ_AFFINE_PATH_TC_GEMV, None) != 0:
+            assert L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(t), ref.data_ptr(), N, None) == 0
         devs.append(dev); xs.append(x); refs.append(ref); ts.append(dev.tensor(H))
         outs.append([torch.full((N, O + 64), float("nan"), dtype=torch.float32, device="cuda") for _ in range(2)])
     n = len(shapes)

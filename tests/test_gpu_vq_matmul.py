@@ -280,10 +280,12 @@ def test_invalid_images_and_arguments(H, L, cuda):
     assert L.hxq_cuda_image_create_ex(t.ref, 0, 64, 8, C.byref(bad)) == H.HXQ_ERR_INVALID_ARG
 
 
-@pytest.mark.parametrize("N", [1, 3, 16])
+@pytest.mark.parametrize("N", [1, 3, 5, 8, 16])
 def test_batch_of_layer_projections(H, L, oracle, cuda, N):
     """A layer's projections (row shards of 7B shapes) in one batch call, two
-    outputs each at a column offset: bit-identical to one call per image."""
+    outputs each at a column offset: bit-identical to one call per image.
+    From 3 tokens the 11008-wide matrix's activations leave one CTA per SM,
+    so the batch splits into two tensor-core launches."""
     torch = cuda
     shapes = [(512, 4096), (256, 4096), (384, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
     imgs, xs, refs, outs = [], [], [], []

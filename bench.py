@@ -743,7 +743,9 @@ def run_fused_matmul_workload(args):
                        "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
                        "hbm_frac_per_rank": per_rank_gbs / hbm,
                        "output_bytes_per_layer": sum(N * m["O"] * 4 for m in mats),
-                       "path": "tensor-core GEMV" if N <= 8 else "tcgen05 GEMM"}
+                       "path": ("tensor-core GEMV" if N <= 8 else
+                                "tensor-core GEMV for the 4096-wide matrices, tcgen05 GEMM for down"
+                                if N <= 16 else "tcgen05 GEMM")}
                 if mode == "p2p":
                     # one step outside the graph: the assembled outputs must equal
                     # the NCCL-gathered shards, bit for bit

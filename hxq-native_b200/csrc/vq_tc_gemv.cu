@@ -67,6 +67,7 @@ constexpr uint32_t kStageBytes = kRows * kRowStageBytes;   // 12 KB
 constexpr uint32_t kMaxStages = 8;
 constexpr uint32_t kCbBytes = 4096u * 4u;              // bf16x2 codebook
 constexpr uint32_t kXPad = 8;                          // activation row pitch: in_f + 8
+constexpr uint32_t kCsStride = 16;                     // sidecar sums per row (tokens)
 
 __device__ uint32_t g_vqtc_err;
 __shared__ __align__(16) uint32_t s_cb[4096];          // the matrix's bf16x2 codebook
@@ -105,8 +106,8 @@ __host__ __device__ inline Layout layout(uint32_t S, uint32_t N, uint32_t in_f)
     o = (o + 127u) & ~127u;
     L.xh = o;    o += N * (in_f + kXPad) * 2u;
     o = (o + 15u) & ~15u;
-    L.red = o;   o += 2u * kConsumers * kRows * 8u * 4u;
-    L.cs = o;    o += 2u * kRows * 8u * 4u;
+    L.red = o;   o += 2u * kConsumers * kRows * 8u * (N > 8u ? 2u : 1u) * 4u;
+    L.cs = o;    o += 2u * kRows * kCsStride * 4u;
     L.total = o + kAlignSlack;
     return L;
 }
@@ -217,7 +218,9 @@ __device__ __forceinline__ void side_add(float (&sn)[NC], uint32_t e4, float dl,
 // Warp sum of sn[n] for n < N <= NC into out[n] (fixed order:
 // deterministic).  NC <= 2: a butterfly per token; else a transposed
 // butterfly (9 shuffles for 8 sums: halves exchanged over lane bits 4, 3, 2,
-// then bits 1, 0), the sum of token n ending in lanes 4n .. 4n + 3.
+// then bits 1, 0; the sum of token n ending in lanes 4n .. 4n + 3), or for
+// 16 sums 16 shuffles over lane bits 4, 3, 2, 1, then 0 (token n in lanes
+// 2n, 2n + 1).
 template <int NC>
 __device__ __forceinline__ void side_reduce(float (&sn)[NC], uint32_t N, uint32_t lane, float *out)
 {
@@ -230,6 +233,21 @@ __device__ __forceinline__ void side_reduce(float (&sn)[NC], uint32_t N, uint32_
                 if (lane == 0) out[n] = sn[n];
             }
         }
+    } else if constexpr (NC == 16) {
+        const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u, b1 = lane & 2u;
+        float v8[8], v4[4], v2[2];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            v8[i] = (b4 ? sn[i + 8] : sn[i]) + __shfl_xor_sync(0xffffffffu, b4 ? sn[i] : sn[i + 8], 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            v4[i] = (b3 ? v8[i + 4] : v8[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v8[i] : v8[i + 4], 8);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+            v2[i] = (b2 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b2 ? v4[i] : v4[i + 2], 4);
+        float v = (b1 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b1 ? v2[0] : v2[1], 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if ((lane & 1u) == 0 && (lane >> 1) < N) out[lane >> 1] = v;
     } else {
         float s8[8];
 #pragma unroll
@@ -249,10 +267,10 @@ __device__ __forceinline__ void side_reduce(float (&sn)[NC], uint32_t N, uint32_
     }
 }
 
-// NT token tiles of 8 (always 1: up to 8 tokens); NC >= N bounds the
-// sidecar's per-token loops.
+// NT token tiles of 8 (1: up to 8 tokens, two CTAs per SM; 2: up to 16,
+// one); NC >= N bounds the sidecar's per-token loops.
 template <int NT, int NC>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, NT == 1 ? 2 : 1)
 vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -411,7 +429,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
             }
             if (++slot == S) { slot = 0; ph ^= 1u; }
         }
-        float *cw = csum + (size_t)(rbi & 1u) * kRows * 8u;
+        float *cw = csum + (size_t)(rbi & 1u) * kRows * kCsStride;
         if (b.prow) {
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
@@ -424,7 +442,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                         side_add<NC>(sn, pe[q][v], pd[q][v], xs, in_f + kXPad, N);
                 for (uint32_t p = pr[q] + 64u + lane; p < pr[q + 1]; p += 32u)
                     side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
-                side_reduce<NC>(sn, N, lane, cw + (2u * warp + (uint32_t)q) * 8u);
+                side_reduce<NC>(sn, N, lane, cw + (2u * warp + (uint32_t)q) * kCsStride);
             }
         }
 #pragma unroll
@@ -446,7 +464,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 #pragma unroll
                 for (uint32_t w = 0; w < kConsumers; ++w) v += rd[(w * kRows + row) * NTOK + n];
                 const uint32_t o = row0 + row;
-                if (b.prow) v += cw[row * 8u + n];
+                if (b.prow) v += cw[row * kCsStride + n];
                 for (uint32_t k = 0; k < b.out.n; ++k) b.out.y[k][(size_t)n * b.ldy + o] = v;
             }
         }
@@ -460,7 +478,8 @@ struct Plan {
 
 Plan plan_for(uint32_t N, uint32_t in_f)
 {
-    for (uint32_t s = kMaxStages; s >= 2u; --s) {
+    // two 8-token tiles: one CTA per SM (the kernel is built for one)
+    for (uint32_t s = kMaxStages; s >= 2u && N <= 8u; --s) {
         const Layout L = layout(s, N, in_f);
         if (2u * (L.total + kCbBytes + 1024u) <= 233472u) return Plan{s, 2u, L};
     }
@@ -475,7 +494,7 @@ Plan plan_for(uint32_t N, uint32_t in_f)
 
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f)
 {
-    if (N == 0 || N > 8u || in_f == 0 || in_f % 128u != 0 || in_f > 65536u || ((uintptr_t)x & 15u)) return false;
+    if (N == 0 || N > 16u || in_f == 0 || in_f % 128u != 0 || in_f > 65536u || ((uintptr_t)x & 15u)) return false;
     return vqtc::plan_for(N, in_f).stages != 0;
 }
 
@@ -533,10 +552,10 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     using KernelFn = void (*)(Jobs);
-    static const KernelFn kernels[4] = {vq_tc_gemv_kernel<1, 1>, vq_tc_gemv_kernel<1, 2>, vq_tc_gemv_kernel<1, 4>,
-                                        vq_tc_gemv_kernel<1, 8>};
-    const int kv = N <= 1u ? 0 : N <= 2u ? 1 : N <= 4u ? 2 : 3;
-    static std::atomic<uint64_t> configured[4];   // one bit per device
+    static const KernelFn kernels[5] = {vq_tc_gemv_kernel<1, 1>, vq_tc_gemv_kernel<1, 2>, vq_tc_gemv_kernel<1, 4>,
+                                        vq_tc_gemv_kernel<1, 8>, vq_tc_gemv_kernel<2, 16>};
+    const int kv = N <= 1u ? 0 : N <= 2u ? 1 : N <= 4u ? 2 : N <= 8u ? 3 : 4;
+    static std::atomic<uint64_t> configured[5];   // one bit per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return -1; }
     if (!(configured[kv].load(std::memory_order_acquire) & (1ull << dev))) {

@@ -248,7 +248,7 @@ int hxq_cuda_affine_device_status(void);
 hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                uint32_t N, float *d_y, uint32_t ldy, void *stream);
 /* The same with the kernel chosen by the caller: path 0 the exact fp32
- * GEMV, 1 the tcgen05 GEMM, 2 the tensor-core GEMV (1..8 tokens); 1 and 2
+ * GEMV, 1 the tcgen05 GEMM, 2 the tensor-core GEMV (1..16 tokens); 1 and 2
  * need the image's matmul tables (HXQ_ERR_INVALID_ARG otherwise). */
 hxq_error_t hxq_cuda_vq_matmul_path(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                     uint32_t N, float *d_y, uint32_t ldy, int path, void *stream);
@@ -300,10 +300,11 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
  * launch), which pays the per-launch costs once for the batch; any other
  * matrix runs one call of its own.  Returns 0, or -1 on an error. */
 /* A batch of n fused VQ matmuls (e.g. a layer's projections), outputs as
- * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_TC_MAX tokens
- * the images with matmul tables share tensor-core GEMV launches (up to 8
- * images per launch); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the others share
- * exact-GEMV launches; anything else runs one call per image. */
+ * in hxq_affine_group_matmul_bf16_batch.  Up to 16 tokens the images with
+ * matmul tables that suit the tensor-core GEMV share its launches (up to 8
+ * images per launch; a single call takes it only up to
+ * HXQ_VQ_MATMUL_TC_MAX tokens); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the
+ * others share exact-GEMV launches; anything else runs one call per image. */
 hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs,
                                      const uint16_t *const *d_xs, float *const *d_ys,
                                      uint32_t n_out, const uint32_t *ldys, uint32_t N,

@@ -114,13 +114,15 @@ def test_gemm_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
 
 
 @pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 1), (256, 512, 2), (300, 1024, 3), (17, 128, 7), (4096, 4096, 1),
-                                          (11008, 4096, 1), (4096, 11008, 2), (513, 2048, 8), (64, 4096, 5)])
+                                          (11008, 4096, 1), (4096, 11008, 2), (513, 2048, 8), (64, 4096, 5),
+                                          (256, 512, 9), (300, 1024, 12), (17, 128, 16), (4096, 4096, 16)])
 def test_tc_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
-    """The tensor-core GEMV (path 2): ragged row blocks, K with 128- and
-    64-byte index lines (4096: 3072-byte rows; 11008: 8256), a partial last
-    stage, repeated and out-of-range sidecar entries; within the bf16-weight
-    bound of the oracle, and within 1e-4 of a float64 product with the
-    kernel's own weights (bf16 of each final weight)."""
+    """The tensor-core GEMV (path 2), one and two 8-token tiles: ragged row
+    blocks, index rows that are not a multiple of 128 bytes (128: 96-byte
+    rows; 11008: 8256), a partial last stage, repeated and out-of-range
+    sidecar entries; within the bf16-weight bound of the oracle, and within
+    1e-4 of a float64 product with the kernel's own weights (bf16 of each
+    final weight)."""
     d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 11 + in_f + N, dups=True)
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, out_f)
@@ -283,9 +285,10 @@ def test_invalid_images_and_arguments(H, L, cuda):
 @pytest.mark.parametrize("N", [1, 3, 5, 8, 16])
 def test_batch_of_layer_projections(H, L, oracle, cuda, N):
     """A layer's projections (row shards of 7B shapes) in one batch call, two
-    outputs each at a column offset: bit-identical to one call per image.
-    From 3 tokens the 11008-wide matrix's activations leave one CTA per SM,
-    so the batch splits into two tensor-core launches."""
+    outputs each at a column offset: bit-identical to one call per image on
+    the same path.  From 3 tokens the 11008-wide matrix's activations leave
+    one CTA per SM, so the batch splits into two tensor-core launches; at 16
+    they do not fit at all and that matrix takes the GEMM."""
     torch = cuda
     shapes = [(512, 4096), (256, 4096), (384, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
     imgs, xs, refs, outs = [], [], [], []
@@ -298,7 +301,9 @@ def test_batch_of_layer_projections(H, L, oracle, cuda, N):
             xh, _ = synth.activations(N, I, 400 + i)
             x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
             ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
-            assert L.hxq_cuda_vq_matmul(img, x.data_ptr(), N, ref.data_ptr(), O, None) == 0
+            # the batch takes the tensor-core GEMV up to 16 tokens where it fits
+            if N > 16 or L.hxq_cuda_vq_matmul_path(img, x.data_ptr(), N, ref.data_ptr(), O, 2, None) != 0:
+                assert L.hxq_cuda_vq_matmul(img, x.data_ptr(), N, ref.data_ptr(), O, None) == 0
             xs.append(x); refs.append(ref)
             outs.append([torch.full((N, O + 32), float("nan"), dtype=torch.float32, device="cuda") for _ in range(2)])
         n = len(shapes)

@@ -19,9 +19,14 @@
 //              sidecar positions are recomputed in fp32 (codebook value +
 //              deltas in array order) and rounded once.  The packed pairs go
 //              straight into tensor memory (tcgen05.st) as the MMA's A
-//              operand -- no shared-memory staging or swizzle for weights;
-//              at the end the same threads drain the accumulator
-//              (tcgen05.ld), add the bias and store coalesced rows of Y;
+//              operand -- no shared-memory staging or swizzle for weights.
+//              VQ with 256-token tiles instead writes its row of the A tile
+//              to shared memory (the MMA's K-major 128-byte-swizzled layout,
+//              two 32 KB buffers) and patches the sidecar positions there
+//              with 2-byte stores: a patch is one store, where a register
+//              fragment needs a select over its 32 words.  At the end the
+//              same threads drain the accumulator (tcgen05.ld), add the bias
+//              and store coalesced rows of Y;
 //   warp 8     TMA producer: activation tiles [BN tokens x 64 K] bf16 with
 //              128-byte swizzle into a 2-4 stage shared-memory ring;
 //   warp 9     allocates tensor memory and issues tcgen05.mma
@@ -55,29 +60,37 @@ constexpr uint32_t kConvWarps = 8;
 constexpr uint32_t kThreads = (kConvWarps + 2) * 32;
 constexpr uint32_t kProducerWarp = 8;
 constexpr uint32_t kMmaWarp = 9;
+// VQ with 256-token tiles keeps its A tiles in shared memory.
+__host__ __device__ constexpr bool smem_a(uint32_t bn, bool vq) { return vq && bn == 256u; }
+constexpr uint32_t kABytes = kBM * kBK * 2u;   // one A tile: [2 halves of K][128 rows][128 B]
 // Tensor memory: the accumulator takes BN columns from 0, the two A buffers
-// 64 columns each right after it (rounded to 128); a tile of BN <= 128 fits
-// in 256 columns, so two CTAs can share an SM.
+// (when in tensor memory) 64 columns each right after it (rounded to 128); a
+// tile of BN <= 128 fits in 256 columns, so two CTAs can share an SM.
 __host__ __device__ constexpr uint32_t tmem_a_col(uint32_t bn) { return bn <= 128 ? 128u : 256u; }
-__host__ __device__ constexpr uint32_t tmem_cols(uint32_t bn) { return bn <= 128 ? 256u : 512u; }
+__host__ __device__ constexpr uint32_t tmem_cols(uint32_t bn, bool vq)
+{
+    return smem_a(bn, vq) ? bn : bn <= 128 ? 256u : 512u;
+}
 constexpr uint64_t kWaitCycles = 2000000000ull;  // ~1 s at 1.9 GHz
 constexpr uint32_t kErrTimeout = 2u;
 
 __device__ uint32_t g_gemm_err;          // device status word of this kernel
 
 // Ring depth: 3 stages for the large tiles, 4 for the small; the VQ tile of
-// 128 tokens keeps 2 so that two CTAs (with their 16 KB codebooks) share an SM.
+// 128 tokens keeps 2 so that two CTAs (with their 16 KB codebooks) share an
+// SM, and the VQ tile of 256 keeps 2 to make room for its A buffers.
 __host__ __device__ constexpr uint32_t stages_for(uint32_t bn, bool vq)
 {
-    return bn >= 256 ? 3u : bn == 128 ? (vq ? 2u : 3u) : 4u;
+    return bn >= 256 ? (vq ? 2u : 3u) : bn == 128 ? (vq ? 2u : 3u) : 4u;
 }
 __host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
 constexpr uint32_t kCodebookBytes = 4096u * 4u;   // VQ: 4096 bf16 pairs
-// ring | barriers (full[S], empty[S], a_full[2], a_empty[2], d_full) | tmem
-// addr | abort | (VQ) codebook
+// ring | (A tiles in shared memory) A[2] | barriers (full[S], empty[S],
+// a_full[2], a_empty[2], d_full) | tmem addr | abort | (VQ) codebook
 __host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn, bool vq)
 {
-    return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn) + 256u + (vq ? kCodebookBytes : 0u);
+    return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn) + (smem_a(bn, vq) ? 2u * kABytes : 0u) +
+           256u + (vq ? kCodebookBytes : 0u);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -177,6 +190,16 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -258,19 +281,22 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
 {
     constexpr uint32_t S = stages_for(BN, VQ);
     constexpr uint32_t SB = stage_bytes(BN);
+    constexpr bool SA = smem_a(BN, VQ);
     constexpr uint32_t kTmemA = tmem_a_col(BN);
-    constexpr uint32_t kTmemCols = tmem_cols(BN);
+    constexpr uint32_t kTmemCols = tmem_cols(BN, VQ);
+    constexpr uint32_t kAOff = SA ? 2u * kABytes : 0u;   // A tiles after the ring
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *ring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + S * SB);
+    unsigned char *abuf = ring + S * SB;                  // SA: A[2], 1024-byte aligned
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + S * SB + kAOff);
     uint64_t *empty = full + S;
     uint64_t *a_full = empty + S;
     uint64_t *a_empty = a_full + 2;
     uint64_t *d_full = a_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(d_full + 1);
     volatile uint32_t *abort_flag = tmem_slot + 1;
-    uint32_t *cbh = reinterpret_cast<uint32_t *>(ring + S * SB + 256u);   // VQ: bf16 pairs
+    uint32_t *cbh = reinterpret_cast<uint32_t *>(ring + S * SB + kAOff + 256u);   // VQ: bf16 pairs
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t o0 = blockIdx.x * kBM;
@@ -326,10 +352,16 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (!mbar_wait(full + s, (kt / S) & 1u, abort_flag)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t bbase = smem_u32(ring + s * SB);
+                const uint32_t abase = smem_u32(abuf + b * kABytes);
 #pragma unroll
                 for (uint32_t kk = 0; kk < kBK / 16u; ++kk) {
                     const uint64_t bd = smem_desc(bbase + (kk >> 2) * (BN * 128u) + (kk & 3u) * 32u);
-                    mma_ts(tmem, tmem + kTmemA + b * 64u + kk * 8u, bd, idesc, (kt | kk) != 0u ? 1u : 0u);
+                    if constexpr (SA) {
+                        const uint64_t ad = smem_desc(abase + (kk >> 2) * (kBM * 128u) + (kk & 3u) * 32u);
+                        mma_ss(tmem, ad, bd, idesc, (kt | kk) != 0u ? 1u : 0u);
+                    } else {
+                        mma_ts(tmem, tmem + kTmemA + b * 64u + kk * 8u, bd, idesc, (kt | kk) != 0u ? 1u : 0u);
+                    }
                 }
                 mma_commit(a_empty + b);
                 mma_commit(empty + s);
@@ -452,20 +484,46 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 // sidecar: the patches of this half-step replace their weights
                 // with the reference's fp32 value rounded once to bf16
                 const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
+                if constexpr (SA) {
+                    // this thread's 128 bytes of the A tile: row `row` of half h,
+                    // 16-byte unit u at (u ^ (row & 7)) << 4; then the patches,
+                    // one 2-byte store each, into the same bytes
+                    __syncwarp();
+                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                    unsigned char *arow = abuf + b * kABytes + h * (kBM * 128u) + row * 128u;
+#pragma unroll
+                    for (uint32_t u = 0; u < 8u; ++u)
+                        *reinterpret_cast<uint4 *>(arow + ((u ^ (row & 7u)) << 4)) =
+                            make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
 #pragma unroll 1
-                for (uint32_t i = 0; i < n_cur; ++i) {
-                    const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
-                    pc0 = pc1; pc1 = pc2; pc2 = pc3;
-                    const uint32_t local = (q & 0xFFFFu) - k0;
-                    if (local < 64u) patch_pair(v, local, q >> 16);
+                    for (uint32_t i = 0; i < n_cur; ++i) {
+                        const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
+                        pc0 = pc1; pc1 = pc2; pc2 = pc3;
+                        const uint32_t local = (q & 0xFFFFu) - k0;
+                        if (local < 64u)
+                            *reinterpret_cast<uint16_t *>(arow + ((((local >> 3) ^ (row & 7u)) << 4) | ((local & 7u) << 1))) =
+                                (uint16_t)(q >> 16);
+                    }
+                    pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
+                    // the generic-proxy stores, visible to the tensor cores' reads
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(a_full + b);
+                } else {
+#pragma unroll 1
+                    for (uint32_t i = 0; i < n_cur; ++i) {
+                        const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
+                        pc0 = pc1; pc1 = pc2; pc2 = pc3;
+                        const uint32_t local = (q & 0xFFFFu) - k0;
+                        if (local < 64u) patch_pair(v, local, q >> 16);
+                    }
+                    pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
+                    __syncwarp();
+                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                    tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
+                    asm volatile("tcgen05.wait::st.sync.aligned;");
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    mbar_arrive(a_full + b);
                 }
-                pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
-                __syncwarp();
-                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
-                tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
-                asm volatile("tcgen05.wait::st.sync.aligned;");
-                asm volatile("tcgen05.fence::before_thread_sync;");
-                mbar_arrive(a_full + b);
             }
         }
         if (ok && mbar_wait(d_full, 0u, abort_flag)) {

@@ -1070,10 +1070,6 @@ hxq::VqTcMatrix tc_matrix(const hxq_cuda_image_t *img, const uint16_t *x, const 
                            img->rows, img->in_f};
 }
 
-// In a batch the tensor-core GEMV shares its launches across the images and
-// beats per-image GEMMs up to 16 tokens.
-constexpr uint32_t kVqTcBatchMaxTokens = 16;
-
 int default_path(const hxq_cuda_image_t *img, const uint16_t *x, uint32_t N)
 {
     if (!img || !img->has_mm) return 0;
@@ -1182,17 +1178,17 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // The batch in three parts, each image in the first that takes it: up to
-    // 16 tokens, images with matmul tables that suit the tensor-core GEMV
-    // share its launches (8 per launch; a single call takes it only up to
-    // HXQ_VQ_MATMUL_TC_MAX tokens); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the
-    // rest share exact-GEMV launches; anything left runs one call per image.
+    // HXQ_VQ_MATMUL_TC_MAX tokens, images with matmul tables that suit the
+    // tensor-core GEMV share its launches (8 per launch); up to
+    // HXQ_VQ_MATMUL_GEMV_MAX tokens the rest share exact-GEMV launches;
+    // anything left runs one call per image.
     std::vector<uint8_t> done(n, 0);
     std::vector<hxq::VqTcMatrix> tcs;
     for (uint32_t i = 0; i < n; ++i) {
         hxq::OutPtrs o;
         if ((err = outs_of(i, o)) != HXQ_OK) return err;
         if (imgs[i]->rows == 0) { done[i] = 1; continue; }
-        if (imgs[i]->has_mm && N <= kVqTcBatchMaxTokens && hxq::vq_tc_fits(d_xs[i], N, imgs[i]->in_f)) {
+        if (default_path(imgs[i], d_xs[i], N) == 2) {
             tcs.push_back(tc_matrix(imgs[i], d_xs[i], o, ldys[i]));
             done[i] = 1;
         }

@@ -244,7 +244,7 @@ int hxq_cuda_affine_device_status(void);
  *     and fp32 accumulation.
  * Stream-ordered on `stream` (0: the legacy default stream); no sync. */
 #define HXQ_VQ_MATMUL_GEMV_MAX 4
-#define HXQ_VQ_MATMUL_TC_MAX 8
+#define HXQ_VQ_MATMUL_TC_MAX 16
 hxq_error_t hxq_cuda_vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16,
                                uint32_t N, float *d_y, uint32_t ldy, void *stream);
 /* The same with the kernel chosen by the caller: path 0 the exact fp32
@@ -300,11 +300,11 @@ int hxq_affine_group_matmul_bf16_multi(const uint16_t *d_x_bf16,
  * launch), which pays the per-launch costs once for the batch; any other
  * matrix runs one call of its own.  Returns 0, or -1 on an error. */
 /* A batch of n fused VQ matmuls (e.g. a layer's projections), outputs as
- * in hxq_affine_group_matmul_bf16_batch.  Up to 16 tokens the images with
- * matmul tables that suit the tensor-core GEMV share its launches (up to 8
- * images per launch; a single call takes it only up to
- * HXQ_VQ_MATMUL_TC_MAX tokens); up to HXQ_VQ_MATMUL_GEMV_MAX tokens the
- * others share exact-GEMV launches; anything else runs one call per image. */
+ * in hxq_affine_group_matmul_bf16_batch.  Up to HXQ_VQ_MATMUL_TC_MAX
+ * tokens the images with matmul tables that suit the tensor-core GEMV share
+ * its launches (up to 8 images per launch); up to HXQ_VQ_MATMUL_GEMV_MAX
+ * tokens the others share exact-GEMV launches; anything else runs one call
+ * per image. */
 hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs,
                                      const uint16_t *const *d_xs, float *const *d_ys,
                                      uint32_t n_out, const uint32_t *ldys, uint32_t N,

@@ -157,15 +157,15 @@ def test_c5_prefill_2048_sampled(H, L, oracle, cuda):
 
 
 def test_default_path_choice(H, L, oracle, cuda):
-    """With matmul tables, up to 8 tokens take the tensor-core GEMV and more
+    """With matmul tables, up to 16 tokens take the tensor-core GEMV and more
     the GEMM; without tables, the exact GEMV: each bit-identical to its
     explicit path."""
-    d, W, xh, x = _case(oracle, 512, 1024, 9, 99)
+    d, W, xh, x = _case(oracle, 512, 1024, 17, 99)
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, 512)
     plain = _image(H, L, t, 0, 512, matmul=False)
     try:
-        for n, path in ((4, 2), (8, 2), (9, 1)):
+        for n, path in ((4, 2), (8, 2), (9, 2), (16, 2), (17, 1)):
             y_default = _run(cuda, L, img, xh[:n], 512)
             y_path = _run(cuda, L, img, xh[:n], 512, path=path)
             assert np.array_equal(y_default.view(np.uint32), y_path.view(np.uint32)), n

@@ -462,6 +462,7 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
     float *y = out.y[0];
     if (in_f == 0) {  // empty reduction: bias only
         if (!plain) return -1;
+        gemm_chain_break();
         affine_generic_kernel<XT><<<1, 256, 0, s>>>(x, codes, scales, offsets, bias, y, N, in_f, out_f, gs);
         return cudaGetLastError() == cudaSuccess ? 0 : -1;
     }
@@ -470,6 +471,7 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
         const uint16_t *xb = reinterpret_cast<const uint16_t *>(x);
         if ((path == HXQ_AFFINE_PATH_AUTO && N <= kTcGemvMaxTokens) || path == HXQ_AFFINE_PATH_TC_GEMV) {
             const TcMatrix m{xb, codes, scales, offsets, bias, out, ldy, in_f, out_f, gs};
+            gemm_chain_break();
             const int r = launch_tc_gemv(1, &m, N, sm_count(), s);
             if (r <= 0) return r;  // launched (0) or failed (-1); 1 = shape not taken
             if (path == HXQ_AFFINE_PATH_TC_GEMV) return -1;
@@ -482,6 +484,7 @@ int run_affine(const XT *x, const uint8_t *codes, const float *scales, const flo
     } else {
         if (path == HXQ_AFFINE_PATH_TC_GEMV || path == HXQ_AFFINE_PATH_GEMM) return -1;
     }
+    gemm_chain_break();   // a GEMV follows
     const bool fast = gs % 16u == 0 && in_f % 16u == 0 && aligned(x, 16) && aligned(codes, 16);
     if (fast) {
         const int sms = sm_count();
@@ -686,6 +689,8 @@ int hxq_affine_group_matmul_bf16_batch(uint32_t n, const hxq_affine_tensor_t *te
             }
         }
     }
+    // one call per matrix; consecutive GEMMs overlap their wave tails
+    hxq::GemmChainScope chain(s);
     for (uint32_t i = 0; i < n; ++i) {
         if (done[i]) continue;
         const hxq_affine_tensor_t &t = tensors[i];

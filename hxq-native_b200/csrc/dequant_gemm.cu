@@ -34,7 +34,14 @@
 //              thread; tcgen05.commit frees A buffers and ring stages.
 // Tensor memory: accumulator [128 x BN] fp32 from column 0, two A buffers of
 // 64 columns (128 bf16 of K) after it; 256 columns for BN <= 128 (two CTAs
-// per SM), else 512.  Every mbarrier wait is bounded (about one second of
+// per SM), else 512.
+// In a batch, a GEMM that follows an unsplit GEMM of the same batch is
+// launched with programmatic stream serialization: it may start while the
+// previous GEMM's last wave runs (the previous GEMM signals its dependents
+// only after it has waited for its own predecessor, so the activations are
+// ready), and waits for the previous GEMM at its end instead of its start,
+// so that the batch still completes in order.  Other GEMMs are launched in
+// plain stream order.  Every mbarrier wait is bounded (about one second of
 // clock); a wait that runs out records an error word and the CTA unwinds,
 // releasing its tensor memory.
 #include <cuda.h>
@@ -262,6 +269,7 @@ struct Params {
     float *part;              // [splits][T, O] partial sums when splits > 1
     uint32_t T, I, O, gs, ldy;
     uint32_t splits;          // K ranges (gridDim.z); >1 writes partials, no bias
+    uint32_t chain;           // 1: follows an unsplit GEMM of the same batch
 };
 
 // Replace the bf16 at position `local` (0..63) of a thread's 32 packed
@@ -305,6 +313,8 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     const uint32_t kt_lo = (uint32_t)((uint64_t)KT_all * blockIdx.z / p.splits);
     const uint32_t KT = (uint32_t)((uint64_t)KT_all * (blockIdx.z + 1u) / p.splits) - kt_lo;
 
+    if (!p.chain) asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(full + s, 1);
@@ -566,6 +576,8 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
+    // a chained GEMM completes only after the one before it
+    if (p.chain) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // y[n, o] = sum over the K ranges, in order, of the partial sums + bias,
@@ -636,9 +648,21 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
         }
         configured.fetch_or(bit, std::memory_order_acq_rel);
     }
-    dim3 grid((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
-    kern<<<grid, kThreads, smem, s>>>(map, p);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    // only a chained GEMM is launched ahead of its predecessor's end: an
+    // early launch behind other kernels (the GEMVs signal at their start)
+    // measured slower
+    cfg.numAttrs = p.chain ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, map, p) != cudaSuccess) { cudaGetLastError(); return -1; }
+    return 0;
 }
 
 // Partial-sum buffer for split-K, one per (device, stream) so calls on
@@ -663,7 +687,19 @@ float *splitk_buffer(size_t floats, cudaStream_t s)
     return b.p;
 }
 
+// Chain state of the batch being launched on this host thread: whether the
+// last kernel it put on `s` was an unsplit GEMM.
+struct Chain {
+    bool active = false, prev_gemm = false;
+    cudaStream_t s = nullptr;
+};
+thread_local Chain g_chain;
+
 }  // namespace gemm
+
+void gemm_chain_begin(cudaStream_t s) { gemm::g_chain = gemm::Chain{true, false, s}; }
+void gemm_chain_end() { gemm::g_chain = gemm::Chain{}; }
+void gemm_chain_break() { gemm::g_chain.prev_gemm = false; }
 
 namespace {
 
@@ -696,6 +732,10 @@ int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
     p.splits = splits;
     p.out = out;
     p.part = part;
+    gemm::Chain &ch = gemm::g_chain;
+    const bool in_batch = ch.active && ch.s == s;
+    p.chain = in_batch && ch.prev_gemm && splits == 1 ? 1u : 0u;
+    if (in_batch) ch.prev_gemm = false;   // set again below on an unsplit launch
     int r;
     switch (bn) {
     case 16: r = gemm::launch<16, VQ>(x, p, s); break;
@@ -704,6 +744,7 @@ int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
     case 128: r = gemm::launch<128, VQ>(x, p, s); break;
     default: r = gemm::launch<256, VQ>(x, p, s); break;
     }
+    if (r == 0 && splits == 1 && in_batch) ch.prev_gemm = true;
     if (r != 0 || splits == 1) return r;
     const uint64_t total = (uint64_t)T * O;
     uint64_t blocks = (total + 255u) / 256u;

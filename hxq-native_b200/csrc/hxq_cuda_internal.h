@@ -149,6 +149,18 @@ cudaError_t launch_vq_gemv_batch(uint32_t n, const VqGemvJob *jobs, uint32_t nto
 cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *chunk_ptr, const SideEntry *ent,
                            uint32_t n_chunks, uint32_t rows, uint32_t in_f, const uint16_t *x, uint32_t ntok,
                            const OutPtrs &out, uint32_t ldy, int sms, cudaStream_t s);
+// A batch's GEMMs on one stream, launched by this host thread between
+// begin and end, overlap each unsplit GEMM's tail with the next one's start;
+// a batch that launches any other kernel in between calls break after it.
+void gemm_chain_begin(cudaStream_t s);
+void gemm_chain_end();
+void gemm_chain_break();
+struct GemmChainScope {
+    explicit GemmChainScope(cudaStream_t s) { gemm_chain_begin(s); }
+    ~GemmChainScope() { gemm_chain_end(); }
+    GemmChainScope(const GemmChainScope &) = delete;
+    GemmChainScope &operator=(const GemmChainScope &) = delete;
+};
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
                  const uint16_t *kp, const uint32_t *e4, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O,
                  uint32_t ldy, cudaStream_t s);

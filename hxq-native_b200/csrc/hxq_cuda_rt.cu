@@ -1098,6 +1098,7 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if ((err = dev_ready(dev)) != HXQ_OK) return err;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (path != 1) hxq::gemm_chain_break();   // a GEMV follows
     if (path == 2) {
         const hxq::VqTcMatrix m = tc_matrix(img, d_x_bf16, out, ldy);
         const int r = hxq::launch_vq_tc_gemv(1, &m, N, g_dev[dev].sms, s);
@@ -1205,6 +1206,8 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
         g_launches.fetch_add(1, std::memory_order_relaxed);
     }
     if (N > HXQ_VQ_MATMUL_GEMV_MAX) {
+        // one call per image; consecutive GEMMs overlap their wave tails
+        hxq::GemmChainScope chain(s);
         for (uint32_t i = 0; i < n; ++i) {
             if (done[i]) continue;
             hxq::OutPtrs o;

@@ -301,3 +301,39 @@ def test_batch_of_layer_projections(H, L, cuda, N):
             assert torch.equal(o[:, 32:32 + O].contiguous().view(torch.int32), ref.view(torch.int32))
             assert bool(torch.isnan(o[:, :32]).all()) and bool(torch.isnan(o[:, 32 + O:]).all())
     assert L.hxq_cuda_affine_device_status() == 0
+
+
+def test_batch_chained_gemms(H, L, cuda):
+    """A prefill batch whose GEMMs are unsplit (4096 x 256 at 2048 tokens:
+    256 tiles each), so each one after the first is chained to the one
+    before it and overlaps its last wave: every output bit-identical to one
+    call per matrix, and the batch's outputs complete before the next
+    kernel on the stream reads them."""
+    torch = cuda
+    N, shapes = 2048, [(4096, 256)] * 3
+    devs, xs, refs, outs, ts = [], [], [], [], []
+    for i, (O, I) in enumerate(shapes):
+        d = synth.affine(O, I, 128, 700 + i, bias=(i == 1))
+        dev = Dev(torch, d, d["bias"])
+        xh, _ = synth.activations(N, I, 800 + i)
+        x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+        ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+        t = dev.tensor(H)
+        assert L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(t), ref.data_ptr(), N, None) == 0
+        devs.append(dev); xs.append(x); refs.append(ref); ts.append(t)
+        outs.append(torch.full((N, O), float("nan"), dtype=torch.float32, device="cuda"))
+    n = len(shapes)
+    T = (H.AffineTensor * n)(*ts)
+    X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+    Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    LD = (C.c_uint32 * n)(*[O for O, _ in shapes])
+    for _ in range(2):
+        assert L.hxq_affine_group_matmul_bf16_batch(n, T, X, Y, 1, LD, N, None) == 0
+        total = sum(o.sum() for o in outs)   # a kernel that reads every output after the batch
+        torch.cuda.synchronize()
+        assert torch.isfinite(total)
+        for ref, o in zip(refs, outs):
+            assert torch.equal(o.view(torch.int32), ref.view(torch.int32))
+        for o in outs:
+            o.fill_(float("nan"))
+    assert L.hxq_cuda_affine_device_status() == 0

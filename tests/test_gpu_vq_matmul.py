@@ -324,3 +324,42 @@ def test_batch_of_layer_projections(H, L, oracle, cuda, N):
     finally:
         for im, _ in imgs:
             L.hxq_cuda_image_destroy(im)
+
+
+def test_batch_chained_gemms(H, L, oracle, cuda):
+    """A prefill batch whose GEMMs are unsplit (4096 x 256 images at 2048
+    tokens: 256 tiles each), so each one after the first is chained to the
+    one before it: every output bit-identical to one call per image."""
+    torch = cuda
+    N, shapes = 2048, [(4096, 256)] * 3
+    imgs, xs, refs, outs = [], [], [], []
+    try:
+        for i, (O, I) in enumerate(shapes):
+            d = _with_dups_and_oob(synth.vq12(O, I, 900 + i), 900 + i)
+            t = H.Tensor().load(d)
+            img = _image(H, L, t, 0, O)
+            imgs.append((img, t))
+            xh, _ = synth.activations(N, I, 950 + i)
+            x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+            ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+            assert L.hxq_cuda_vq_matmul(img, x.data_ptr(), N, ref.data_ptr(), O, None) == 0
+            xs.append(x); refs.append(ref)
+            outs.append(torch.full((N, O), float("nan"), dtype=torch.float32, device="cuda"))
+        n = len(shapes)
+        IM = (C.c_void_p * n)(*[im.value for im, _ in imgs])
+        X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+        Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        LD = (C.c_uint32 * n)(*[O for O, _ in shapes])
+        for _ in range(2):
+            assert L.hxq_cuda_vq_matmul_batch(n, IM, X, Y, 1, LD, N, None) == 0
+            total = sum(o.sum() for o in outs)   # reads every output after the batch
+            torch.cuda.synchronize()
+            assert torch.isfinite(total)
+            for ref, o in zip(refs, outs):
+                assert torch.equal(o.view(torch.int32), ref.view(torch.int32))
+            for o in outs:
+                o.fill_(float("nan"))
+        assert L.hxq_cuda_affine_device_status() == 0
+    finally:
+        for im, _ in imgs:
+            L.hxq_cuda_image_destroy(im)

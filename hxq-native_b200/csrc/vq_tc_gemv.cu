@@ -31,9 +31,10 @@
 //     codebook pair carry d = bf16(final weight) - bf16(codebook value)
 //     (image table, one entry per position, rows in order).  After a row
 //     block's products, consumer warp w sums d x[n, col] over the positions
-//     of rows 2w and 2w + 1 (lanes strided over the positions, activations
-//     from the staged copy, a fixed butterfly across lanes) and the sum is
-//     added to the output it stores.  The result equals the tcgen05 VQ
+//     of rows 2w and 2w + 1, one row per half-warp (16 lanes strided over
+//     the row's positions, activations from the staged copy, a transposed
+//     butterfly over the half) and the sum is added to the output it
+//     stores.  The result equals the tcgen05 VQ
 //     GEMM's weights: bf16 of each final weight (|error| <= 2^-9 sum |x w|
 //     per output, fp32 accumulation).
 //   * The 8 warps' sums of a row block are added in warp order
@@ -215,56 +216,29 @@ __device__ __forceinline__ void side_add(float (&sn)[NC], uint32_t e4, float dl,
             sn[n] = fmaf(dl, __uint_as_float((uint32_t)xc[(uint32_t)n * ldx] << 16), sn[n]);
 }
 
-// Warp sum of sn[n] for n < N <= NC into out[n] (fixed order:
-// deterministic).  NC <= 2: a butterfly per token; else a transposed
-// butterfly (9 shuffles for 8 sums: halves exchanged over lane bits 4, 3, 2,
-// then bits 1, 0; the sum of token n ending in lanes 4n .. 4n + 3), or for
-// 16 sums 16 shuffles over lane bits 4, 3, 2, 1, then 0 (token n in lanes
-// 2n, 2n + 1).
+// Sum over each half-warp (lanes 0-15, 16-31) of sn[n] for the tokens
+// n < N <= NC, in a fixed order (deterministic): a transposed butterfly
+// exchanges halves of the NC values over lane bits 3, 2, ... (log2 NC steps,
+// NC - 1 shuffles), then a plain butterfly over the bits left; token n ends
+// in lanes n * (16 / NC) .. of the half, the first of which stores it.
 template <int NC>
-__device__ __forceinline__ void side_reduce(float (&sn)[NC], uint32_t N, uint32_t lane, float *out)
+__device__ __forceinline__ void side_reduce_half(float (&sn)[NC], uint32_t N, uint32_t lane, float *out)
 {
-    if constexpr (NC <= 2) {
+    float v[NC];
 #pragma unroll
-        for (int n = 0; n < NC; ++n) {
-            if (NC == 1 || (uint32_t)n < N) {
+    for (int n = 0; n < NC; ++n) v[n] = sn[n];
+    uint32_t token = 0;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sn[n] += __shfl_xor_sync(0xffffffffu, sn[n], o);
-                if (lane == 0) out[n] = sn[n];
-            }
-        }
-    } else if constexpr (NC == 16) {
-        const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u, b1 = lane & 2u;
-        float v8[8], v4[4], v2[2];
+    for (int cnt = NC, bit = 8; cnt > 1; cnt >>= 1, bit >>= 1) {
+        const bool up = lane & (uint32_t)bit;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            v8[i] = (b4 ? sn[i + 8] : sn[i]) + __shfl_xor_sync(0xffffffffu, b4 ? sn[i] : sn[i + 8], 16);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            v4[i] = (b3 ? v8[i + 4] : v8[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v8[i] : v8[i + 4], 8);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-            v2[i] = (b2 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b2 ? v4[i] : v4[i + 2], 4);
-        float v = (b1 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b1 ? v2[0] : v2[1], 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        if ((lane & 1u) == 0 && (lane >> 1) < N) out[lane >> 1] = v;
-    } else {
-        float s8[8];
-#pragma unroll
-        for (int n = 0; n < 8; ++n) s8[n] = n < NC ? sn[n < NC ? n : 0] : 0.0f;
-        const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
-        float v4[4], v2[2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            v4[i] = (b4 ? s8[i + 4] : s8[i]) + __shfl_xor_sync(0xffffffffu, b4 ? s8[i] : s8[i + 4], 16);
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-            v2[i] = (b3 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v4[i] : v4[i + 2], 8);
-        float v = (b2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? v2[0] : v2[1], 4);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        if ((lane & 3u) == 0 && (lane >> 2) < N) out[lane >> 2] = v;
+        for (int i = 0; i < cnt / 2; ++i)
+            v[i] = (up ? v[i + cnt / 2] : v[i]) + __shfl_xor_sync(0xffffffffu, up ? v[i] : v[i + cnt / 2], bit);
+        token += up ? (uint32_t)(cnt / 2) : 0u;
     }
+#pragma unroll
+    for (int bit = 8 / NC; bit >= 1; bit >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], bit);
+    if ((lane & (16u / NC - 1u)) == 0 && token < N) out[token] = v[0];
 }
 
 // NT token tiles of 8 (1: up to 8 tokens, two CTAs per SM; 2: up to 16,
@@ -366,19 +340,21 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         const uint32_t row0 = (rb - b.rb_begin) * kRows;
         const uint32_t rv = min(kRows, b.rows - row0);
         const uint32_t nst = (in_f + kKC - 1u) / kKC;
-        uint32_t pe[2][2] = {{0u, 0u}, {0u, 0u}};
-        float pd[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        // sidecar: half h of the warp takes row 2w + h, its 16 lanes the
+        // row's entries lo + s16 + 16m (the first 64 loaded here)
+        const uint32_t sh = lane >> 4, s16 = lane & 15u;
+        uint32_t plo = sh ? pr[1] : pr[0], phi = sh ? pr[2] : pr[1];
+        uint32_t pe[4] = {0u, 0u, 0u, 0u};
+        float pd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (b.prow) {
 #pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-                for (int v = 0; v < 2; ++v) {
-                    const uint32_t p = pr[q] + lane + 32u * (uint32_t)v;
-                    if (p < pr[q + 1]) {
-                        pe[q][v] = ldg_pinned(b.e4 + p);
-                        pd[q][v] = ldg_pinned(b.ed + p);
-                    }
+            for (int m = 0; m < 4; ++m) {
+                const uint32_t p = plo + s16 + 16u * (uint32_t)m;
+                if (p < phi) {
+                    pe[m] = ldg_pinned(b.e4 + p);
+                    pd[m] = ldg_pinned(b.ed + p);
                 }
+            }
         }
         uint32_t pn[3] = {0u, 0u, 0u};
         if (rb + 1u < rb1) side_rows(J, rb + 1u, warp, pn);
@@ -431,19 +407,15 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         }
         float *cw = csum + (size_t)(rbi & 1u) * kRows * kCsStride;
         if (b.prow) {
+            float sn[NC];
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                float sn[NC];
+            for (int n = 0; n < NC; ++n) sn[n] = 0.0f;
 #pragma unroll
-                for (int n = 0; n < NC; ++n) sn[n] = 0.0f;
-#pragma unroll
-                for (int v = 0; v < 2; ++v)
-                    if (pr[q] + lane + 32u * (uint32_t)v < pr[q + 1])
-                        side_add<NC>(sn, pe[q][v], pd[q][v], xs, in_f + kXPad, N);
-                for (uint32_t p = pr[q] + 64u + lane; p < pr[q + 1]; p += 32u)
-                    side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
-                side_reduce<NC>(sn, N, lane, cw + (2u * warp + (uint32_t)q) * kCsStride);
-            }
+            for (int m = 0; m < 4; ++m)
+                if (plo + s16 + 16u * (uint32_t)m < phi) side_add<NC>(sn, pe[m], pd[m], xs, in_f + kXPad, N);
+            for (uint32_t p = plo + 64u + s16; p < phi; p += 16u)
+                side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
+            side_reduce_half<NC>(sn, N, lane, cw + (2u * warp + sh) * kCsStride);
         }
 #pragma unroll
         for (int q = 0; q < 3; ++q) pr[q] = pn[q];

@@ -17,9 +17,9 @@
 // store.  Launched with programmatic stream serialization: the codes do not
 // depend on the kernel before it on the stream, so their loads start early
 // and the kernel waits (griddepcontrol.wait) only before the activations.
-// With bf16 activations, 1..8 tokens go to the tensor-core GEMV
-// (affine_tc_gemv.cu) and larger token counts to the tcgen05 GEMM
-// (dequant_gemm.cu) when the shape allows it; this file's GEMVs take fp32
+// With bf16 activations, 1..8 tokens (up to 16 in a batch) go to the
+// tensor-core GEMV (affine_tc_gemv.cu) and larger token counts to the
+// tcgen05 GEMM (dequant_gemm.cu) when the shape allows it; this file's GEMVs take fp32
 // activations and the shapes those kernels do not.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

@@ -200,7 +200,8 @@ struct VqTcMatrix {
     OutPtrs out;
     uint32_t ldy, rows, in_f;
 };
-// 1 <= N <= 8, in_f a multiple of 128 (at most 65536), x 16-byte aligned.
+// 1 <= N <= 16, in_f a multiple of 128 (at most 65536), x 16-byte aligned,
+// and the activations fit in shared memory.
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f);
 // How many of m[0..n) (at most kMaxTcJobs) share one launch without costing
 // the first ones residency (CTAs per SM).

@@ -1,4 +1,4 @@
-// vq_tc_gemv.cu -- fused 12-bit VQ dequant-matmul for 1..8 bf16 tokens on
+// vq_tc_gemv.cu -- fused 12-bit VQ dequant-matmul for 1..16 bf16 tokens on
 // the tensor cores: y[n, o] = sum_i x[n, i] W[o, i], W never written.
 //
 // The weights are the bf16 codebook pairs of the image's matmul tables

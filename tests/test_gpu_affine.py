@@ -337,3 +337,36 @@ def test_batch_chained_gemms(H, L, cuda):
         for o in outs:
             o.fill_(float("nan"))
     assert L.hxq_cuda_affine_device_status() == 0
+
+
+def test_batch_chain_breaks_at_other_kernels(H, L, cuda):
+    """Prefill batch of GEMM matrices with one between them that the GEMM
+    does not take (group size 32: the CUDA-core GEMV): the chain of GEMMs
+    breaks there; every output bit-identical to one call per matrix."""
+    torch = cuda
+    N = 2048
+    specs = [(4096, 256, 128), (4096, 256, 128), (512, 256, 32), (4096, 256, 128), (4096, 256, 128)]
+    devs, xs, refs, outs, ts = [], [], [], [], []
+    for i, (O, I, gs) in enumerate(specs):
+        d = synth.affine(O, I, gs, 1400 + i)
+        dev = Dev(torch, d)
+        xh, _ = synth.activations(N, I, 1500 + i)
+        x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+        ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+        t = dev.tensor(H)
+        assert L.hxq_affine_group_matmul_bf16(x.data_ptr(), C.byref(t), ref.data_ptr(), N, None) == 0
+        devs.append(dev); xs.append(x); refs.append(ref); ts.append(t)
+        outs.append(torch.full((N, O), float("nan"), dtype=torch.float32, device="cuda"))
+    n = len(specs)
+    T = (H.AffineTensor * n)(*ts)
+    X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+    Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    LD = (C.c_uint32 * n)(*[O for O, _, _ in specs])
+    for _ in range(3):
+        assert L.hxq_affine_group_matmul_bf16_batch(n, T, X, Y, 1, LD, N, None) == 0
+        torch.cuda.synchronize()
+        for ref, o in zip(refs, outs):
+            assert torch.equal(o.view(torch.int32), ref.view(torch.int32))
+        for o in outs:
+            o.fill_(float("nan"))
+    assert L.hxq_cuda_affine_device_status() == 0

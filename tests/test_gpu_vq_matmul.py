@@ -363,3 +363,42 @@ def test_batch_chained_gemms(H, L, oracle, cuda):
     finally:
         for im, _ in imgs:
             L.hxq_cuda_image_destroy(im)
+
+
+def test_batch_chain_breaks_at_other_kernels(H, L, oracle, cuda):
+    """Prefill batch of GEMM images with an image without matmul tables
+    between them (it takes the exact GEMV): the chain of GEMMs breaks there,
+    so the GEMM after the GEMV waits for it; every output bit-identical to
+    one call per image, over several repetitions."""
+    torch = cuda
+    N = 2048
+    specs = [(4096, 256, True), (4096, 256, True), (512, 256, False), (4096, 256, True), (4096, 256, True)]
+    imgs, xs, refs, outs = [], [], [], []
+    try:
+        for i, (O, I, mm) in enumerate(specs):
+            d = _with_dups_and_oob(synth.vq12(O, I, 1200 + i), 1200 + i)
+            t = H.Tensor().load(d)
+            img = _image(H, L, t, 0, O, matmul=mm)
+            imgs.append((img, t))
+            xh, _ = synth.activations(N, I, 1300 + i)
+            x = torch.from_numpy(np.ascontiguousarray(xh.view(np.int16))).cuda()
+            ref = torch.empty((N, O), dtype=torch.float32, device="cuda")
+            assert L.hxq_cuda_vq_matmul(img, x.data_ptr(), N, ref.data_ptr(), O, None) == 0
+            xs.append(x); refs.append(ref)
+            outs.append(torch.full((N, O), float("nan"), dtype=torch.float32, device="cuda"))
+        n = len(specs)
+        IM = (C.c_void_p * n)(*[im.value for im, _ in imgs])
+        X = (C.c_void_p * n)(*[x.data_ptr() for x in xs])
+        Y = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+        LD = (C.c_uint32 * n)(*[O for O, _, _ in specs])
+        for _ in range(3):
+            assert L.hxq_cuda_vq_matmul_batch(n, IM, X, Y, 1, LD, N, None) == 0
+            torch.cuda.synchronize()
+            for ref, o in zip(refs, outs):
+                assert torch.equal(o.view(torch.int32), ref.view(torch.int32))
+            for o in outs:
+                o.fill_(float("nan"))
+        assert L.hxq_cuda_affine_device_status() == 0
+    finally:
+        for im, _ in imgs:
+            L.hxq_cuda_image_destroy(im)

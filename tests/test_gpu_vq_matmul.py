@@ -96,11 +96,12 @@ def test_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
 
 @pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 5), (129, 128, 16), (300, 1024, 33), (4096, 4096, 16),
                                           (1024, 2048, 100), (256, 384, 257), (11008, 4096, 16),
-                                          (4096, 11008, 16), (200, 256, 2), (1024, 4096, 256)])
+                                          (4096, 11008, 16), (200, 256, 2), (1024, 4096, 256), (513, 2048, 24)])
 def test_gemm_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
-    """The tcgen05 GEMM (path 1): token tiles of 16 to 256, ragged rows and
-    tiles, split K (1024 x 4096 at 256 tokens: 256-token tiles in 16 splits),
-    repeated and out-of-range sidecar entries."""
+    """The tcgen05 GEMM (path 1): token tiles of 16 to 256 (256 with the A
+    tiles in shared memory), ragged rows and tiles, split K
+    (1024 x 4096 at 256 tokens: 256-token tiles in 16 splits), repeated and
+    out-of-range sidecar entries."""
     d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 7 + in_f + N, dups=True)
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, out_f)

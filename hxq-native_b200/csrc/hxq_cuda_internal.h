@@ -55,8 +55,10 @@ struct VqJob {
     uint32_t         k;          // codebook entries (index bound)
     uint32_t         unit_begin; // first global unit of the job (also its first slot)
     uint32_t         n_units;
-    double          *sumsq;      // optional device output
-    float           *conf;       // optional device output
+    double          *sumsq;      // optional device output: exact sum of squares
+    float           *conf;       // optional device output: receives ref_conf
+    float            ref_conf;   // the reference's confidence for the job
+    uint32_t         pad_;
 };
 
 struct VqLaunch {
@@ -122,6 +124,10 @@ struct GenericJob {
     int               bf16;
     double           *sumsq;
     float            *conf;
+    // value stored into *conf: ref_conf, or sqrt of the kernel's exact sum
+    // of squares when conf_exact is set
+    float             ref_conf;
+    int               conf_exact;
 };
 cudaError_t launch_generic(const GenericJob &j, const Scratch &sc,
                            cudaStream_t s);

@@ -56,6 +56,7 @@ struct hxq_cuda_image {
     uint32_t  n_ent = 0;
     double    sumsq = 0.0;     // exact sum of squared in-range deltas
     float     ref_l2 = 0.0f;   // sqrtf of the fp32 running sum in array order
+    float     ref_l2_tensor = 0.0f;  // the same over every row of the tensor
     // fused-matmul extras (12-bit, k = 4096, in_features % 128 == 0): bf16
     // codebook pairs; per row the first patch; per (row, 128-wide K step)
     // the 16-bit offset of its first patch from the row's; patches
@@ -241,25 +242,33 @@ struct HostEntry { uint64_t pos; float val; };
 // order is inherently sequential, and over 1e5 terms its rounding drifts a
 // few 1e-5 from the true value, beyond reach of any parallel reduction; it
 // depends only on the loaded sidecar, so it is computed here once.
+// *seq_tensor is the same value over every row of the tensor, which a row
+// slice carries so that a matrix split over GPUs can still report it.
 void collect_sidecar(const hxq_tensor_t *t, uint32_t r0, uint32_t r1,
-                     std::vector<HostEntry> &ents, double &sumsq, float *seq)
+                     std::vector<HostEntry> &ents, double &sumsq, float *seq,
+                     float *seq_tensor)
 {
     sumsq = 0.0;
-    volatile float run = 0.0f;  // one rounded product, one rounded add per term
+    volatile float run = 0.0f;   // one rounded product, one rounded add per term
+    volatile float run_all = 0.0f;
     *seq = 0.0f;
+    *seq_tensor = 0.0f;
     ents.clear();
     if (t->sidecar_nnz == 0 || !t->sidecar_rows || !t->sidecar_cols || !t->sidecar_vals) return;
     const uint32_t in_f = t->in_features, out_f = t->out_features;
     for (uint32_t i = 0; i < t->sidecar_nnz; ++i) {
         const uint32_t r = t->sidecar_rows[i], c = t->sidecar_cols[i];
-        if (r >= out_f || c >= in_f || r < r0 || r >= r1) continue;
+        if (r >= out_f || c >= in_f) continue;
         const float v = t->sidecar_vals[i];
+        volatile float sq = v * v;
+        run_all = run_all + sq;
+        if (r < r0 || r >= r1) continue;
         ents.push_back({(uint64_t)(r - r0) * in_f + c, v});
         sumsq += (double)v * (double)v;
-        volatile float sq = v * v;
         run = run + sq;
     }
     *seq = sqrtf(run);
+    *seq_tensor = sqrtf(run_all);
     bool sorted = true;
     for (size_t i = 1; i < ents.size() && sorted; ++i) sorted = ents[i - 1].pos <= ents[i].pos;
     if (!sorted)
@@ -426,7 +435,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
 
     std::vector<HostEntry> ents;
-    collect_sidecar(t, r0, r1, ents, img->sumsq, &img->ref_l2);
+    collect_sidecar(t, r0, r1, ents, img->sumsq, &img->ref_l2, &img->ref_l2_tensor);
     const bool fast = img->kind == kKindScalar || img->kind == kKindVq12;
     if (!fast && img->numel > 0xFFFFFFFFull) { delete img; return HXQ_ERR_INVALID_ARG; }
 
@@ -596,6 +605,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
         J.n_units = units_of(im);
         J.sumsq = d_sumsq ? d_sumsq + i : nullptr;
         J.conf = d_conf ? d_conf + i : nullptr;
+        J.ref_conf = im->ref_l2;
         units += J.n_units;
     }
     if (units > sc.n_slots) return HXQ_ERR_INVALID_ARG;
@@ -668,6 +678,8 @@ hxq_error_t launch_images(hxq_cuda_image *const *imgs, uint32_t n, void *d_out,
         j.bf16 = bf16;
         j.sumsq = d_sumsq ? d_sumsq + i : nullptr;
         j.conf = d_conf ? d_conf + i : nullptr;
+        j.ref_conf = im->ref_l2;
+        j.conf_exact = 0;
         j.ent = im->d_ent;
         j.n_ent = im->n_ent;
         if (im->kind == kKindScalar || im->kind == kKindVq12) {
@@ -1042,6 +1054,8 @@ double hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img) { return img ? 
 
 float hxq_cuda_image_reference_confidence(const hxq_cuda_image_t *img) { return img ? img->ref_l2 : 0.0f; }
 
+float hxq_cuda_image_tensor_confidence(const hxq_cuda_image_t *img) { return img ? img->ref_l2_tensor : 0.0f; }
+
 hxq_error_t hxq_cuda_decompress_images(hxq_cuda_image_t *const *imgs, uint32_t n,
                                        void *d_out, const size_t *out_offsets,
                                        hxq_out_dtype_t dtype, double *d_sumsq,
@@ -1378,6 +1392,7 @@ float hxq_cuda_apply_sidecar(const uint32_t *d_rows, const uint32_t *d_cols,
     j.n_ent = (uint32_t)de.size();
     j.out = d_output;
     j.conf = sc->conf;
+    j.conf_exact = 1;  // this launcher's L2 is a parallel sum, not hxq.c's order
     if (cudaMemcpy(d_ent, de.data(), de.size() * sizeof(SideEntry), cudaMemcpyHostToDevice) == cudaSuccess &&
         launch_generic(j, *sc, (cudaStream_t)0) == cudaSuccess &&
         sync_and_check(dev, (cudaStream_t)0, &conf) == HXQ_OK) {
@@ -1498,20 +1513,28 @@ extern "C" hxq_error_t hxq_cuda_decompress_images_noalloc(hxq_cuda_image_t *cons
     // The array keeps whatever the last call left: clear the error word and
     // the counters the kernel expects at zero.  (Unit slots are written
     // before they are read.)
+    // Once anything is enqueued, an error return first waits for the stream
+    // (ignoring what that reports), so the shared array is idle when the
+    // call returns, as the synchronous contract says.
+    auto drain_and = [s](hxq_error_t e) {
+        cudaStreamSynchronize(s);
+        cudaGetLastError();
+        return e;
+    };
     cudaError_t ce = cudaMemsetAsync(na->ptr, 0, kNoAllocHead, s);
     for (uint32_t i : empty) {
         if (ce == cudaSuccess && d_sumsq) ce = cudaMemsetAsync(d_sumsq + i, 0, sizeof(double), s);
         if (ce == cudaSuccess && d_conf) ce = cudaMemsetAsync(d_conf + i, 0, sizeof(float), s);
     }
-    if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+    if (ce != cudaSuccess) return drain_and(map_cuda(ce));
     const std::vector<uint32_t> *groups[3] = {&g_vq12, &g_vq12k, &g_scalar};
     for (const std::vector<uint32_t> *g : groups) {
         if (g->empty()) continue;
         ce = cudaMemsetAsync(na->ptr + kNoAllocOffCounters, 0, kNoAllocHead - kNoAllocOffCounters, s);
-        if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
+        if (ce != cudaSuccess) return drain_and(map_cuda(ce));
         if ((err = launch_fast_group(*g, imgs, base, out_offsets, elem, bf16, d_sumsq, d_conf, sc,
                                      na->sms, s)) != HXQ_OK)
-            return err;
+            return drain_and(err);
     }
     // Synchronous: wait for the work, then read the device error word.
     uint32_t word = 0;

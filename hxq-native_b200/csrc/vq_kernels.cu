@@ -3,8 +3,12 @@
 // Fast kernel (scalar k=256 and 12-bit k=4096 x dim 2 with in_features % 4
 // == 0).  Semantics follow the reference CPU decoder (hxq-native
 // src/hxq.c:218-235 scalar, :239-298 12-bit, :330-350 sidecar):
-//   W = codebook[index], then in-range sidecar deltas added in array order,
-//   confidence = sqrt(sum of squared in-range deltas).
+//   W = codebook[index], then in-range sidecar deltas added in array order;
+//   the sum of squared in-range deltas is reduced exactly (fp64), and the
+//   confidence output receives the reference's own value (sqrtf of its fp32
+//   running sum in array order), which the host fixes when the image is
+//   built: that sum is sequential by definition, so no parallel reduction
+//   can reproduce its rounding.
 // Design (not a port of src/hxq_cuda.cu):
 //   * the tensor is a flat stream of 2048-weight chunks; one warp owns one
 //     chunk at a time and needs no CTA-wide barrier inside a chunk;
@@ -21,7 +25,7 @@
 //     index so no global read-modify-write is needed; squared deltas are
 //     accumulated in fp64, reduced with warp shuffles, per CTA into a fixed
 //     slot, and the last CTA of a job adds the slots in order (deterministic,
-//     no host round trip);
+//     no host round trip) and stores the job's sum and confidence;
 //   * one launch covers up to 64 jobs (e.g. a whole transformer layer) over
 //     a grid of 4 CTAs per SM with contiguous chunk ranges per CTA.
 #include <cuda_bf16.h>
@@ -318,7 +322,7 @@ __device__ __forceinline__ void finish_unit(const VqLaunch &p, uint32_t j, uint3
     t = warp_sum(t);
     if (lane == 0) {
         if (J.sumsq) *J.sumsq = t;
-        if (J.conf) *J.conf = (float)sqrt(t);
+        if (J.conf) *J.conf = J.ref_conf;
         p.counters[j] = 0u;  // leave scratch zeroed for the next launch
     }
 }
@@ -572,7 +576,7 @@ __global__ void generic_sidecar_kernel(const __grid_constant__ GenericJob j,
             double tot = 0.0;
             for (uint32_t i = 0; i < gridDim.x; ++i) tot += __ldcg(slots + i);
             if (j.sumsq) *j.sumsq = tot;
-            if (j.conf) *j.conf = (float)sqrt(tot);
+            if (j.conf) *j.conf = j.conf_exact ? (float)sqrt(tot) : j.ref_conf;
             *counter = 0u;
         }
     }

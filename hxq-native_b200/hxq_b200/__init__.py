@@ -118,6 +118,7 @@ SIGNATURES = {
     "hxq_cuda_image_device_bytes": (C.c_size_t, [P]),
     "hxq_cuda_image_sidecar_sumsq": (C.c_double, [P]),
     "hxq_cuda_image_reference_confidence": (C.c_float, [P]),
+    "hxq_cuda_image_tensor_confidence": (C.c_float, [P]),
     "hxq_cuda_decompress_images": (C.c_int, [C.POINTER(P), C.c_uint32, P, C.POINTER(C.c_size_t), C.c_int, P, P, P]),
     "hxq_cuda_stream_synchronize": (C.c_int, [P]),
     "hxq_cuda_decompress_images_noalloc": (C.c_int, [C.POINTER(P), C.c_uint32, P, C.POINTER(C.c_size_t), C.c_int, P, P, P]),

@@ -92,12 +92,19 @@ size_t      hxq_cuda_image_device_bytes(const hxq_cuda_image_t *img);
  * tensor's, and sqrt of the total is its confidence. */
 double      hxq_cuda_image_sidecar_sumsq(const hxq_cuda_image_t *img);
 /* The confidence as the reference library reports it for these rows:
- * sqrtf of a float running sum of squares in the sidecar's array order.
- * hxq_dequant and hxq_tensor_decompress return this value, bit-identical
- * to the reference; over ~1e5 entries it differs from the exact value
- * (sqrt of hxq_cuda_image_sidecar_sumsq, and the d_conf output of
- * hxq_cuda_decompress_images) by the reference's own fp32 rounding. */
+ * sqrtf of a float running sum of squares in the sidecar's array order
+ * (src/hxq.c:335-349).  hxq_dequant, hxq_tensor_decompress and the d_conf
+ * output of hxq_cuda_decompress_images return this value, bit-identical to
+ * the reference.  Over ~1e5 entries it differs from the exact value (sqrt
+ * of hxq_cuda_image_sidecar_sumsq, and of the d_sumsq output) by the
+ * reference's own fp32 rounding, a few 1e-5 relative. */
 float       hxq_cuda_image_reference_confidence(const hxq_cuda_image_t *img);
+/* The reference's confidence for the whole tensor the image was cut from
+ * (every row, not only the image's): what hxq_dequant reports for that
+ * tensor.  Lets a matrix split by rows over several GPUs report the
+ * reference's value without gathering its sidecar; equal to
+ * hxq_cuda_image_reference_confidence for an image of all rows. */
+float       hxq_cuda_image_tensor_confidence(const hxq_cuda_image_t *img);
 
 /* Streamed image: the same preprocessed block, kept in pinned host memory
  * instead of HBM, for weights that live on the host and cross PCIe each
@@ -130,7 +137,9 @@ unsigned long long hxq_cuda_launch_count(void);
 /* Decompress n images in one stream-ordered launch.  Image i is written
  * at element offset out_offsets[i] of d_out (elements of `dtype`).
  * d_sumsq (n doubles) and d_conf (n floats) are optional device outputs:
- * each image's sum of squared deltas and sqrt of it, reduced on the GPU.
+ * each image's exact sum of squared sidecar deltas, reduced on the GPU in
+ * fp64 in a fixed order, and its confidence as the reference reports it
+ * (hxq_cuda_image_reference_confidence, bit-identical to hxq.c).
  * Device-side errors (an index >= k) are reported by
  * hxq_cuda_stream_synchronize.  n <= HXQ_CUDA_MAX_BATCH. */
 #define HXQ_CUDA_MAX_BATCH 64

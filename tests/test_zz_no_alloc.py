@@ -7,6 +7,10 @@ calls.  Collected last on purpose (file name), so a failure here cannot stop
 the rest of the suite; it also passes when run alone in a fresh process.
 """
 import ctypes as C
+import os
+import subprocess
+import sys
+import textwrap
 
 import numpy as np
 import pytest
@@ -81,3 +85,57 @@ def test_noalloc_rejects_beyond_its_fixed_scratch(H, L, cuda):
     assert L.hxq_cuda_decompress_images_noalloc(arr, 1, out.data_ptr() + 4, offs, H.HXQ_OUT_F32, None, None,
                                                 None) == H.HXQ_ERR_INVALID_ARG
     L.hxq_cuda_image_destroy(img)
+
+
+# Run in a fresh process: after one warm-up call (which looks up the array's
+# address and loads the kernels), calls on a stream the library has never
+# seen must leave the device's free memory unchanged.  The regular entry
+# point would cudaMalloc reduction scratch for that new stream.
+_NO_ALLOC_PROBE = textwrap.dedent("""
+    import ctypes as C, sys
+    import torch
+    sys.path[:0] = [REPO, PKG]
+    import hxq_b200 as H
+    from hxq_b200 import synth
+    torch.cuda.init()
+    L = H.lib()
+    ds = [synth.vq12(512, 2048, 51), synth.scalar(256, 512, 52, frac=0.01)]
+    ts = [H.Tensor().load(d) for d in ds]
+    imgs = []
+    for t, d in zip(ts, ds):
+        img = C.c_void_p()
+        assert L.hxq_cuda_image_create(t.ref, 0, d["out_f"], C.byref(img)) == 0
+        imgs.append(img)
+    offs = [0, 512 * 2048]
+    out = torch.empty(512 * 2048 + 256 * 512, dtype=torch.float32, device="cuda")
+    ss = torch.empty(2, dtype=torch.float64, device="cuda")
+    cf = torch.empty(2, dtype=torch.float32, device="cuda")
+    arr = (C.c_void_p * 2)(*[i.value for i in imgs])
+    offs_c = (C.c_size_t * 2)(*offs)
+    def call(stream):
+        return L.hxq_cuda_decompress_images_noalloc(arr, 2, out.data_ptr(), offs_c, 0, ss.data_ptr(),
+                                                    cf.data_ptr(), stream.cuda_stream)
+    warm = torch.cuda.Stream()
+    assert call(warm) == 0
+    torch.cuda.synchronize()
+    same = 0
+    for trial in range(3):
+        fresh = torch.cuda.Stream()
+        before = torch.cuda.mem_get_info()[0]
+        for _ in range(3):
+            assert call(fresh) == 0
+        torch.cuda.synchronize()
+        after = torch.cuda.mem_get_info()[0]
+        print("free bytes", before, after)
+        same += before == after
+    print("NOALLOC_OK" if same >= 1 else "NOALLOC_CHANGED")
+""")
+
+
+def test_noalloc_allocates_no_device_memory(H, cuda):
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    pkg = os.path.join(repo, "hxq-native_b200")
+    code = "REPO = %r\nPKG = %r\n" % (repo, pkg) + _NO_ALLOC_PROBE
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "NOALLOC_OK" in r.stdout, r.stdout

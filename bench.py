@@ -8,17 +8,24 @@ matrix 12-bit 2D-VQ (k=4096 x dim 2 codebook ~N(0,0.02), uniform indices,
 rows [r*O/N, (r+1)*O/N) of every matrix (no collective on this path) and
 decompresses a whole layer per launch into one reusable device arena.
 
-A step = decompress all 224 matrices once (each rank its row shards).
-  value: compressed images already resident in HBM, CUDA-graph replay.
-  e2e:   through the public C API with host buffers: every step uploads each
-         matrix's compressed image from pinned host memory (overlapped with
-         the previous layer's decompress) and reads the 224 confidences back.
+A step = decompress all 224 matrices once (each rank its row shards; the
+driver is the library's hxq_b200.sharded.ShardedDecompress).
+  value:      compressed images already resident in HBM, CUDA-graph replay.
+  e2e:        through the public C API with host buffers: every step uploads
+              each matrix's compressed image from pinned host memory
+              (overlapped with the previous layer's decompress) and reads the
+              224 confidences back.
+  e2e_dropin: the reference's own entry point, hxq_dequant(HXQ_BACKEND_CUDA),
+              called once per matrix into a device arena (N=1).
+  aux:        one short measurement of each other configuration (c1, c2,
+              c3 at one token, c5 one-token layer), N=1.
 Inputs per step (5.3 GB compressed, 25.9 GB written) exceed the 126 MB L2,
 so no L2 flush is needed between steps.
 
 `--impl reference` times the reference C library (hxq.c built from source,
-oracle/_ref) on the host cores: every step decompresses layer 0's seven
-matrices with all host threads (pthreads via ctypes over row slices).
+oracle/_ref) on the host cores over the same 32 layers: every step
+decompresses all 224 matrices with all host threads (threads over row
+slices, each with its own reused shared buffer).
 """
 from __future__ import annotations
 
@@ -39,7 +46,7 @@ for p in (HERE, PKG):
 
 import numpy as np  # noqa: E402
 
-from hxq_b200.shard import shard_rows, slice_rows  # noqa: E402
+from hxq_b200.shard import slice_rows  # noqa: E402
 
 METRIC = "dequant weights/s (7B-shaped 12-bit 2D-VQ decompress, sidecar + confidence fused)"
 UNIT = "weights/s"
@@ -117,29 +124,6 @@ def gen_matrix(torch, seed: int, out_f: int, in_f: int) -> dict:
                 vals=vals.cpu().numpy())
 
 
-def build_images(torch, H, L, rank: int, world: int, layers: int):
-    """Streamed images of this rank's row shards, layer by layer."""
-    from hxq_b200 import synth
-    imgs, meta = [], []
-    for layer in range(layers):
-        li, lm = [], []
-        for p, (_, o, i) in enumerate(synth.LLAMA7B_PROJ):
-            r0, r1 = shard_rows(o, rank, world)
-            d = slice_rows(gen_matrix(torch, synth.llama7b_seed(layer, p), o, i), r0, r1)
-            t = H.Tensor().load(d)
-            img = C.c_void_p()
-            H.check(L.hxq_cuda_image_create_streamed(t.ref, 0, r1 - r0, C.byref(img)), "image")
-            t.free()
-            li.append(img)
-            lm.append(dict(rows=r1 - r0, in_f=i, nnz=len(d["rows"]), numel=(r1 - r0) * i,
-                           block=int(L.hxq_cuda_image_block_bytes(img))))
-        imgs.append(li)
-        meta.append(lm)
-        if layer == 0:
-            log(f"[rank {rank}] layer 0 images built")
-    return imgs, meta
-
-
 # ---------------------------------------------------------------------------
 # clocks
 
@@ -194,54 +178,54 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference library on the host cores
 
-def cpu_reference_runner(layer0: list[dict], threads: int | None = None):
-    """Returns (run_once() -> seconds, cores, kind, weights) for layer 0 on
-    `threads` host threads (default: all), each running the unchanged
-    reference function on a slice of rows."""
+def cpu_reference_runner(matrices, threads: int | None = None):
+    """Returns (run_once() -> seconds, cores, kind, weights) for the given
+    matrices (host dicts, or zero-argument callables returning one) on
+    `threads` host threads (default: all).  Each job runs the unchanged
+    reference function hxq_dequant (CPU) on a slice of rows into the calling
+    thread's own shared buffer, reused across jobs as the reference reuses
+    one buffer for a whole model."""
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle.oracle import Oracle, Reference, ref_available
     cores = threads or os.cpu_count() or 1
     kind = "reference" if ref_available() else "port"
-    jobs = []  # (callable) per row slice
+    local = threading.local()
     if kind == "reference":
+        from oracle.oracle import _RefBuf, _RefResult
         ref = Reference()
         Lr = ref.L
-        from oracle.oracle import _RefBuf, _RefResult
-        for d in layer0:
-            o = d["out_f"]
-            step = max(1, o // max(1, cores // 2))
-            for r0 in range(0, o, step):
-                r1 = min(o, r0 + step)
-                sl = slice_rows(d, r0, r1)
-                t = ref.tensor(sl)
-                buf = _RefBuf()
-                Lr.ref_hxq_shared_buffer_init(C.byref(buf), (r1 - r0) * d["in_f"])
-                res = _RefResult()
-                jobs.append((t, buf, res))
-
-        def one(job):
-            t, buf, res = job
-            err = Lr.ref_hxq_dequant(C.byref(t), C.byref(buf), 1, C.byref(res))
-            assert err == 0, err
-        work = one
     else:
         orc = Oracle()
-        for d in layer0:
-            o = d["out_f"]
-            step = max(1, o // max(1, cores // 2))
-            for r0 in range(0, o, step):
-                r1 = min(o, r0 + step)
-                sl = slice_rows(d, r0, r1)
-                jobs.append((sl, np.zeros((r1 - r0) * d["in_f"], np.float32)))
+    jobs, weights = [], 0
+    for m in matrices:
+        d = m() if callable(m) else m
+        o = d["out_f"]
+        weights += o * d["in_f"]
+        step = max(1, o // max(1, cores // 2))
+        for r0 in range(0, o, step):
+            sl = slice_rows(d, r0, min(o, r0 + step))
+            jobs.append(ref.tensor(sl) if kind == "reference" else sl)
+        del d
+    keep = []  # every thread's buffer stays alive with the runner
 
-        def one(job):
-            sl, out = job
-            err, _, _ = orc.decompress(sl, out=out)
+    if kind == "reference":
+        def work(t):
+            if getattr(local, "buf", None) is None:
+                local.buf, local.res = _RefBuf(), _RefResult()
+                Lr.ref_hxq_shared_buffer_init(C.byref(local.buf), 0)
+                keep.append(local.buf)
+            err = Lr.ref_hxq_dequant(C.byref(t), C.byref(local.buf), 1, C.byref(local.res))
+            assert err == 0, err
+    else:
+        def work(sl):
+            n = sl["out_f"] * sl["in_f"]
+            if getattr(local, "buf", None) is None or local.buf.size < n:
+                local.buf = np.zeros(n, np.float32)
+                keep.append(local.buf)
+            err, _, _ = orc.decompress(sl, out=local.buf[:n])
             assert err == 0
-        work = one
     pool = ThreadPoolExecutor(max_workers=cores)
-    weights = sum(d["out_f"] * d["in_f"] for d in layer0)
 
     def run_once() -> float:
         t0 = time.perf_counter()
@@ -250,33 +234,46 @@ def cpu_reference_runner(layer0: list[dict], threads: int | None = None):
     return run_once, cores, kind, weights
 
 
-def layer0_host(torch, rank_world=(0, 1)):
+def layer_matrices(torch, layer: int = 0, lazy: bool = False):
+    """The seven matrices of one 7B layer (q, k, v, o, gate, up, down), or
+    zero-argument callables that generate them."""
     from hxq_b200 import synth
     out = []
     for p, (_, o, i) in enumerate(synth.LLAMA7B_PROJ):
-        out.append(gen_matrix(torch, synth.llama7b_seed(0, p), o, i))
+        def f(s=synth.llama7b_seed(layer, p), o=o, i=i):
+            return gen_matrix(torch, s, o, i)
+        out.append(f if lazy else f())
     return out
 
 
 def run_reference_arm(args):
+    """The reference C library (hxq.c compiled from its sources, oracle/_ref)
+    on all host threads over the same workload as our arm: every step
+    decompresses all 224 matrices of the 32 layers (row slices per thread,
+    one reused shared buffer per thread)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the reference arm runs on rank 0 only
     import torch
     torch.cuda.set_device(0)
-    layer0 = layer0_host(torch)
-    run_once, cores, kind, weights = cpu_reference_runner(layer0)
+    nl = args.layers
+    mats = [m for layer in range(nl) for m in layer_matrices(torch, layer, lazy=True)]
+    t0 = time.time()
+    run_once, cores, kind, weights = cpu_reference_runner(mats)
+    log(f"[reference] {len(mats)} matrices loaded in {time.time() - t0:.1f}s")
     for _ in range(args.warmup):
         run_once()
     times = [run_once() for _ in range(args.steps)]
     total = sum(times)
     value = weights * args.steps / total
-    sample = f"layer 0 of the 7B workload (7 matrices, {weights} weights) per step, {cores} host threads"
+    sample = (f"all {nl} layers of the 7B workload ({len(mats)} matrices, {weights} weights) per step, "
+              f"{cores} host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "llama7b-vq12-decompress", "sample": "layer 0"},
+        "data": "synthetic", "config": {"workload": "llama7b-vq12-decompress", "layers": nl,
+                                        "matrices": len(mats), "weights": weights},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -546,8 +543,9 @@ def run_fused_matmul_workload(args):
     down): the same matrices as 12-bit 2D-VQ images (codebook gather +
     sidecar, no dense weights) and as affine 4-bit codes in groups of 128,
     bf16 activations at 1, 16 and 2048 tokens.  Output features are split
-    across the ranks (each rank holds the rows of its shard).  With more
-    than one rank two ways of assembling the full outputs are timed:
+    across the ranks (hxq_b200.sharded.ColumnSplitLayer: each rank holds the
+    rows of its shard).  With more than one rank two ways of assembling the
+    full outputs are timed:
       nccl: each matrix's output shard is all-gathered over NCCL into
             [ranks * tokens, rows];
       p2p:  every rank's [tokens, out_features] output buffer is mapped into
@@ -556,13 +554,14 @@ def run_fused_matmul_workload(args):
             matmuls one flag kernel tells the peers, one wait kernel waits
             for them.  Two buffers alternate by step parity.
     One step = the 7 matrices (+ assembly), captured in a CUDA graph; device
-    time, max over ranks."""
+    time, max over ranks, and every rank's own time."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
 
     import hxq_b200 as H
     from hxq_b200 import synth
+    from hxq_b200.sharded import ColumnSplitLayer
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -574,80 +573,23 @@ def run_fused_matmul_workload(args):
     hbm, peak_kind = measured_peaks()
     steps = args.steps + (args.steps % 2)          # even: the p2p buffers alternate by parity
 
-    def max_over_ranks(x: float) -> float:
+    def over_ranks(x: float) -> list:
         if world == 1:
-            return x
+            return [x]
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return [float(q.item()) for q in parts]
 
-    # this rank's rows of every matrix, both formats
-    mats = []
-    vq_bytes = aff_bytes = 0
-    for p, (name, O, I) in enumerate(synth.LLAMA7B_PROJ):
-        r0, r1 = shard_rows(O, rank, world)
-        d = synth.vq12(O, I, synth.llama7b_seed(0, p))
-        t = H.Tensor().load(d)
-        img = C.c_void_p()
-        H.check(L.hxq_cuda_image_create_ex(t.ref, r0, r1, H.HXQ_IMAGE_MATMUL, C.byref(img)), "image")
-        assert L.hxq_cuda_image_has_matmul_tables(img) == 1
-        nnz = int(np.count_nonzero((d["rows"] >= r0) & (d["rows"] < r1)))
-        vq_bytes += (r1 - r0) * I * 3 // 4 + CB_BYTES + 12 * nnz
-        da = synth.affine(O, I, 128, synth.llama7b_seed(0, p) + 1000)
-        ng = I // 128
-        codes = torch.from_numpy(np.ascontiguousarray(da["codes"].reshape(O, I)[r0:r1])).cuda()
-        scales = torch.from_numpy(np.ascontiguousarray(da["scales"].reshape(O, ng)[r0:r1])).cuda()
-        offs = torch.from_numpy(np.ascontiguousarray(da["offsets"].reshape(O, ng)[r0:r1])).cuda()
-        at = H.AffineTensor(codes.data_ptr(), scales.data_ptr(), offs.data_ptr(), None, r1 - r0, I, 128)
-        aff_bytes += (r1 - r0) * I + 2 * (r1 - r0) * ng * 4
-        mats.append(dict(name=name, O=O, I=I, r0=r0, rows=r1 - r0, img=img, tensor=t, aff=at,
-                         keep=(codes, scales, offs)))
-    weights = 2.0 * sum(m["O"] * m["I"] for m in mats)   # flops per token per layer
     Ns = (1, 16, 2048)
-
-    # p2p: per matrix and parity an IPC output buffer [max tokens, O] on every
-    # rank, mapped into every other rank; one flag array per rank
-    p2p = None
-    if world > 1:
-        nmax = max(Ns)
-        handle = lambda: (C.c_char * 64)()  # noqa: E731
-        own, hnd = [], []
-        for m in mats:
-            for q in range(2):
-                ptr, h = C.c_void_p(), handle()
-                H.check(L.hxq_cuda_ipc_alloc(nmax * m["O"] * 4, C.byref(ptr), h), "ipc alloc")
-                own.append(ptr)
-                hnd.append(bytes(h))
-        fptr, fh = C.c_void_p(), handle()
-        H.check(L.hxq_cuda_ipc_alloc(256, C.byref(fptr), fh), "ipc alloc")
-        all_h = [None] * world
-        dist.all_gather_object(all_h, (hnd, bytes(fh)))
-        opened = []
-        bufs = [[None] * world for _ in range(2 * len(mats))]    # [matrix*2 + parity][rank]
-        flag_ptrs = [None] * world
-        for pr in range(world):
-            for j in range(2 * len(mats)):
-                if pr == rank:
-                    bufs[j][pr] = own[j].value
-                else:
-                    dp = C.c_void_p()
-                    H.check(L.hxq_cuda_ipc_open((C.c_char * 64).from_buffer_copy(all_h[pr][0][j]), C.byref(dp)),
-                            "ipc open")
-                    opened.append(dp)
-                    bufs[j][pr] = dp.value
-            if pr == rank:
-                flag_ptrs[pr] = fptr.value
-            else:
-                dp = C.c_void_p()
-                H.check(L.hxq_cuda_ipc_open((C.c_char * 64).from_buffer_copy(all_h[pr][1]), C.byref(dp)), "ipc open")
-                opened.append(dp)
-                flag_ptrs[pr] = dp.value
-        counter = torch.zeros(1, dtype=torch.int32, device="cuda")
-        status = torch.zeros(1, dtype=torch.int32, device="cuda")
-        p2p = dict(own=own, fptr=fptr, opened=opened, bufs=bufs,
-                   flags=(C.c_void_p * world)(*flag_ptrs), counter=counter, status=status)
-        torch.cuda.synchronize()
-        dist.barrier()
+    mats = []
+    for p, (name, O, I) in enumerate(synth.LLAMA7B_PROJ):
+        mats.append(dict(name=name, O=O, I=I, vq=synth.vq12(O, I, synth.llama7b_seed(0, p)),
+                         affine=synth.affine(O, I, 128, synth.llama7b_seed(0, p) + 1000)))
+    layers = {fmt: ColumnSplitLayer(mats, fmt, p2p=world > 1, max_tokens=max(Ns), rank=rank, world=world,
+                                    torch=torch, lib=L) for fmt in ("vq12", "affine")}
+    del mats
+    flops_per_token = 2.0 * sum(O * I for _, O, I in synth.LLAMA7B_PROJ)
 
     def time_graph(step):
         with torch.cuda.stream(stream):
@@ -670,116 +612,56 @@ def run_fused_matmul_workload(args):
             graph.replay()
         e1.record(stream)
         e1.synchronize()
-        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        per_rank = over_ranks(e0.elapsed_time(e1) / steps)
         del graph
-        return ms
+        return max(per_rank), per_rank
 
     results = []
     for fmt in ("vq12", "affine"):
+        layer = layers[fmt]
         for N in Ns:
             xh4, _ = synth.activations(N, 4096, synth.SEED_C5 + N)
             xh11, _ = synth.activations(N, 11008, synth.SEED_C5 + N + 1)
-            x4 = torch.from_numpy(xh4.view(np.int16)).cuda()
-            x11 = torch.from_numpy(xh11.view(np.int16)).cuda()
-            ys = [torch.empty((N, m["rows"]), dtype=torch.float32, device="cuda") for m in mats]
-            # [ranks * tokens, rows]: rank r's shard at rows r*N .. r*N + N - 1
-            gathered = [torch.empty((world * N, m["rows"]), dtype=torch.float32, device="cuda") for m in mats]
-
-            def matmul(m, outs, ldy):
-                x = x11 if m["I"] == 11008 else x4
-                n_out = len(outs)
-                arr = (C.c_void_p * n_out)(*outs)
-                if fmt == "vq12":
-                    H.check(L.hxq_cuda_vq_matmul_multi(m["img"], x.data_ptr(), N, arr, n_out, ldy,
-                                                       C.c_void_p(stream.cuda_stream)), "vq matmul")
-                elif L.hxq_affine_group_matmul_bf16_multi(x.data_ptr(), C.byref(m["aff"]), arr, n_out, ldy, N,
-                                                          C.c_void_p(stream.cuda_stream)) != 0:
-                    raise RuntimeError("affine matmul failed")
-
-            aff_tensors = (H.AffineTensor * len(mats))(*[m["aff"] for m in mats])
-            vq_imgs = (C.c_void_p * len(mats))(*[m["img"].value for m in mats])
-            aff_xs = (C.c_void_p * len(mats))(*[(x11 if m["I"] == 11008 else x4).data_ptr() for m in mats])
-
-            def matmuls(outs_per_matrix, ldys):
-                """The layer's seven matmuls as one batch call."""
-                n_out = len(outs_per_matrix[0])
-                if fmt == "vq12":
-                    Y = (C.c_void_p * (len(mats) * n_out))(*[p for outs in outs_per_matrix for p in outs])
-                    LD = (C.c_uint32 * len(mats))(*ldys)
-                    H.check(L.hxq_cuda_vq_matmul_batch(len(mats), vq_imgs, aff_xs, Y, n_out, LD, N,
-                                                       C.c_void_p(stream.cuda_stream)), "vq matmul batch")
-                    return
-                Y = (C.c_void_p * (len(mats) * n_out))(*[p for outs in outs_per_matrix for p in outs])
-                LD = (C.c_uint32 * len(mats))(*ldys)
-                if L.hxq_affine_group_matmul_bf16_batch(len(mats), aff_tensors, aff_xs, Y, n_out, LD, N,
-                                                        C.c_void_p(stream.cuda_stream)) != 0:
-                    raise RuntimeError("affine matmul batch failed")
-
-            def step_nccl(k):
-                matmuls([[y.data_ptr()] for y in ys], [m["rows"] for m in mats])
-                if world > 1:
-                    for y, g in zip(ys, gathered):
-                        dist.all_gather_into_tensor(g, y)
-
-            def step_p2p(k):
-                matmuls([[b + 4 * m["r0"] for b in p2p["bufs"][2 * j + (k & 1)]] for j, m in enumerate(mats)],
-                        [m["O"] for m in mats])
-                H.check(L.hxq_cuda_peer_signal(p2p["flags"], world, rank, p2p["counter"].data_ptr(),
-                                               C.c_void_p(stream.cuda_stream)), "peer signal")
-                H.check(L.hxq_cuda_peer_wait(p2p["flags"][rank], world, p2p["counter"].data_ptr(),
-                                             p2p["status"].data_ptr(), C.c_void_p(stream.cuda_stream)), "peer wait")
-
-            modes = [("nccl" if world > 1 else "local", step_nccl)]
-            if p2p is not None:
-                modes.append(("p2p", step_p2p))
-            for mode, step in modes:
-                ms = time_graph(step)
-                if fmt == "vq12":
-                    assert L.hxq_cuda_affine_device_status() == 0
-                wbytes = vq_bytes if fmt == "vq12" else aff_bytes
-                per_rank_gbs = wbytes / (ms * 1e-3) / 1e9
+            xs = {4096: torch.from_numpy(xh4.view(np.int16)).cuda(), 11008: torch.from_numpy(xh11.view(np.int16)).cuda()}
+            modes = ["nccl" if world > 1 else "local"] + (["p2p"] if world > 1 else [])
+            for mode in modes:
+                ms, per_rank = time_graph(lambda k: layer.forward(xs, N, stream, step=k, assembly=mode))
+                if L.hxq_cuda_affine_device_status() != 0:
+                    raise RuntimeError("a tensor-core kernel reported a timeout")
+                per_rank_gbs = layer.weight_bytes / (ms * 1e-3) / 1e9
                 res = {"case": f"{fmt} 7B layer N={N} {mode}", "format": fmt, "tokens": N, "assembly": mode,
-                       "us_per_layer": ms * 1e3, "tflops": weights * N / (ms * 1e-3) / 1e12,
-                       "weight_bytes_per_rank": wbytes, "weight_gbs_per_rank": per_rank_gbs,
+                       "us_per_layer": ms * 1e3, "tflops": flops_per_token * N / (ms * 1e-3) / 1e12,
+                       "weight_bytes_per_rank": layer.weight_bytes, "weight_gbs_per_rank": per_rank_gbs,
                        "hbm_frac_per_rank": per_rank_gbs / hbm,
-                       "output_bytes_per_layer": sum(N * m["O"] * 4 for m in mats),
+                       "output_bytes_per_layer": sum(N * O * 4 for _, O, _ in synth.LLAMA7B_PROJ),
                        "path": ("tensor-core GEMV" if N <= 8 else
                                 "tensor-core GEMV for the 4096-wide matrices, tcgen05 GEMM for down"
                                 if N <= 16 else "tcgen05 GEMM")}
+                if world > 1:
+                    res["per_rank_us"] = [t * 1e3 for t in per_rank]
                 if mode == "p2p":
                     # one step outside the graph: the assembled outputs must equal
                     # the NCCL-gathered shards, bit for bit
                     torch.cuda.synchronize()
                     dist.barrier()
                     with torch.cuda.stream(stream):
-                        step_nccl(0)
-                        step_p2p(0)
+                        layer.forward(xs, N, stream, step=0, assembly="nccl")
+                        layer.forward(xs, N, stream, step=0, assembly="p2p")
                     stream.synchronize()
-                    same = True
-                    for j, (m, g) in enumerate(zip(mats, gathered)):
-                        full = H.device_view(torch, p2p["own"][2 * j].value, N * m["O"]).view(N, m["O"])
-                        ref = g.view(world, N, m["rows"]).permute(1, 0, 2).reshape(N, m["O"])
-                        same = same and bool(torch.equal(full.view(torch.int32), ref.contiguous().view(torch.int32)))
+                    same = all(bool(torch.equal(a.view(torch.int32), b.contiguous().view(torch.int32)))
+                               for a, b in zip(layer.outputs(N, 0, "p2p"), layer.outputs(N, 0, "nccl")))
                     t = torch.tensor([1.0 if same else 0.0], dtype=torch.float64, device="cuda")
                     dist.all_reduce(t, op=dist.ReduceOp.MIN)
                     res["p2p_equals_nccl"] = bool(t.item() == 1.0)
-                    res["peer_wait_status"] = int(p2p["status"].item())
+                    res["peer_wait_status"] = layer.peer_wait_status()
                 results.append(res)
-            del x4, x11, ys, gathered
-    if p2p is not None:
-        torch.cuda.synchronize()
-        dist.barrier()
-        for dp in p2p["opened"]:
-            L.hxq_cuda_ipc_close(dp)
-        torch.cuda.synchronize()
-        dist.barrier()
-        for ptr in p2p["own"] + [p2p["fptr"]]:
-            L.hxq_cuda_ipc_free(ptr)
-    for m in mats:
-        L.hxq_cuda_image_destroy(m["img"])
+            del xs
+    for layer in layers.values():
+        layer.close()
     if rank == 0:
         print(json.dumps({"workload": "c5", "data": "synthetic", "n_gpus": world,
                           "parallelism": f"output features split x{world}",
+                          "driver": "hxq_b200.sharded.ColumnSplitLayer",
                           "peak": {"hbm_gbs": hbm, "kind": peak_kind}, "results": results}), flush=True)
     if world > 1:
         dist.barrier()
@@ -840,6 +722,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-aux", action="store_true",
+                    help="skip the short measurements of the other configurations (c1, c2, c3, c5)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers to run (profiling aid; the workload is 32 layers)")
     ap.add_argument("--workload", choices=["llama7b", "c1", "c2", "c3", "c5", "kernels", "lloyd", "pq"],
@@ -900,69 +784,27 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    def gather_over_ranks(x: float) -> list:
+        if world == 1:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return [float(p.item()) for p in parts]
+
+    from hxq_b200.sharded import ShardedDecompress
+
     t_setup = time.time()
     nl = args.layers
-    imgs, meta = build_images(torch, H, L, rank, world, nl)
+    layers = [layer_matrices(torch, layer, lazy=True) for layer in range(nl)]
+    model = ShardedDecompress(layers, rank=rank, world=world, torch=torch, lib=L, log=log)
     log(f"[rank {rank}] images built in {time.time() - t_setup:.1f}s")
-
-    # device residency: every block uploaded once into a pool
-    blocks = [[m["block"] for m in lm] for lm in meta]
-    align = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    pool_bytes = sum(align(b) for lb in blocks for b in lb)
-    pool = torch.empty(pool_bytes, dtype=torch.uint8, device="cuda")
-    off = 0
-    for li, lb in zip(imgs, blocks):
-        for img, b in zip(li, lb):
-            H.check(L.hxq_cuda_image_upload(img, pool.data_ptr() + off, None), "upload")
-            off += align(b)
-    torch.cuda.synchronize()
-
-    # The shared device arena.  Each launch decompresses a group of layers
-    # (as many as there are ranks, at most 8 = 56 matrices), so every launch
-    # carries about one full layer's weights whatever N is; the arena holds
-    # one group and is reused by all groups.
-    lpl = max(1, min(8, world, nl))
-    groups = [list(range(g, min(g + lpl, nl))) for g in range(0, nl, lpl)]
-    g_imgs, g_offs, g_numel = [], [], []
-    for grp in groups:
-        o, pos, gi = [], 0, []
-        for layer in grp:
-            for img, m in zip(imgs[layer], meta[layer]):
-                o.append(pos)
-                pos += m["numel"]
-                gi.append(img)
-        g_imgs.append((C.c_void_p * len(gi))(*[i.value for i in gi]))
-        g_offs.append((C.c_size_t * len(o))(*o))
-        g_numel.append(pos)
-    arena = H.SharedBuffer()
-    H.check(L.hxq_cuda_arena_init(C.byref(arena), max(g_numel)), "arena")
-    # per-layer views for the e2e path (one layer per launch)
-    offs = []
-    for lm in meta:
-        o, pos = [], 0
-        for m in lm:
-            o.append(pos)
-            pos += m["numel"]
-        offs.append((C.c_size_t * 7)(*o))
-    arrs = [(C.c_void_p * 7)(*[i.value for i in li]) for li in imgs]
-    n_mat = nl * 7
-    conf = torch.zeros(n_mat, dtype=torch.float32, device="cuda")
-    sumsq = torch.zeros(n_mat, dtype=torch.float64, device="cuda")
-    f32 = C.sizeof(C.c_float)
-
-    def step(stream_ptr):
-        for gi, grp in enumerate(groups):
-            first = 7 * grp[0]
-            e = L.hxq_cuda_decompress_images(g_imgs[gi], 7 * len(grp), arena.data, g_offs[gi], 0,
-                                             sumsq.data_ptr() + 8 * first, conf.data_ptr() + f32 * first,
-                                             stream_ptr)
-            if e != 0:
-                raise RuntimeError(f"decompress failed: {e}")
+    n_mat = model.n_matrices
 
     stream = torch.cuda.Stream()
     launches0 = L.hxq_cuda_launch_count()
     with torch.cuda.stream(stream):
-        step(stream.cuda_stream)  # creates the stream's scratch before any capture
+        model.step(stream.cuda_stream)  # creates the stream's scratch before any capture
     stream.synchronize()
     H.check(L.hxq_cuda_stream_synchronize(C.c_void_p(stream.cuda_stream)), "first step")
     launches_per_step = L.hxq_cuda_launch_count() - launches0
@@ -972,7 +814,7 @@ def main():
         try:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                step(stream.cuda_stream)
+                model.step(stream.cuda_stream)
             graph = g
         except Exception as e:  # keep direct launches if capture is refused
             log(f"[rank {rank}] graph capture failed, direct launches: {e}")
@@ -985,7 +827,7 @@ def main():
                 if graph is not None:
                     graph.replay()
                 else:
-                    step(stream.cuda_stream)
+                    model.step(stream.cuda_stream)
 
     run_steps(args.warmup)
     stream.synchronize()
@@ -1011,11 +853,18 @@ def main():
     my_ms = ev0.elapsed_time(ev1)
     H.check(L.hxq_cuda_stream_synchronize(C.c_void_p(stream.cuda_stream)), "timed steps")
     ms = max_over_ranks(my_ms)
-    total_weights = int(sum_over_ranks(float(sum(m["numel"] for lm in meta for m in lm))))
+    per_rank_ms = gather_over_ranks(my_ms)
+    total_weights = int(sum_over_ranks(float(model.numel())))
     value = total_weights * args.steps / (ms / 1e3)
 
+    # the confidences every matrix reports after a step: the reference's
+    # (fp32 running sum, bit-identical to hxq.c) and the exact fp64 one
+    ref_conf = model.reference_confidences()
+    exact_conf = model.exact_confidences()
+    conf_rel = max((abs(a - b) / b if b else abs(a)) for a, b in zip(exact_conf, ref_conf)) if ref_conf else 0.0
+
     # roofline of the fused decompress kernel (the only kernel in the step)
-    my_bytes = sum(algorithmic_bytes(m["rows"], m["in_f"], m["nnz"]) for lm in meta for m in lm)
+    my_bytes = model.algorithmic_bytes()
     my_launch_ms = my_ms / (args.steps * launches_per_step)
     achieved = my_bytes / launches_per_step / (my_launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
@@ -1024,12 +873,15 @@ def main():
     # end to end through the public API: host images streamed every step
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(torch, H, L, imgs, meta, arena, offs, arrs, conf, sumsq, args, world, rank,
-                      max_over_ranks, sum_over_ranks)
+        e2e = run_e2e(torch, H, L, model, args, world, max_over_ranks, sum_over_ranks)
+        model.restore_pool()
+    dropin = None
+    if not args.no_e2e and world == 1:
+        dropin = run_dropin(torch, H, L, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        layer0 = layer0_host(torch)
+        layer0 = layer_matrices(torch, 0)
         run_once, cores, kind, weights = cpu_reference_runner(layer0)
         run_once()
         times, t_end = [], time.time() + 10.0
@@ -1042,8 +894,14 @@ def main():
         run1, _, _, _ = cpu_reference_runner(layer0, threads=1)
         t1 = [run1() for _ in range(3)]
         cpu["value_1core"] = weights / statistics.median(t1)
+        del layer0
+
+    aux = None
+    if rank == 0 and world == 1 and not args.no_aux:
+        aux = run_aux_block(torch, H, L, args)
 
     if rank == 0:
+        lpl = len(model.groups[0]) if model.groups else 1
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -1052,7 +910,7 @@ def main():
                        "weights": total_weights, "sidecar_frac": SIDECAR_FRAC, "shard": "rows by out_features",
                        "launch": f"one per {lpl} layer(s) ({7 * lpl} matrices)", "graph": graph is not None,
                        "l2": "no flush: 5.3 GB read + 25.9 GB written per step >> 126 MB L2",
-                       "parallelism": f"row-shard x{world}"},
+                       "parallelism": f"row-shard x{world}", "driver": "hxq_b200.sharded.ShardedDecompress"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "kernel": "vq_fast_kernel (12-bit, fp32 out)",
@@ -1060,54 +918,35 @@ def main():
                          "launch_ms": my_launch_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "e2e_dropin": dropin,
+            "confidence": {"reported": "reference (hxq.c fp32 running sum), every matrix",
+                           "max_rel_exact_vs_reference": conf_rel},
             "clocks": clk,
             "gpu_launches": int(launches_per_step * args.steps),
         }
+        if world > 1:
+            line["per_rank_ms_per_step"] = [t / args.steps for t in per_rank_ms]
+            line["rank_spread"] = max(per_rank_ms) / min(per_rank_ms)
+        if aux is not None:
+            line["aux"] = aux
         print(json.dumps(line), flush=True)
 
     del graph
+    model.close()
     barrier()
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_e2e(torch, H, L, imgs, meta, arena, offs, arrs, conf, sumsq, args, world, rank, max_over_ranks,
-            sum_over_ranks):
+def run_e2e(torch, H, L, model, args, world, max_over_ranks, sum_over_ranks):
     """Weights live in pinned host memory; every step uploads every layer's
     images (copy stream) while the previous layer decompresses (compute
     stream), then reads the confidences back."""
-    align = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    layer_bytes = [sum(align(m["block"]) for m in lm) for lm in meta]
-    stage = [torch.empty(max(layer_bytes), dtype=torch.uint8, device="cuda") for _ in range(2)]
     copy_s, comp_s = torch.cuda.Stream(), torch.cuda.Stream()
-    up = [torch.cuda.Event() for _ in range(2)]
-    done = [torch.cuda.Event() for _ in range(2)]
-    host_conf = torch.empty(len(meta) * 7, dtype=torch.float32, pin_memory=True)
-    f32 = C.sizeof(C.c_float)
-
-    def one_step():
-        for layer in range(len(meta)):
-            s = layer % 2
-            copy_s.wait_event(done[s])
-            off = 0
-            for img, m in zip(imgs[layer], meta[layer]):
-                H.check(L.hxq_cuda_image_upload(img, stage[s].data_ptr() + off, C.c_void_p(copy_s.cuda_stream)),
-                        "upload")
-                off += align(m["block"])
-            up[s].record(copy_s)
-            comp_s.wait_event(up[s])
-            e = L.hxq_cuda_decompress_images(arrs[layer], 7, arena.data, offs[layer], 0,
-                                             sumsq.data_ptr() + 8 * 7 * layer, conf.data_ptr() + f32 * 7 * layer,
-                                             C.c_void_p(comp_s.cuda_stream))
-            if e != 0:
-                raise RuntimeError(f"decompress failed: {e}")
-            done[s].record(comp_s)
-        with torch.cuda.stream(comp_s):
-            host_conf.copy_(conf, non_blocking=True)
-
+    host_conf = torch.empty(model.n_matrices, dtype=torch.float32, pin_memory=True)
     steps = args.e2e_steps or max(3, min(args.steps, 10))
     for _ in range(2):
-        one_step()
+        model.stream_step(copy_s, comp_s, host_conf)
     comp_s.synchronize()
     torch.cuda.synchronize()
     if world > 1:
@@ -1116,18 +955,110 @@ def run_e2e(torch, H, L, imgs, meta, arena, offs, arrs, conf, sumsq, args, world
     e0.record(comp_s)
     copy_s.wait_event(e0)
     for _ in range(steps):
-        one_step()
+        model.stream_step(copy_s, comp_s, host_conf)
     e1.record(comp_s)
     e1.synchronize()
     H.check(L.hxq_cuda_stream_synchronize(C.c_void_p(comp_s.cuda_stream)), "e2e")
     ms = max_over_ranks(e0.elapsed_time(e1))
-    h2d = sum_over_ranks(float(sum(align(m["block"]) for lm in meta for m in lm)))
-    weights = sum_over_ranks(float(sum(m["numel"] for lm in meta for m in lm)))
+    h2d = sum_over_ranks(float(model.host_block_bytes()))
+    weights = sum_over_ranks(float(model.numel()))
     return {"value": weights * steps / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(len(meta) * 7 * 4 * world), "steps": steps,
+            "d2h_bytes_per_step": int(model.n_matrices * 4 * world), "steps": steps,
             "ms_per_step": ms / steps,
             "path": "hxq_cuda_image_upload (pinned host -> HBM) + hxq_cuda_decompress_images, "
                     "copy/compute overlapped by layer, confidences read back"}
+
+
+def run_dropin(torch, H, L, args):
+    """The reference's own entry point, unchanged: hxq_dequant(t, arena,
+    HXQ_BACKEND_CUDA, &result) once per matrix, all 224 of them in turn, into
+    one device arena (the shared buffer), each call synchronous with its
+    confidence written back.  The first pass builds each tensor's device image
+    (host preprocessing + upload) and is reported separately; timed passes
+    reuse the cached images, as a model that stays loaded does."""
+    nl = args.layers
+    tensors = []
+    for layer in range(nl):
+        for d in layer_matrices(torch, layer):
+            tensors.append((H.Tensor().load(d), d["out_f"] * d["in_f"]))
+            del d
+    arena = H.SharedBuffer()
+    H.check(L.hxq_cuda_arena_init(C.byref(arena), 0), "arena")
+    r = H.Result()
+
+    def one_pass():
+        for t, _ in tensors:
+            H.check(L.hxq_dequant(t.ref, C.byref(arena), H.HXQ_BACKEND_CUDA, C.byref(r)), "hxq_dequant")
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    one_pass()
+    first = time.perf_counter() - t0
+    one_pass()
+    steps = max(3, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_pass()
+    dt = (time.perf_counter() - t0) / steps
+    weights = sum(n for _, n in tensors)
+    L.hxq_shared_buffer_free(C.byref(arena))
+    for t, _ in tensors:
+        t.free()
+    return {"value": weights / dt, "unit": UNIT, "ms_per_step": dt * 1e3, "steps": steps,
+            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 20 * len(tensors),
+            "first_pass_s": first,
+            "path": "hxq_dequant(HXQ_BACKEND_CUDA) per matrix into a device arena (the reference API), "
+                    "synchronous, host wall clock; device images cached after the first pass, whose "
+                    "time (image build + upload) is first_pass_s"}
+
+
+def run_aux_block(torch, H, L, args) -> list:
+    """The other configurations, one short measurement each, beside the
+    headline: c1 12-bit 2048x2048 fp32, c2 scalar 4096x4096 fp32 and bf16
+    (fused decompress, HBM roofline), the c3 affine GEMV 4096x4096 at one
+    token, and one 7B layer of the fused dequant-matmul at one token (VQ and
+    affine, HBM roofline of the weight bytes)."""
+    from hxq_b200 import synth
+    from hxq_b200.sharded import ColumnSplitLayer
+    stream = torch.cuda.Stream()
+    a = argparse.Namespace(steps=max(2, min(args.steps, 10)), warmup=3)
+    out = []
+    d = synth.vq12(2048, 2048, synth.SEED_C1)
+    nnz = len(d["rows"])
+    r = _decompress_case(torch, H, L, "c1 12-bit 2048x2048", d, 0,
+                         2048 * 2048 * 3 // 4 + CB_BYTES + 12 * nnz + 4 * 2048 * 2048, stream, a)
+    out.append({"case": "c1 vq12 2048x2048 fp32", "us": r["us_per_launch"], "frac": r["roofline"]["frac"],
+                "gbs": r["roofline"]["achieved"], "weights_per_s": r["weights_per_s"]})
+    d = synth.scalar(4096, 4096, synth.SEED_C2)
+    nnz, n = len(d["rows"]), 4096 * 4096
+    for dt, ob in ((0, 4), (1, 2)):
+        r = _decompress_case(torch, H, L, "c2 scalar 4096x4096", d, dt, n + 1024 + 12 * nnz + ob * n, stream, a)
+        out.append({"case": f"c2 scalar 4096x4096 {'fp32' if dt == 0 else 'bf16'}", "us": r["us_per_launch"],
+                    "frac": r["roofline"]["frac"], "gbs": r["roofline"]["achieved"],
+                    "weights_per_s": r["weights_per_s"],
+                    "dequant_api_sync_us_median": r["dequant_api_sync_us_median"]})
+    r = _affine_case(torch, H, L, 1, stream, a)
+    out.append({"case": "c3 affine 4096x4096 g128 N=1", "us": r["us_per_call"], "frac": r["hbm_frac"],
+                "gbs": r["gbs"]})
+    hbm, _ = measured_peaks()
+    mats = []
+    for p, (name, O, I) in enumerate(synth.LLAMA7B_PROJ):
+        mats.append(dict(name=name, O=O, I=I, vq=gen_matrix(torch, synth.llama7b_seed(0, p), O, I),
+                         affine=dict(synth.affine(O, I, 128, synth.llama7b_seed(0, p) + 1000), gs=128)))
+    xh4, _ = synth.activations(1, 4096, synth.SEED_C5 + 1)
+    xh11, _ = synth.activations(1, 11008, synth.SEED_C5 + 2)
+    xs = {4096: torch.from_numpy(xh4.view(np.int16)).cuda(), 11008: torch.from_numpy(xh11.view(np.int16)).cuda()}
+    for fmt in ("vq12", "affine"):
+        layer = ColumnSplitLayer(mats, fmt, max_tokens=1, rank=0, world=1, torch=torch, lib=L)
+        n_launch = 10 * a.steps
+        ms = _graph_ms(torch, stream, lambda: layer.forward(xs, 1, stream), n_launch, a.warmup)
+        gbs = layer.weight_bytes / (ms * 1e-3) / 1e9
+        out.append({"case": f"c5 7B layer {fmt} N=1", "us": ms * 1e3, "frac": gbs / hbm, "gbs": gbs,
+                    "weight_bytes": layer.weight_bytes})
+        layer.close()
+    if L.hxq_cuda_affine_device_status() != 0:
+        raise RuntimeError("a tensor-core kernel reported a timeout")
+    return out
 
 
 if __name__ == "__main__":

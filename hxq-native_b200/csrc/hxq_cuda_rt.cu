@@ -899,9 +899,13 @@ hxq_error_t hxqi_cuda_decompress_to_host(hxq_tensor_t *t, float *h_out, float *l
         }
         stage = d.stage;
     }
-    // columns the 12-bit decoder leaves untouched must keep the caller's data
+    // Columns the 12-bit decoder leaves untouched (an odd pair count per
+    // row, hxq.c:290-294) must keep the caller's data, so only those images
+    // copy the buffer in first; every other kind writes each element.
+    hxq_cuda_image *img = nullptr;
+    if ((err = tensor_image(t, dev, &img)) != HXQ_OK) return err;
     cudaError_t ce = cudaSuccess;
-    if (n) ce = cudaMemcpy(stage, h_out, n * sizeof(float), cudaMemcpyHostToDevice);
+    if (n && img->kind == kKindVq12Any) ce = cudaMemcpy(stage, h_out, n * sizeof(float), cudaMemcpyHostToDevice);
     if (ce != cudaSuccess) { cudaGetLastError(); return map_cuda(ce); }
     float conf = 0.0f;
     if ((err = decompress_sync(t, stage, 0, &conf)) != HXQ_OK) return err;

@@ -1,11 +1,10 @@
 """Row sharding of HXQ tensors by out_features.
 
 Rank r of N owns rows [r*O/N, (r+1)*O/N) of every matrix.  Every output row
-is independent, so each rank decompresses its rows alone; the only shared
-quantity is a matrix's confidence, sqrt of the sum over ranks of the
-shards' sums of squared sidecar deltas.  These helpers cut a host-side
-tensor (the dict layout of hxq_b200.synth) to a row range with the same
-rules hxq_cuda_image_create applies to a loaded tensor.
+is independent, so each rank decompresses its rows alone (the driver that
+does so is hxq_b200.sharded).  These helpers cut a host-side tensor (the
+dict layout of hxq_b200.synth) to a row range with the same rules
+hxq_cuda_image_create applies to a loaded tensor.
 """
 from __future__ import annotations
 
@@ -46,12 +45,3 @@ def slice_rows(d: dict, r0: int, r1: int) -> dict:
         out["cols"] = cols[keep]
         out["vals"] = np.asarray(d["vals"], np.float32)[keep]
     return out
-
-
-def combine_confidence(sumsq_per_rank) -> float:
-    """Confidence of a sharded matrix from the shards' sums of squares,
-    added in rank order."""
-    total = 0.0
-    for s in sumsq_per_rank:
-        total += float(s)
-    return float(np.float32(np.sqrt(total)))

@@ -183,6 +183,27 @@ def test_dequant_cuda_backend_host_buffer(H, L, oracle, cuda):
     L.hxq_shared_buffer_free(C.byref(buf))
 
 
+@pytest.mark.parametrize("name", ["vq12_odd_6x10", "vq12_ragged_5x7", "vq12_64x256", "scalar_64x96"])
+def test_dequant_cuda_backend_host_buffer_golden(H, L, cuda, name):
+    """HXQ_BACKEND_CUDA into a host buffer: columns the 12-bit decoder never
+    writes (odd pair counts) keep the buffer's contents, as in hxq.c; other
+    shapes are written in full."""
+    g = load_golden(name)
+    t = _golden_tensor(H, g)
+    n = g["out_f"] * g["in_f"]
+    buf = H.SharedBuffer()
+    assert L.hxq_shared_buffer_init(C.byref(buf), n) == 0
+    host = np.ctypeslib.as_array(C.cast(buf.data, C.POINTER(C.c_float)), shape=(n,))
+    host[:] = g["out_init"]
+    r = H.Result()
+    assert L.hxq_dequant(t.ref, C.byref(buf), H.HXQ_BACKEND_CUDA, C.byref(r)) == g["expect_err"]
+    if g["expect_err"] == 0:
+        w = np.ctypeslib.as_array(C.cast(r.weights, C.POINTER(C.c_float)), shape=(n,)).copy()
+        assert np.array_equal(_bits(w), _bits(g["expect_w"]))
+        _check_conf(r.confidence, float(g["expect_conf"]))
+    L.hxq_shared_buffer_free(C.byref(buf))
+
+
 def _image(H, L, t, r0, r1):
     img = C.c_void_p()
     assert L.hxq_cuda_image_create(t.ref, r0, r1, C.byref(img)) == 0

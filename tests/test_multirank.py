@@ -1,10 +1,13 @@
 """Row sharding across ranks, on CPU with world-size-2 gloo process groups.
 
 Each rank cuts its rows out of a tensor (hxq_b200.shard.slice_rows, the
-cut bench.py applies before building the rank's images), decompresses them
-with the oracle, and the ranks gather weights and sums of squared sidecar
-deltas.  Rank 0 checks the reassembled matrix is bit-identical to the
-whole-tensor result and that the combined confidence equals the exact one.
+same rows hxq_b200.sharded.ShardedDecompress gives a rank), decompresses
+them with the oracle, and the ranks gather weights and sums of squared
+sidecar deltas.  Rank 0 checks the reassembled matrix is bit-identical to
+the whole-tensor result and that the combined confidence
+(sharded.combine_sumsq) equals the exact one.  The column-split matmul's
+output assembly (sharded.assemble_gathered) is checked the same way, and
+the driver's launch grouping and offsets on their own.
 """
 import os
 import socket
@@ -30,7 +33,8 @@ def _worker(rank: int, world: int, port: int, kind: str, q):
     from datetime import timedelta
 
     from hxq_b200 import synth
-    from hxq_b200.shard import combine_confidence, shard_rows, slice_rows
+    from hxq_b200.shard import shard_rows, slice_rows
+    from hxq_b200.sharded import combine_sumsq
     from oracle.oracle import Oracle
 
     dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
@@ -59,7 +63,7 @@ def _worker(rank: int, world: int, port: int, kind: str, q):
             whole = np.concatenate([p[3] for p in pieces])
             ok_w = np.array_equal(whole.view(np.uint32), w_full.view(np.uint32))
             exact = orc.l2_exact(d)
-            conf = combine_confidence(got_ss)
+            conf = combine_sumsq(got_ss)
             ok_c = abs(conf - exact) <= 1e-6 * exact
             q.put((ok_w, ok_c, conf, exact))
     finally:
@@ -108,6 +112,7 @@ def _matmul_worker(rank: int, world: int, port: int, q):
 
     from hxq_b200 import synth
     from hxq_b200.shard import shard_rows, slice_rows
+    from hxq_b200.sharded import assemble_gathered
     from oracle.oracle import Oracle
 
     dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}",
@@ -124,7 +129,7 @@ def _matmul_worker(rank: int, world: int, port: int, q):
         g = torch.empty((world * N, r1 - r0), dtype=torch.float32)
         dist.all_gather_into_tensor(g, y)
         if rank == 0:
-            whole = g.view(world, N, r1 - r0).permute(1, 0, 2).reshape(N, out_f).numpy()
+            whole = assemble_gathered(g, world, N, r1 - r0).numpy()
             e_full, w_full, _ = orc.decompress(d)
             ref = orc.dense_matmul(x, w_full.reshape(out_f, in_f))
             q.put((err == 0 and e_full == 0, bool(np.array_equal(whole.view(np.uint32), ref.view(np.uint32)))))
@@ -146,3 +151,28 @@ def test_column_split_matmul_gloo_world2():
     ok_err, ok_y = q.get(timeout=10)
     assert ok_err
     assert ok_y, "gathered output shards differ from the whole-matrix product"
+
+
+def test_launch_groups_and_offsets():
+    from hxq_b200.sharded import MAX_LAYERS_PER_LAUNCH, launch_groups, packed_offsets
+    for nl in (1, 5, 32):
+        for world in (1, 2, 3, 8, 16):
+            groups = launch_groups(nl, world)
+            flat = [layer for g in groups for layer in g]
+            assert flat == list(range(nl))
+            per = min(MAX_LAYERS_PER_LAUNCH, world, nl)
+            assert all(len(g) == per for g in groups[:-1]) and 1 <= len(groups[-1]) <= per
+    offs, total = packed_offsets([5, 0, 7])
+    assert offs == [0, 5, 5] and total == 12
+
+
+def test_assemble_gathered_numpy_and_torch():
+    import torch
+
+    from hxq_b200.sharded import assemble_gathered
+    world, N, rows = 3, 2, 4
+    full = np.arange(N * world * rows, dtype=np.float32).reshape(N, world * rows)
+    shards = [full[:, r * rows:(r + 1) * rows] for r in range(world)]
+    g = np.concatenate(shards, axis=0)                      # [world * N, rows]
+    assert np.array_equal(assemble_gathered(g, world, N, rows), full)
+    assert torch.equal(assemble_gathered(torch.from_numpy(g), world, N, rows), torch.from_numpy(full))

@@ -38,10 +38,12 @@ enum ImageKind : uint32_t {
 struct SideEntry { uint32_t x; uint32_t y; };
 
 // Work of the fast kernel is handed out dynamically in units of
-// kChunksPerWarp * kWarps chunks (chunk k*kWarps + w of a unit goes to warp
-// w); units never span two jobs.
+// cpw * kWarps chunks (chunk k*kWarps + w of a unit goes to warp w), cpw =
+// chunks per warp of the launch: 2, or 1 when a launch has too few units to
+// give every CTA several (single tensors); units never span two jobs.
 constexpr uint32_t kChunksPerWarp = 2;
-constexpr uint32_t kUnitChunks = kChunksPerWarp * kWarps;
+constexpr uint32_t kUnitChunks = kChunksPerWarp * kWarps;   // the largest unit
+__host__ __device__ constexpr uint32_t unit_chunks(uint32_t cpw) { return cpw * kWarps; }
 
 // One job of a launch of the fast kernel.
 struct VqJob {
@@ -66,7 +68,7 @@ struct VqLaunch {
     uint32_t  n_jobs;
     uint32_t  grid;
     uint32_t  total_units;
-    uint32_t  pad_;
+    uint32_t  cpw;               // chunks per warp and unit (1 or 2)
     double   *slots;             // one partial sum per unit (scratch)
     uint32_t *counters;          // per job: units finished (scratch, zero)
     uint32_t *work;              // [0] next unit to hand out, [1] CTAs done (zero)
@@ -105,6 +107,9 @@ cudaError_t configure_vq_kernels();
 cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
                            int check_k, cudaStream_t s);
 uint32_t    fast_grid(uint64_t total_chunks, int sms, uint32_t kind);
+// Chunks per warp for a launch of `chunks` chunks in total: 2, or 1 when
+// units of two would not give every resident CTA about four of them.
+uint32_t    fast_cpw(uint64_t chunks, int sms, uint32_t kind);
 
 // Generic kernels (any shape/alignment; one image per launch).
 struct GenericJob {

@@ -577,7 +577,12 @@ void destroy_image(hxq_cuda_image *img)
 
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
-uint32_t units_of(const hxq_cuda_image *im) { return (im->n_chunks + kUnitChunks - 1) / kUnitChunks; }
+// Work units of an image at `cpw` chunks per warp (the default: the largest
+// units, which the no-alloc limit counts).
+uint32_t units_of(const hxq_cuda_image *im, uint32_t cpw = kChunksPerWarp)
+{
+    return (im->n_chunks + unit_chunks(cpw) - 1) / unit_chunks(cpw);
+}
 
 hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
                               hxq_cuda_image *const *imgs, char *out_base,
@@ -588,6 +593,9 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
     if (which.empty()) return HXQ_OK;
     VqLaunch p;
     std::memset(&p, 0, sizeof(p));
+    uint64_t chunks = 0;
+    for (uint32_t i : which) chunks += imgs[i]->n_chunks;
+    const uint32_t cpw = fast_cpw(chunks, sms, imgs[which[0]]->kind);
     uint32_t units = 0;
     for (uint32_t n = 0; n < which.size(); ++n) {
         const uint32_t i = which[n];
@@ -602,7 +610,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
         J.n_chunks = im->n_chunks;
         J.k = im->k;
         J.unit_begin = units;
-        J.n_units = units_of(im);
+        J.n_units = units_of(im, cpw);
         J.sumsq = d_sumsq ? d_sumsq + i : nullptr;
         J.conf = d_conf ? d_conf + i : nullptr;
         J.ref_conf = im->ref_l2;
@@ -611,6 +619,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
     if (units > sc.n_slots) return HXQ_ERR_INVALID_ARG;
     p.n_jobs = (uint32_t)which.size();
     p.total_units = units;
+    p.cpw = cpw;
     p.grid = fast_grid(units, sms, imgs[which[0]]->kind);
     p.slots = sc.slots;
     p.counters = sc.counters;
@@ -630,7 +639,7 @@ hxq_error_t launch_images(hxq_cuda_image *const *imgs, uint32_t n, void *d_out,
     hxq_error_t err;
     uint32_t need = 0;
     for (uint32_t i = 0; i < n; ++i)
-        if (imgs[i] && (imgs[i]->kind == kKindScalar || imgs[i]->kind == kKindVq12)) need += units_of(imgs[i]);
+        if (imgs[i] && (imgs[i]->kind == kKindScalar || imgs[i]->kind == kKindVq12)) need += units_of(imgs[i], 1u);
     {
         std::lock_guard<std::mutex> lk(g_mu);
         if ((err = dev_ready(dev)) != HXQ_OK) return err;

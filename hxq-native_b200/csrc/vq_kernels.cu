@@ -82,24 +82,50 @@ template <uint32_t KIND, bool BF16>
 __device__ __forceinline__ void load_codebook(unsigned char *cb_area,
                                               const VqJob &J, uint32_t tid)
 {
+    // Every load of the table is in flight before a CTA waits for it, so it
+    // costs one memory round trip per codebook, not one per loop trip: the
+    // fp32 table is copied with asynchronous 16-byte copies (no registers;
+    // the caller's barrier follows the wait), the bf16 table is converted in
+    // batches small enough not to spill (the next chunk's index registers
+    // are live meanwhile).
     if (KIND == kKindVq12) {
-        const uint32_t n = J.k < 4096u ? J.k : 4096u;
-        const float2 *src = reinterpret_cast<const float2 *>(J.cb);
+        // k is 256 or 4096 entries (even): two float2 entries per 16 bytes
+        const uint32_t n2 = (J.k < 4096u ? J.k : 4096u) / 2u;
+        const uint4 *src = reinterpret_cast<const uint4 *>(J.cb);
         if (!BF16) {
-            float2 *dst = reinterpret_cast<float2 *>(cb_area);
-            for (uint32_t i = tid; i < n; i += kThreads) dst[i] = __ldg(src + i);
+            const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(cb_area));
+            for (uint32_t i = tid; i < n2; i += kThreads)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * i), "l"(src + i)
+                             : "memory");
+            asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
-            uint32_t *dst = reinterpret_cast<uint32_t *>(cb_area);
-            for (uint32_t i = tid; i < n; i += kThreads) {
-                float2 v = __ldg(src + i);
-                dst[i] = pack_bf16x2(v.x, v.y);
+#pragma unroll 1
+            for (uint32_t i0 = tid; i0 < n2; i0 += 2u * kThreads) {
+                uint4 v[2];
+#pragma unroll
+                for (uint32_t m = 0; m < 2u; ++m)
+                    if (i0 + m * kThreads < n2) v[m] = __ldg(src + i0 + m * kThreads);
+#pragma unroll
+                for (uint32_t m = 0; m < 2u; ++m) {
+                    const uint32_t i = i0 + m * kThreads;
+                    if (i < n2)
+                        reinterpret_cast<uint2 *>(cb_area)[i] =
+                            make_uint2(pack_bf16x2(__uint_as_float(v[m].x), __uint_as_float(v[m].y)),
+                                       pack_bf16x2(__uint_as_float(v[m].z), __uint_as_float(v[m].w)));
+                }
             }
         }
     } else {
         // lane-replicated scalar table: entry e for lane l at e*32 + l
         float *dst = reinterpret_cast<float *>(cb_area);
-        for (uint32_t i = tid; i < 256u * 32u; i += kThreads)
-            dst[i] = __ldg(J.cb + (i >> 5));
+#pragma unroll 1
+        for (uint32_t i0 = tid; i0 < 256u * 32u; i0 += 8u * kThreads) {
+            float v[8];
+#pragma unroll
+            for (uint32_t m = 0; m < 8u; ++m) v[m] = __ldg(J.cb + ((i0 + m * kThreads) >> 5));
+#pragma unroll
+            for (uint32_t m = 0; m < 8u; ++m) dst[i0 + m * kThreads] = v[m];
+        }
     }
 }
 
@@ -339,6 +365,7 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
     uint4 *stage = reinterpret_cast<uint4 *>(smem + kCbBytes + warp * stage_bytes<KIND>());
     constexpr uint32_t VPL = (KIND == kKindVq12) ? 3u : 4u;
     const uint32_t total = p.total_units;
+    const uint32_t cpw = p.cpw, unit_chunks = cpw * kWarps;   // chunk c*kWarps + w of a unit -> warp w
 
     // Units are handed out by an atomic counter, two ahead of use, so a
     // warp knows its next chunk (and prefetches it) while it works on the
@@ -356,7 +383,7 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
     bool have_cur = false;
     if (u < total) {
         j = job_of_unit(p, 0, u);
-        const uint32_t c = (u - p.job[j].unit_begin) * kUnitChunks + warp;
+        const uint32_t c = (u - p.job[j].unit_begin) * unit_chunks + warp;
         if (c < p.job[j].n_chunks) {
             prefetch_chunk<VPL>(p.job[j], c, lane, cur);
             prefetch_entry<VPL>(p.job[j], lane, cur);
@@ -372,16 +399,16 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
         const uint32_t un = s_unit[(it + 1u) % 3u];
         if (tid == 0) s_unit[(it + 2u) % 3u] = un < total ? atomicAdd(p.work, 1u) : total;
         const uint32_t jn = un < total ? job_of_unit(p, j, un) : j;
-        const uint32_t ubase = (u - p.job[j].unit_begin) * kUnitChunks + warp;
+        const uint32_t ubase = (u - p.job[j].unit_begin) * unit_chunks + warp;
         double acc = 0.0;
 #pragma unroll 1
-        for (uint32_t k = 0; k < kChunksPerWarp; ++k) {
+        for (uint32_t k = 0; k < cpw; ++k) {
             // stage this chunk first: its index registers are then free for the next one
             if (have_cur) stage_chunk<VPL>(cur, stage, lane);
             // this warp's next chunk: the unit's next one, else the first of unit un
             bool have_nxt = false;
             uint32_t jx = j;
-            if (k + 1u < kChunksPerWarp) {
+            if (k + 1u < cpw) {
                 const uint32_t c = ubase + (k + 1u) * kWarps;
                 if (c < p.job[j].n_chunks) {
                     prefetch_chunk<VPL>(p.job[j], c, lane, nxt);
@@ -389,7 +416,7 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
                 }
             } else if (un < total) {
                 jx = jn;
-                const uint32_t c = (un - p.job[jn].unit_begin) * kUnitChunks + warp;
+                const uint32_t c = (un - p.job[jn].unit_begin) * unit_chunks + warp;
                 if (c < p.job[jn].n_chunks) {
                     prefetch_chunk<VPL>(p.job[jn], c, lane, nxt);
                     have_nxt = true;
@@ -603,6 +630,12 @@ cudaError_t configure_vq_kernels()
     if ((e = configure_one<kKindVq12, true, true>()) != cudaSuccess) return e;
     if ((e = configure_one<kKindScalar, false, false>()) != cudaSuccess) return e;
     return configure_one<kKindScalar, true, false>();
+}
+
+uint32_t fast_cpw(uint64_t chunks, int sms, uint32_t kind)
+{
+    const uint64_t resident = (uint64_t)(sms > 0 ? sms : 148) * ctas_per_sm(kind);
+    return chunks >= 4u * resident * unit_chunks(kChunksPerWarp) ? kChunksPerWarp : 1u;
 }
 
 uint32_t fast_grid(uint64_t total_units, int sms, uint32_t kind)

@@ -198,12 +198,13 @@ int launch_tc_gemv(uint32_t n, const TcMatrix *m, uint32_t N, int sms, cudaStrea
 // Reads and clears the kernel's status word (nonzero: a wait ran out).
 uint32_t tc_gemv_status_take();
 
-// One image of a tensor-core VQ GEMV launch (vq_tc_gemv.cu): packed 12-bit
-// indices [rows][in_f * 3 / 4], the image's matmul tables (bf16x2 codebook,
-// first patch per row, patch columns, patch weight differences), bf16
-// activations [N][in_f].
+// One image of a tensor-core VQ GEMV launch (vq_tc_gemv.cu): the image's
+// GEMV index stream [rows][in_f / 2] (per pair the byte offset of its entry
+// in the two-copy shared codebook), the image's matmul tables (bf16x2
+// codebook, first patch per row, patch columns, patch weight differences),
+// bf16 activations [N][in_f].
 struct VqTcMatrix {
-    const uint8_t *idx;
+    const uint16_t *tx;
     const uint32_t *cbh, *rb, *e4;
     const float *ed;
     uint32_t n_patch;

@@ -20,6 +20,7 @@
 #include <map>
 #include <mutex>
 #include <numeric>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -63,9 +64,10 @@ struct hxq_cuda_image {
     // col | bf16(final weight) << 16, one per distinct sidecar position
     // and per patch bf16(final weight) - bf16(codebook value) in fp32
     bool      has_mm = false;
-    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0;
+    // and the tensor-core GEMV's own index stream (build_tc_stream)
+    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0, o_tx = 0;
     uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr;
-    uint16_t *d_kp = nullptr;
+    uint16_t *d_kp = nullptr, *d_tx = nullptr;
     float    *d_ed = nullptr;
     uint32_t  n_patch = 0;
 };
@@ -308,6 +310,7 @@ void bind_image(hxq_cuda_image *img, void *base)
         img->d_kp = reinterpret_cast<uint16_t *>(b + img->o_kp);
         img->d_e4 = reinterpret_cast<uint32_t *>(b + img->o_e4);
         img->d_ed = reinterpret_cast<float *>(b + img->o_ed);
+        img->d_tx = reinterpret_cast<uint16_t *>(b + img->o_tx);
     }
 }
 
@@ -373,6 +376,139 @@ bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows
         }
     }
     return true;
+}
+
+// Index stream of the tensor-core GEMV (vq_tc_gemv.cu).  Its shared
+// codebook holds the 4096 bf16 pairs twice: copy 0 has entry c at word c
+// (bank c & 31), copy 1 at word 4096 + (c ^ ((c >> 5) & 31)), whose bank
+// is independent of c's.  Every pair of the matrix is stored as the 16-bit
+// byte offset of the copy its lane reads: 4c, or 16384 + 4 * perm(c).  A
+// gather instruction of the GEMV is one of a lane's sixteen per 64-weight
+// chunk, and the lanes that make it up are known from the kernel's layout
+// (lane (g, t) of warp w, chunk u, word jj, half h, row set s reads pair
+// 512 st + 64 w + 16 t + 8 u + 2 jj + h of row 16 rb + g + 8 s); per
+// instruction the copies are chosen here so that the fullest bank holds as
+// few distinct words as possible (the instruction's shared-memory
+// wavefronts): about 2 for 32 random entries, against 3.5 with one copy.
+uint32_t tc_perm(uint32_t c) { return c ^ ((c >> 5) & 31u); }
+
+uint32_t idx12_at(const uint8_t *row, uint32_t pair)
+{
+    const uint8_t *b = row + (size_t)(pair >> 1) * 3u;
+    return (pair & 1u) ? (((uint32_t)(b[1] & 15u) << 8) | b[2]) : (((uint32_t)b[0] << 4) | (b[1] >> 4));
+}
+
+// Copies for the 32 lanes of one gather instruction (c[l] entry of lane l;
+// live[l] false for a lane past the matrix, which reads word 0 of copy 0).
+void choose_copies(const uint32_t (&c)[32], const bool (&live)[32], uint8_t (&copy)[32])
+{
+    uint16_t words[32][32];   // distinct words per bank
+    uint8_t refs[32][32];     // lanes per (bank, word)
+    uint8_t load[32] = {0};
+    auto find = [&](uint32_t b, uint16_t w) -> int {
+        for (uint32_t i = 0; i < load[b]; ++i)
+            if (words[b][i] == w) return (int)i;
+        return -1;
+    };
+    auto add = [&](uint32_t b, uint16_t w) {
+        const int i = find(b, w);
+        if (i >= 0) { ++refs[b][i]; return; }
+        words[b][load[b]] = w;
+        refs[b][load[b]] = 1;
+        ++load[b];
+    };
+    auto remove = [&](uint32_t b, uint16_t w) {
+        const int i = find(b, w);
+        if (--refs[b][i] == 0) {
+            --load[b];
+            words[b][i] = words[b][load[b]];
+            refs[b][i] = refs[b][load[b]];
+        }
+    };
+    auto opt = [&](uint32_t l, uint32_t k, uint32_t &b, uint16_t &w) {
+        if (k == 0) { w = (uint16_t)c[l]; b = c[l] & 31u; }
+        else { const uint32_t q = tc_perm(c[l]); w = (uint16_t)(4096u + q); b = q & 31u; }
+    };
+    auto cost = [&](uint32_t b, uint16_t w) { return find(b, w) >= 0 ? load[b] : load[b] + 1u; };
+    for (uint32_t l = 0; l < 32; ++l) {
+        copy[l] = 0;
+        if (!live[l]) { add(0, 0); continue; }
+        uint32_t b0, b1;
+        uint16_t w0, w1;
+        opt(l, 0, b0, w0);
+        opt(l, 1, b1, w1);
+        copy[l] = cost(b1, w1) < cost(b0, w0) ? 1 : 0;
+        if (copy[l]) add(b1, w1); else add(b0, w0);
+    }
+    // move lanes out of the fullest banks while that lowers them
+    for (int pass = 0; pass < 4; ++pass) {
+        uint32_t L = 0;
+        for (uint32_t b = 0; b < 32; ++b) L = load[b] > L ? load[b] : L;
+        bool moved = false;
+        for (uint32_t l = 0; l < 32; ++l) {
+            if (!live[l]) continue;
+            uint32_t bc, ba;
+            uint16_t wc, wa;
+            opt(l, copy[l], bc, wc);
+            opt(l, copy[l] ^ 1u, ba, wa);
+            if (load[bc] != L || refs[bc][find(bc, wc)] != 1) continue;
+            if (cost(ba, wa) < L) {
+                remove(bc, wc);
+                add(ba, wa);
+                copy[l] ^= 1u;
+                moved = true;
+            }
+        }
+        if (!moved) break;
+    }
+}
+
+// The stream for rows [0, rows) of a 12-bit image (in_f % 128 == 0): one
+// uint16 per pair, rows of in_f / 2 pairs.
+void build_tc_stream(const uint8_t *idx_rows, uint32_t rows, uint32_t in_f, std::vector<uint16_t> &tx)
+{
+    const uint32_t pairs = in_f / 2u, n_rb = (rows + 15u) / 16u, n_st = (in_f + 1023u) / 1024u;
+    const size_t row_bytes = (size_t)(in_f / 4u) * 3u;
+    tx.assign((size_t)rows * pairs, 0u);
+    auto work = [&](uint32_t rb_lo, uint32_t rb_hi) {
+        uint32_t c[32];
+        bool live[32];
+        uint8_t copy[32];
+        for (uint32_t rb = rb_lo; rb < rb_hi; ++rb)
+            for (uint32_t st = 0; st < n_st; ++st)
+                for (uint32_t w = 0; w < 8u; ++w) {
+                    const uint32_t p0 = st * 512u + w * 64u;
+                    if (p0 >= pairs) continue;   // the warp's window is past the row (kernel skips it)
+                    for (uint32_t u = 0; u < 2u; ++u)
+                        for (uint32_t jj = 0; jj < 4u; ++jj)
+                            for (uint32_t h = 0; h < 2u; ++h)
+                                for (uint32_t s = 0; s < 2u; ++s) {
+                                    for (uint32_t l = 0; l < 32u; ++l) {
+                                        const uint32_t g = l >> 2, t = l & 3u;
+                                        const uint32_t row = rb * 16u + g + 8u * s;
+                                        const uint32_t pr = p0 + 16u * t + 8u * u + 2u * jj + h;
+                                        live[l] = row < rows;
+                                        c[l] = live[l] ? idx12_at(idx_rows + (size_t)row * row_bytes, pr) : 0u;
+                                    }
+                                    choose_copies(c, live, copy);
+                                    for (uint32_t l = 0; l < 32u; ++l) {
+                                        if (!live[l]) continue;
+                                        const uint32_t g = l >> 2, t = l & 3u;
+                                        const uint32_t row = rb * 16u + g + 8u * s;
+                                        const uint32_t pr = p0 + 16u * t + 8u * u + 2u * jj + h;
+                                        tx[(size_t)row * pairs + pr] =
+                                            (uint16_t)(copy[l] ? 16384u + 4u * tc_perm(c[l]) : 4u * c[l]);
+                                    }
+                                }
+                }
+    };
+    unsigned nt = std::thread::hardware_concurrency();
+    nt = nt == 0 ? 1u : std::min(nt, 16u);
+    if ((uint64_t)rows * in_f < (1u << 22) || nt == 1) { work(0, n_rb); return; }
+    std::vector<std::thread> th;
+    for (unsigned i = 0; i < nt; ++i)
+        th.emplace_back(work, (uint32_t)((uint64_t)n_rb * i / nt), (uint32_t)((uint64_t)n_rb * (i + 1) / nt));
+    for (auto &x : th) x.join();
 }
 
 hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev,
@@ -477,12 +613,13 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     img->n_ent = (uint32_t)dev_ents.size();
 
     std::vector<uint32_t> mm_cbh, mm_rb, mm_e4;
-    std::vector<uint16_t> mm_kp;
+    std::vector<uint16_t> mm_kp, mm_tx;
     std::vector<float> mm_ed;
     if (matmul && img->kind == kKindVq12 && !img->check_k && img->k == 4096u && img->in_f % 128u == 0u &&
         img->in_f <= 65536u)
         img->has_mm = build_patches(t, t->indices_raw + idx_off, img->rows, img->in_f, ents, mm_cbh, mm_rb,
                                     mm_kp, mm_e4, mm_ed);
+    if (img->has_mm) build_tc_stream(t->indices_raw + idx_off, img->rows, img->in_f, mm_tx);
     img->n_patch = (uint32_t)mm_e4.size();
 
     // one block: idx | cb | scales | offsets | chunk_ptr | entries
@@ -505,6 +642,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         img->o_kp = off;   off = align256(off + mm_kp.size() * 2);
         img->o_e4 = off;   off = align256(off + (mm_e4.size() + 4) * 4);   // + speculative-read slack
         img->o_ed = off;   off = align256(off + std::max<size_t>(mm_ed.size(), 1) * 4);
+        img->o_tx = off;   off = align256(off + std::max<size_t>(mm_tx.size(), 8) * 2);
     }
     img->block_bytes = off;
     img->has_cb = cb_floats > 0;
@@ -535,6 +673,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         std::memcpy(hb + img->o_kp, mm_kp.data(), mm_kp.size() * 2);
         if (!mm_e4.empty()) std::memcpy(hb + img->o_e4, mm_e4.data(), mm_e4.size() * 4);
         if (!mm_ed.empty()) std::memcpy(hb + img->o_ed, mm_ed.data(), mm_ed.size() * 4);
+        if (!mm_tx.empty()) std::memcpy(hb + img->o_tx, mm_tx.data(), mm_tx.size() * 2);
     }
 
     if (streamed) {
@@ -1093,7 +1232,7 @@ namespace {
 // (1 and 2 need the image's matmul tables).
 hxq::VqTcMatrix tc_matrix(const hxq_cuda_image_t *img, const uint16_t *x, const hxq::OutPtrs &out, uint32_t ldy)
 {
-    return hxq::VqTcMatrix{img->d_idx, img->d_cbh, img->d_rb, img->d_e4, img->d_ed, img->n_patch, x, out, ldy,
+    return hxq::VqTcMatrix{img->d_tx, img->d_cbh, img->d_rb, img->d_e4, img->d_ed, img->n_patch, x, out, ldy,
                            img->rows, img->in_f};
 }
 

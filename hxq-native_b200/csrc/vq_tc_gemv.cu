@@ -6,22 +6,27 @@
 // pair of consecutive weights, and its bf16x2 codebook entry is exactly one
 // A-fragment register of an m16n8k16 product (two consecutive K values of
 // one row).  So a lane's A fragment is one 4-byte gather per register from a
-// 16 KB shared codebook, no conversion; the activations are bf16 already.
-//   * Index stream: a producer thread copies each 16-row block of packed
-//     indices, 1024 weights of K per stage (768 B per row), as six TMA
-//     tensor copies of 128 bytes x 16 rows (128-byte swizzle: the 16-byte
-//     units of row r XOR r & 7); bytes past a row and rows past the image
-//     read as zero.
+// shared codebook, no conversion; the activations are bf16 already.
+//   * Codebook: the 4096 pairs twice (32 KB, static shared): copy 0 holds
+//     entry c at word c, copy 1 at word 4096 + (c ^ ((c >> 5) & 31)), a bank
+//     independent of c's.  A warp-wide gather of 32 random entries from one
+//     copy needs about 3.5 shared-memory wavefronts (the fullest of 32 banks);
+//     with each lane's copy chosen when the image is built, about 2.
+//   * Index stream: the image's GEMV stream holds, per pair, the byte offset
+//     of the entry in the copy its lane reads (16 bits), in the matrix's
+//     row-major pair order.  A producer thread copies each 16-row block, 1024
+//     weights of K per stage (1 KB per row), as eight TMA tensor copies of
+//     128 bytes x 16 rows (128-byte swizzle: the 16-byte units of row r XOR
+//     r & 7); bytes past a row and rows past the image read as zero.
 //   * Fragments: a consumer warp owns a 128-weight window of K of every
-//     stage (two 64-weight chunks).  Lane (g, t) takes the window's pairs
-//     [16t, 16t + 16) of rows g and g + 8: 24 contiguous index bytes per row
-//     (three 64-bit loads through the swizzle), pairs [16t + 8u, +8) in
-//     chunk u.  Product jj of chunk u takes index triple jj of the lane's
-//     12 bytes: its even pair is the A register of MMA column pair t, its
-//     odd pair that of column pair t + 4 (the K permutation, shared with the
-//     activations).  A triple (b0, b1, b2) is turned into both codebook byte
-//     offsets by one byte permute and two shift-and-mask steps; the
-//     codebook is a static shared array, so its base is the loads' immediate.
+//     stage (two 64-weight chunks), one TMA box.  Lane (g, t) takes the
+//     window's pairs [16t, 16t + 16) of rows g and g + 8: in chunk u pairs
+//     [16t + 8u, +8), one 128-bit load per row (units 2t + u; rows g and
+//     g ^ 1 of a quarter-warp have swizzle phases of different parity, so the
+//     loads are free of bank conflicts).  Word jj of the load holds pairs 2jj
+//     (low half: the A register of MMA column pair t) and 2jj + 1 (high half:
+//     column pair t + 4) -- the K permutation, shared with the activations;
+//     each half is directly the gather's byte offset.
 //   * Activations: raw bf16 staged once per matrix in fragment order (within
 //     each 128-weight window: chunk, then lane t, then its 16 weights; rows
 //     of in_f + 8 so that the 8 tokens' 16-byte loads fall in distinct
@@ -63,18 +68,18 @@ constexpr uint32_t kChunk = 64;                       // weights of K per chunk
 constexpr uint32_t kWarpK = 2u * kChunk;              // per warp per stage
 constexpr uint32_t kKC = kWarpK * kConsumers;         // 1024 per stage
 constexpr uint32_t kRows = 16;
-constexpr uint32_t kRowStageBytes = kKC / 4u * 3u;    // 768 B of indices per row per stage
-constexpr uint32_t kStageBytes = kRows * kRowStageBytes;   // 12 KB
+constexpr uint32_t kRowStageBytes = kKC / 2u * 2u;    // 1 KB of pair offsets per row per stage
+constexpr uint32_t kStageBytes = kRows * kRowStageBytes;   // 16 KB
 constexpr uint32_t kMaxStages = 8;
-constexpr uint32_t kCbBytes = 4096u * 4u;              // bf16x2 codebook
+constexpr uint32_t kCbBytes = 2u * 4096u * 4u;         // two copies of the bf16x2 codebook
 constexpr uint32_t kXPad = 8;                          // activation row pitch: in_f + 8
 constexpr uint32_t kCsStride = 16;                     // sidecar sums per row (tokens)
 
 __device__ uint32_t g_vqtc_err;
-__shared__ __align__(16) uint32_t s_cb[4096];          // the matrix's bf16x2 codebook
+__shared__ __align__(16) uint32_t s_cb[2u * 4096u];    // the matrix's bf16x2 codebook, two copies
 
 struct Job {
-    CUtensorMap map;            // indices [rows][row_bytes], boxes of 128 B x 16 rows
+    CUtensorMap map;            // pair offsets [rows][in_f bytes], boxes of 128 B x 16 rows
     const uint32_t *cbh;        // bf16x2 pairs [4096]
     const uint16_t *x;          // bf16 [N][in_f]
     const uint32_t *prow;       // sidecar: first entry of each row (null: none)
@@ -101,7 +106,7 @@ constexpr uint32_t kAlignSlack = 1024;
 __host__ __device__ inline Layout layout(uint32_t S, uint32_t N, uint32_t in_f)
 {
     Layout L;
-    uint32_t o = S * kStageBytes;                 // 12 KB stages: 1024-byte aligned
+    uint32_t o = S * kStageBytes;                 // 16 KB stages: 1024-byte aligned
     L.bars = o;  o += 2u * kMaxStages * 8u;
     L.abort = o; o += 16u;
     o = (o + 127u) & ~127u;
@@ -134,41 +139,26 @@ __device__ __forceinline__ uint32_t stage_off(uint32_t r, uint32_t o)
     return (o >> 7) * 2048u + r * 128u + ((((b >> 4) ^ (r & 7u)) << 4) | (b & 15u));
 }
 
-// Codebook entry at byte offset o (a multiple of 4 below 16 KB).
+// Codebook entry at byte offset o (a multiple of 4 below 32 KB).
 __device__ __forceinline__ uint32_t cb_at(uint32_t o)
 {
     return *reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint8_t *>(s_cb) + o);
 }
 
-// Triple (b0, b1, b2) -> b1 | b0 << 8 | b2 << 16 | b1 << 24: bits 2..13 of
-// v >> 2 are 4 x the even index (b0 << 4 | b1 >> 4), bits 2..13 of v >> 14
-// are 4 x the odd index ((b1 & 15) << 8 | b2).
-__device__ __forceinline__ uint32_t even_off(uint32_t v) { return (v >> 2) & 0x3FFCu; }
-__device__ __forceinline__ uint32_t odd_off(uint32_t v) { return (v >> 14) & 0x3FFCu; }
-
-// One 64-weight chunk: w[0..2] / h[0..2] are the lane's 12 index bytes of
-// rows g / g + 8 (four triples), xb its 32 activation bytes per token tile
+// One 64-weight chunk: w[0..3] / h[0..3] are the lane's 8 pair offsets of
+// rows g / g + 8 (two per word), xb its 32 activation bytes per token tile
 // (four 8-byte B fragments); two accumulation chains.
 template <int NT>
 __device__ __forceinline__ void chunk(const uint32_t *w, const uint32_t *h, const uint4 (&xb)[NT][2],
                                       float (&d)[NT][4], float (&e)[NT][4])
 {
-    uint32_t vg[4], vh[4];
-    vg[0] = __byte_perm(w[0], 0u, 0x1201u);
-    vg[1] = __byte_perm(w[0], w[1], 0x4534u);
-    vg[2] = __byte_perm(w[1], w[2], 0x3423u);
-    vg[3] = __byte_perm(w[2], 0u, 0x2312u);
-    vh[0] = __byte_perm(h[0], 0u, 0x1201u);
-    vh[1] = __byte_perm(h[0], h[1], 0x4534u);
-    vh[2] = __byte_perm(h[1], h[2], 0x3423u);
-    vh[3] = __byte_perm(h[2], 0u, 0x2312u);
     uint32_t ag[8], ah[8];
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-        ag[2 * jj] = cb_at(even_off(vg[jj]));
-        ag[2 * jj + 1] = cb_at(odd_off(vg[jj]));
-        ah[2 * jj] = cb_at(even_off(vh[jj]));
-        ah[2 * jj + 1] = cb_at(odd_off(vh[jj]));
+        ag[2 * jj] = cb_at(w[jj] & 0xFFFFu);
+        ag[2 * jj + 1] = cb_at(w[jj] >> 16);
+        ah[2 * jj] = cb_at(h[jj] & 0xFFFFu);
+        ah[2 * jj + 1] = cb_at(h[jj] >> 16);
     }
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
@@ -299,11 +289,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t ct = threadIdx.x;
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    // MMA rows g and g + 8 are rows gr and gr + 8 of the block: the four
-    // rows of a half-warp then have box lines with swizzle phases 0, 2, 4, 6
-    // (or 1, 3, 5, 7), and the 64-bit index loads are free of bank conflicts
-    const uint32_t gr = 2u * (g & 3u) + (g >> 2);
+    const uint32_t g = lane >> 2, t = lane & 3u;   // MMA rows g and g + 8 are block rows g and g + 8
     const uint32_t N = J.N;
     constexpr uint32_t NTOK = 8u * NT;
     const uint32_t stage_a = smem_u32(smem), xh_a = smem_u32(smem + L.xh);
@@ -322,11 +308,20 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         const Job &b = J.job[j];
         const uint32_t in_f = b.in_f;
         if (j != cur) {
-            // the matrix's codebook and activations (raw bf16 in fragment order,
-            // rows of in_f + 8)
+            // the matrix's codebook, both copies (four entries per 16-byte
+            // load: copy 0 in place, copy 1 at its permuted words), and its
+            // activations (raw bf16 in fragment order, rows of in_f + 8)
             const uint4 *cs = reinterpret_cast<const uint4 *>(b.cbh);
             uint4 *cd = reinterpret_cast<uint4 *>(s_cb);
-            for (uint32_t i = ct; i < kCbBytes / 16u; i += kConsumers * 32u) cd[i] = __ldg(cs + i);
+            for (uint32_t i = ct; i < 4096u / 4u; i += kConsumers * 32u) {
+                const uint4 v = __ldg(cs + i);
+                cd[i] = v;
+                const uint32_t c0 = 4u * i, r = (c0 >> 5) & 31u;   // the same r for the four entries
+                s_cb[4096u + (c0 ^ r)] = v.x;
+                s_cb[4096u + ((c0 + 1u) ^ r)] = v.y;
+                s_cb[4096u + ((c0 + 2u) ^ r)] = v.z;
+                s_cb[4096u + ((c0 + 3u) ^ r)] = v.w;
+            }
             const uint32_t per_tok = in_f / 8u;
             uint16_t *xh = reinterpret_cast<uint16_t *>(smem + L.xh);
             for (uint32_t p = ct; p < N * per_tok; p += kConsumers * 32u) {
@@ -358,10 +353,11 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
         }
         uint32_t pn[3] = {0u, 0u, 0u};
         if (rb + 1u < rb1) side_rows(J, rb + 1u, warp, pn);
-        // this lane's index bytes: 8-byte piece i of its 24 of row gr (row gr + 8: 1 KB on)
-        uint32_t wo[3];
+        // this lane's pair offsets of chunk u: unit 2t + u of row g's line in
+        // box `warp` (row g + 8: eight lines, 1 KB, on)
+        uint32_t wo[2];
 #pragma unroll
-        for (int i = 0; i < 3; ++i) wo[i] = stage_off(gr, warp * 96u + t * 24u + (uint32_t)i * 8u);
+        for (int u = 0; u < 2; ++u) wo[u] = stage_off(g, warp * 128u + t * 32u + (uint32_t)u * 16u);
         uint32_t xa0[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
@@ -379,15 +375,15 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
             if (ok && kb < in_f) {
                 // in_f is a multiple of 128: both chunks of the warp are inside K
                 const uint32_t sa = stage_a + slot * kStageBytes;
-                uint32_t wg[6], wh[6];
+                uint32_t wg[8], wh[8];
 #pragma unroll
-                for (int i = 0; i < 3; ++i) {
-                    const uint2 a = lds64(sa + wo[i]), c = lds64(sa + wo[i] + 1024u);
-                    wg[2 * i] = a.x; wg[2 * i + 1] = a.y;
-                    wh[2 * i] = c.x; wh[2 * i + 1] = c.y;
+                for (int u = 0; u < 2; ++u) {
+                    const uint4 a = lds128(sa + wo[u]), c = lds128(sa + wo[u] + 1024u);
+                    wg[4 * u] = a.x; wg[4 * u + 1] = a.y; wg[4 * u + 2] = a.z; wg[4 * u + 3] = a.w;
+                    wh[4 * u] = c.x; wh[4 * u + 1] = c.y; wh[4 * u + 2] = c.z; wh[4 * u + 3] = c.w;
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(empty + slot);   // the stage's indices are in registers
+                if (lane == 0) mbar_arrive(empty + slot);   // the stage's offsets are in registers
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     uint4 xb[NT][2];
@@ -397,7 +393,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                         xb[tt][0] = lds128(xa);
                         xb[tt][1] = lds128(xa + 16u);
                     }
-                    chunk<NT>(wg + 3 * u, wh + 3 * u, xb, d, e);
+                    chunk<NT>(wg + 4 * u, wh + 4 * u, xb, d, e);
                 }
             } else {
                 __syncwarp();
@@ -423,10 +419,10 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
             const uint32_t n0 = (uint32_t)tt * 8u + 2u * t;
-            rd[(warp * kRows + gr) * NTOK + n0] = d[tt][0] + e[tt][0];
-            rd[(warp * kRows + gr) * NTOK + n0 + 1u] = d[tt][1] + e[tt][1];
-            rd[(warp * kRows + gr + 8u) * NTOK + n0] = d[tt][2] + e[tt][2];
-            rd[(warp * kRows + gr + 8u) * NTOK + n0 + 1u] = d[tt][3] + e[tt][3];
+            rd[(warp * kRows + g) * NTOK + n0] = d[tt][0] + e[tt][0];
+            rd[(warp * kRows + g) * NTOK + n0 + 1u] = d[tt][1] + e[tt][1];
+            rd[(warp * kRows + g + 8u) * NTOK + n0] = d[tt][2] + e[tt][2];
+            rd[(warp * kRows + g + 8u) * NTOK + n0 + 1u] = d[tt][3] + e[tt][3];
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         for (uint32_t idx = ct; idx < kRows * NTOK; idx += kConsumers * 32u) {
@@ -496,10 +492,10 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     for (uint32_t i = 0; i < n; ++i) {
         const VqTcMatrix &a = m[i];
         if (!vq_tc_fits(a.x, N, a.in_f) || a.out.n == 0 || a.out.n > HXQ_CUDA_MAX_PEERS || a.ldy < a.rows) return 1;
-        const uint64_t row_bytes = (uint64_t)a.in_f / 4u * 3u;
+        const uint64_t row_bytes = (uint64_t)a.in_f;   // one 16-bit offset per pair
         Job &b = J.job[i];
         std::memset(&b.map, 0, sizeof(b.map));
-        if (!pipe::encode_bytes_2d(&b.map, a.idx, row_bytes, a.rows, kRows)) return 1;
+        if (!a.tx || !pipe::encode_bytes_2d(&b.map, a.tx, row_bytes, a.rows, kRows)) return 1;
         b.cbh = a.cbh; b.x = a.x; b.out = a.out; b.ldy = a.ldy; b.rows = a.rows; b.in_f = a.in_f;
         if (a.n_patch) {
             if (!a.rb || !a.e4 || !a.ed) return 1;

@@ -83,21 +83,30 @@ constexpr uint32_t kErrTimeout = 2u;
 
 __device__ uint32_t g_gemm_err;          // device status word of this kernel
 
-// Ring depth: 3 stages for the large tiles, 4 for the small; the VQ tile of
-// 128 tokens keeps 2 so that two CTAs (with their 16 KB codebooks) share an
+// Activation ring depth: 3 stages for the affine tile of 256 tokens, 4 for
+// the small tiles; the tiles of 128 tokens keep 2 so that two CTAs share an
 // SM, and the VQ tile of 256 keeps 2 to make room for its A buffers.
 __host__ __device__ constexpr uint32_t stages_for(uint32_t bn, bool vq)
 {
-    return bn >= 256 ? (vq ? 2u : 3u) : bn == 128 ? (vq ? 2u : 3u) : 4u;
+    return bn >= 256 ? (vq ? 2u : 3u) : bn == 128 ? 2u : 4u;
 }
 __host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
 constexpr uint32_t kCodebookBytes = 4096u * 4u;   // VQ: 4096 bf16 pairs
-// ring | (A tiles in shared memory) A[2] | barriers (full[S], empty[S],
-// a_full[2], a_empty[2], d_full) | tmem addr | abort | (VQ) codebook
+// Weight ring: each K step's weight bytes of the CTA's 128 rows arrive by
+// TMA -- affine codes 128 x 128 B (128-byte swizzle), VQ index bytes
+// 128 x 96 B -- instead of one 16-byte load per thread from 32 rows' lines
+// per warp instruction.  Two stages; one for the VQ tile of 256 tokens,
+// whose A buffers leave room for no more (its converters take a stage's
+// bytes into registers at once, so the next copy overlaps the conversion).
+__host__ __device__ constexpr uint32_t wstage_bytes(bool vq) { return kBM * (vq ? 96u : 128u); }
+__host__ __device__ constexpr uint32_t wstages_for(uint32_t bn, bool vq) { return (vq && bn >= 256) ? 1u : 2u; }
+// ring | (A tiles in shared memory) A[2] | weight ring | barriers (full[S],
+// empty[S], a_full[2], a_empty[2], d_full, w_full[W], w_empty[W]) | tmem
+// addr | abort | (VQ) codebook
 __host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn, bool vq)
 {
     return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn) + (smem_a(bn, vq) ? 2u * kABytes : 0u) +
-           256u + (vq ? kCodebookBytes : 0u);
+           wstages_for(bn, vq) * wstage_bytes(vq) + 256u + (vq ? kCodebookBytes : 0u);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -285,7 +294,8 @@ __device__ __forceinline__ void patch_pair(uint32_t (&v)[32], uint32_t local, ui
 
 template <uint32_t BN, bool VQ>
 __global__ void __launch_bounds__(kThreads, BN <= 128 ? 2 : 1)
-dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ Params p)
+dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                    const __grid_constant__ Params p)
 {
     constexpr uint32_t S = stages_for(BN, VQ);
     constexpr uint32_t SB = stage_bytes(BN);
@@ -293,18 +303,23 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     constexpr uint32_t kTmemA = tmem_a_col(BN);
     constexpr uint32_t kTmemCols = tmem_cols(BN, VQ);
     constexpr uint32_t kAOff = SA ? 2u * kABytes : 0u;   // A tiles after the ring
+    constexpr uint32_t W = wstages_for(BN, VQ);
+    constexpr uint32_t WB = wstage_bytes(VQ);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *ring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
     unsigned char *abuf = ring + S * SB;                  // SA: A[2], 1024-byte aligned
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + S * SB + kAOff);
+    unsigned char *wring = ring + S * SB + kAOff;         // weight ring, 1024-byte aligned
+    uint64_t *full = reinterpret_cast<uint64_t *>(wring + W * WB);
     uint64_t *empty = full + S;
     uint64_t *a_full = empty + S;
     uint64_t *a_empty = a_full + 2;
     uint64_t *d_full = a_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(d_full + 1);
+    uint64_t *w_full = d_full + 1;
+    uint64_t *w_empty = w_full + W;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + W);
     volatile uint32_t *abort_flag = tmem_slot + 1;
-    uint32_t *cbh = reinterpret_cast<uint32_t *>(ring + S * SB + kAOff + 256u);   // VQ: bf16 pairs
+    uint32_t *cbh = reinterpret_cast<uint32_t *>(wring + W * WB + 256u);   // VQ: bf16 pairs
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t o0 = blockIdx.x * kBM;
@@ -325,6 +340,10 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             mbar_init(a_empty + b, 1);
         }
         mbar_init(d_full, 1);
+        for (uint32_t s = 0; s < W; ++s) {
+            mbar_init(w_full + s, 1);
+            mbar_init(w_empty + s, kConvWarps);
+        }
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -339,10 +358,27 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = *tmem_slot;
 
-    uint32_t issued = 0;  // producer: loads issued
+    uint32_t issued = 0, w_issued = 0;  // producer: activation and weight loads issued
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            for (uint32_t kt = 0; kt < KT; ++kt) {
+            // a step's weight tile goes first (the converters need it before
+            // the MMA needs the step's activations); the weight ring runs up
+            // to W steps ahead of the converters, the activation ring S ahead
+            // of the MMA
+            uint32_t kw = 0;
+            bool ok = true;
+            auto issue_w = [&](uint32_t k) {
+                const uint32_t sw = k % W;
+                if (k >= W && !mbar_wait(w_empty + sw, ((k / W) - 1u) & 1u, abort_flag)) return false;
+                mbar_expect_tx(w_full + sw, WB);
+                const uint32_t xw = (kt_lo + k) * (VQ ? 96u : kBK);
+                tma_load_2d(wring + sw * WB, &wmap, w_full + sw, (int32_t)xw, (int32_t)o0);
+                w_issued = k + 1u;
+                return true;
+            };
+            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+                for (; kw < KT && kw <= kt + W - 1u && ok; ++kw) ok = issue_w(kw);
+                if (!ok) break;
                 const uint32_t s = kt % S;
                 if (kt >= S && !mbar_wait(empty + s, ((kt / S) - 1u) & 1u, abort_flag)) break;
                 mbar_expect_tx(full + s, SB);
@@ -388,31 +424,29 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         bool ok = true;
         if constexpr (!VQ) {
             const uint32_t ng = p.I / p.gs;
-            const uint8_t *crow = p.codes + (size_t)(valid ? o : 0u) * p.I;
-            // codes, scale and offset of the next K step are loaded while the
-            // current one is converted
-            uint4 cn[4];
+            // scale and offset of the next K step are loaded while the
+            // current one is converted; the codes come from the weight ring
+            // (row `row` of the stage: 128 B, its 16-byte units swizzled by
+            // row & 7, so a warp's loads are free of bank conflicts)
             float scn = 0.0f, ofn = 0.0f;
             auto fetch = [&](uint32_t kt) {
-                const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
                 if (valid) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(crow + k0);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) cn[i] = __ldg(src + i);
-                    const uint32_t g = k0 / p.gs;
+                    const uint32_t g = ((kt_lo + kt) * kBK + h * 64u) / p.gs;
                     scn = __ldg(p.scales + (size_t)o * ng + g);
                     ofn = __ldg(p.offsets + (size_t)o * ng + g);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) cn[i] = make_uint4(0u, 0u, 0u, 0u);
                 }
             };
             if (KT > 0) fetch(0);
             for (uint32_t kt = 0; kt < KT && ok; ++kt) {
-                const uint32_t b = kt & 1u;
+                const uint32_t b = kt & 1u, sw = kt % W;
+                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) { ok = false; break; }
                 uint4 c[4];
+                const unsigned char *wr = wring + sw * WB + row * 128u;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) c[i] = cn[i];
+                for (uint32_t i = 0; i < 4u; ++i)
+                    c[i] = *reinterpret_cast<const uint4 *>(wr + (((4u * h + i) ^ (row & 7u)) << 4));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(w_empty + sw);
                 const float sc = scn, of = ofn;
                 if (kt + 1u < KT) fetch(kt + 1u);
                 uint32_t v[32];
@@ -440,8 +474,6 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             // index gathers exactly one TMEM column (low half = even k)
             for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
                 reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
-            const size_t row_bytes = (size_t)(p.I / 4u) * 3u;
-            const uint8_t *vrow = p.vidx + (size_t)(valid ? o : 0u) * row_bytes;
             // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
             // this row, from this CTA's first step); the offsets are read two
             // steps ahead and the first four patches of a step one step ahead
@@ -461,23 +493,22 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 q3 = n > 3u ? __ldg(src + 3) : 0u;
             };
             if (KT > 0) load4(k_cur, k_nxt, pc0, pc1, pc2, pc3);
-            // 64 weights = 16 byte triples = 3 x 16 bytes per thread and step
-            uint4 cn[3];
-            auto fetch = [&](uint32_t kt) {
-                const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
-                const uint4 *src = reinterpret_cast<const uint4 *>(vrow + (size_t)(k0 / 4u) * 3u);
-#pragma unroll
-                for (int i = 0; i < 3; ++i) cn[i] = __ldg(src + i);
-            };
-            if (KT > 0) fetch(0);
             asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
             for (uint32_t kt = 0; kt < KT && ok; ++kt) {
-                const uint32_t b = kt & 1u;
+                const uint32_t b = kt & 1u, sw = kt % W;
+                // 64 weights = 16 byte triples = 3 x 16 bytes of this thread's
+                // row of the weight ring stage (96 B per row)
+                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) { ok = false; break; }
+                uint4 cn[3];
+                const unsigned char *wr = wring + sw * WB + row * 96u + h * 48u;
+#pragma unroll
+                for (uint32_t i = 0; i < 3u; ++i) cn[i] = *reinterpret_cast<const uint4 *>(wr + 16u * i);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(w_empty + sw);
                 const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
                                         cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
                 const uint32_t n_cur = k_nxt - k_cur, lo_cur = k_cur;
                 if (kt + 1u < KT) {
-                    fetch(kt + 1u);
                     load4(k_nxt, k_nn, pn0, pn1, pn2, pn3);
                     k_cur = k_nxt;
                     k_nxt = k_nn;
@@ -569,6 +600,8 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     if (warp == kMmaWarp && lane == 0) mbar_drain(d_full, 0u);
     if (warp == kProducerWarp && lane == 0) {
         for (uint32_t kt = issued > S ? issued - S : 0u; kt < issued; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u);
+        for (uint32_t kt = w_issued > W ? w_issued - W : 0u; kt < w_issued; ++kt)
+            mbar_drain(w_full + kt % W, (kt / W) & 1u);
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -634,6 +667,20 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
+    // the weights: affine codes [O][I] in boxes of 128 B x 128 rows with
+    // 128-byte swizzle, or VQ index bytes [O][I * 3 / 4] in boxes of 96 B x
+    // 128 rows (no swizzle); rows past O read as zero
+    CUtensorMap wmap;
+    std::memset(&wmap, 0, sizeof(wmap));
+    const cuuint64_t wrow = VQ ? (cuuint64_t)(p.I / 4u) * 3u : (cuuint64_t)p.I;
+    const cuuint64_t wdims[2] = {wrow, p.O};
+    const cuuint64_t wstrides[1] = {wrow};
+    const cuuint32_t wbox[2] = {VQ ? 96u : 128u, kBM};
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(VQ ? p.vidx : p.codes), wdims, wstrides,
+            wbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            VQ ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
     auto kern = dequant_gemm_kernel<BN, VQ>;
     const uint32_t smem = smem_bytes(BN, VQ);
     // the shared-memory opt-in is made once per device and instantiation
@@ -661,7 +708,7 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
     // early launch behind other kernels (the GEMVs signal at their start)
     // measured slower
     cfg.numAttrs = p.chain ? 1 : 0;
-    if (cudaLaunchKernelEx(&cfg, kern, map, p) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (cudaLaunchKernelEx(&cfg, kern, map, wmap, p) != cudaSuccess) { cudaGetLastError(); return -1; }
     return 0;
 }
 

@@ -16,7 +16,9 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.dirname(_HERE)
 REPO_DIR = os.path.dirname(PKG_DIR)
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libhxq.so")
+# HXQ_LIB names another build of the library (e.g. one made with different
+# EXTRA flags); by default the one `make -C hxq-native_b200` puts in lib/.
+LIB_PATH = os.environ.get("HXQ_LIB") or os.path.join(PKG_DIR, "lib", "libhxq.so")
 INCLUDE_DIR = os.path.join(REPO_DIR, "include")
 
 # -- status codes (include/hxq.h, include/hxq_cuda.h) ------------------------

@@ -249,6 +249,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32])
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15])
+        : "r"(taddr));
+}
+
+template <uint32_t EW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[EW])
+{
+    if constexpr (EW == 32u) tmem_ld32(taddr, v);
+    else tmem_ld16(taddr, v);
+}
+
 __device__ __forceinline__ float code_f32(uint32_t word, uint32_t i)
 {
     return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u + i)) - 8388608.0f;
@@ -576,16 +594,19 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             // this half's accumulator columns; a 32-column load may read past
             // them (inside the allocation) when BN < 64: those are not stored
             const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
+            // 32 columns per load for the wide tiles, 16 for BN <= 64 (whose
+            // converters hold fewer registers free)
+            constexpr uint32_t EW = BN >= 128 ? 32u : 16u;
 #pragma unroll 1
-            for (uint32_t c0 = cbeg; c0 < cend; c0 += 32u) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_base + c0, v);
+            for (uint32_t c0 = cbeg; c0 < cend; c0 += EW) {
+                uint32_t v[EW];
+                tmem_ld<EW>(tmem + lane_base + c0, v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;");
                 if (valid) {
                     for (uint32_t k = 0; k < nout; ++k) {
                         float *yo = partial ? p.part + (size_t)blockIdx.z * p.T * p.O : p.out.y[k];
 #pragma unroll
-                        for (uint32_t j = 0; j < 32u; ++j) {
+                        for (uint32_t j = 0; j < EW; ++j) {
                             const uint32_t n = n0 + c0 + j;
                             if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
                         }

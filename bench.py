@@ -648,11 +648,18 @@ def run_fused_matmul_workload(args):
                         layer.forward(xs, N, stream, step=0, assembly="nccl")
                         layer.forward(xs, N, stream, step=0, assembly="p2p")
                     stream.synchronize()
-                    same = all(bool(torch.equal(a.view(torch.int32), b.contiguous().view(torch.int32)))
-                               for a, b in zip(layer.outputs(N, 0, "p2p"), layer.outputs(N, 0, "nccl")))
-                    t = torch.tensor([1.0 if same else 0.0], dtype=torch.float64, device="cuda")
-                    dist.all_reduce(t, op=dist.ReduceOp.MIN)
-                    res["p2p_equals_nccl"] = bool(t.item() == 1.0)
+                    # differing outputs, in this rank's own columns and in the
+                    # columns its peers stored over NVLink
+                    bad = torch.zeros(2, dtype=torch.float64, device="cuda")
+                    for e, a, b in zip(layer.mats, layer.outputs(N, 0, "p2p"), layer.outputs(N, 0, "nccl")):
+                        diff = a.view(torch.int32) != b.contiguous().view(torch.int32)
+                        cols = torch.arange(e["O"], device="cuda")
+                        mine = (cols >= e["r0"]) & (cols < e["r0"] + e["rows"])
+                        bad[0] += diff[:, mine].sum()
+                        bad[1] += diff[:, ~mine].sum()
+                    dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+                    res["p2p_equals_nccl"] = bool(bad.sum().item() == 0)
+                    res["p2p_mismatch"] = {"own_columns": int(bad[0].item()), "peer_columns": int(bad[1].item())}
                     res["peer_wait_status"] = layer.peer_wait_status()
                 results.append(res)
             del xs

@@ -505,6 +505,7 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     r += qs;
                     if (gg >= ng) { gg -= ng; ++r; }
                 }
+                async_proxy_fence();   // sbuf is refilled by the next row block's bulk copy
                 asm volatile(HXQ_TC_BAR_CONSUMERS ::: "memory");
                 if (ok && lane == 0) mbar_arrive(sdone);
             }
@@ -518,8 +519,7 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 for (int tt = 0; tt < NT; ++tt) xa[tt] = xa0[tt] + 2u * kb;
                 if constexpr (MERGE) {
                     pair_mma<NT>(sa + coff0, sa + coff1, xa, d);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
+                    warp_release(empty + slot, lane);   // the stage's codes are in registers
                     pair_apply<NT>(d, sf_a + (kb >> gsh) * (kSfStride * 4u) + 8u * g, ca0, ca1, kb >> 6, as, af);
                 } else {
                     chunk_mma<NT>(sa + coff0, xa, d);
@@ -527,8 +527,7 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
 #pragma unroll
                     for (int tt = 0; tt < NT; ++tt) xa[tt] += 2u * kChunk;
                     chunk_mma<NT>(sa + coff1, xa, d);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(empty + slot);   // the stage's codes are in registers
+                    warp_release(empty + slot, lane);   // the stage's codes are in registers
                     const uint32_t k1 = kb + kChunk;
                     chunk_apply<NT>(d, sf_a + (k1 >> gsh) * (kSfStride * 4u) + 8u * g, ca0, ca1, k1 >> 6, as, af);
                 }

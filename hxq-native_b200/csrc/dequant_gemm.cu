@@ -124,6 +124,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Order this thread's reads of a shared-memory buffer (generic proxy)
+// before the TMA copy that will overwrite it (async proxy); without it the
+// copy can land before reads still in flight (measured: nondeterministic
+// GEMM results with the two-stage weight ring).
+__device__ __forceinline__ void async_proxy_fence()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
@@ -463,6 +472,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
 #pragma unroll
                 for (uint32_t i = 0; i < 4u; ++i)
                     c[i] = *reinterpret_cast<const uint4 *>(wr + (((4u * h + i) ^ (row & 7u)) << 4));
+                async_proxy_fence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
                 const float sc = scn, of = ofn;
@@ -521,6 +531,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 const unsigned char *wr = wring + sw * WB + row * 96u + h * 48u;
 #pragma unroll
                 for (uint32_t i = 0; i < 3u; ++i) cn[i] = *reinterpret_cast<const uint4 *>(wr + 16u * i);
+                async_proxy_fence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
                 const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,

@@ -31,6 +31,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Order this thread's reads of a shared-memory buffer (generic proxy)
+// before a TMA or bulk copy that will overwrite it (async proxy).  Without
+// it the copy can land before reads still in flight and they see the new
+// data (measured: nondeterministic results in a two-stage TMA ring).
+__device__ __forceinline__ void async_proxy_fence()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Hand back a buffer this warp has read to the copy that refills it: every
+// lane's proxy fence, then one arrival per warp.
+__device__ __forceinline__ void warp_release(uint64_t *bar, uint32_t lane)
+{
+    async_proxy_fence();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)

@@ -382,8 +382,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     wg[4 * u] = a.x; wg[4 * u + 1] = a.y; wg[4 * u + 2] = a.z; wg[4 * u + 3] = a.w;
                     wh[4 * u] = c.x; wh[4 * u + 1] = c.y; wh[4 * u + 2] = c.z; wh[4 * u + 3] = c.w;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty + slot);   // the stage's offsets are in registers
+                warp_release(empty + slot, lane);   // the stage's offsets are in registers
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     uint4 xb[NT][2];

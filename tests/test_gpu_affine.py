@@ -370,3 +370,30 @@ def test_batch_chain_breaks_at_other_kernels(H, L, cuda):
         for o in outs:
             o.fill_(float("nan"))
     assert L.hxq_cuda_affine_device_status() == 0
+
+
+def test_gemm_batch_repeatable(H, L, cuda):
+    """The tcgen05 GEMMs of a 7B layer's shard (2048 / 5504 rows, as one of
+    two GPUs holds them) at 2048 tokens, repeated: every run bit-identical to
+    the first.  (A shared-memory stage refilled by TMA while reads of it were
+    still in flight once made a few rows differ from run to run.)"""
+    torch = cuda
+    from hxq_b200.sharded import ColumnSplitLayer
+    N = 2048
+    mats = [dict(name=n, O=O, I=I, affine=synth.affine(O, I, 128, 7000 + p))
+            for p, (n, O, I) in enumerate(synth.LLAMA7B_PROJ)]
+    xs = {I: torch.from_numpy(synth.activations(N, I, 7100 + I)[0].view(np.int16)).cuda() for I in (4096, 11008)}
+    layer = ColumnSplitLayer(mats, "affine", max_tokens=N, rank=0, world=2, torch=torch, lib=L)
+    stream = torch.cuda.Stream()
+    ref = None
+    for _ in range(12):
+        layer.forward(xs, N, stream, assembly="local")
+        stream.synchronize()
+        outs = [y.clone() for y in layer.local_outputs(N)]
+        if ref is None:
+            ref = outs
+            continue
+        for j, (a, b) in enumerate(zip(outs, ref)):
+            assert torch.equal(a.view(torch.int32), b.view(torch.int32)), mats[j]["name"]
+    assert L.hxq_cuda_affine_device_status() == 0
+    layer.close()

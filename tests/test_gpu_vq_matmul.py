@@ -403,3 +403,29 @@ def test_batch_chain_breaks_at_other_kernels(H, L, oracle, cuda):
     finally:
         for im, _ in imgs:
             L.hxq_cuda_image_destroy(im)
+
+
+def test_vq_gemm_and_gemv_repeatable(H, L, cuda):
+    """VQ GEMM (2048 tokens) and tensor-core GEMV (1 token) on two 7B-shaped
+    images, repeated: every run bit-identical to the first (their TMA stages
+    are refilled only after the reads of the previous fill are ordered)."""
+    torch = cuda
+    from hxq_b200.sharded import ColumnSplitLayer
+    mats = [dict(name="q", O=4096, I=4096, vq=synth.vq12(4096, 4096, 7200)),
+            dict(name="down", O=4096, I=11008, vq=synth.vq12(4096, 11008, 7201))]
+    layer = ColumnSplitLayer(mats, "vq12", max_tokens=2048, rank=0, world=1, torch=torch, lib=L)
+    stream = torch.cuda.Stream()
+    for N in (1, 2048):
+        xs = {I: torch.from_numpy(synth.activations(N, I, 7300 + I)[0].view(np.int16)).cuda() for I in (4096, 11008)}
+        ref = None
+        for _ in range(8):
+            layer.forward(xs, N, stream)
+            stream.synchronize()
+            outs = [y.clone() for y in layer.outputs(N)]
+            if ref is None:
+                ref = outs
+                continue
+            for a, b in zip(outs, ref):
+                assert torch.equal(a.view(torch.int32), b.view(torch.int32)), N
+    assert L.hxq_cuda_affine_device_status() == 0
+    layer.close()

@@ -343,18 +343,3 @@ def load_modules(path: str) -> dict[str, dict]:
     for prefix, names in hxq_modules(tensors.keys()).items():
         out[prefix] = module_tensor({part: tensors[name] for part, name in names.items()})
     return out
-
-
-def dense_reference(parts: dict[str, np.ndarray]) -> np.ndarray:
-    """The module's weights as the file defines them (codebook lookup, then
-    each sidecar value replacing its position, later entries winning), for
-    checking."""
-    cb = np.asarray(parts["codebook"], dtype=np.float32)
-    idx = np.asarray(parts["indices"])
-    idx = (idx.view(np.uint8) if idx.dtype == np.int8 else idx).astype(np.int64)
-    W = (cb[idx] if cb.ndim == 1 else cb[idx].reshape(idx.shape[0], -1)).reshape(-1).copy()
-    pos = parts.get("sidecar_positions")
-    if pos is not None:
-        for p, v in zip(np.asarray(pos).reshape(-1), np.asarray(parts["sidecar_values"], np.float32).reshape(-1)):
-            W[int(p)] = v
-    return W

@@ -200,6 +200,25 @@ class _RefResult(C.Structure):
                 ("in_features", C.c_uint32)]
 
 
+def container_dense(parts: dict) -> np.ndarray:
+    """Dense fp32 weights of one helix-substrate module as the reference's
+    converter defines them (tools/convert_hxq_to_gguf.py:268-295,
+    dequant_hxq_tensor): codebook lookup (a 2-D codebook gives a pair per
+    index), then every sidecar value REPLACES the weight at its flat
+    position, in array order, so the last of repeated positions wins.
+    Pinned to fixtures made by that function itself
+    (tests/golden/make_container_golden.py)."""
+    cb = np.asarray(parts["codebook"], dtype=np.float32)
+    idx = np.asarray(parts["indices"])
+    idx = (idx.view(np.uint8) if idx.dtype == np.int8 else idx).astype(np.int64)
+    W = (cb[idx] if cb.ndim == 1 else cb[idx].reshape(idx.shape[0], -1)).reshape(-1).copy()
+    pos = parts.get("sidecar_positions")
+    if pos is not None:
+        for q, v in zip(np.asarray(pos).reshape(-1), np.asarray(parts["sidecar_values"], np.float32).reshape(-1)):
+            W[int(q)] = v
+    return W
+
+
 def ref_available(path: str = REF_SO) -> bool:
     return os.path.exists(path)
 

@@ -60,7 +60,11 @@ def load_golden(name: str) -> dict:
 
 
 def golden_names(prefix: str = "") -> list[str]:
-    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz") and f.startswith(prefix))
+    """Fixtures of the reference library (hxq.c, hxq_affine.c) whose names
+    start with `prefix`; the container converter's fixtures (container_*)
+    only when asked for by that prefix."""
+    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz") and f.startswith(prefix)
+                  and (prefix.startswith("container") or not f.startswith("container")))
 
 
 @pytest.fixture(scope="session")

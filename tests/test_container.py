@@ -12,7 +12,9 @@ import struct
 import numpy as np
 import pytest
 
+from conftest import golden_names, load_golden
 from hxq_b200 import container as CT
+from oracle.oracle import container_dense
 
 
 def _rng(seed):
@@ -153,7 +155,7 @@ def test_safetensors_modules_decode_bit_exact(tmp_path, H, L, oracle, vdim, k, o
     assert d["mode"] == (0 if vdim == 1 else 2)
     assert len(np.unique(d["rows"].astype(np.int64) * in_f + d["cols"])) == \
         (len(np.unique(parts["sidecar_positions"])) if nnz else 0)
-    want = CT.dense_reference(parts)
+    want = container_dense(parts)
     w_orc, w_lib = _decode_all(H, L, oracle, d)
     assert np.array_equal(w_orc.view(np.uint32), want.view(np.uint32))
     assert np.array_equal(w_lib.view(np.uint32), want.view(np.uint32))
@@ -168,7 +170,24 @@ def test_gguf_compressed_scalar_module_decodes_bit_exact(tmp_path, H, L, oracle)
     p = str(tmp_path / "model.gguf")
     CT.write_gguf(p, st)
     d = CT.load_modules(p)["blk.3.ffn_down"]
-    want = CT.dense_reference(parts)
+    want = container_dense(parts)
+    w_orc, w_lib = _decode_all(H, L, oracle, d)
+    assert np.array_equal(w_orc.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(w_lib.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", golden_names("container_"))
+def test_reference_converter_fixtures(H, L, oracle, name):
+    """Fixtures made by the reference converter's own dequant_hxq_tensor
+    (tools/convert_hxq_to_gguf.py:268-295): the oracle's restatement equals
+    it, and the module converted to hxq.c ADD deltas decodes to exactly it
+    on the oracle and on the library's CPU backend."""
+    g = load_golden(name)
+    parts = {k: g[k] for k in ("codebook", "indices", "sidecar_positions", "sidecar_values")}
+    want = g["expect"]
+    assert np.array_equal(container_dense(parts).view(np.uint32), want.view(np.uint32))
+    d = CT.module_tensor(parts)
+    assert (d["out_f"], d["in_f"]) == (g["out_f"], g["in_f"])
     w_orc, w_lib = _decode_all(H, L, oracle, d)
     assert np.array_equal(w_orc.view(np.uint32), want.view(np.uint32))
     assert np.array_equal(w_lib.view(np.uint32), want.view(np.uint32))
@@ -200,7 +219,7 @@ def test_two_add_entries_in_array_order(H, L, oracle):
     parts = {"codebook": cb, "indices": idx, "sidecar_positions": pos, "sidecar_values": tgt}
     d = CT.module_tensor(parts)
     assert len(d["rows"]) > len(pos)
-    want = CT.dense_reference(parts)
+    want = container_dense(parts)
     w_orc, w_lib = _decode_all(H, L, oracle, d)
     assert np.array_equal(w_orc.view(np.uint32), want.view(np.uint32))
     assert np.array_equal(w_lib.view(np.uint32), want.view(np.uint32))
@@ -235,7 +254,7 @@ def test_gpu_layers_from_a_model_file(tmp_path, H, L, oracle, cuda, world):
             "m.o": _module(72, 96, 160, 1, 256, 120, dup=10)}
     p = str(tmp_path / "m.safetensors")
     CT.write_safetensors(p, {f"{m}.{n}": a for m, parts in mods.items() for n, a in parts.items()})
-    wants = {m: CT.dense_reference(parts).reshape(parts["indices"].shape[0], -1) for m, parts in mods.items()}
+    wants = {m: container_dense(parts).reshape(parts["indices"].shape[0], -1) for m, parts in mods.items()}
     for rank in range(world):
         layers = load_linears(p, (rank, world))
         assert set(layers) == set(mods)

@@ -127,6 +127,7 @@ affine_gemv_kernel(const XT *__restrict__ x, const uint8_t *__restrict__ codes,
         for (uint32_t o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_f; o += warps)
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(codes + (size_t)o * in_f), "r"(in_f)
                          : "memory");
+    __syncwarp();   // lane 0's prefetches are issued before any lane blocks in griddepcontrol.wait
     if (staged) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         for (uint32_t i = threadIdx.x; i < ntok * in_f; i += blockDim.x)

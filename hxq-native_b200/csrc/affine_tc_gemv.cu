@@ -433,7 +433,13 @@ affine_tc_gemv_kernel(const __grid_constant__ Jobs J)
             // every issued copy has landed before shared memory is released
             for (uint32_t kt = it > S ? it - S : 0u; kt < it; ++kt) mbar_drain(full + kt % S, (kt / S) & 1u, &g_tc_err);
         }
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // The producer reads only weights, so it never waits for the
+        // previous kernel.  Lanes 1-31 must not execute griddepcontrol.wait
+        // either: the warp is diverged around lane 0's loop, and a blocked
+        // wait on the other path held lane 0's copies back until the
+        // previous kernel had finished (measured: the codes were issued
+        // after, not before, the consumers' wait).
+        __syncwarp();
         return;
     }
 

@@ -451,19 +451,24 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         bool ok = true;
         if constexpr (!VQ) {
             const uint32_t ng = p.I / p.gs;
-            // scale and offset of the next K step are loaded while the
-            // current one is converted; the codes come from the weight ring
-            // (row `row` of the stage: 128 B, its 16-byte units swizzled by
-            // row & 7, so a warp's loads are free of bank conflicts)
-            float scn = 0.0f, ofn = 0.0f;
-            auto fetch = [&](uint32_t kt) {
-                if (valid) {
+            // scales and offsets are loaded four K steps ahead into a
+            // register queue (one step ahead left the converters waiting on
+            // the loads); the codes come from the weight ring (row `row` of
+            // the stage: 128 B, its 16-byte units swizzled by row & 7, so a
+            // warp's loads are free of bank conflicts)
+            float sq0 = 0.0f, sq1 = 0.0f, sq2 = 0.0f, sq3 = 0.0f;
+            float oq0 = 0.0f, oq1 = 0.0f, oq2 = 0.0f, oq3 = 0.0f;
+            auto fetch = [&](uint32_t kt, float &sv, float &fv) {
+                if (valid && kt < KT) {
                     const uint32_t g = ((kt_lo + kt) * kBK + h * 64u) / p.gs;
-                    scn = __ldg(p.scales + (size_t)o * ng + g);
-                    ofn = __ldg(p.offsets + (size_t)o * ng + g);
+                    sv = __ldg(p.scales + (size_t)o * ng + g);
+                    fv = __ldg(p.offsets + (size_t)o * ng + g);
                 }
             };
-            if (KT > 0) fetch(0);
+            fetch(0, sq0, oq0);
+            fetch(1, sq1, oq1);
+            fetch(2, sq2, oq2);
+            fetch(3, sq3, oq3);
             for (uint32_t kt = 0; kt < KT && ok; ++kt) {
                 const uint32_t b = kt & 1u, sw = kt % W;
                 if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) { ok = false; break; }
@@ -475,8 +480,10 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 async_proxy_fence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
-                const float sc = scn, of = ofn;
-                if (kt + 1u < KT) fetch(kt + 1u);
+                const float sc = sq0, of = oq0;
+                sq0 = sq1; sq1 = sq2; sq2 = sq3;
+                oq0 = oq1; oq1 = oq2; oq2 = oq3;
+                fetch(kt + 4u, sq3, oq3);
                 uint32_t v[32];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {

@@ -283,7 +283,10 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
             for (uint32_t kt = it > S ? it - S : 0u; kt < it; ++kt)
                 mbar_drain(full + kt % S, (kt / S) & 1u, &g_vqtc_err);
         }
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        // No griddepcontrol.wait in the producer warp: it reads only the
+        // image, and a wait blocked on lanes 1-31 would hold lane 0's copies
+        // back until the previous kernel had finished.
+        __syncwarp();
         return;
     }
 

@@ -451,11 +451,13 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         bool ok = true;
         if constexpr (!VQ) {
             const uint32_t ng = p.I / p.gs;
-            // scales and offsets are loaded four K steps ahead into a
-            // register queue (one step ahead left the converters waiting on
-            // the loads); the codes come from the weight ring (row `row` of
+            // scales and offsets are loaded four K steps ahead, into one
+            // register pair per step modulo 4: the loop is unrolled by four so
+            // that no register holding a load in flight is ever copied (a
+            // copy waits for the load, which would shrink the distance to
+            // one step).  The codes come from the weight ring (row `row` of
             // the stage: 128 B, its 16-byte units swizzled by row & 7, so a
-            // warp's loads are free of bank conflicts)
+            // warp's loads are free of bank conflicts).
             float sq0 = 0.0f, sq1 = 0.0f, sq2 = 0.0f, sq3 = 0.0f;
             float oq0 = 0.0f, oq1 = 0.0f, oq2 = 0.0f, oq3 = 0.0f;
             auto fetch = [&](uint32_t kt, float &sv, float &fv) {
@@ -469,9 +471,11 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             fetch(1, sq1, oq1);
             fetch(2, sq2, oq2);
             fetch(3, sq3, oq3);
-            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+            // one K step: the codes into bf16 weights, into A buffer kt & 1;
+            // false if a wait ran out
+            auto step = [&](uint32_t kt, float &sq, float &oq) -> bool {
                 const uint32_t b = kt & 1u, sw = kt % W;
-                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) return false;
                 uint4 c[4];
                 const unsigned char *wr = wring + sw * WB + row * 128u;
 #pragma unroll
@@ -480,10 +484,8 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 async_proxy_fence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
-                const float sc = sq0, of = oq0;
-                sq0 = sq1; sq1 = sq2; sq2 = sq3;
-                oq0 = oq1; oq1 = oq2; oq2 = oq3;
-                fetch(kt + 4u, sq3, oq3);
+                const float sc = sq, of = oq;
+                fetch(kt + 4u, sq, oq);
                 uint32_t v[32];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -498,11 +500,18 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                         v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
                     }
                 }
-                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
                 tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
                 asm volatile("tcgen05.wait::st.sync.aligned;");
                 asm volatile("tcgen05.fence::before_thread_sync;");
                 mbar_arrive(a_full + b);
+                return true;
+            };
+            for (uint32_t kt = 0; kt < KT && ok; kt += 4u) {
+                ok = step(kt, sq0, oq0);
+                if (ok && kt + 1u < KT) ok = step(kt + 1u, sq1, oq1);
+                if (ok && kt + 2u < KT) ok = step(kt + 2u, sq2, oq2);
+                if (ok && kt + 3u < KT) ok = step(kt + 3u, sq3, oq3);
             }
         } else {
             // the image's bf16 codebook, one 32-bit pair per entry: an
@@ -510,30 +519,37 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
                 reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
             // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
-            // this row, from this CTA's first step); the offsets are read two
-            // steps ahead and the first four patches of a step one step ahead
+            // this row, from this CTA's first step).  The offsets kp[kt + j]
+            // sit in four slots, each refilled four steps ahead; the first
+            // four patches of a step in one of two sets, loaded two steps
+            // ahead.  The loop is unrolled by four so that the slots and sets
+            // are fixed registers: a register holding a load in flight is never
+            // copied (a copy would wait for the load).
             const uint16_t *kpr = p.kp + (size_t)(valid ? o : 0u) * (KT_all + 1u) + kt_lo;
             const uint32_t pb = valid ? __ldg(p.rb + o) : 0u;
-            uint32_t k_cur = valid && KT > 0 ? __ldg(kpr) : 0u;          // start of step kt
-            uint32_t k_nxt = valid && KT > 0 ? __ldg(kpr + 1) : 0u;      // start of step kt + 1
-            uint32_t k_nn = valid && KT > 1 ? __ldg(kpr + 2) : k_nxt;    // start of step kt + 2
-            uint32_t pc0 = 0, pc1 = 0, pc2 = 0, pc3 = 0;                 // patches of step kt
-            uint32_t pn0 = 0, pn1 = 0, pn2 = 0, pn3 = 0;                 // patches of step kt + 1
-            auto load4 = [&](uint32_t lo, uint32_t hi, uint32_t &q0, uint32_t &q1, uint32_t &q2, uint32_t &q3) {
+            auto kload = [&](uint32_t j) -> uint32_t { return valid && j <= KT ? (uint32_t)__ldg(kpr + j) : 0u; };
+            auto load4 = [&](uint32_t lo, uint32_t hi, uint32_t (&q)[4]) {
                 const uint32_t *src = p.e4 + pb + lo;
                 const uint32_t n = hi - lo;
-                q0 = n > 0u ? __ldg(src) : 0u;
-                q1 = n > 1u ? __ldg(src + 1) : 0u;
-                q2 = n > 2u ? __ldg(src + 2) : 0u;
-                q3 = n > 3u ? __ldg(src + 3) : 0u;
+                q[0] = n > 0u ? __ldg(src) : 0u;
+                q[1] = n > 1u ? __ldg(src + 1) : 0u;
+                q[2] = n > 2u ? __ldg(src + 2) : 0u;
+                q[3] = n > 3u ? __ldg(src + 3) : 0u;
             };
-            if (KT > 0) load4(k_cur, k_nxt, pc0, pc1, pc2, pc3);
+            uint32_t kq0 = kload(0), kq1 = kload(1), kq2 = kload(2), kq3 = kload(3);
+            uint32_t pa[4] = {0u, 0u, 0u, 0u}, pz[4] = {0u, 0u, 0u, 0u};
+            if (KT > 0) load4(kq0, kq1, pa);
+            if (KT > 1) load4(kq1, kq2, pz);
             asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
-            for (uint32_t kt = 0; kt < KT && ok; ++kt) {
+            // one K step: k_lo = kp[kt] (its slot, refilled with kp[kt + 4]),
+            // k_hi, k_2, k_3 = kp[kt + 1 .. kt + 3]; P the step's first four
+            // patches (refilled with those of step kt + 2); false if a wait ran out
+            auto step = [&](uint32_t kt, uint32_t &k_lo, uint32_t k_hi, uint32_t k_2, uint32_t k_3,
+                            uint32_t (&P)[4]) -> bool {
                 const uint32_t b = kt & 1u, sw = kt % W;
                 // 64 weights = 16 byte triples = 3 x 16 bytes of this thread's
                 // row of the weight ring stage (96 B per row)
-                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) return false;
                 uint4 cn[3];
                 const unsigned char *wr = wring + sw * WB + row * 96u + h * 48u;
 #pragma unroll
@@ -543,13 +559,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (lane == 0) mbar_arrive(w_empty + sw);
                 const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
                                         cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
-                const uint32_t n_cur = k_nxt - k_cur, lo_cur = k_cur;
-                if (kt + 1u < KT) {
-                    load4(k_nxt, k_nn, pn0, pn1, pn2, pn3);
-                    k_cur = k_nxt;
-                    k_nxt = k_nn;
-                    k_nn = valid && kt + 3u <= KT ? __ldg(kpr + kt + 3u) : k_nn;
-                }
+                const uint32_t n_cur = k_hi - k_lo, lo_cur = k_lo;
                 uint32_t v[32];
 #pragma unroll
                 for (uint32_t t = 0; t < 16u; ++t) {
@@ -561,12 +571,13 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 // sidecar: the patches of this half-step replace their weights
                 // with the reference's fp32 value rounded once to bf16
                 const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
+                uint32_t r0 = P[0], r1 = P[1], r2 = P[2], r3 = P[3];
                 if constexpr (SA) {
                     // this thread's 128 bytes of the A tile: row `row` of half h,
                     // 16-byte unit u at (u ^ (row & 7)) << 4; then the patches,
                     // one 2-byte store each, into the same bytes
                     __syncwarp();
-                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
                     unsigned char *arow = abuf + b * kABytes + h * (kBM * 128u) + row * 128u;
 #pragma unroll
                     for (uint32_t u = 0; u < 8u; ++u)
@@ -574,33 +585,40 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                             make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
 #pragma unroll 1
                     for (uint32_t i = 0; i < n_cur; ++i) {
-                        const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
-                        pc0 = pc1; pc1 = pc2; pc2 = pc3;
+                        const uint32_t q = i < 4u ? r0 : __ldg(p.e4 + pb + lo_cur + i);
+                        r0 = r1; r1 = r2; r2 = r3;
                         const uint32_t local = (q & 0xFFFFu) - k0;
                         if (local < 64u)
                             *reinterpret_cast<uint16_t *>(arow + ((((local >> 3) ^ (row & 7u)) << 4) | ((local & 7u) << 1))) =
                                 (uint16_t)(q >> 16);
                     }
-                    pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
                     // the generic-proxy stores, visible to the tensor cores' reads
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mbar_arrive(a_full + b);
                 } else {
 #pragma unroll 1
                     for (uint32_t i = 0; i < n_cur; ++i) {
-                        const uint32_t q = i < 4u ? pc0 : __ldg(p.e4 + pb + lo_cur + i);
-                        pc0 = pc1; pc1 = pc2; pc2 = pc3;
+                        const uint32_t q = i < 4u ? r0 : __ldg(p.e4 + pb + lo_cur + i);
+                        r0 = r1; r1 = r2; r2 = r3;
                         const uint32_t local = (q & 0xFFFFu) - k0;
                         if (local < 64u) patch_pair(v, local, q >> 16);
                     }
-                    pc0 = pn0; pc1 = pn1; pc2 = pn2; pc3 = pn3;
                     __syncwarp();
-                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) { ok = false; break; }
+                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
                     tmem_st32(tmem + lane_base + kTmemA + b * 64u + h * 32u, v);
                     asm volatile("tcgen05.wait::st.sync.aligned;");
                     asm volatile("tcgen05.fence::before_thread_sync;");
                     mbar_arrive(a_full + b);
                 }
+                if (kt + 2u < KT) load4(k_2, k_3, P);
+                k_lo = kload(kt + 4u);
+                return true;
+            };
+            for (uint32_t kt = 0; kt < KT && ok; kt += 4u) {
+                ok = step(kt, kq0, kq1, kq2, kq3, pa);
+                if (ok && kt + 1u < KT) ok = step(kt + 1u, kq1, kq2, kq3, kq0, pz);
+                if (ok && kt + 2u < KT) ok = step(kt + 2u, kq2, kq3, kq0, kq1, pa);
+                if (ok && kt + 3u < KT) ok = step(kt + 3u, kq3, kq0, kq1, kq2, pz);
             }
         }
         if (ok && mbar_wait(d_full, 0u, abort_flag)) {

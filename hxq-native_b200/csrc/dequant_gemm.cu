@@ -41,9 +41,13 @@
 // only after it has waited for its own predecessor, so the activations are
 // ready), and waits for the previous GEMM at its end instead of its start,
 // so that the batch still completes in order.  Other GEMMs are launched in
-// plain stream order.  Every mbarrier wait is bounded (about one second of
-// clock); a wait that runs out records an error word and the CTA unwinds,
-// releasing its tensor memory.
+// plain stream order.  A GEMM outside a batch whose 256-token tiles leave a
+// last wave filling at most half of the SMs splits those last tiles along K
+// into two ranges (one CTA each): both store partial sums to a scratch
+// buffer and count themselves, and the second adds the other's sums to its
+// own (4096 x 4096 VQ at 4096 tokens: 200.9 -> 184.4 us).  Every mbarrier
+// wait is bounded (about one second of clock); a wait that runs out records
+// an error word and the CTA unwinds, releasing its tensor memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -306,6 +310,15 @@ struct Params {
     uint32_t T, I, O, gs, ldy;
     uint32_t splits;          // K ranges (gridDim.z); >1 writes partials, no bias
     uint32_t chain;           // 1: follows an unsplit GEMM of the same batch
+    // Last-wave split (tail_s > 0; a one-dimensional grid): CTAs below n_full
+    // take tiles 0 .. n_full-1 whole (tile t: row tile t % tiles_m, token
+    // tile t / tiles_m); the others take the remaining tiles' K steps in
+    // tail_s ranges each, write partial sums to ws ([tail tile][range][BN
+    // columns][128 rows]) and count themselves in cnt[tail tile]; the last
+    // to arrive adds the ranges in order and stores the tile.
+    uint32_t tiles_m, n_full, tail_s;
+    float *ws;
+    uint32_t *cnt;
 };
 
 // Replace the bf16 at position `local` (0..63) of a thread's 32 packed
@@ -346,14 +359,33 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     uint64_t *w_empty = w_full + W;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(w_empty + W);
     volatile uint32_t *abort_flag = tmem_slot + 1;
+    volatile uint32_t *last_flag = tmem_slot + 2;     // last-wave tile: this CTA adds the ranges
     uint32_t *cbh = reinterpret_cast<uint32_t *>(wring + W * WB + 256u);   // VQ: bf16 pairs
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-    const uint32_t o0 = blockIdx.x * kBM;
-    const uint32_t n0 = blockIdx.y * BN;
     const uint32_t KT_all = p.I / kBK;                          // K steps of the matrix
-    const uint32_t kt_lo = (uint32_t)((uint64_t)KT_all * blockIdx.z / p.splits);
-    const uint32_t KT = (uint32_t)((uint64_t)KT_all * (blockIdx.z + 1u) / p.splits) - kt_lo;
+    uint32_t o0, n0, kt_lo, KT;
+    uint32_t tail = 0xFFFFFFFFu, trange = 0;   // last-wave tile and K range
+    if (BN < 256u || p.tail_s == 0u) {
+        o0 = blockIdx.x * kBM;
+        n0 = blockIdx.y * BN;
+        kt_lo = (uint32_t)((uint64_t)KT_all * blockIdx.z / p.splits);
+        KT = (uint32_t)((uint64_t)KT_all * (blockIdx.z + 1u) / p.splits) - kt_lo;
+    } else {
+        uint32_t t = blockIdx.x;
+        kt_lo = 0;
+        KT = KT_all;
+        if (t >= p.n_full) {
+            const uint32_t j = t - p.n_full;
+            tail = j / p.tail_s;
+            trange = j % p.tail_s;
+            t = p.n_full + tail;
+            kt_lo = (uint32_t)((uint64_t)KT_all * trange / p.tail_s);
+            KT = (uint32_t)((uint64_t)KT_all * (trange + 1u) / p.tail_s) - kt_lo;
+        }
+        o0 = (t % p.tiles_m) * kBM;
+        n0 = (t / p.tiles_m) * BN;
+    }
 
     if (!p.chain) asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -621,30 +653,91 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (ok && kt + 3u < KT) ok = step(kt + 3u, kq3, kq0, kq1, kq2, pz);
             }
         }
-        if (ok && mbar_wait(d_full, 0u, abort_flag)) {
-            asm volatile("tcgen05.fence::after_thread_sync;");
-            const bool partial = p.splits > 1u;
-            const float bo = (valid && p.bias && !partial) ? __ldg(p.bias + o) : 0.0f;
-            const uint32_t nout = partial ? 1u : p.out.n;
-            const uint32_t ld = partial ? p.O : p.ldy;
-            // this half's accumulator columns; a 32-column load may read past
-            // them (inside the allocation) when BN < 64: those are not stored
-            const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
-            // 32 columns per load for the wide tiles, 16 for BN <= 64 (whose
-            // converters hold fewer registers free)
-            constexpr uint32_t EW = BN >= 128 ? 32u : 16u;
+        // this half's accumulator columns; a 32-column load may read past
+        // them (inside the allocation) when BN < 64: those are not stored.
+        // 32 columns per load for the wide tiles, 16 for BN <= 64 (whose
+        // converters hold fewer registers free)
+        const uint32_t cbeg = h * (BN / 2u), cend = cbeg + BN / 2u;
+        constexpr uint32_t EW = BN >= 128 ? 32u : 16u;
+        const bool done = ok && mbar_wait(d_full, 0u, abort_flag);
+        if (done) asm volatile("tcgen05.fence::after_thread_sync;");
+        if (BN < 256u || tail == 0xFFFFFFFFu) {
+            if (done) {
+                const bool partial = p.splits > 1u;
+                const float bo = (valid && p.bias && !partial) ? __ldg(p.bias + o) : 0.0f;
+                const uint32_t nout = partial ? 1u : p.out.n;
+                const uint32_t ld = partial ? p.O : p.ldy;
 #pragma unroll 1
-            for (uint32_t c0 = cbeg; c0 < cend; c0 += EW) {
-                uint32_t v[EW];
-                tmem_ld<EW>(tmem + lane_base + c0, v);
-                asm volatile("tcgen05.wait::ld.sync.aligned;");
-                if (valid) {
-                    for (uint32_t k = 0; k < nout; ++k) {
-                        float *yo = partial ? p.part + (size_t)blockIdx.z * p.T * p.O : p.out.y[k];
+                for (uint32_t c0 = cbeg; c0 < cend; c0 += EW) {
+                    uint32_t v[EW];
+                    tmem_ld<EW>(tmem + lane_base + c0, v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;");
+                    if (valid) {
+                        for (uint32_t k = 0; k < nout; ++k) {
+                            float *yo = partial ? p.part + (size_t)blockIdx.z * p.T * p.O : p.out.y[k];
 #pragma unroll
-                        for (uint32_t j = 0; j < EW; ++j) {
-                            const uint32_t n = n0 + c0 + j;
-                            if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
+                            for (uint32_t j = 0; j < EW; ++j) {
+                                const uint32_t n = n0 + c0 + j;
+                                if (c0 + j < cend && n < p.T) yo[(size_t)n * ld + o] = __uint_as_float(v[j]) + bo;
+                            }
+                        }
+                    }
+                }
+            }
+        } else if constexpr (BN == 256u) {
+            // a last-wave tile in two K ranges: both write their partial
+            // sums (column-major, so that a warp's stores of one column are
+            // 128 contiguous bytes) and count themselves; the second to
+            // arrive adds the other's partial sums to its own, still in
+            // tensor memory.  x0 + x1 == x1 + x0 in IEEE arithmetic, so the
+            // result does not depend on which range arrives last.
+            float *tile_ws = p.ws + (size_t)tail * 2u * (BN * kBM);
+            if (done) {
+                float *wp = tile_ws + (size_t)trange * (BN * kBM);
+#pragma unroll 1
+                for (uint32_t c0 = cbeg; c0 < cend; c0 += EW) {
+                    uint32_t v[EW];
+                    tmem_ld<EW>(tmem + lane_base + c0, v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;");
+#pragma unroll
+                    for (uint32_t j = 0; j < EW; ++j)
+                        if (c0 + j < cend) wp[(c0 + j) * kBM + row] = __uint_as_float(v[j]);
+                }
+            }
+            __threadfence();
+            // every converter thread reaches both barriers, also after a wait
+            // gave up (it set the abort flag first); then nothing is counted
+            asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+            if (tid == 0) {
+                uint32_t last = 0;
+                if (!*abort_flag) {
+                    last = atomicAdd(p.cnt + tail, 1u) == 1u ? 1u : 0u;
+                    if (last) p.cnt[tail] = 0u;   // both ranges counted: ready for the next launch
+                }
+                *last_flag = last;
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+            if (*last_flag) {
+                __threadfence();
+                const float *other = tile_ws + (size_t)(1u - trange) * (BN * kBM);
+                const float bo = (valid && p.bias) ? __ldg(p.bias + o) : 0.0f;
+#pragma unroll 1
+                for (uint32_t c0 = cbeg; c0 < cend; c0 += EW) {
+                    uint32_t v[EW];
+                    float ot[EW];
+#pragma unroll
+                    for (uint32_t j = 0; j < EW; ++j)
+                        ot[j] = c0 + j < cend ? __ldcg(other + (c0 + j) * kBM + row) : 0.0f;
+                    tmem_ld<EW>(tmem + lane_base + c0, v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;");
+                    if (valid) {
+                        for (uint32_t k = 0; k < p.out.n; ++k) {
+#pragma unroll
+                            for (uint32_t j = 0; j < EW; ++j) {
+                                const uint32_t n = n0 + c0 + j;
+                                if (c0 + j < cend && n < p.T)
+                                    p.out.y[k][(size_t)n * p.ldy + o] = (__uint_as_float(v[j]) + ot[j]) + bo;
+                            }
                         }
                     }
                 }
@@ -756,7 +849,9 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
+    const uint32_t tiles = ((p.O + kBM - 1) / kBM) * ((p.T + BN - 1) / BN);
+    cfg.gridDim = p.tail_s ? dim3(p.n_full + (tiles - p.n_full) * p.tail_s, 1, 1)
+                           : dim3((p.O + kBM - 1) / kBM, (p.T + BN - 1) / BN, p.splits);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -791,6 +886,52 @@ float *splitk_buffer(size_t floats, cudaStream_t s)
     return b.p;
 }
 
+// Last-wave split state, one per (device, stream) like the split-K buffer:
+// partial sums of the last wave's tiles and their arrival counters.  The
+// counters start at zero when allocated and every completed tile returns its
+// counter to zero; a launch that gave up (device status set) can leave one
+// counted, so gemm_reset_tail_counters() clears them when that status is
+// taken.
+struct TailBuf {
+    float *ws = nullptr;
+    size_t cap = 0;
+    uint32_t *cnt = nullptr;
+};
+constexpr uint32_t kMaxTailTiles = 1024;
+std::mutex g_tail_mu;
+std::map<std::pair<int, cudaStream_t>, TailBuf> g_tail;
+
+bool tail_buffer(size_t floats, cudaStream_t s, float **ws, uint32_t **cnt)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return false; }
+    std::lock_guard<std::mutex> lk(g_tail_mu);
+    TailBuf &b = g_tail[{dev, s}];
+    if (!b.cnt) {
+        if (cudaMalloc(&b.cnt, kMaxTailTiles * sizeof(uint32_t)) != cudaSuccess) {
+            cudaGetLastError();
+            b.cnt = nullptr;
+            return false;
+        }
+        if (cudaMemsetAsync(b.cnt, 0, kMaxTailTiles * sizeof(uint32_t), s) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(b.cnt);
+            b.cnt = nullptr;
+            return false;
+        }
+    }
+    if (b.cap < floats) {
+        if (b.ws) { cudaStreamSynchronize(s); cudaFree(b.ws); }
+        b.ws = nullptr;
+        b.cap = 0;
+        if (cudaMalloc(&b.ws, floats * sizeof(float)) != cudaSuccess) { cudaGetLastError(); return false; }
+        b.cap = floats;
+    }
+    *ws = b.ws;
+    *cnt = b.cnt;
+    return true;
+}
+
 // Chain state of the batch being launched on this host thread: whether the
 // last kernel it put on `s` was an unsplit GEMM.
 struct Chain {
@@ -802,6 +943,16 @@ thread_local Chain g_chain;
 }  // namespace gemm
 
 void gemm_chain_begin(cudaStream_t s) { gemm::g_chain = gemm::Chain{true, false, s}; }
+
+void gemm_reset_tail_counters()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return; }
+    std::lock_guard<std::mutex> lk(gemm::g_tail_mu);
+    for (auto &kv : gemm::g_tail)
+        if (kv.first.first == dev && kv.second.cnt)
+            if (cudaMemset(kv.second.cnt, 0, gemm::kMaxTailTiles * sizeof(uint32_t)) != cudaSuccess) cudaGetLastError();
+}
 void gemm_chain_end() { gemm::g_chain = gemm::Chain{}; }
 void gemm_chain_break() { gemm::g_chain.prev_gemm = false; }
 
@@ -838,6 +989,27 @@ int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
     p.part = part;
     gemm::Chain &ch = gemm::g_chain;
     const bool in_batch = ch.active && ch.s == s;
+    // Last-wave split: when whole waves of tiles leave a last wave that
+    // fills at most half of the GPU, its tiles are split along K into two
+    // ranges: 512 tiles of 128 x 256 on 148 SMs run as 3 waves and one of
+    // half-length tiles instead of 4 waves.  Not inside a batch, whose GEMMs
+    // already overlap one another's last waves; only for the 256-token tiles
+    // (the smaller ones are split along K whenever they leave SMs idle).
+    p.tiles_m = (O + gemm::kBM - 1) / gemm::kBM;
+    p.n_full = tiles;
+    p.tail_s = 0;
+    if (bn == 256u && splits == 1 && !in_batch && tiles > resident && KT >= 8u) {
+        const uint32_t rem = tiles % resident;
+        if (rem != 0 && rem * 2u <= resident && rem <= gemm::kMaxTailTiles) {
+            float *ws = nullptr;
+            uint32_t *cnt = nullptr;
+            if (!gemm::tail_buffer((size_t)rem * 2u * gemm::kBM * bn, s, &ws, &cnt)) return -1;
+            p.n_full = tiles - rem;
+            p.tail_s = 2;
+            p.ws = ws;
+            p.cnt = cnt;
+        }
+    }
     p.chain = in_batch && ch.prev_gemm && splits == 1 ? 1u : 0u;
     if (in_batch) ch.prev_gemm = false;   // set again below on an unsplit launch
     int r;
@@ -909,6 +1081,7 @@ extern "C" int hxq_cuda_affine_device_status(void)
     if (v) {
         const uint32_t z = 0;
         cudaMemcpyToSymbol(hxq::gemm::g_gemm_err, &z, sizeof(z));
+        hxq::gemm_reset_tail_counters();
     }
     const uint32_t tc = hxq::tc_gemv_status_take(), vq = hxq::vq_tc_status_take();
     if (tc == 0xFFFFFFFFu || vq == 0xFFFFFFFFu) return -1;

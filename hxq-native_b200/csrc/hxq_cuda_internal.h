@@ -166,6 +166,9 @@ cudaError_t launch_vq_gemv(const uint8_t *idx, const float *cb, const uint32_t *
 void gemm_chain_begin(cudaStream_t s);
 void gemm_chain_end();
 void gemm_chain_break();
+// Zero the tcgen05 GEMMs' last-wave counters of the current device (after a
+// launch gave up; the device must be idle).
+void gemm_reset_tail_counters();
 struct GemmChainScope {
     explicit GemmChainScope(cudaStream_t s) { gemm_chain_begin(s); }
     ~GemmChainScope() { gemm_chain_end(); }

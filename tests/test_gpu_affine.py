@@ -172,6 +172,33 @@ def test_tcgen05_gemm_shapes(H, L, oracle, cuda, O, I, gs, N):
     _check(y, yd, sc, 1e-4)
 
 
+def test_gemm_last_wave_split(H, L, oracle, cuda):
+    """2400 x 2048 at 2000 tokens: 19 x 8 = 152 tiles of 128 x 256 on 148
+    SMs, so the last 4 tiles (row tiles 15-18, the last ragged in rows, of the
+    last, ragged token tile) are split along K into 4 ranges whose partial
+    sums the last arriving CTA adds in order.  Sampled token rows cover whole
+    tiles and split ones; the result is the same on every run."""
+    O, I, gs, N = 2400, 2048, 128, 2000
+    d = synth.affine(O, I, gs, 2400, bias=True)
+    xh, x = synth.activations(N, I, 2401)
+    dev = Dev(cuda, d, d["bias"])
+    y = _run_bf16(cuda, H, L, dev, xh, path=H.HXQ_AFFINE_PATH_GEMM)
+    y2 = _run_bf16(cuda, H, L, dev, xh, path=H.HXQ_AFFINE_PATH_GEMM)
+    assert L.hxq_cuda_affine_device_status() == 0
+    assert np.array_equal(y, y2)
+    ng = I // gs
+    q = d["codes"].reshape(O, I).astype(np.float64)
+    s64 = np.repeat(d["scales"].reshape(O, ng).astype(np.float64), gs, axis=1)
+    f64 = np.repeat(d["offsets"].reshape(O, ng).astype(np.float64), gs, axis=1)
+    Wb = synth.bf16_to_f32(synth.bf16_round((q * s64 + f64).astype(np.float32))).astype(np.float64).reshape(O, I)
+    for n in (0, 1000, 1791, 1792, 1900, 1999):
+        ref = oracle.affine_matmul(x, d, bias=d["bias"], n0=n, n1=n + 1)
+        sc = _scale(oracle, x[n:n + 1], d)
+        _check(y[n:n + 1], ref, sc, GEMM_TOL)
+        yd = x[n:n + 1].astype(np.float64) @ Wb.T + d["bias"].astype(np.float64)
+        _check(y[n:n + 1], yd, sc, 1e-4)
+
+
 @pytest.mark.parametrize("shape", [(2048, 2048), (11008, 2048), (2048, 11008)])
 def test_reference_shapes_6bit_codes(H, L, oracle, cuda, shape):
     # test/test_affine_cuda.cu:194-272 shapes at N=1 with 6-bit codes

@@ -117,6 +117,36 @@ def test_gemm_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
     _check(y, oracle.dense_matmul_f64(x, Wb), sc, 1e-4)
 
 
+def test_gemm_last_wave_split(H, L, oracle, cuda):
+    """2400 x 2048 at 2000 tokens: 152 tiles of 128 x 256 on 148 SMs; the
+    last 4 (ragged rows and tokens) are split along K into 4 ranges added in
+    order by the last arriving CTA.  Sampled token rows cover whole and split
+    tiles; repeated and out-of-range sidecar entries; the same result on
+    every run."""
+    out_f, in_f, N = 2400, 2048, 2000
+    d = synth.vq12(out_f, in_f, 2402)
+    d = _with_dups_and_oob(d, 2402)
+    err, w, _ = oracle.decompress(d)
+    assert err == 0
+    W = w.reshape(out_f, in_f)
+    xh, x = synth.activations(N, in_f, 2403)
+    t = H.Tensor().load(d)
+    img = _image(H, L, t, 0, out_f)
+    try:
+        y = _run(cuda, L, img, xh, out_f, path=1)
+        y2 = _run(cuda, L, img, xh, out_f, path=1)
+    finally:
+        L.hxq_cuda_image_destroy(img)
+    assert L.hxq_cuda_affine_device_status() == 0
+    assert np.array_equal(y, y2)
+    Wb = synth.bf16_to_f32(synth.bf16_round(W)).reshape(out_f, in_f)
+    rows = [0, 1000, 1791, 1792, 1900, 1999]
+    xs = x[rows]
+    sc = _scale(xs, W)
+    _check(y[rows], oracle.dense_matmul(xs, W), sc, GEMM_TOL)
+    _check(y[rows], oracle.dense_matmul_f64(xs, Wb), sc, 1e-4)
+
+
 @pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 1), (256, 512, 2), (300, 1024, 3), (17, 128, 7), (4096, 4096, 1),
                                           (11008, 4096, 1), (4096, 11008, 2), (513, 2048, 8), (64, 4096, 5),
                                           (256, 512, 9), (300, 1024, 12), (17, 128, 16), (4096, 4096, 16)])

@@ -909,12 +909,13 @@ hxq_error_t decompress_sync(hxq_tensor_t *t, void *d_out, int bf16, float *l2)
         if ((err = get_scratch(dev, (cudaStream_t)0, &sc)) != HXQ_OK) return err;
     }
     const size_t off0 = 0;
-    err = launch_images(&img, 1, d_out, &off0, bf16, sc->sumsq, sc->conf, dev, (cudaStream_t)0);
+    // The drop-in API reports the reference's own value (see
+    // collect_sidecar), which the image carries; the exact sum of squares is
+    // not asked for, so the kernel skips its cross-CTA reduction.
+    err = launch_images(&img, 1, d_out, &off0, bf16, nullptr, sc->conf, dev, (cudaStream_t)0);
     if (err != HXQ_OK) return err;
-    float gpu_l2 = 0.0f;
-    if ((err = sync_and_check(dev, (cudaStream_t)0, &gpu_l2)) != HXQ_OK) return err;
-    // The drop-in API reports the reference's own value (see collect_sidecar);
-    // the kernel's fused fp64 reduction (gpu_l2) is the exact one.
+    float gpu_conf = 0.0f;
+    if ((err = sync_and_check(dev, (cudaStream_t)0, &gpu_conf)) != HXQ_OK) return err;
     *l2 = img->ref_l2;
     return HXQ_OK;
 }

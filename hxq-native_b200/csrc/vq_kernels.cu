@@ -320,6 +320,12 @@ __device__ __forceinline__ void finish_unit(const VqLaunch &p, uint32_t j, uint3
                                             const double *red, uint32_t lane)
 {
     const VqJob &J = p.job[j];
+    if (!J.sumsq) {
+        // no exact sum requested: the confidence is the image's own value,
+        // stored by the job's first unit; no slots, counters or fences
+        if (lane == 0 && u == J.unit_begin && J.conf) *J.conf = J.ref_conf;
+        return;
+    }
     uint32_t last = 0;
     if (lane == 0) {
         double s = 0.0;
@@ -369,10 +375,18 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
 
     // Units are handed out by an atomic counter, two ahead of use, so a
     // warp knows its next chunk (and prefetches it) while it works on the
-    // current one, and faster SMs simply take more units.
+    // current one, and faster SMs simply take more units.  A launch with one
+    // CTA per unit (small tensors) takes unit blockIdx.x without the counter,
+    // whose round trips would sit on its critical path.
+    const bool one_each = total <= gridDim.x;
     if (tid == 0) {
-        s_unit[0] = atomicAdd(p.work, 1u);
-        s_unit[1] = s_unit[0] < total ? atomicAdd(p.work, 1u) : total;
+        if (one_each) {
+            s_unit[0] = blockIdx.x;
+            s_unit[1] = total;
+        } else {
+            s_unit[0] = atomicAdd(p.work, 1u);
+            s_unit[1] = s_unit[0] < total ? atomicAdd(p.work, 1u) : total;
+        }
     }
     __syncthreads();
 
@@ -397,7 +411,7 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
             cb_job = j;
         }
         const uint32_t un = s_unit[(it + 1u) % 3u];
-        if (tid == 0) s_unit[(it + 2u) % 3u] = un < total ? atomicAdd(p.work, 1u) : total;
+        if (tid == 0) s_unit[(it + 2u) % 3u] = (un < total && !one_each) ? atomicAdd(p.work, 1u) : total;
         const uint32_t jn = un < total ? job_of_unit(p, j, un) : j;
         const uint32_t ubase = (u - p.job[j].unit_begin) * unit_chunks + warp;
         double acc = 0.0;
@@ -442,7 +456,7 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
         j = jn;
     }
     if (CHECK_K && errflag) atomicOr(p.err, errflag);
-    if (tid == 0) {  // the last CTA out leaves the work counters at zero
+    if (tid == 0 && !one_each) {  // the last CTA out leaves the work counters at zero
         __threadfence();
         if (atomicAdd(p.work + 1, 1u) + 1u == gridDim.x) {
             p.work[0] = 0u;

@@ -106,6 +106,9 @@ constexpr uint32_t kErrIndexOOB = 1u;
 cudaError_t configure_vq_kernels();
 cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
                            int check_k, cudaStream_t s);
+// Kernels launch_vq_fast puts on the stream: 1, or 2 when a job requests the
+// exact sum of squares (the ordered reduction runs as a second kernel).
+uint32_t vq_fast_launches(const VqLaunch &p);
 uint32_t    fast_grid(uint64_t total_chunks, int sms, uint32_t kind);
 // Chunks per warp for a launch of `chunks` chunks in total: 2, or 1 when
 // units of two would not give every resident CTA about four of them.

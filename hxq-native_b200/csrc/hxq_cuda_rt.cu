@@ -766,7 +766,7 @@ hxq_error_t launch_fast_group(const std::vector<uint32_t> &which,
     p.err = sc.err;
     const hxq_cuda_image *first = imgs[which[0]];
     const cudaError_t e = launch_vq_fast(p, first->kind, bf16, first->check_k ? 1 : 0, s);
-    if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e == cudaSuccess) g_launches.fetch_add(vq_fast_launches(p), std::memory_order_relaxed);
     return map_cuda(e);
 }
 

@@ -311,52 +311,27 @@ __device__ __forceinline__ uint32_t job_of_unit(const VqLaunch &p, uint32_t j, u
     return j;
 }
 
-// Warp 0, after the CTA barrier that completed unit u: lane 0 adds the eight
-// warp partials in order into the unit's slot; the warp that finishes a
-// job's last unit adds the job's slots in a fixed order (per-lane strided
-// sums, then a fixed butterfly), so the result does not depend on which SM
-// ran what.
+// A unit's warp partials are added in order into the unit's slot (lane 0
+// of warp 0, after the CTA barrier that completed the unit).  The slots are
+// added per job by sumsq_reduce_kernel, launched after this kernel on the
+// same stream: no fences or counters here, whose round trips stalled the
+// CTA at its next barrier and, for the last job, sat on the launch's tail
+// (7B layer: 173.3 us with them, 162.7 without).  Without a requested
+// exact sum the job's first unit stores the confidence (the image's own
+// value).
 __device__ __forceinline__ void finish_unit(const VqLaunch &p, uint32_t j, uint32_t u,
                                             const double *red, uint32_t lane)
 {
     const VqJob &J = p.job[j];
+    if (lane != 0) return;
     if (!J.sumsq) {
-        // no exact sum requested: the confidence is the image's own value,
-        // stored by the job's first unit; no slots, counters or fences
-        if (lane == 0 && u == J.unit_begin && J.conf) *J.conf = J.ref_conf;
+        if (u == J.unit_begin && J.conf) *J.conf = J.ref_conf;
         return;
     }
-    uint32_t last = 0;
-    if (lane == 0) {
-        double s = 0.0;
+    double s = 0.0;
 #pragma unroll
-        for (uint32_t w = 0; w < kWarps; ++w) s += red[w];
-        p.slots[u] = s;
-        __threadfence();
-        last = (atomicAdd(p.counters + j, 1u) + 1u == J.n_units) ? 1u : 0u;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    // eight independent loads in flight per lane, then a fixed-order combine
-    double part[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) part[q] = 0.0;
-    const double *sl = p.slots + J.unit_begin;
-    for (uint32_t i0 = 0; i0 < J.n_units; i0 += 256u) {
-#pragma unroll
-        for (uint32_t q = 0; q < 8u; ++q) {
-            const uint32_t i = i0 + q * 32u + lane;
-            if (i < J.n_units) part[q] += __ldcg(sl + i);
-        }
-    }
-    double t = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
-    t = warp_sum(t);
-    if (lane == 0) {
-        if (J.sumsq) *J.sumsq = t;
-        if (J.conf) *J.conf = J.ref_conf;
-        p.counters[j] = 0u;  // leave scratch zeroed for the next launch
-    }
+    for (uint32_t w = 0; w < kWarps; ++w) s += red[w];
+    p.slots[u] = s;
 }
 
 template <uint32_t KIND, bool BF16, bool CHECK_K>
@@ -461,6 +436,42 @@ vq_fast_kernel(const __grid_constant__ VqLaunch p)
         if (atomicAdd(p.work + 1, 1u) + 1u == gridDim.x) {
             p.work[0] = 0u;
             p.work[1] = 0u;
+        }
+    }
+}
+
+// The exact sum of squared sidecar deltas of job blockIdx.x (when
+// requested): its unit slots added in a fixed order -- thread i sums slots
+// i, i + 256, ... in order, eight loads in flight, then warp 0 adds eight
+// per lane in order and the lanes by a fixed butterfly -- so the result does
+// not depend on which SM ran which unit.  Stores the sum and the confidence.
+__global__ void __launch_bounds__(kThreads) sumsq_reduce_kernel(const __grid_constant__ VqLaunch p)
+{
+    __shared__ double red[kThreads];
+    const VqJob &J = p.job[blockIdx.x];
+    if (!J.sumsq) return;
+    const uint32_t tid = threadIdx.x;
+    const double *sl = p.slots + J.unit_begin;
+    double v[8];
+#pragma unroll
+    for (uint32_t q = 0; q < 8u; ++q) {
+        const uint32_t i = tid + q * kThreads;
+        v[q] = i < J.n_units ? sl[i] : 0.0;
+    }
+    double t = 0.0;
+#pragma unroll
+    for (uint32_t q = 0; q < 8u; ++q) t += v[q];
+    for (uint32_t i = tid + 8u * kThreads; i < J.n_units; i += kThreads) t += sl[i];
+    red[tid] = t;
+    __syncthreads();
+    if (tid < 32u) {
+        double w = 0.0;
+#pragma unroll
+        for (uint32_t q = 0; q < kThreads / 32u; ++q) w += red[tid * (kThreads / 32u) + q];
+        w = warp_sum(w);
+        if (tid == 0) {
+            *J.sumsq = w;
+            if (J.conf) *J.conf = J.ref_conf;
         }
     }
 }
@@ -662,14 +673,29 @@ uint32_t fast_grid(uint64_t total_units, int sms, uint32_t kind)
 cudaError_t launch_vq_fast(const VqLaunch &p, uint32_t kind, int bf16,
                            int check_k, cudaStream_t s)
 {
+    cudaError_t e;
     if (kind == kKindVq12) {
-        if (bf16) return check_k ? launch_one<kKindVq12, true, true>(p, s)
-                                 : launch_one<kKindVq12, true, false>(p, s);
-        return check_k ? launch_one<kKindVq12, false, true>(p, s)
-                       : launch_one<kKindVq12, false, false>(p, s);
+        if (bf16) e = check_k ? launch_one<kKindVq12, true, true>(p, s)
+                              : launch_one<kKindVq12, true, false>(p, s);
+        else e = check_k ? launch_one<kKindVq12, false, true>(p, s)
+                         : launch_one<kKindVq12, false, false>(p, s);
+    } else {
+        e = bf16 ? launch_one<kKindScalar, true, false>(p, s)
+                 : launch_one<kKindScalar, false, false>(p, s);
     }
-    return bf16 ? launch_one<kKindScalar, true, false>(p, s)
-                : launch_one<kKindScalar, false, false>(p, s);
+    if (e != cudaSuccess) return e;
+    bool sums = false;
+    for (uint32_t j = 0; j < p.n_jobs; ++j) sums |= p.job[j].sumsq != nullptr;
+    if (!sums) return cudaSuccess;
+    sumsq_reduce_kernel<<<p.n_jobs, kThreads, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+uint32_t vq_fast_launches(const VqLaunch &p)
+{
+    for (uint32_t j = 0; j < p.n_jobs; ++j)
+        if (p.job[j].sumsq) return 2u;
+    return 1u;
 }
 
 cudaError_t launch_generic(const GenericJob &j, const Scratch &sc, cudaStream_t s)

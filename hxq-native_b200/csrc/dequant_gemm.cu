@@ -291,6 +291,35 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+__device__ __forceinline__ uint64_t f32x2_splat(float f)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(f));
+    return r;
+}
+
+// Codes i and i + 1 (bytes of `word`) as bf16 weights RN(fma(code, s, off))
+// packed into one word (code i in the low half), two fp32 lanes at a time:
+// a byte permute puts each code into the float 2^23 + code, a packed
+// subtraction of 2^23 makes it exact, a packed fma rounds each weight once,
+// as two scalar fmaf would.  Half the fp32 instructions of the scalar form.
+__device__ __forceinline__ uint32_t code_pair_bf16(uint32_t word, uint32_t i, uint64_t s2, uint64_t o2)
+{
+    const uint32_t m0 = __byte_perm(word, 0x4B000000u, 0x7440u + i);
+    const uint32_t m1 = __byte_perm(word, 0x4B000000u, 0x7441u + i);
+    uint32_t out;
+    asm("{\n\t.reg .b64 c, m;\n\t.reg .f32 lo, hi;\n\t"
+        "mov.b64 c, {%1, %2};\n\t"
+        "mov.b64 m, {%5, %5};\n\t"
+        "sub.rn.f32x2 c, c, m;\n\t"
+        "fma.rn.f32x2 c, c, %3, %4;\n\t"
+        "mov.b64 {lo, hi}, c;\n\t"
+        "cvt.rn.bf16x2.f32 %0, hi, lo;\n\t}"
+        : "=r"(out)
+        : "r"(m0), "r"(m1), "l"(s2), "l"(o2), "r"(0x4B000000u));
+    return out;
+}
+
 struct Params {
     // affine weights
     const uint8_t *codes;     // [O, I]
@@ -517,6 +546,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
                 const float sc = sq, of = oq;
+                const uint64_t s2 = BN >= 256 ? f32x2_splat(sc) : 0ull, o2 = BN >= 256 ? f32x2_splat(of) : 0ull;
                 fetch(kt + 4u, sq, oq);
                 uint32_t v[32];
 #pragma unroll
@@ -524,12 +554,19 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const float f0 = fmaf(code_f32(w4[j], 0), sc, of);
-                        const float f1 = fmaf(code_f32(w4[j], 1), sc, of);
-                        const float f2 = fmaf(code_f32(w4[j], 2), sc, of);
-                        const float f3 = fmaf(code_f32(w4[j], 3), sc, of);
-                        v[8 * i + 2 * j] = bf16x2(f0, f1);
-                        v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
+                        if constexpr (BN >= 256) {
+                            v[8 * i + 2 * j] = code_pair_bf16(w4[j], 0u, s2, o2);
+                            v[8 * i + 2 * j + 1] = code_pair_bf16(w4[j], 2u, s2, o2);
+                        } else {
+                            // (the two-CTA tiles have no registers to spare
+                            // for the packed operands)
+                            const float f0 = fmaf(code_f32(w4[j], 0), sc, of);
+                            const float f1 = fmaf(code_f32(w4[j], 1), sc, of);
+                            const float f2 = fmaf(code_f32(w4[j], 2), sc, of);
+                            const float f3 = fmaf(code_f32(w4[j], 3), sc, of);
+                            v[8 * i + 2 * j] = bf16x2(f0, f1);
+                            v[8 * i + 2 * j + 1] = bf16x2(f2, f3);
+                        }
                     }
                 }
                 if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;

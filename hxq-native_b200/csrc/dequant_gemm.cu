@@ -334,6 +334,11 @@ struct Params {
     const uint32_t *rb;
     const uint16_t *kp;
     const uint32_t *e4;
+    // (tiles of 256 tokens) the same patches grouped per 32 rows and half
+    // step: group g = (row / 32) * (I / 64) + col / 64 is g4[gp[g] ..
+    // gp[g + 1]), each (row % 32) << 22 | (col % 64) << 16 | bf16
+    const uint32_t *g4;
+    const uint32_t *gp;
     OutPtrs out;              // the [T, ldy] outputs (all get the same values)
     float *part;              // [splits][T, O] partial sums when splits > 1
     uint32_t T, I, O, gs, ldy;
@@ -582,9 +587,104 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (ok && kt + 2u < KT) ok = step(kt + 2u, sq2, oq2);
                 if (ok && kt + 3u < KT) ok = step(kt + 3u, sq3, oq3);
             }
+        } else if constexpr (SA) {
+            // VQ, tiles of 256 tokens: A tiles in shared memory.  The image's
+            // bf16 codebook, one 32-bit pair per entry: an index gathers one
+            // packed pair of the A row.
+            for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
+                reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
+            // Sidecar patches by warp: warp (q, h) owns rows 32q .. 32q + 31
+            // of the tile and half h of each K step, which is one group of
+            // the grouped table; after its rows are stored, lane i applies
+            // the group's entry i (one 2-byte store into the A tile; past 32
+            // entries, again).  A lane per row walking its own row's patches
+            // made the warp loop as often as its busiest row (sidecar
+            // patching was 17% of the 4096 x 4096 launch at 2048 tokens).
+            // The group offsets sit in four slots, each refilled four steps
+            // ahead; a step's first 32 entries (one per lane) in one of two
+            // registers, loaded two steps ahead.  The loop is unrolled by four
+            // so that the slots are fixed registers: a register holding a load
+            // in flight is never copied (a copy would wait for the load).
+            const uint32_t NH = p.I / 64u;
+            const uint32_t grp = o0 / 32u + q;
+            const bool gvalid = grp * 32u < p.O;
+            const uint32_t *gpp = p.gp + (size_t)(gvalid ? grp : 0u) * NH + 2u * kt_lo + h;
+            auto gload = [&](uint32_t k) -> uint2 {
+                return (gvalid && k < KT) ? make_uint2(__ldg(gpp + 2u * k), __ldg(gpp + 2u * k + 1u))
+                                          : make_uint2(0u, 0u);
+            };
+            auto eload = [&](uint2 r) -> uint32_t { return lane < r.y - r.x ? __ldg(p.g4 + r.x + lane) : 0u; };
+            uint2 gq0 = gload(0), gq1 = gload(1), gq2 = gload(2), gq3 = gload(3);
+            uint32_t ea = KT > 0 ? eload(gq0) : 0u, ez = KT > 1 ? eload(gq1) : 0u;
+            asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+            // one K step: g_cur the group offsets of step kt (its slot,
+            // refilled with step kt + 4's), g_2 those of step kt + 2, E this
+            // lane's first entry of step kt (refilled with step kt + 2's);
+            // false if a wait ran out
+            auto step = [&](uint32_t kt, uint2 &g_cur, uint2 g_2, uint32_t &E) -> bool {
+                const uint32_t b = kt & 1u, sw = kt % W;
+                // 64 weights = 16 byte triples = 3 x 16 bytes of this thread's
+                // row of the weight ring stage (96 B per row)
+                if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) return false;
+                uint4 cn[3];
+                const unsigned char *wr = wring + sw * WB + row * 96u + h * 48u;
+#pragma unroll
+                for (uint32_t i = 0; i < 3u; ++i) cn[i] = *reinterpret_cast<const uint4 *>(wr + 16u * i);
+                async_proxy_fence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(w_empty + sw);
+                const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
+                                        cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
+                uint32_t v[32];
+#pragma unroll
+                for (uint32_t t = 0; t < 16u; ++t) {
+                    const uint32_t byte = 3u * t, wq = byte >> 2;
+                    const uint32_t B = __byte_perm(w[wq], w[wq + 1u < 12u ? wq + 1u : 11u], 0x3012u + (byte & 3u) * 0x1111u);
+                    v[2u * t] = cbh[(B >> 12) & 0xFFFu];
+                    v[2u * t + 1u] = cbh[B & 0xFFFu];
+                }
+                // this thread's 128 bytes of the A tile: row `row` of half h,
+                // 16-byte unit u at (u ^ (row & 7)) << 4
+                __syncwarp();
+                if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
+                unsigned char *ah = abuf + b * kABytes + h * (kBM * 128u);
+                unsigned char *arow = ah + row * 128u;
+#pragma unroll
+                for (uint32_t u = 0; u < 8u; ++u)
+                    *reinterpret_cast<uint4 *>(arow + ((u ^ (row & 7u)) << 4)) =
+                        make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
+                // the warp's patches: the reference's fp32 value rounded once
+                // to bf16, over the codebook pair's half, once all the warp's
+                // rows are stored
+                __syncwarp();
+                const uint32_t n = g_cur.y - g_cur.x;
+                unsigned char *ag = ah + (32u * q) * 128u;
+                auto apply = [&](uint32_t e) {
+                    const uint32_t r = (e >> 22) & 31u, lc = (e >> 16) & 63u;
+                    *reinterpret_cast<uint16_t *>(ag + r * 128u + ((((lc >> 3) ^ (r & 7u)) << 4) | ((lc & 7u) << 1))) =
+                        (uint16_t)e;
+                };
+                if (lane < n) apply(E);
+#pragma unroll 1
+                for (uint32_t base = 32u; base < n; base += 32u)
+                    if (base + lane < n) apply(__ldg(p.g4 + g_cur.x + base + lane));
+                // the generic-proxy stores, visible to the tensor cores' reads
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(a_full + b);
+                if (kt + 2u < KT) E = eload(g_2);
+                g_cur = gload(kt + 4u);
+                return true;
+            };
+            for (uint32_t kt = 0; kt < KT && ok; kt += 4u) {
+                ok = step(kt, gq0, gq2, ea);
+                if (ok && kt + 1u < KT) ok = step(kt + 1u, gq1, gq3, ez);
+                if (ok && kt + 2u < KT) ok = step(kt + 2u, gq2, gq0, ea);
+                if (ok && kt + 3u < KT) ok = step(kt + 3u, gq3, gq1, ez);
+            }
         } else {
-            // the image's bf16 codebook, one 32-bit pair per entry: an
-            // index gathers exactly one TMEM column (low half = even k)
+            // VQ, tiles of up to 128 tokens: A into tensor memory.  The
+            // image's bf16 codebook, one 32-bit pair per entry: an index
+            // gathers exactly one TMEM column (low half = even k)
             for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
                 reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
             // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
@@ -641,30 +741,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 // with the reference's fp32 value rounded once to bf16
                 const uint32_t k0 = (kt_lo + kt) * kBK + h * 64u;
                 uint32_t r0 = P[0], r1 = P[1], r2 = P[2], r3 = P[3];
-                if constexpr (SA) {
-                    // this thread's 128 bytes of the A tile: row `row` of half h,
-                    // 16-byte unit u at (u ^ (row & 7)) << 4; then the patches,
-                    // one 2-byte store each, into the same bytes
-                    __syncwarp();
-                    if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
-                    unsigned char *arow = abuf + b * kABytes + h * (kBM * 128u) + row * 128u;
-#pragma unroll
-                    for (uint32_t u = 0; u < 8u; ++u)
-                        *reinterpret_cast<uint4 *>(arow + ((u ^ (row & 7u)) << 4)) =
-                            make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
-#pragma unroll 1
-                    for (uint32_t i = 0; i < n_cur; ++i) {
-                        const uint32_t q = i < 4u ? r0 : __ldg(p.e4 + pb + lo_cur + i);
-                        r0 = r1; r1 = r2; r2 = r3;
-                        const uint32_t local = (q & 0xFFFFu) - k0;
-                        if (local < 64u)
-                            *reinterpret_cast<uint16_t *>(arow + ((((local >> 3) ^ (row & 7u)) << 4) | ((local & 7u) << 1))) =
-                                (uint16_t)(q >> 16);
-                    }
-                    // the generic-proxy stores, visible to the tensor cores' reads
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive(a_full + b);
-                } else {
+                {
 #pragma unroll 1
                     for (uint32_t i = 0; i < n_cur; ++i) {
                         const uint32_t q = i < 4u ? r0 : __ldg(p.e4 + pb + lo_cur + i);
@@ -1094,15 +1171,16 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
 // [T, I], y fp32 [T, ldy].  Returns 1 when the shape is not one it takes, 0
 // on launch, -1 on error.
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
-                 const uint16_t *kp, const uint32_t *e4, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O,
-                 uint32_t ldy, cudaStream_t s)
+                 const uint16_t *kp, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
+                 const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O, uint32_t ldy, cudaStream_t s)
 {
     if (T == 0 || O == 0) return 1;
     if (I == 0 || I % gemm::kBK != 0 || ldy < O) return 1;
     if (((uintptr_t)x & 15u) || ((uintptr_t)idx & 15u) || ((uintptr_t)cbh & 15u)) return 1;
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
     gemm::Params p{};
-    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4;
+    if (!g4 || !gp) return 1;
+    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4; p.g4 = g4; p.gp = gp;
     if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
     p.T = T; p.I = I; p.O = O; p.gs = 0; p.ldy = ldy;
     return run<true>(x, p, out, s);

@@ -65,8 +65,10 @@ struct hxq_cuda_image {
     // and per patch bf16(final weight) - bf16(codebook value) in fp32
     bool      has_mm = false;
     // and the tensor-core GEMV's own index stream (build_tc_stream)
-    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0, o_tx = 0;
-    uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr;
+    // and the same patches grouped per 32 rows and 64-wide half step for
+    // the tcgen05 GEMM's 256-token tiles (build_patches)
+    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0, o_tx = 0, o_g4 = 0, o_gp = 0;
+    uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr, *d_g4 = nullptr, *d_gp = nullptr;
     uint16_t *d_kp = nullptr, *d_tx = nullptr;
     float    *d_ed = nullptr;
     uint32_t  n_patch = 0;
@@ -311,6 +313,8 @@ void bind_image(hxq_cuda_image *img, void *base)
         img->d_e4 = reinterpret_cast<uint32_t *>(b + img->o_e4);
         img->d_ed = reinterpret_cast<float *>(b + img->o_ed);
         img->d_tx = reinterpret_cast<uint16_t *>(b + img->o_tx);
+        img->d_g4 = reinterpret_cast<uint32_t *>(b + img->o_g4);
+        img->d_gp = reinterpret_cast<uint32_t *>(b + img->o_gp);
     }
 }
 
@@ -334,10 +338,19 @@ float bf16_to_float(uint32_t h)
     return f;
 }
 
+// The fused matmuls' patch tables (see hxq_cuda_image): per distinct
+// sidecar position of rows [0, rows) col | bf16(final weight) << 16 (e4, rows
+// in order) and bf16(final) - bf16(codebook value) (ed); per row its first
+// entry (rb); per (row, 128-wide K step) the offset of the step's first
+// entry from the row's (kp); and the same entries grouped per 32 rows and
+// 64-wide half step for the tcgen05 GEMM's 256-token tiles (a converter
+// warp's rows and half of a K step): group g = (row / 32) * (in_f / 64) +
+// col / 64 holds g4[gp[g] .. gp[g + 1]), each (row % 32) << 22 | (col % 64)
+// << 16 | bf16(final).
 bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows, uint32_t in_f,
                    const std::vector<HostEntry> &ents, std::vector<uint32_t> &cbh,
                    std::vector<uint32_t> &rb, std::vector<uint16_t> &kp, std::vector<uint32_t> &e4,
-                   std::vector<float> &ed)
+                   std::vector<float> &ed, std::vector<uint32_t> &g4, std::vector<uint32_t> &gp)
 {
     const uint32_t KT = in_f / 128u;
     const size_t row_bytes = (size_t)(in_f / 4u) * 3u;
@@ -374,6 +387,17 @@ bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows
             if (f - e > 0xFFFFu) return false;
             kp[(size_t)r * (KT + 1u) + kt] = (uint16_t)(f - e);
         }
+    }
+    const uint32_t NH = in_f / 64u;
+    const size_t n_groups = (size_t)((rows + 31u) / 32u) * NH;
+    gp.assign(n_groups + 1u, 0u);
+    for (size_t i = 0; i < e4.size(); ++i) ++gp[(size_t)(erow[i] / 32u) * NH + (e4[i] & 0xFFFFu) / 64u + 1u];
+    for (size_t g = 0; g < n_groups; ++g) gp[g + 1u] += gp[g];
+    g4.assign(e4.size(), 0u);
+    std::vector<uint32_t> fill(gp.begin(), gp.end() - 1);
+    for (size_t i = 0; i < e4.size(); ++i) {
+        const uint32_t c = e4[i] & 0xFFFFu;
+        g4[fill[(size_t)(erow[i] / 32u) * NH + c / 64u]++] = ((erow[i] & 31u) << 22) | ((c & 63u) << 16) | (e4[i] >> 16);
     }
     return true;
 }
@@ -612,13 +636,13 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
     img->n_ent = (uint32_t)dev_ents.size();
 
-    std::vector<uint32_t> mm_cbh, mm_rb, mm_e4;
+    std::vector<uint32_t> mm_cbh, mm_rb, mm_e4, mm_g4, mm_gp;
     std::vector<uint16_t> mm_kp, mm_tx;
     std::vector<float> mm_ed;
     if (matmul && img->kind == kKindVq12 && !img->check_k && img->k == 4096u && img->in_f % 128u == 0u &&
         img->in_f <= 65536u)
         img->has_mm = build_patches(t, t->indices_raw + idx_off, img->rows, img->in_f, ents, mm_cbh, mm_rb,
-                                    mm_kp, mm_e4, mm_ed);
+                                    mm_kp, mm_e4, mm_ed, mm_g4, mm_gp);
     if (img->has_mm) build_tc_stream(t->indices_raw + idx_off, img->rows, img->in_f, mm_tx);
     img->n_patch = (uint32_t)mm_e4.size();
 
@@ -643,6 +667,8 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         img->o_e4 = off;   off = align256(off + (mm_e4.size() + 4) * 4);   // + speculative-read slack
         img->o_ed = off;   off = align256(off + std::max<size_t>(mm_ed.size(), 1) * 4);
         img->o_tx = off;   off = align256(off + std::max<size_t>(mm_tx.size(), 8) * 2);
+        img->o_g4 = off;   off = align256(off + std::max<size_t>(mm_g4.size(), 1) * 4);
+        img->o_gp = off;   off = align256(off + mm_gp.size() * 4);
     }
     img->block_bytes = off;
     img->has_cb = cb_floats > 0;
@@ -674,6 +700,8 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
         if (!mm_e4.empty()) std::memcpy(hb + img->o_e4, mm_e4.data(), mm_e4.size() * 4);
         if (!mm_ed.empty()) std::memcpy(hb + img->o_ed, mm_ed.data(), mm_ed.size() * 4);
         if (!mm_tx.empty()) std::memcpy(hb + img->o_tx, mm_tx.data(), mm_tx.size() * 2);
+        if (!mm_g4.empty()) std::memcpy(hb + img->o_g4, mm_g4.data(), mm_g4.size() * 4);
+        std::memcpy(hb + img->o_gp, mm_gp.data(), mm_gp.size() * 4);
     }
 
     if (streamed) {
@@ -1272,7 +1300,7 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else if (path == 1) {
         const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
-                                        out, N, img->in_f, img->rows, ldy, s);
+                                        img->d_g4, img->d_gp, out, N, img->in_f, img->rows, ldy, s);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else {
         const cudaError_t e = hxq::launch_vq_gemv(img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent,

@@ -249,6 +249,56 @@ def test_batched_images_mixed_kinds(H, L, oracle, cuda):
         L.hxq_cuda_image_destroy(im)
 
 
+def test_exact_sums_optional_and_deterministic(H, L, oracle, cuda):
+    """Two 4096 x 4096 12-bit images (units handed out by the counter) and a
+    small scalar one (one CTA per unit, no counter): without a sum-of-squares
+    output the call is one launch and still stores every confidence; with
+    one, a second kernel adds each image's unit sums in a fixed order, so two
+    calls give the same bits; the weights are the same either way."""
+    torch = cuda
+    ds = [synth.vq12(4096, 4096, 61), synth.vq12(4096, 4096, 62), synth.scalar(64, 256, 63, frac=0.02)]
+    ts = [H.Tensor().load(d) for d in ds]
+    imgs = [_image(H, L, t, 0, d["out_f"]) for t, d in zip(ts, ds)]
+    sizes = [d["out_f"] * d["in_f"] for d in ds]
+    offs, pos = [], 0
+    for n in sizes:
+        offs.append(pos)
+        pos += (n + 63) // 64 * 64
+    arr = (C.c_void_p * len(ds))(*[i.value for i in imgs])
+    offs_c = (C.c_size_t * len(ds))(*offs)
+    refs = [oracle.decompress(d) for d in ds]
+
+    def run(with_sums):
+        out = torch.full((pos,), float("nan"), dtype=torch.float32, device="cuda")
+        ss = torch.full((len(ds),), -1.0, dtype=torch.float64, device="cuda")
+        cf = torch.full((len(ds),), -1.0, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        n0 = L.hxq_cuda_launch_count()
+        assert L.hxq_cuda_decompress_images(arr, len(ds), out.data_ptr(), offs_c, H.HXQ_OUT_F32,
+                                            ss.data_ptr() if with_sums else None, cf.data_ptr(), None) == 0
+        launches = L.hxq_cuda_launch_count() - n0
+        assert L.hxq_cuda_stream_synchronize(None) == 0
+        return out.cpu().numpy(), ss.cpu().numpy(), cf.cpu().numpy(), launches
+
+    out0, ss0, cf0, l0 = run(False)
+    out1, ss1, cf1, l1 = run(True)
+    _, ss2, _, _ = run(True)
+    # one launch per kind (12-bit and scalar), and each followed by its sums
+    assert (l0, l1) == (2, 4), (l0, l1)
+    assert np.array_equal(_bits(out0), _bits(out1))
+    assert np.array_equal(ss1.view(np.uint64), ss2.view(np.uint64))
+    assert np.all(ss0 == -1.0)
+    for i, d in enumerate(ds):
+        err, w_ref, c_ref = refs[i]
+        assert err == 0
+        assert np.array_equal(_bits(out0[offs[i]: offs[i] + sizes[i]]), _bits(w_ref)), i
+        _check_conf(float(cf0[i]), c_ref)
+        _check_conf(float(cf1[i]), c_ref)
+        _check_sumsq(ss1[i], oracle.l2_exact(d), c_ref, len(d["rows"]))
+    for im in imgs:
+        L.hxq_cuda_image_destroy(im)
+
+
 def test_row_shards_reassemble(H, L, oracle, cuda):
     torch = cuda
     d = synth.vq12(1376 * 3, 4096, 9)  # 11008/8-style ragged row count per shard

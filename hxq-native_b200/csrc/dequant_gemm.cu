@@ -20,15 +20,22 @@
 //              deltas in array order) and rounded once.  The packed pairs go
 //              straight into tensor memory (tcgen05.st) as the MMA's A
 //              operand -- no shared-memory staging or swizzle for weights.
-//              VQ with 256-token tiles instead writes its row of the A tile
-//              to shared memory (the MMA's K-major 128-byte-swizzled layout,
-//              two 32 KB buffers) and patches the sidecar positions there
-//              with 2-byte stores: a patch is one store, where a register
-//              fragment needs a select over its 32 words.  At the end the
-//              same threads drain the accumulator (tcgen05.ld), add the bias
-//              and store coalesced rows of Y;
+//              VQ with 256-token tiles instead takes the tensor-core
+//              GEMV's lane layout (lane (g, t) of warp w: rows 16w + g and
+//              16w + g + 8, pairs 16t .. 16t + 15 of the step), reads the
+//              image's GEMV offset stream (16-bit offsets into a two-copy
+//              codebook, bank-balanced per gather instruction when the image
+//              was built) from its own TMA ring, writes the A tile to shared
+//              memory (the MMA's K-major 128-byte-swizzled layout, two 32 KB
+//              buffers) and patches the sidecar positions there by warp from
+//              a table grouped per 32 rows and half step (a patch is one
+//              2-byte store, where a register fragment needs a select over
+//              its 32 words).  At the end the converters drain the
+//              accumulator (tcgen05.ld), add the bias and store coalesced
+//              rows of Y;
 //   warp 8     TMA producer: activation tiles [BN tokens x 64 K] bf16 with
-//              128-byte swizzle into a 2-4 stage shared-memory ring;
+//              128-byte swizzle into a 2-4 stage shared-memory ring (the VQ
+//              tile of 256 tokens: three half steps, a box each);
 //   warp 9     allocates tensor memory and issues tcgen05.mma
 //              (kind::f16, bf16 x bf16 -> fp32, M=128, N=BN, K=16) from one
 //              thread; tcgen05.commit frees A buffers and ring stages.
@@ -87,31 +94,48 @@ constexpr uint32_t kErrTimeout = 2u;
 
 __device__ uint32_t g_gemm_err;          // device status word of this kernel
 
+// The VQ tile of 256 tokens moves its activations in half steps (64 of K,
+// one TMA box each) through a ring of three, 96 KB where two whole steps
+// took 128 KB: the room goes to a two-copy codebook and a ring for the
+// GEMV's offset stream (below).
+__host__ __device__ constexpr bool half_steps(uint32_t bn, bool vq) { return vq && bn == 256u; }
 // Activation ring depth: 3 stages for the affine tile of 256 tokens, 4 for
 // the small tiles; the tiles of 128 tokens keep 2 so that two CTAs share an
-// SM, and the VQ tile of 256 keeps 2 to make room for its A buffers.
+// SM; the VQ tile of 256 keeps 3 half steps.
 __host__ __device__ constexpr uint32_t stages_for(uint32_t bn, bool vq)
 {
-    return bn >= 256 ? (vq ? 2u : 3u) : bn == 128 ? 2u : 4u;
+    return (void)vq, bn >= 256 ? 3u : bn == 128 ? 2u : 4u;
 }
-__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return bn * kBK * 2u; }
-constexpr uint32_t kCodebookBytes = 4096u * 4u;   // VQ: 4096 bf16 pairs
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn, bool vq)
+{
+    return bn * (half_steps(bn, vq) ? kBK / 2u : kBK) * 2u;
+}
+// VQ: the 4096 bf16 pairs once, or (the tile of 256 tokens) twice: copy 0
+// at word c, copy 1 at word 4096 + (c ^ ((c >> 5) & 31)), the copies the
+// image's offset stream was balanced for
+__host__ __device__ constexpr uint32_t codebook_bytes(uint32_t bn) { return bn >= 256 ? 32768u : 16384u; }
 // Weight ring: each K step's weight bytes of the CTA's 128 rows arrive by
 // TMA -- affine codes 128 x 128 B (128-byte swizzle), VQ index bytes
-// 128 x 96 B -- instead of one 16-byte load per thread from 32 rows' lines
-// per warp instruction.  Two stages; one for the VQ tile of 256 tokens,
-// whose A buffers leave room for no more (its converters take a stage's
-// bytes into registers at once, so the next copy overlaps the conversion).
-__host__ __device__ constexpr uint32_t wstage_bytes(bool vq) { return kBM * (vq ? 96u : 128u); }
-__host__ __device__ constexpr uint32_t wstages_for(uint32_t bn, bool vq) { return (vq && bn >= 256) ? 1u : 2u; }
+// 128 x 96 B, or for the VQ tile of 256 tokens the GEMV offset stream,
+// 128 x 128 B (64 pairs x 16 bits, 128-byte swizzle) -- instead of one
+// 16-byte load per thread from 32 rows' lines per warp instruction.  Two
+// stages.
+__host__ __device__ constexpr uint32_t wstage_bytes(uint32_t bn, bool vq)
+{
+    return kBM * ((vq && bn < 256) ? 96u : 128u);
+}
+__host__ __device__ constexpr uint32_t wstages_for(uint32_t bn, bool vq) { return (void)bn, (void)vq, 2u; }
 // ring | (A tiles in shared memory) A[2] | weight ring | barriers (full[S],
 // empty[S], a_full[2], a_empty[2], d_full, w_full[W], w_empty[W]) | tmem
 // addr | abort | (VQ) codebook
 __host__ __device__ constexpr uint32_t smem_bytes(uint32_t bn, bool vq)
 {
-    return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn) + (smem_a(bn, vq) ? 2u * kABytes : 0u) +
-           wstages_for(bn, vq) * wstage_bytes(vq) + 256u + (vq ? kCodebookBytes : 0u);
+    return 1024u /* alignment slack */ + stages_for(bn, vq) * stage_bytes(bn, vq) +
+           (smem_a(bn, vq) ? 2u * kABytes : 0u) + wstages_for(bn, vq) * wstage_bytes(bn, vq) + 256u +
+           (vq ? codebook_bytes(bn) : 0u);
 }
+static_assert(smem_bytes(256, true) <= 232448u, "VQ tile of 256 tokens: shared memory");
+static_assert(smem_bytes(256, false) <= 232448u, "affine tile of 256 tokens: shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {
@@ -339,6 +363,7 @@ struct Params {
     // gp[g + 1]), each (row % 32) << 22 | (col % 64) << 16 | bf16
     const uint32_t *g4;
     const uint32_t *gp;
+    const uint16_t *tx;       // (tiles of 256 tokens) the GEMV offset stream [O][I / 2]
     OutPtrs out;              // the [T, ldy] outputs (all get the same values)
     float *part;              // [splits][T, O] partial sums when splits > 1
     uint32_t T, I, O, gs, ldy;
@@ -372,13 +397,14 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     const __grid_constant__ Params p)
 {
     constexpr uint32_t S = stages_for(BN, VQ);
-    constexpr uint32_t SB = stage_bytes(BN);
+    constexpr uint32_t SB = stage_bytes(BN, VQ);
+    constexpr bool HS = half_steps(BN, VQ);
     constexpr bool SA = smem_a(BN, VQ);
     constexpr uint32_t kTmemA = tmem_a_col(BN);
     constexpr uint32_t kTmemCols = tmem_cols(BN, VQ);
     constexpr uint32_t kAOff = SA ? 2u * kABytes : 0u;   // A tiles after the ring
     constexpr uint32_t W = wstages_for(BN, VQ);
-    constexpr uint32_t WB = wstage_bytes(VQ);
+    constexpr uint32_t WB = wstage_bytes(BN, VQ);
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *ring = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~(uintptr_t)1023u);
@@ -464,7 +490,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 const uint32_t sw = k % W;
                 if (k >= W && !mbar_wait(w_empty + sw, ((k / W) - 1u) & 1u, abort_flag)) return false;
                 mbar_expect_tx(w_full + sw, WB);
-                const uint32_t xw = (kt_lo + k) * (VQ ? 96u : kBK);
+                const uint32_t xw = (kt_lo + k) * ((VQ && !HS) ? 96u : kBK);
                 tma_load_2d(wring + sw * WB, &wmap, w_full + sw, (int32_t)xw, (int32_t)o0);
                 w_issued = k + 1u;
                 return true;
@@ -472,14 +498,28 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (uint32_t kt = 0; kt < KT && ok; ++kt) {
                 for (; kw < KT && kw <= kt + W - 1u && ok; ++kw) ok = issue_w(kw);
                 if (!ok) break;
-                const uint32_t s = kt % S;
-                if (kt >= S && !mbar_wait(empty + s, ((kt / S) - 1u) & 1u, abort_flag)) break;
-                mbar_expect_tx(full + s, SB);
-                unsigned char *dst = ring + s * SB;
                 const uint32_t kg = (kt_lo + kt) * kBK;
-                tma_load_2d(dst, &xmap, full + s, (int32_t)kg, (int32_t)n0);
-                tma_load_2d(dst + BN * 128u, &xmap, full + s, (int32_t)(kg + 64u), (int32_t)n0);
-                issued = kt + 1u;
+                if constexpr (HS) {
+                    // two half steps, a ring slot each (issued counts half steps)
+                    for (uint32_t hh = 0; hh < 2u && ok; ++hh) {
+                        const uint32_t u = 2u * kt + hh, s = u % S;
+                        if (u >= S && !mbar_wait(empty + s, ((u / S) - 1u) & 1u, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(full + s, SB);
+                        tma_load_2d(ring + s * SB, &xmap, full + s, (int32_t)(kg + 64u * hh), (int32_t)n0);
+                        issued = u + 1u;
+                    }
+                } else {
+                    const uint32_t s = kt % S;
+                    if (kt >= S && !mbar_wait(empty + s, ((kt / S) - 1u) & 1u, abort_flag)) break;
+                    mbar_expect_tx(full + s, SB);
+                    unsigned char *dst = ring + s * SB;
+                    tma_load_2d(dst, &xmap, full + s, (int32_t)kg, (int32_t)n0);
+                    tma_load_2d(dst + BN * 128u, &xmap, full + s, (int32_t)(kg + 64u), (int32_t)n0);
+                    issued = kt + 1u;
+                }
             }
         }
     } else if (warp == kMmaWarp) {
@@ -488,6 +528,31 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (uint32_t kt = 0; kt < KT; ++kt) {
                 const uint32_t s = kt % S, b = kt & 1u;
                 if (!mbar_wait(a_full + b, (kt >> 1) & 1u, abort_flag)) break;
+                if constexpr (HS) {
+                    // both operands from shared memory; each half step's
+                    // activations free their slot as soon as its four MMAs end
+                    const uint32_t abase = smem_u32(abuf + b * kABytes);
+                    bool good = true;
+                    for (uint32_t hh = 0; hh < 2u; ++hh) {
+                        const uint32_t u = 2u * kt + hh, su = u % S;
+                        if (!mbar_wait(full + su, (u / S) & 1u, abort_flag)) {
+                            good = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;");
+                        const uint32_t bbase = smem_u32(ring + su * SB);
+#pragma unroll
+                        for (uint32_t k4 = 0; k4 < 4u; ++k4) {
+                            const uint32_t kk = 4u * hh + k4;
+                            mma_ss(tmem, smem_desc(abase + hh * (kBM * 128u) + k4 * 32u), smem_desc(bbase + k4 * 32u),
+                                   idesc, (kt | kk) != 0u ? 1u : 0u);
+                        }
+                        mma_commit(empty + su);
+                    }
+                    if (!good) break;
+                    mma_commit(a_empty + b);
+                    continue;
+                }
                 if (!mbar_wait(full + s, (kt / S) & 1u, abort_flag)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t bbase = smem_u32(ring + s * SB);
@@ -589,85 +654,112 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             }
         } else if constexpr (SA) {
             // VQ, tiles of 256 tokens: A tiles in shared memory.  The image's
-            // bf16 codebook, one 32-bit pair per entry: an index gathers one
-            // packed pair of the A row.
-            for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
-                reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
-            // Sidecar patches by warp: warp (q, h) owns rows 32q .. 32q + 31
-            // of the tile and half h of each K step, which is one group of
-            // the grouped table; after its rows are stored, lane i applies
-            // the group's entry i (one 2-byte store into the A tile; past 32
-            // entries, again).  A lane per row walking its own row's patches
-            // made the warp loop as often as its busiest row (sidecar
-            // patching was 17% of the 4096 x 4096 launch at 2048 tokens).
+            // bf16 codebook twice (copy 0 at word c, copy 1 at word 4096 +
+            // (c ^ ((c >> 5) & 31))): a pair's offset names one packed pair.
+            for (uint32_t i = tid; i < 4096u; i += kConvWarps * 32u) {
+                const uint32_t e = __ldg(p.cbh + i);
+                cbh[i] = e;
+                cbh[4096u + (i ^ ((i >> 5) & 31u))] = e;
+            }
+            // The weights come from the image's GEMV offset stream -- per
+            // pair the 16-bit byte offset of its entry in the two-copy
+            // codebook, in natural pair order, the copy chosen when the image
+            // was built so that each gather instruction of the GEMV's lane
+            // layout (8 rows x 4 pair slots of a 64-pair window) spreads over
+            // the banks: about 2 shared-memory wavefronts per warp-wide
+            // gather against 3.5 from one copy.  A K step is one such window
+            // and the converters take the GEMV's lanes: lane (g, t) of warp w
+            // converts tile rows 16w + g and 16w + g + 8, pairs [16t, 16t +
+            // 16) of the step, so each of its 32 gathers per step is one of
+            // the builder's instructions.  The stream comes through the
+            // weight ring (128 rows x 128 B per step, 128-byte swizzle).
+            const unsigned char *cbb = reinterpret_cast<const unsigned char *>(cbh);
+            const uint32_t g = lane >> 2, t = lane & 3u;
+            const uint32_t ra = 16u * warp + g;              // tile rows ra and ra + 8 (both = g mod 8)
+            // Sidecar patches by warp from the table grouped per 32 rows and
+            // half K step: warp w's rows are half of group o0 / 32 + w / 2,
+            // and a K step is two consecutive groups (both halves, adjacent
+            // in the table); lane i takes the step's entry i (past 32,
+            // again) and applies it when its row is one of the warp's 16.
             // The group offsets sit in four slots, each refilled four steps
             // ahead; a step's first 32 entries (one per lane) in one of two
             // registers, loaded two steps ahead.  The loop is unrolled by four
             // so that the slots are fixed registers: a register holding a load
             // in flight is never copied (a copy would wait for the load).
             const uint32_t NH = p.I / 64u;
-            const uint32_t grp = o0 / 32u + q;
+            const uint32_t grp = o0 / 32u + (warp >> 1), rsel = warp & 1u;
             const bool gvalid = grp * 32u < p.O;
-            const uint32_t *gpp = p.gp + (size_t)(gvalid ? grp : 0u) * NH + 2u * kt_lo + h;
-            auto gload = [&](uint32_t k) -> uint2 {
-                return (gvalid && k < KT) ? make_uint2(__ldg(gpp + 2u * k), __ldg(gpp + 2u * k + 1u))
-                                          : make_uint2(0u, 0u);
+            const uint32_t *gpp = p.gp + (size_t)(gvalid ? grp : 0u) * NH + 2u * kt_lo;
+            auto gload = [&](uint32_t k) -> uint3 {
+                return (gvalid && k < KT)
+                           ? make_uint3(__ldg(gpp + 2u * k), __ldg(gpp + 2u * k + 1u), __ldg(gpp + 2u * k + 2u))
+                           : make_uint3(0u, 0u, 0u);
             };
-            auto eload = [&](uint2 r) -> uint32_t { return lane < r.y - r.x ? __ldg(p.g4 + r.x + lane) : 0u; };
-            uint2 gq0 = gload(0), gq1 = gload(1), gq2 = gload(2), gq3 = gload(3);
+            auto eload = [&](uint3 r) -> uint32_t { return lane < r.z - r.x ? __ldg(p.g4 + r.x + lane) : 0u; };
+            uint3 gq0 = gload(0), gq1 = gload(1), gq2 = gload(2), gq3 = gload(3);
             uint32_t ea = KT > 0 ? eload(gq0) : 0u, ez = KT > 1 ? eload(gq1) : 0u;
             asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+            // 16 packed pairs of one row from its two 16-byte units of offsets
+            auto gather = [&](const uint4 &q0, const uint4 &q1, uint32_t (&v)[16]) {
+                const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (uint32_t i = 0; i < 8u; ++i) {
+                    v[2u * i] = *reinterpret_cast<const uint32_t *>(cbb + (w[i] & 0xFFFFu));
+                    v[2u * i + 1u] = *reinterpret_cast<const uint32_t *>(cbb + (w[i] >> 16));
+                }
+            };
+            // one row's 64 bytes of the A tile: K half t / 2, 16-byte units
+            // 4 (t & 1) .. +3, unit u at (u ^ g) << 4
+            auto put = [&](unsigned char *arow, const uint32_t (&v)[16]) {
+                const uint32_t ub = (t & 1u) * 4u;
+#pragma unroll
+                for (uint32_t u = 0; u < 4u; ++u)
+                    *reinterpret_cast<uint4 *>(arow + (((ub + u) ^ g) << 4)) =
+                        make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
+            };
             // one K step: g_cur the group offsets of step kt (its slot,
             // refilled with step kt + 4's), g_2 those of step kt + 2, E this
             // lane's first entry of step kt (refilled with step kt + 2's);
             // false if a wait ran out
-            auto step = [&](uint32_t kt, uint2 &g_cur, uint2 g_2, uint32_t &E) -> bool {
+            auto step = [&](uint32_t kt, uint3 &g_cur, uint3 g_2, uint32_t &E) -> bool {
                 const uint32_t b = kt & 1u, sw = kt % W;
-                // 64 weights = 16 byte triples = 3 x 16 bytes of this thread's
-                // row of the weight ring stage (96 B per row)
                 if (!mbar_wait(w_full + sw, (kt / W) & 1u, abort_flag)) return false;
-                uint4 cn[3];
-                const unsigned char *wr = wring + sw * WB + row * 96u + h * 48u;
-#pragma unroll
-                for (uint32_t i = 0; i < 3u; ++i) cn[i] = *reinterpret_cast<const uint4 *>(wr + 16u * i);
+                // units 2t and 2t + 1 of lines ra and ra + 8 (unit u of line r
+                // at (u ^ (r & 7)) << 4): a quarter-warp's eight loads cover
+                // all 32 banks
+                const unsigned char *ws = wring + sw * WB;
+                const uint4 q0 = *reinterpret_cast<const uint4 *>(ws + ra * 128u + (((2u * t) ^ g) << 4));
+                const uint4 q1 = *reinterpret_cast<const uint4 *>(ws + ra * 128u + (((2u * t + 1u) ^ g) << 4));
+                const uint4 q2 = *reinterpret_cast<const uint4 *>(ws + (ra + 8u) * 128u + (((2u * t) ^ g) << 4));
+                const uint4 q3 = *reinterpret_cast<const uint4 *>(ws + (ra + 8u) * 128u + (((2u * t + 1u) ^ g) << 4));
                 async_proxy_fence();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(w_empty + sw);
-                const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
-                                        cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
-                uint32_t v[32];
-#pragma unroll
-                for (uint32_t t = 0; t < 16u; ++t) {
-                    const uint32_t byte = 3u * t, wq = byte >> 2;
-                    const uint32_t B = __byte_perm(w[wq], w[wq + 1u < 12u ? wq + 1u : 11u], 0x3012u + (byte & 3u) * 0x1111u);
-                    v[2u * t] = cbh[(B >> 12) & 0xFFFu];
-                    v[2u * t + 1u] = cbh[B & 0xFFFu];
-                }
-                // this thread's 128 bytes of the A tile: row `row` of half h,
-                // 16-byte unit u at (u ^ (row & 7)) << 4
+                uint32_t v0[16], v1[16];
+                gather(q0, q1, v0);
+                gather(q2, q3, v1);
                 __syncwarp();
                 if (kt >= 2 && !mbar_wait(a_empty + b, ((kt >> 1) - 1u) & 1u, abort_flag)) return false;
-                unsigned char *ah = abuf + b * kABytes + h * (kBM * 128u);
-                unsigned char *arow = ah + row * 128u;
-#pragma unroll
-                for (uint32_t u = 0; u < 8u; ++u)
-                    *reinterpret_cast<uint4 *>(arow + ((u ^ (row & 7u)) << 4)) =
-                        make_uint4(v[4u * u], v[4u * u + 1u], v[4u * u + 2u], v[4u * u + 3u]);
+                unsigned char *ab = abuf + b * kABytes;
+                put(ab + (t >> 1) * (kBM * 128u) + ra * 128u, v0);
+                put(ab + (t >> 1) * (kBM * 128u) + (ra + 8u) * 128u, v1);
                 // the warp's patches: the reference's fp32 value rounded once
                 // to bf16, over the codebook pair's half, once all the warp's
                 // rows are stored
                 __syncwarp();
-                const uint32_t n = g_cur.y - g_cur.x;
-                unsigned char *ag = ah + (32u * q) * 128u;
-                auto apply = [&](uint32_t e) {
+                const uint32_t n = g_cur.z - g_cur.x;
+                unsigned char *ag = ab + (32u * (warp >> 1)) * 128u;
+                auto apply = [&](uint32_t i, uint32_t e) {
                     const uint32_t r = (e >> 22) & 31u, lc = (e >> 16) & 63u;
-                    *reinterpret_cast<uint16_t *>(ag + r * 128u + ((((lc >> 3) ^ (r & 7u)) << 4) | ((lc & 7u) << 1))) =
-                        (uint16_t)e;
+                    if ((r >> 4) != rsel) return;
+                    const uint32_t half = g_cur.x + i >= g_cur.y ? 1u : 0u;
+                    *reinterpret_cast<uint16_t *>(ag + half * (kBM * 128u) + r * 128u +
+                                                  ((((lc >> 3) ^ (r & 7u)) << 4) | ((lc & 7u) << 1))) = (uint16_t)e;
                 };
-                if (lane < n) apply(E);
+                if (lane < n) apply(lane, E);
 #pragma unroll 1
                 for (uint32_t base = 32u; base < n; base += 32u)
-                    if (base + lane < n) apply(__ldg(p.g4 + g_cur.x + base + lane));
+                    if (base + lane < n) apply(base + lane, __ldg(p.g4 + g_cur.x + base + lane));
                 // the generic-proxy stores, visible to the tensor cores' reads
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive(a_full + b);
@@ -685,7 +777,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             // VQ, tiles of up to 128 tokens: A into tensor memory.  The
             // image's bf16 codebook, one 32-bit pair per entry: an index
             // gathers exactly one TMEM column (low half = even k)
-            for (uint32_t i = tid; i < kCodebookBytes / 16u; i += kConvWarps * 32u)
+            for (uint32_t i = tid; i < codebook_bytes(BN) / 16u; i += kConvWarps * 32u)
                 reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
             // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
             // this row, from this CTA's first step).  The offsets kp[kt + j]
@@ -932,18 +1024,22 @@ int launch(const uint16_t *x, const Params &p, cudaStream_t s)
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
     // the weights: affine codes [O][I] in boxes of 128 B x 128 rows with
-    // 128-byte swizzle, or VQ index bytes [O][I * 3 / 4] in boxes of 96 B x
-    // 128 rows (no swizzle); rows past O read as zero
+    // 128-byte swizzle, VQ index bytes [O][I * 3 / 4] in boxes of 96 B x
+    // 128 rows (no swizzle), or for the VQ tile of 256 tokens the GEMV
+    // offset stream [O][I bytes] in boxes of 128 B x 128 rows with 128-byte
+    // swizzle; rows past O read as zero
+    constexpr bool HSL = half_steps(BN, VQ);
     CUtensorMap wmap;
     std::memset(&wmap, 0, sizeof(wmap));
-    const cuuint64_t wrow = VQ ? (cuuint64_t)(p.I / 4u) * 3u : (cuuint64_t)p.I;
+    const cuuint64_t wrow = (VQ && !HSL) ? (cuuint64_t)(p.I / 4u) * 3u : (cuuint64_t)p.I;
     const cuuint64_t wdims[2] = {wrow, p.O};
     const cuuint64_t wstrides[1] = {wrow};
-    const cuuint32_t wbox[2] = {VQ ? 96u : 128u, kBM};
-    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(VQ ? p.vidx : p.codes), wdims, wstrides,
-            wbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            VQ ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    const cuuint32_t wbox[2] = {(VQ && !HSL) ? 96u : 128u, kBM};
+    const void *wbase = HSL ? static_cast<const void *>(p.tx) : VQ ? static_cast<const void *>(p.vidx)
+                                                                    : static_cast<const void *>(p.codes);
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(wbase), wdims, wstrides, wbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, (VQ && !HSL) ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
     auto kern = dequant_gemm_kernel<BN, VQ>;
     const uint32_t smem = smem_bytes(BN, VQ);
@@ -1172,15 +1268,16 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
 // on launch, -1 on error.
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
                  const uint16_t *kp, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
-                 const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O, uint32_t ldy, cudaStream_t s)
+                 const uint16_t *tx, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O, uint32_t ldy,
+                 cudaStream_t s)
 {
     if (T == 0 || O == 0) return 1;
     if (I == 0 || I % gemm::kBK != 0 || ldy < O) return 1;
     if (((uintptr_t)x & 15u) || ((uintptr_t)idx & 15u) || ((uintptr_t)cbh & 15u)) return 1;
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
     gemm::Params p{};
-    if (!g4 || !gp) return 1;
-    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4; p.g4 = g4; p.gp = gp;
+    if (!g4 || !gp || !tx || ((uintptr_t)tx & 15u)) return 1;
+    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4; p.g4 = g4; p.gp = gp; p.tx = tx;
     if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
     p.T = T; p.I = I; p.O = O; p.gs = 0; p.ldy = ldy;
     return run<true>(x, p, out, s);

@@ -1300,7 +1300,7 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else if (path == 1) {
         const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
-                                        img->d_g4, img->d_gp, out, N, img->in_f, img->rows, ldy, s);
+                                        img->d_g4, img->d_gp, img->d_tx, out, N, img->in_f, img->rows, ldy, s);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else {
         const cudaError_t e = hxq::launch_vq_gemv(img->d_idx, img->d_cb, img->d_chunk_ptr, img->d_ent,

@@ -220,13 +220,19 @@ struct VqTcMatrix {
     uint32_t ldy, rows, in_f;
 };
 // 1 <= N <= 16, in_f a multiple of 128 (at most 65536), x 16-byte aligned,
-// and the activations fit in shared memory.
+// and the activations fit in shared memory whole or in at most 8 K parts.
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f);
-// How many of m[0..n) (at most kMaxTcJobs) share one launch without costing
-// the first ones residency (CTAs per SM).
+// Jobs of one VQ GEMV launch (a matrix split along K: one per part).
+constexpr uint32_t kMaxVqTcJobs = 8;
+// How many of m[0..n) share one launch (at most kMaxVqTcJobs jobs, a matrix
+// split along K counting one per part) without costing the first ones
+// residency (CTAs per SM).
 uint32_t vq_tc_group(uint32_t n, const VqTcMatrix *m, uint32_t N);
-// Up to kMaxTcJobs images in one launch: 0 launched, 1 not taken, -1 error.
-int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s);
+// Up to kMaxVqTcJobs jobs in one launch, plus one part-sum launch per matrix
+// split along K: 0 launched (*launched: how many kernels), 1 not taken,
+// -1 error.
+int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s,
+                      uint32_t *launched = nullptr);
 uint32_t vq_tc_status_take();
 
 }  // namespace hxq

@@ -427,7 +427,7 @@ uint32_t idx12_at(const uint8_t *row, uint32_t pair)
 void choose_copies(const uint32_t (&c)[32], const bool (&live)[32], uint8_t (&copy)[32])
 {
     uint16_t words[32][32];   // distinct words per bank
-    uint8_t refs[32][32];     // lanes per (bank, word)
+    uint8_t refs[32][32] = {};   // lanes per (bank, word)
     uint8_t load[32] = {0};
     auto find = [&](uint32_t b, uint16_t w) -> int {
         for (uint32_t i = 0; i < load[b]; ++i)
@@ -1296,8 +1296,10 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
     if (path != 1) hxq::gemm_chain_break();   // a GEMV follows
     if (path == 2) {
         const hxq::VqTcMatrix m = tc_matrix(img, d_x_bf16, out, ldy);
-        const int r = hxq::launch_vq_tc_gemv(1, &m, N, g_dev[dev].sms, s);
+        uint32_t nl = 0;
+        const int r = hxq::launch_vq_tc_gemv(1, &m, N, g_dev[dev].sms, s, &nl);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
+        g_launches.fetch_add(nl - 1u, std::memory_order_relaxed);   // the part sums, if any
     } else if (path == 1) {
         const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
                                         img->d_g4, img->d_gp, img->d_tx, out, N, img->in_f, img->rows, ldy, s);
@@ -1375,7 +1377,8 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // The batch in three parts, each image in the first that takes it: up to
     // HXQ_VQ_MATMUL_TC_MAX tokens, images with matmul tables that suit the
-    // tensor-core GEMV share its launches (8 per launch); up to
+    // tensor-core GEMV share its launches (up to 8 jobs, a matrix split
+    // along K counting one per part); up to
     // HXQ_VQ_MATMUL_GEMV_MAX tokens the rest share exact-GEMV launches;
     // anything left runs one call per image.
     std::vector<uint8_t> done(n, 0);
@@ -1395,10 +1398,11 @@ hxq_error_t hxq_cuda_vq_matmul_batch(uint32_t n, hxq_cuda_image_t *const *imgs, 
                      [](const hxq::VqTcMatrix &a, const hxq::VqTcMatrix &b) { return a.in_f < b.in_f; });
     for (size_t j0 = 0; j0 < tcs.size();) {
         const uint32_t cnt = hxq::vq_tc_group((uint32_t)(tcs.size() - j0), tcs.data() + j0, N);
-        const int r = hxq::launch_vq_tc_gemv(cnt, tcs.data() + j0, N, g_dev[dev].sms, s);
+        uint32_t nl = 0;
+        const int r = hxq::launch_vq_tc_gemv(cnt, tcs.data() + j0, N, g_dev[dev].sms, s, &nl);
         j0 += cnt;
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
-        g_launches.fetch_add(1, std::memory_order_relaxed);
+        g_launches.fetch_add(nl, std::memory_order_relaxed);
     }
     if (N > HXQ_VQ_MATMUL_GEMV_MAX) {
         // one call per image; consecutive GEMMs overlap their wave tails

@@ -52,6 +52,9 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "hxq_cuda.h"
 #include "hxq_cuda_internal.h"
@@ -87,16 +90,18 @@ struct Job {
     const float *ed;            // sidecar weight differences
     uint32_t n_patch;
     OutPtrs out;
-    uint32_t ldy, rows, in_f;
+    uint32_t ldy, rows, in_f;   // in_f: the K length this job covers
+    uint32_t k0, ldx;           // its first K column in the matrix; x's row stride (the matrix's in_f)
     uint32_t rb_begin;
     uint64_t w_begin;
 };
 
 struct Jobs {
-    Job job[kMaxTcJobs];
+    Job job[kMaxVqTcJobs];
     uint32_t n, N, total_rb, in_max, stages;
     uint64_t total_w;
 };
+static_assert(sizeof(Jobs) <= 4096, "kernel parameters are limited to 4 KB");
 
 struct Layout {
     uint32_t bars, abort, xh, red, cs, total;
@@ -180,7 +185,8 @@ __device__ __forceinline__ uint32_t xpos(uint32_t k)
 }
 
 // Sidecar ranges of rows 2w, 2w + 1 of row block rb: entries [pr[0], pr[1])
-// and [pr[1], pr[2]) (rows past the image: empty; no sidecar: all zero).
+// and [pr[1], pr[2]) (rows past the image: empty; no sidecar: all zero).  A
+// K part walks its rows' whole ranges and adds the entries of its columns.
 __device__ __forceinline__ void side_rows(const Jobs &J, uint32_t rb, uint32_t warp, uint32_t (&pr)[3])
 {
     uint32_t j = 0;
@@ -197,9 +203,13 @@ __device__ __forceinline__ void side_rows(const Jobs &J, uint32_t rb, uint32_t w
 // ldx in fragment order).
 template <int NC>
 __device__ __forceinline__ void side_add(float (&sn)[NC], uint32_t e4, float dl, const uint16_t *xs, uint32_t ldx,
-                                         uint32_t N)
+                                         uint32_t N, uint32_t k0, uint32_t klen)
 {
-    const uint16_t *xc = xs + xpos(e4 & 0xFFFFu);
+    // only the entries of this job's K range [k0, k0 + klen), whose
+    // activations are the ones staged
+    const uint32_t kc = (e4 & 0xFFFFu) - k0;
+    if (kc >= klen) return;
+    const uint16_t *xc = xs + xpos(kc);
 #pragma unroll
     for (int n = 0; n < NC; ++n)
         if (NC == 1 || (uint32_t)n < N)
@@ -268,6 +278,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 const Job &b = J.job[j];
                 const uint32_t row0 = (rb - b.rb_begin) * kRows;
                 const uint32_t nst = (b.in_f + kKC - 1u) / kKC;
+                const uint32_t kx = b.k0;
                 for (uint32_t st = 0; st < nst; ++st, ++it) {
                     if (it >= S && !mbar_wait(empty + slot, ph ^ 1u, abort_flag, &g_vqtc_err)) {
                         ok = false;
@@ -276,7 +287,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                     mbar_expect_tx(full + slot, kStageBytes);   // the full boxes, zero fill included
                     for (uint32_t c = 0; c < kRowStageBytes / 128u; ++c)
                         tma_load_2d(smem + slot * kStageBytes + c * 2048u, &b.map, full + slot,
-                                    (int32_t)(st * kRowStageBytes + c * 128u), (int32_t)row0);
+                                    (int32_t)(kx + st * kRowStageBytes + c * 128u), (int32_t)row0);
                     if (++slot == S) { slot = 0; ph ^= 1u; }
                 }
             }
@@ -309,7 +320,7 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
     for (uint32_t rb = rb0; rb < rb1; ++rb, ++rbi) {
         while (j + 1u < J.n && rb >= J.job[j + 1u].rb_begin) ++j;
         const Job &b = J.job[j];
-        const uint32_t in_f = b.in_f;
+        const uint32_t in_f = b.in_f, k0 = b.k0;
         if (j != cur) {
             // the matrix's codebook, both copies (four entries per 16-byte
             // load: copy 0 in place, copy 1 at its permuted words), and its
@@ -325,11 +336,14 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
                 s_cb[4096u + ((c0 + 2u) ^ r)] = v.z;
                 s_cb[4096u + ((c0 + 3u) ^ r)] = v.w;
             }
-            const uint32_t per_tok = in_f / 8u;
+            // (the job's fields read once: the stores below could alias
+            // them as far as the compiler knows)
+            const uint32_t per_tok = in_f / 8u, ldx = b.ldx;
+            const uint16_t *xsrc = b.x + k0;
             uint16_t *xh = reinterpret_cast<uint16_t *>(smem + L.xh);
             for (uint32_t p = ct; p < N * per_tok; p += kConsumers * 32u) {
                 const uint32_t n = p / per_tok, k8 = p - n * per_tok;
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(b.x + (size_t)n * in_f) + k8);
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xsrc + (size_t)n * ldx) + k8);
                 *reinterpret_cast<uint4 *>(xh + (size_t)n * (in_f + kXPad) + xpos(k8 * 8u)) = v;
             }
             asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -410,9 +424,9 @@ vq_tc_gemv_kernel(const __grid_constant__ Jobs J)
             for (int n = 0; n < NC; ++n) sn[n] = 0.0f;
 #pragma unroll
             for (int m = 0; m < 4; ++m)
-                if (plo + s16 + 16u * (uint32_t)m < phi) side_add<NC>(sn, pe[m], pd[m], xs, in_f + kXPad, N);
+                if (plo + s16 + 16u * (uint32_t)m < phi) side_add<NC>(sn, pe[m], pd[m], xs, in_f + kXPad, N, k0, in_f);
             for (uint32_t p = plo + 64u + s16; p < phi; p += 16u)
-                side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N);
+                side_add<NC>(sn, __ldg(b.e4 + p), __ldg(b.ed + p), xs, in_f + kXPad, N, k0, in_f);
             side_reduce_half<NC>(sn, N, lane, cw + (2u * warp + sh) * kCsStride);
         }
 #pragma unroll
@@ -460,57 +474,153 @@ Plan plan_for(uint32_t N, uint32_t in_f)
     return Plan{0u, 0u, {}};
 }
 
+// K parts of a matrix whose activations do not fit the staging whole: the
+// fewest parts (at most kMaxParts, each `len` columns, a multiple of 128;
+// the last one shorter) whose staging leaves room for two stages.  Each part
+// is a job of its own that stores its partial products [N][rows] to a
+// scratch buffer; part_sum_kernel adds them in part order.  The split
+// depends only on N and in_f, so a matrix sums the same way alone and in a
+// batch.
+constexpr uint32_t kMaxParts = 8;
+struct Split {
+    uint32_t parts, len;
+};
+Split split_for(uint32_t N, uint32_t in_f)
+{
+    const uint32_t w = in_f / 128u;
+    for (uint32_t P = 1; P <= kMaxParts && P <= w; ++P) {
+        const uint32_t len = (w + P - 1u) / P * 128u;
+        if (plan_for(N, len).stages != 0) return Split{(in_f + len - 1u) / len, len};
+    }
+    return Split{0u, 0u};
+}
+
+// y[n, o] = sum over the K parts, in part order, of their partial products
+// (part p's [N][rows] at part + p * N * rows), stored into every output.
+__global__ void part_sum_kernel(const float *__restrict__ part, const __grid_constant__ OutPtrs out, uint32_t N,
+                                uint32_t rows, uint32_t ldy, uint32_t parts)
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t total = N * rows;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        for (uint32_t p = 0; p < parts; ++p) v += __ldg(part + (size_t)p * total + i);
+        const uint32_t n = i / rows, o = i - n * rows;
+        for (uint32_t k = 0; k < out.n; ++k) out.y[k][(size_t)n * ldy + o] = v;
+    }
+}
+
+// Partial-product scratch, one per (device, stream) so that launches on
+// different streams never share it; grown on demand (the first split call of
+// a size on a stream allocates, later ones -- under graph capture too --
+// reuse it).
+float *part_buffer(size_t floats, cudaStream_t s)
+{
+    struct Buf {
+        float *p = nullptr;
+        size_t cap = 0;
+    };
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, Buf> bufs;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    std::lock_guard<std::mutex> lk(mu);
+    Buf &b = bufs[{dev, s}];
+    if (b.cap < floats) {
+        if (b.p) { cudaStreamSynchronize(s); cudaFree(b.p); }
+        b.p = nullptr;
+        b.cap = 0;
+        if (cudaMalloc(&b.p, floats * sizeof(float)) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        b.cap = floats;
+    }
+    return b.p;
+}
+
 }  // namespace vqtc
 
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f)
 {
     if (N == 0 || N > 16u || in_f == 0 || in_f % 128u != 0 || in_f > 65536u || ((uintptr_t)x & 15u)) return false;
-    return vqtc::plan_for(N, in_f).stages != 0;
+    return vqtc::split_for(N, in_f).parts != 0;
 }
 
 uint32_t vq_tc_group(uint32_t n, const VqTcMatrix *m, uint32_t N)
 {
     if (n == 0) return 0;
-    uint32_t in_max = m[0].in_f, k = 1;
+    const vqtc::Split s0 = vqtc::split_for(N, m[0].in_f);
+    uint32_t in_max = s0.len, jobs = s0.parts, k = 1;
     vqtc::Plan P = vqtc::plan_for(N, in_max);
-    for (; k < n && k < kMaxTcJobs; ++k) {
-        const uint32_t in2 = m[k].in_f > in_max ? m[k].in_f : in_max;
+    for (; k < n; ++k) {
+        const vqtc::Split q = vqtc::split_for(N, m[k].in_f);
+        if (q.parts == 0 || jobs + q.parts > kMaxVqTcJobs) break;
+        const uint32_t in2 = q.len > in_max ? q.len : in_max;
         const vqtc::Plan Q = vqtc::plan_for(N, in2);
         if (Q.per_sm < P.per_sm) break;   // a second launch costs less than half the CTAs
         in_max = in2;
         P = Q;
+        jobs += q.parts;
     }
     return k;
 }
 
-int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s)
+int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cudaStream_t s, uint32_t *launched)
 {
     using namespace vqtc;
+    if (launched) *launched = 0;
     if (n == 0 || N == 0) return 0;
-    if (n > kMaxTcJobs) return 1;
-    Jobs J{};
-    uint32_t rb = 0, in_max = 0;
-    uint64_t w = 0;
+    if (n > kMaxVqTcJobs) return 1;
+    Split sp[kMaxVqTcJobs];
+    uint32_t n_jobs = 0;
+    size_t part_floats = 0;
     for (uint32_t i = 0; i < n; ++i) {
         const VqTcMatrix &a = m[i];
         if (!vq_tc_fits(a.x, N, a.in_f) || a.out.n == 0 || a.out.n > HXQ_CUDA_MAX_PEERS || a.ldy < a.rows) return 1;
-        const uint64_t row_bytes = (uint64_t)a.in_f;   // one 16-bit offset per pair
-        Job &b = J.job[i];
-        std::memset(&b.map, 0, sizeof(b.map));
-        if (!a.tx || !pipe::encode_bytes_2d(&b.map, a.tx, row_bytes, a.rows, kRows)) return 1;
-        b.cbh = a.cbh; b.x = a.x; b.out = a.out; b.ldy = a.ldy; b.rows = a.rows; b.in_f = a.in_f;
-        if (a.n_patch) {
-            if (!a.rb || !a.e4 || !a.ed) return 1;
-            b.prow = a.rb; b.e4 = a.e4; b.ed = a.ed; b.n_patch = a.n_patch;
-        }
-        b.rb_begin = rb;
-        b.w_begin = w;
-        const uint32_t nrb = (a.rows + kRows - 1u) / kRows;
-        rb += nrb;
-        w += (uint64_t)nrb * kRows * a.in_f;
-        in_max = a.in_f > in_max ? a.in_f : in_max;
+        if (!a.tx || (a.n_patch && (!a.rb || !a.e4 || !a.ed))) return 1;
+        sp[i] = split_for(N, a.in_f);
+        n_jobs += sp[i].parts;
+        if (sp[i].parts > 1u) part_floats += (size_t)sp[i].parts * N * a.rows;
     }
-    J.n = n;
+    if (n_jobs > kMaxVqTcJobs) return 1;
+    float *part = nullptr;
+    if (part_floats && !(part = part_buffer(part_floats, s))) return -1;
+    Jobs J{};
+    uint32_t rb = 0, in_max = 0, jn = 0;
+    uint64_t w = 0;
+    size_t po = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const VqTcMatrix &a = m[i];
+        const uint64_t row_bytes = (uint64_t)a.in_f;   // one 16-bit offset per pair
+        CUtensorMap map;
+        std::memset(&map, 0, sizeof(map));
+        if (!pipe::encode_bytes_2d(&map, a.tx, row_bytes, a.rows, kRows)) return 1;
+        const uint32_t nrb = (a.rows + kRows - 1u) / kRows;
+        for (uint32_t q = 0; q < sp[i].parts; ++q) {
+            // part q: K columns [q len, q len + in_f) of the matrix
+            Job &b = J.job[jn++];
+            b.map = map;
+            b.cbh = a.cbh; b.x = a.x; b.rows = a.rows;
+            b.k0 = q * sp[i].len;
+            b.in_f = a.in_f - b.k0 < sp[i].len ? a.in_f - b.k0 : sp[i].len;
+            b.ldx = a.in_f;
+            if (sp[i].parts > 1u) {
+                b.out = OutPtrs{};
+                b.out.y[0] = part + po + (size_t)q * N * a.rows;
+                b.out.n = 1;
+                b.ldy = a.rows;
+            } else {
+                b.out = a.out;
+                b.ldy = a.ldy;
+            }
+            if (a.n_patch) { b.prow = a.rb; b.e4 = a.e4; b.ed = a.ed; b.n_patch = a.n_patch; }
+            b.rb_begin = rb;
+            b.w_begin = w;
+            rb += nrb;
+            w += (uint64_t)nrb * kRows * b.in_f;
+            in_max = b.in_f > in_max ? b.in_f : in_max;
+        }
+        if (sp[i].parts > 1u) po += (size_t)sp[i].parts * N * a.rows;
+    }
+    J.n = n_jobs;
     J.N = N;
     J.total_rb = rb;
     J.total_w = w;
@@ -546,6 +656,31 @@ int launch_vq_tc_gemv(uint32_t n, const VqTcMatrix *m, uint32_t N, int sms, cuda
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (cudaLaunchKernelEx(&cfg, kernels[kv], J) != cudaSuccess) { cudaGetLastError(); return -1; }
+    uint32_t nl = 1;
+    // the split matrices' part sums, each launched to overlap the tail of
+    // the kernel before it (its threads wait for that kernel's stores)
+    po = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (sp[i].parts < 2u) continue;
+        const uint32_t total = N * m[i].rows;
+        uint32_t blocks = (total + 255u) / 256u;
+        const uint32_t cap = (uint32_t)(sms > 0 ? sms : 148) * 4u;
+        if (blocks > cap) blocks = cap;
+        cudaLaunchConfig_t rc = {};
+        rc.gridDim = dim3(blocks);
+        rc.blockDim = dim3(256);
+        rc.stream = s;
+        rc.attrs = attr;
+        rc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&rc, part_sum_kernel, (const float *)(part + po), m[i].out, N, m[i].rows, m[i].ldy,
+                               sp[i].parts) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        po += (size_t)sp[i].parts * N * m[i].rows;
+        ++nl;
+    }
+    if (launched) *launched = nl;
     return 0;
 }
 

@@ -381,14 +381,27 @@ struct Params {
 };
 
 // Replace the bf16 at position `local` (0..63) of a thread's 32 packed
-// pairs; the register array is indexed statically.
+// pairs.  The register array is indexed statically: a switch on the word
+// (a branch to the one update that applies) instead of a compare and
+// select on all 32 registers per patch.
 __device__ __forceinline__ void patch_pair(uint32_t (&v)[32], uint32_t local, uint32_t nb)
 {
-    const uint32_t word = local >> 1;
-    const bool hi = (local & 1u) != 0u;
-#pragma unroll
-    for (uint32_t i = 0; i < 32u; ++i)
-        if (i == word) v[i] = hi ? ((v[i] & 0xFFFFu) | (nb << 16)) : ((v[i] & 0xFFFF0000u) | nb);
+    const uint32_t keep = (local & 1u) ? 0xFFFFu : 0xFFFF0000u;
+    const uint32_t put = (local & 1u) ? (nb << 16) : nb;
+    switch (local >> 1) {
+#define HXQ_PATCH_WORD(i) \
+    case i: v[i] = (v[i] & keep) | put; break;
+        HXQ_PATCH_WORD(0) HXQ_PATCH_WORD(1) HXQ_PATCH_WORD(2) HXQ_PATCH_WORD(3)
+        HXQ_PATCH_WORD(4) HXQ_PATCH_WORD(5) HXQ_PATCH_WORD(6) HXQ_PATCH_WORD(7)
+        HXQ_PATCH_WORD(8) HXQ_PATCH_WORD(9) HXQ_PATCH_WORD(10) HXQ_PATCH_WORD(11)
+        HXQ_PATCH_WORD(12) HXQ_PATCH_WORD(13) HXQ_PATCH_WORD(14) HXQ_PATCH_WORD(15)
+        HXQ_PATCH_WORD(16) HXQ_PATCH_WORD(17) HXQ_PATCH_WORD(18) HXQ_PATCH_WORD(19)
+        HXQ_PATCH_WORD(20) HXQ_PATCH_WORD(21) HXQ_PATCH_WORD(22) HXQ_PATCH_WORD(23)
+        HXQ_PATCH_WORD(24) HXQ_PATCH_WORD(25) HXQ_PATCH_WORD(26) HXQ_PATCH_WORD(27)
+        HXQ_PATCH_WORD(28) HXQ_PATCH_WORD(29) HXQ_PATCH_WORD(30) HXQ_PATCH_WORD(31)
+#undef HXQ_PATCH_WORD
+        default: break;
+    }
 }
 
 template <uint32_t BN, bool VQ>

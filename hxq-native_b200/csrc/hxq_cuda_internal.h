@@ -220,7 +220,7 @@ struct VqTcMatrix {
     uint32_t ldy, rows, in_f;
 };
 // 1 <= N <= 16, in_f a multiple of 128 (at most 65536), x 16-byte aligned,
-// and the activations fit in shared memory whole or in at most 8 K parts.
+// and the activations fit in shared memory whole or in two K parts.
 bool vq_tc_fits(const uint16_t *x, uint32_t N, uint32_t in_f);
 // Jobs of one VQ GEMV launch (a matrix split along K: one per part).
 constexpr uint32_t kMaxVqTcJobs = 8;

@@ -150,7 +150,7 @@ def test_gemm_last_wave_split(H, L, oracle, cuda):
 @pytest.mark.parametrize("out_f,in_f,N", [(256, 512, 1), (256, 512, 2), (300, 1024, 3), (17, 128, 7), (4096, 4096, 1),
                                           (11008, 4096, 1), (4096, 11008, 2), (513, 2048, 8), (64, 4096, 5),
                                           (256, 512, 9), (300, 1024, 12), (17, 128, 16), (4096, 4096, 16),
-                                          (4096, 11008, 8), (300, 11008, 12), (4096, 11008, 16), (77, 9856, 16)])
+                                          (4096, 11008, 8), (300, 11008, 12), (4096, 11008, 13), (77, 9856, 12)])
 def test_tc_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
     """The tensor-core GEMV (path 2), one and two 8-token tiles: ragged row
     blocks, index rows that are not a multiple of 128 bytes (128: 96-byte
@@ -158,9 +158,9 @@ def test_tc_gemv_vs_oracle(H, L, oracle, cuda, out_f, in_f, N):
     sidecar entries; within the bf16-weight bound of the oracle, and within
     1e-4 of a float64 product with the kernel's own weights (bf16 of each
     final weight).  Activations too wide for the staging (11008 from 8
-    tokens, 9856 at 16) run as K parts of whole 128-column windows, the
-    last one shorter (11008 at 16 tokens: 3712, 3712, 3584; 9856: 3328,
-    3328, 3200), whose partial products a second kernel adds."""
+    tokens, 9856 at 12) run as two K parts of whole 128-column windows, the
+    second one shorter where the windows are odd (9856: 4992, 4864), whose
+    partial products a second kernel adds."""
     d, W, xh, x = _case(oracle, out_f, in_f, N, out_f * 11 + in_f + N, dups=True)
     t = H.Tensor().load(d)
     img = _image(H, L, t, 0, out_f)
@@ -326,8 +326,9 @@ def test_batch_of_layer_projections(H, L, oracle, cuda, N):
     outputs each at a column offset: bit-identical to one call per image on
     the same path.  From 3 tokens the 11008-wide matrix's activations leave
     one CTA per SM, so the batch splits into two tensor-core launches; from
-    7 tokens that matrix runs as K parts added by a part-sum kernel (8
-    tokens: two, sharing the first launch; 16: three, in a second launch)."""
+    8 to 13 tokens that matrix runs as two K parts sharing the first launch,
+    added by a part-sum kernel; at 16 it would need three, so it takes the
+    GEMM."""
     torch = cuda
     shapes = [(512, 4096), (256, 4096), (384, 4096), (512, 4096), (1376, 4096), (1376, 4096), (512, 11008)]
     imgs, xs, refs, outs = [], [], [], []
@@ -441,18 +442,18 @@ def test_batch_chain_breaks_at_other_kernels(H, L, oracle, cuda):
 
 
 def test_vq_gemm_and_gemv_repeatable(H, L, cuda):
-    """VQ GEMM (2048 tokens) and tensor-core GEMV (1 and 16 tokens; at 16 the
-    11008-wide matrix in K parts) on two 7B-shaped images, repeated: every
-    run bit-identical to the first (their TMA stages are refilled only after
-    the reads of the previous fill are ordered; the parts are added in
-    order)."""
+    """VQ GEMM (16 and 2048 tokens) and tensor-core GEMV (1, 8 and 16
+    tokens; at 8 the 11008-wide matrix in two K parts) on two 7B-shaped
+    images, repeated: every run bit-identical to the first (their TMA stages
+    are refilled only after the reads of the previous fill are ordered; the
+    parts are added in order)."""
     torch = cuda
     from hxq_b200.sharded import ColumnSplitLayer
     mats = [dict(name="q", O=4096, I=4096, vq=synth.vq12(4096, 4096, 7200)),
             dict(name="down", O=4096, I=11008, vq=synth.vq12(4096, 11008, 7201))]
     layer = ColumnSplitLayer(mats, "vq12", max_tokens=2048, rank=0, world=1, torch=torch, lib=L)
     stream = torch.cuda.Stream()
-    for N in (1, 16, 2048):
+    for N in (1, 8, 16, 2048):
         xs = {I: torch.from_numpy(synth.activations(N, I, 7300 + I)[0].view(np.int16)).cuda() for I in (4096, 11008)}
         ref = None
         for _ in range(8):

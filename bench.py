@@ -678,8 +678,9 @@ def run_fused_matmul_workload(args):
 def run_kernel_cases(args):
     """One call each of the matmul kernels on a 4096 x 4096 matrix, for
     profiling: affine GEMV (1 token), VQ GEMV (1 token), VQ tcgen05 GEMM
-    (2048 tokens), affine tcgen05 GEMM (4096 tokens); bf16 activations.
-    Prints each call's device time (CUDA events, cold start)."""
+    (2048 tokens), affine tcgen05 GEMM (4096 tokens), VQ tcgen05 GEMM with
+    the small tile (64 tokens, split along K); bf16 activations.  Prints
+    each call's device time (CUDA events, cold start)."""
     import torch
 
     import hxq_b200 as H
@@ -695,12 +696,13 @@ def run_kernel_cases(args):
     t = H.Tensor().load(dv)
     img = C.c_void_p()
     H.check(L.hxq_cuda_image_create_ex(t.ref, 0, 4096, H.HXQ_IMAGE_MATMUL, C.byref(img)), "image")
-    xs = {n: torch.from_numpy(synth.activations(n, 4096, 11 + n)[0].view(np.int16)).cuda() for n in (1, 2048, 4096)}
+    xs = {n: torch.from_numpy(synth.activations(n, 4096, 11 + n)[0].view(np.int16)).cuda() for n in (1, 64, 2048, 4096)}
     y = torch.empty(4096 * 4096, dtype=torch.float32, device="cuda")
     cases = [("affine GEMV N=1", lambda: L.hxq_affine_group_matmul_bf16(xs[1].data_ptr(), C.byref(at), y.data_ptr(), 1, None)),
              ("vq12 GEMV N=1", lambda: L.hxq_cuda_vq_matmul(img, xs[1].data_ptr(), 1, y.data_ptr(), 4096, None)),
              ("vq12 GEMM N=2048", lambda: L.hxq_cuda_vq_matmul(img, xs[2048].data_ptr(), 2048, y.data_ptr(), 4096, None)),
-             ("affine GEMM N=4096", lambda: L.hxq_affine_group_matmul_bf16(xs[4096].data_ptr(), C.byref(at), y.data_ptr(), 4096, None))]
+             ("affine GEMM N=4096", lambda: L.hxq_affine_group_matmul_bf16(xs[4096].data_ptr(), C.byref(at), y.data_ptr(), 4096, None)),
+             ("vq12 GEMM N=64", lambda: L.hxq_cuda_vq_matmul(img, xs[64].data_ptr(), 64, y.data_ptr(), 4096, None))]
     out = []
     for name, fn in cases:
         torch.cuda.synchronize()

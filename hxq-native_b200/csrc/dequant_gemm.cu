@@ -352,11 +352,12 @@ struct Params {
     const float *bias;        // [O] or null
     // 12-bit VQ weights (an image with its matmul tables): rows of I*3/4
     // packed bytes; bf16 codebook pairs; sidecar patches (col | bf16 << 16)
-    // of row o from rb[o], those of K step kt from offset kp[o*(I/128+1)+kt]
+    // of row o from rb[o], those of half step hs (64 columns) from offset
+    // kq[o*(I/64)+hs] & 0xFFFF, kq[...] >> 16 of them
     const uint8_t *vidx;
     const uint32_t *cbh;
     const uint32_t *rb;
-    const uint16_t *kp;
+    const uint32_t *kq;
     const uint32_t *e4;
     // (tiles of 256 tokens) the same patches grouped per 32 rows and half
     // step: group g = (row / 32) * (I / 64) + col / 64 is g4[gp[g] ..
@@ -792,19 +793,21 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             // gathers exactly one TMEM column (low half = even k)
             for (uint32_t i = tid; i < codebook_bytes(BN) / 16u; i += kConvWarps * 32u)
                 reinterpret_cast<uint4 *>(cbh)[i] = __ldg(reinterpret_cast<const uint4 *>(p.cbh) + i);
-            // patches: those of step kt are [pb + kp[kt], pb + kp[kt + 1]) (kp of
-            // this row, from this CTA's first step).  The offsets kp[kt + j]
-            // sit in four slots, each refilled four steps ahead; the first
-            // four patches of a step in one of two sets, loaded two steps
-            // ahead.  The loop is unrolled by four so that the slots and sets
-            // are fixed registers: a register holding a load in flight is never
-            // copied (a copy would wait for the load).
-            const uint16_t *kpr = p.kp + (size_t)(valid ? o : 0u) * (KT_all + 1u) + kt_lo;
+            // patches: those of this thread's half of step kt are n entries
+            // from pb + lo, kq[2 kt + h] = lo | n << 16 (kq of this row,
+            // from this CTA's first step), so a warp walks only its own
+            // 64 columns' patches.  The entries sit in four slots, each
+            // refilled four steps ahead; the first four patches of a step in
+            // one of two sets, loaded two steps ahead.  The loop is unrolled
+            // by four so that the slots and sets are fixed registers: a
+            // register holding a load in flight is never copied (a copy
+            // would wait for the load).
+            const uint32_t *kqr = p.kq + (size_t)(valid ? o : 0u) * (2u * KT_all) + 2u * kt_lo + h;
             const uint32_t pb = valid ? __ldg(p.rb + o) : 0u;
-            auto kload = [&](uint32_t j) -> uint32_t { return valid && j <= KT ? (uint32_t)__ldg(kpr + j) : 0u; };
-            auto load4 = [&](uint32_t lo, uint32_t hi, uint32_t (&q)[4]) {
-                const uint32_t *src = p.e4 + pb + lo;
-                const uint32_t n = hi - lo;
+            auto kload = [&](uint32_t j) -> uint32_t { return valid && j < KT ? __ldg(kqr + 2u * j) : 0u; };
+            auto load4 = [&](uint32_t k, uint32_t (&q)[4]) {
+                const uint32_t *src = p.e4 + pb + (k & 0xFFFFu);
+                const uint32_t n = k >> 16;
                 q[0] = n > 0u ? __ldg(src) : 0u;
                 q[1] = n > 1u ? __ldg(src + 1) : 0u;
                 q[2] = n > 2u ? __ldg(src + 2) : 0u;
@@ -812,14 +815,13 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             };
             uint32_t kq0 = kload(0), kq1 = kload(1), kq2 = kload(2), kq3 = kload(3);
             uint32_t pa[4] = {0u, 0u, 0u, 0u}, pz[4] = {0u, 0u, 0u, 0u};
-            if (KT > 0) load4(kq0, kq1, pa);
-            if (KT > 1) load4(kq1, kq2, pz);
+            if (KT > 0) load4(kq0, pa);
+            if (KT > 1) load4(kq1, pz);
             asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
-            // one K step: k_lo = kp[kt] (its slot, refilled with kp[kt + 4]),
-            // k_hi, k_2, k_3 = kp[kt + 1 .. kt + 3]; P the step's first four
+            // one K step: k_lo = kq entry of step kt (its slot, refilled with
+            // step kt + 4's), k_2 step kt + 2's; P the step's first four
             // patches (refilled with those of step kt + 2); false if a wait ran out
-            auto step = [&](uint32_t kt, uint32_t &k_lo, uint32_t k_hi, uint32_t k_2, uint32_t k_3,
-                            uint32_t (&P)[4]) -> bool {
+            auto step = [&](uint32_t kt, uint32_t &k_lo, uint32_t k_2, uint32_t (&P)[4]) -> bool {
                 const uint32_t b = kt & 1u, sw = kt % W;
                 // 64 weights = 16 byte triples = 3 x 16 bytes of this thread's
                 // row of the weight ring stage (96 B per row)
@@ -833,7 +835,7 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (lane == 0) mbar_arrive(w_empty + sw);
                 const uint32_t w[12] = {cn[0].x, cn[0].y, cn[0].z, cn[0].w, cn[1].x, cn[1].y,
                                         cn[1].z, cn[1].w, cn[2].x, cn[2].y, cn[2].z, cn[2].w};
-                const uint32_t n_cur = k_hi - k_lo, lo_cur = k_lo;
+                const uint32_t n_cur = k_lo >> 16, lo_cur = k_lo & 0xFFFFu;
                 uint32_t v[32];
 #pragma unroll
                 for (uint32_t t = 0; t < 16u; ++t) {
@@ -861,15 +863,15 @@ dequant_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     asm volatile("tcgen05.fence::before_thread_sync;");
                     mbar_arrive(a_full + b);
                 }
-                if (kt + 2u < KT) load4(k_2, k_3, P);
+                if (kt + 2u < KT) load4(k_2, P);
                 k_lo = kload(kt + 4u);
                 return true;
             };
             for (uint32_t kt = 0; kt < KT && ok; kt += 4u) {
-                ok = step(kt, kq0, kq1, kq2, kq3, pa);
-                if (ok && kt + 1u < KT) ok = step(kt + 1u, kq1, kq2, kq3, kq0, pz);
-                if (ok && kt + 2u < KT) ok = step(kt + 2u, kq2, kq3, kq0, kq1, pa);
-                if (ok && kt + 3u < KT) ok = step(kt + 3u, kq3, kq0, kq1, kq2, pz);
+                ok = step(kt, kq0, kq2, pa);
+                if (ok && kt + 1u < KT) ok = step(kt + 1u, kq1, kq3, pz);
+                if (ok && kt + 2u < KT) ok = step(kt + 2u, kq2, kq0, pa);
+                if (ok && kt + 3u < KT) ok = step(kt + 3u, kq3, kq1, pz);
             }
         }
         // this half's accumulator columns; a 32-column load may read past
@@ -1280,7 +1282,7 @@ int affine_gemm_bf16(const uint16_t *x, const uint8_t *codes, const float *scale
 // [T, I], y fp32 [T, ldy].  Returns 1 when the shape is not one it takes, 0
 // on launch, -1 on error.
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
-                 const uint16_t *kp, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
+                 const uint32_t *kq, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
                  const uint16_t *tx, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O, uint32_t ldy,
                  cudaStream_t s)
 {
@@ -1290,7 +1292,7 @@ int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, con
     if ((uint64_t)T * I >= (1ull << 40)) return 1;
     gemm::Params p{};
     if (!g4 || !gp || !tx || ((uintptr_t)tx & 15u)) return 1;
-    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kp = kp; p.e4 = e4; p.g4 = g4; p.gp = gp; p.tx = tx;
+    p.vidx = idx; p.cbh = cbh; p.rb = rb; p.kq = kq; p.e4 = e4; p.g4 = g4; p.gp = gp; p.tx = tx;
     if (out.n == 0 || out.n > HXQ_CUDA_MAX_PEERS) return 1;
     p.T = T; p.I = I; p.O = O; p.gs = 0; p.ldy = ldy;
     return run<true>(x, p, out, s);

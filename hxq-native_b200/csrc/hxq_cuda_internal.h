@@ -179,7 +179,7 @@ struct GemmChainScope {
     GemmChainScope &operator=(const GemmChainScope &) = delete;
 };
 int vq_gemm_bf16(const uint16_t *x, const uint8_t *idx, const uint32_t *cbh, const uint32_t *rb,
-                 const uint16_t *kp, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
+                 const uint32_t *kq, const uint32_t *e4, const uint32_t *g4, const uint32_t *gp,
                  const uint16_t *tx, const OutPtrs &out, uint32_t T, uint32_t I, uint32_t O, uint32_t ldy,
                  cudaStream_t s);
 bool affine_gemm_fits(const uint16_t *x, const uint8_t *codes, uint32_t T, uint32_t I, uint32_t O, uint32_t gs);

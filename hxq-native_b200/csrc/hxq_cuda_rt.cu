@@ -59,17 +59,18 @@ struct hxq_cuda_image {
     float     ref_l2 = 0.0f;   // sqrtf of the fp32 running sum in array order
     float     ref_l2_tensor = 0.0f;  // the same over every row of the tensor
     // fused-matmul extras (12-bit, k = 4096, in_features % 128 == 0): bf16
-    // codebook pairs; per row the first patch; per (row, 128-wide K step)
-    // the 16-bit offset of its first patch from the row's; patches
+    // codebook pairs; per row the first patch; per (row, 64-wide half K
+    // step) the 16-bit offset of its first patch from the row's | its patch
+    // count << 16; patches
     // col | bf16(final weight) << 16, one per distinct sidecar position
     // and per patch bf16(final weight) - bf16(codebook value) in fp32
     bool      has_mm = false;
     // and the tensor-core GEMV's own index stream (build_tc_stream)
     // and the same patches grouped per 32 rows and 64-wide half step for
     // the tcgen05 GEMM's 256-token tiles (build_patches)
-    size_t    o_cbh = 0, o_rb = 0, o_kp = 0, o_e4 = 0, o_ed = 0, o_tx = 0, o_g4 = 0, o_gp = 0;
-    uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_e4 = nullptr, *d_g4 = nullptr, *d_gp = nullptr;
-    uint16_t *d_kp = nullptr, *d_tx = nullptr;
+    size_t    o_cbh = 0, o_rb = 0, o_kq = 0, o_e4 = 0, o_ed = 0, o_tx = 0, o_g4 = 0, o_gp = 0;
+    uint32_t *d_cbh = nullptr, *d_rb = nullptr, *d_kq = nullptr, *d_e4 = nullptr, *d_g4 = nullptr, *d_gp = nullptr;
+    uint16_t *d_tx = nullptr;
     float    *d_ed = nullptr;
     uint32_t  n_patch = 0;
 };
@@ -309,7 +310,7 @@ void bind_image(hxq_cuda_image *img, void *base)
     if (img->has_mm) {
         img->d_cbh = reinterpret_cast<uint32_t *>(b + img->o_cbh);
         img->d_rb = reinterpret_cast<uint32_t *>(b + img->o_rb);
-        img->d_kp = reinterpret_cast<uint16_t *>(b + img->o_kp);
+        img->d_kq = reinterpret_cast<uint32_t *>(b + img->o_kq);
         img->d_e4 = reinterpret_cast<uint32_t *>(b + img->o_e4);
         img->d_ed = reinterpret_cast<float *>(b + img->o_ed);
         img->d_tx = reinterpret_cast<uint16_t *>(b + img->o_tx);
@@ -341,15 +342,16 @@ float bf16_to_float(uint32_t h)
 // The fused matmuls' patch tables (see hxq_cuda_image): per distinct
 // sidecar position of rows [0, rows) col | bf16(final weight) << 16 (e4, rows
 // in order) and bf16(final) - bf16(codebook value) (ed); per row its first
-// entry (rb); per (row, 128-wide K step) the offset of the step's first
-// entry from the row's (kp); and the same entries grouped per 32 rows and
+// entry (rb); per (row, 64-wide half K step) the offset of the half step's
+// first entry from the row's | its entry count << 16 (kq); and the same
+// entries grouped per 32 rows and
 // 64-wide half step for the tcgen05 GEMM's 256-token tiles (a converter
 // warp's rows and half of a K step): group g = (row / 32) * (in_f / 64) +
 // col / 64 holds g4[gp[g] .. gp[g + 1]), each (row % 32) << 22 | (col % 64)
 // << 16 | bf16(final).
 bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows, uint32_t in_f,
                    const std::vector<HostEntry> &ents, std::vector<uint32_t> &cbh,
-                   std::vector<uint32_t> &rb, std::vector<uint16_t> &kp, std::vector<uint32_t> &e4,
+                   std::vector<uint32_t> &rb, std::vector<uint32_t> &kq, std::vector<uint32_t> &e4,
                    std::vector<float> &ed, std::vector<uint32_t> &g4, std::vector<uint32_t> &gp)
 {
     const uint32_t KT = in_f / 128u;
@@ -374,18 +376,17 @@ bool build_patches(const hxq_tensor_t *t, const uint8_t *idx_rows, uint32_t rows
         erow.push_back(r);
     }
     rb.assign(rows, 0u);
-    kp.assign((size_t)rows * (KT + 1u), 0u);
+    kq.assign((size_t)rows * 2u * KT, 0u);
     size_t e = 0;
     for (uint32_t r = 0; r < rows; ++r) {
         while (e < e4.size() && erow[e] < r) ++e;
         rb[r] = (uint32_t)e;
         size_t f = e;
-        for (uint32_t kt = 0; kt <= KT; ++kt) {
-            while (f < e4.size() && erow[f] == r && (e4[f] & 0xFFFFu) < kt * 128u) ++f;
-            if (kt == KT)
-                while (f < e4.size() && erow[f] == r) ++f;
-            if (f - e > 0xFFFFu) return false;
-            kp[(size_t)r * (KT + 1u) + kt] = (uint16_t)(f - e);
+        for (uint32_t hs = 0; hs < 2u * KT; ++hs) {
+            const size_t f0 = f;
+            while (f < e4.size() && erow[f] == r && (e4[f] & 0xFFFFu) < (hs + 1u) * 64u) ++f;
+            if (f0 - e > 0xFFFFu) return false;
+            kq[(size_t)r * 2u * KT + hs] = (uint32_t)(f0 - e) | ((uint32_t)(f - f0) << 16);
         }
     }
     const uint32_t NH = in_f / 64u;
@@ -636,13 +637,13 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     }
     img->n_ent = (uint32_t)dev_ents.size();
 
-    std::vector<uint32_t> mm_cbh, mm_rb, mm_e4, mm_g4, mm_gp;
-    std::vector<uint16_t> mm_kp, mm_tx;
+    std::vector<uint32_t> mm_cbh, mm_rb, mm_kq, mm_e4, mm_g4, mm_gp;
+    std::vector<uint16_t> mm_tx;
     std::vector<float> mm_ed;
     if (matmul && img->kind == kKindVq12 && !img->check_k && img->k == 4096u && img->in_f % 128u == 0u &&
         img->in_f <= 65536u)
         img->has_mm = build_patches(t, t->indices_raw + idx_off, img->rows, img->in_f, ents, mm_cbh, mm_rb,
-                                    mm_kp, mm_e4, mm_ed, mm_g4, mm_gp);
+                                    mm_kq, mm_e4, mm_ed, mm_g4, mm_gp);
     if (img->has_mm) build_tc_stream(t->indices_raw + idx_off, img->rows, img->in_f, mm_tx);
     img->n_patch = (uint32_t)mm_e4.size();
 
@@ -663,7 +664,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     if (img->has_mm) {
         img->o_cbh = off;  off = align256(off + mm_cbh.size() * 4);
         img->o_rb = off;   off = align256(off + std::max<size_t>(mm_rb.size(), 1) * 4);
-        img->o_kp = off;   off = align256(off + mm_kp.size() * 2);
+        img->o_kq = off;   off = align256(off + std::max<size_t>(mm_kq.size(), 1) * 4);
         img->o_e4 = off;   off = align256(off + (mm_e4.size() + 4) * 4);   // + speculative-read slack
         img->o_ed = off;   off = align256(off + std::max<size_t>(mm_ed.size(), 1) * 4);
         img->o_tx = off;   off = align256(off + std::max<size_t>(mm_tx.size(), 8) * 2);
@@ -696,7 +697,7 @@ hxq_error_t build_image(const hxq_tensor_t *t, uint32_t r0, uint32_t r1, int dev
     if (img->has_mm) {
         std::memcpy(hb + img->o_cbh, mm_cbh.data(), mm_cbh.size() * 4);
         if (!mm_rb.empty()) std::memcpy(hb + img->o_rb, mm_rb.data(), mm_rb.size() * 4);
-        std::memcpy(hb + img->o_kp, mm_kp.data(), mm_kp.size() * 2);
+        if (!mm_kq.empty()) std::memcpy(hb + img->o_kq, mm_kq.data(), mm_kq.size() * 4);
         if (!mm_e4.empty()) std::memcpy(hb + img->o_e4, mm_e4.data(), mm_e4.size() * 4);
         if (!mm_ed.empty()) std::memcpy(hb + img->o_ed, mm_ed.data(), mm_ed.size() * 4);
         if (!mm_tx.empty()) std::memcpy(hb + img->o_tx, mm_tx.data(), mm_tx.size() * 2);
@@ -1301,7 +1302,7 @@ hxq_error_t vq_matmul(const hxq_cuda_image_t *img, const uint16_t *d_x_bf16, uin
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
         g_launches.fetch_add(nl - 1u, std::memory_order_relaxed);   // the part sums, if any
     } else if (path == 1) {
-        const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kp, img->d_e4,
+        const int r = hxq::vq_gemm_bf16(d_x_bf16, img->d_idx, img->d_cbh, img->d_rb, img->d_kq, img->d_e4,
                                         img->d_g4, img->d_gp, img->d_tx, out, N, img->in_f, img->rows, ldy, s);
         if (r != 0) { cudaGetLastError(); return r > 0 ? HXQ_ERR_INVALID_ARG : HXQ_ERR_CUDA; }
     } else {

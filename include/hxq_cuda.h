@@ -245,8 +245,10 @@ int hxq_cuda_affine_device_status(void);
  * (HXQ_ERR_INVALID_ARG otherwise), resident or uploaded.  d_x: bf16 bit
  * patterns [N, in_features], 16-byte aligned; d_y: fp32, ldy >= rows.
  *   - Images with the matmul tables (HXQ_IMAGE_MATMUL), up to
- *     HXQ_VQ_MATMUL_TC_MAX tokens: the tensor-core GEMV; more tokens: the
- *     tcgen05 dequant-GEMM.  Both use each weight rounded to bf16 (the bf16
+ *     HXQ_VQ_MATMUL_TC_MAX tokens: the tensor-core GEMV, where the
+ *     activations fit its shared memory whole or in two K parts
+ *     (in_features 11008: up to 13 tokens); otherwise, and for more tokens:
+ *     the tcgen05 dequant-GEMM.  Both use each weight rounded to bf16 (the bf16
  *     codebook pair, or bf16 of the sidecar-corrected weight):
  *     |error| <= 2^-9 sum_i |x_i w_i| per output, fp32 accumulation.
  *   - Images without the tables: the fused GEMV with exact fp32 weights

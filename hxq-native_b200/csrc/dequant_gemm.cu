@@ -1200,7 +1200,12 @@ int run(const uint16_t *x, gemm::Params p, const OutPtrs &out, cudaStream_t s)
     uint32_t splits = 1;
     if (tiles < resident) {
         splits = resident / tiles;                 // one wave: tiles * splits <= resident
-        if (splits > KT / 2u) splits = KT / 2u;  // keep at least two K steps per CTA
+        // at least two K steps per CTA; eight for the affine converters,
+        // which reach the split's one-wave time with fewer, longer ranges
+        // (4096 x 4096 at 64 / 128 tokens: 4 ranges 15.7 / 19.4 us, 9 ranges
+        // 16.5 / 21.3), where the VQ converters want every resident CTA
+        const uint32_t min_steps = VQ ? 2u : 8u;
+        if (splits > KT / min_steps) splits = KT / min_steps;
         if (splits > 16u) splits = 16u;
         if (splits < 1u) splits = 1u;
     }
